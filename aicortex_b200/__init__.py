@@ -1,0 +1,13 @@
+"""B200 (sm_100a) implementation of the AICortex inference hot path.
+
+The compute lives in libaicortex_b200.so (CUDA kernels + C ABI declared in
+include/aicortex.h); this package binds it with ctypes and mirrors the
+reference's layer classes. Importing the package fails if the library is not
+built: there is no fallback path.
+"""
+from ._lib import AicError, lib  # noqa: F401  (fails loudly when the .so is missing)
+from .layers import (ConvBlock, ConvLayer, Cortex, Critic, MambaBlock, MambaLayer, empty_f, gap, gap_f16,  # noqa: F401
+                     pack_f32, residual_add, set_actions, stem_pack)
+
+__all__ = ["AicError", "ConvBlock", "ConvLayer", "Cortex", "Critic", "MambaBlock", "MambaLayer", "empty_f", "gap",
+           "gap_f16", "pack_f32", "residual_add", "set_actions", "stem_pack"]

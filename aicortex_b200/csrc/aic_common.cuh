@@ -1,0 +1,100 @@
+// Device-side primitives of the packed int4 format used on the whole
+// inference path, plus launch/error plumbing shared by the kernels.
+//
+// Format ("F", AICortex kernels.h:56-85): a group is 32 signed 4-bit codes in
+// four little-endian u32 words (code i sits in word i>>3 at bits 4*(i&7)) and
+// one int8 exponent s. The value of code q is q * max(2^s / 7, 2^-13).
+// Activations are NHWC: position p, group g -> words [p*C/8 + 4g .. +3] and
+// exponent [p*C/32 + g].
+//
+// The quantisation rules (absmax -> stored exponent rn(log2 absmax) clamped to
+// +-120, codes rn(v * 7 / absmax) clamped to [-8, 7], absmax < 2^-13 treated
+// as 1) are the reference's; they are restated here because parity with packed
+// weights and activations produced by the reference must be bit-exact.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace aic {
+
+constexpr float kEps = 1.0f / 8192.0f;   // kernels.h: epsilon (base_constants.h:33)
+constexpr float kQMax = 7.0f;            // quant_int4_max
+constexpr float kScaleMin = -120.0f;     // quant_scale_min
+constexpr float kScaleMax = 120.0f;      // quant_scale_max
+constexpr int kNormChunk = 256;          // RMSNorm chunk of the quantized convs and out-proj
+
+// Sign-extended code e (0..7) of a packed word.
+__device__ __forceinline__ int code_of(uint32_t w, int e)
+{
+    int r;
+    asm("bfe.s32 %0, %1, %2, 4;" : "=r"(r) : "r"(w), "r"(e << 2));
+    return r;
+}
+
+// Stored exponent of a group whose (clamped) absmax is `scale`.
+__device__ __forceinline__ int8_t exponent_of(float scale)
+{
+    return static_cast<int8_t>(__float2int_rn(fmaxf(kScaleMin, fminf(kScaleMax, __log2f(scale)))));
+}
+
+// Dequantisation factor max(2^s/7, 2^-13).
+__device__ __forceinline__ float unit_of(int8_t s)
+{
+    return fmaxf(exp2f(static_cast<float>(s)) * (1.0f / kQMax), kEps);
+}
+
+// Code of value v given inv = 7 / absmax, round to nearest even.
+__device__ __forceinline__ uint32_t code_rn(float v, float inv)
+{
+    return static_cast<uint32_t>(max(-8, min(7, __float2int_rn(v * inv)))) & 0xFu;
+}
+
+// Exact sum over 8 code pairs of qa*qb. Each nibble is moved to the top of
+// its byte (16*q as a signed byte) so one dp4a covers four pairs; the two
+// partial dot products carry a factor 256 that is shifted out exactly.
+__device__ __forceinline__ int dot8(uint32_t a, uint32_t b)
+{
+    const int hi = __dp4a(static_cast<int>(a & 0xF0F0F0F0u), static_cast<int>(b & 0xF0F0F0F0u), 0);
+    const int lo = __dp4a(static_cast<int>((a << 4) & 0xF0F0F0F0u), static_cast<int>((b << 4) & 0xF0F0F0F0u), hi);
+    return lo >> 8;
+}
+
+__device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
+// Quantise 32 values held as 8 per lane across 4 consecutive lanes (lane & 3
+// selects the word). Returns this lane's packed word; *exp_out gets the
+// exponent on every lane.
+__device__ __forceinline__ uint32_t quantize_word_x4(const float (&v)[8], int8_t* exp_out)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    const float scale = amax < kEps ? 1.0f : amax;
+    const float inv = kQMax * __frcp_rn(scale);
+    uint32_t w = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w |= code_rn(v[i], inv) << (i << 2);
+    *exp_out = exponent_of(scale);
+    return w;
+}
+
+// Quantise 32 values held by one thread into 4 words + exponent.
+__device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* words, int8_t* exp_out)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float scale = amax < kEps ? 1.0f : amax;
+    const float inv = kQMax * __frcp_rn(scale);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn(v[i], inv) << ((i & 7) << 2);
+    *words = make_uint4(w[0], w[1], w[2], w[3]);
+    *exp_out = exponent_of(scale);
+}
+
+}  // namespace aic

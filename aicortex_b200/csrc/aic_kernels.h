@@ -1,0 +1,70 @@
+// Host-side launchers for the CUDA kernels of the inference path. Every
+// launcher is asynchronous on `stream`, validates nothing beyond what it needs
+// to size its grid (the C-ABI layer validates arguments) and returns the
+// launch status.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+namespace aic {
+
+// A1: fp32 [n] -> packed int4 groups (n % 32 == 0). stochastic != 0 selects
+// the weight packer (position hash seeded with add_idx). The hash uses the
+// group index modulo row_groups (0 = no wrap) as the reference's thread index,
+// so a batch of rows packs each row as one reference call would.
+cudaError_t launch_pack_f32(const float* in, int64_t n, uint32_t* out, int8_t* out_s, bool stochastic,
+                            int32_t add_idx, int64_t row_groups, cudaStream_t stream);
+
+// A2: fp16 planes [frames][planes][dim][dim] (channels >= planes are zero)
+// -> NHWC packed int4 [frames*dim*dim][channels].
+cudaError_t launch_stem_pack(const __half* planes, int64_t frames, int planes_present, int channels, int dim,
+                             uint32_t* out, int8_t* out_s, cudaStream_t stream);
+
+// A5: depthwise k x k conv (k in {3,5,7}), stride 1/2, pad k/2, + bias, requant.
+cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
+                           const float* bias, uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize,
+                           int stride, int Din, int Dout, cudaStream_t stream);
+
+// A3/A4 on CUDA cores: quantized conv (pointwise when ksize == 1) with the fused
+// RMSNorm(256-chunk) + bias (+SiLU) + requant epilogue; reproduces the
+// reference accumulation order exactly.
+cudaError_t launch_conv_gemm_simt(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
+                                  const float* bias, uint32_t* out, int8_t* out_s, int64_t frames, int InC,
+                                  int OutC, int ksize, int stride, int Din, int Dout, bool act, cudaStream_t stream);
+
+// A6: out = requant(q_main * s_main * main_mult + q_res * s_res), one exponent per position.
+cudaError_t launch_residual(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res, const int8_t* res_s,
+                            uint32_t* out, int8_t* out_s, int64_t positions, int C, float main_mult, bool skipped,
+                            cudaStream_t stream);
+
+// A8: global average pool of [frames][HW][C] -> fp32 [frames][C] (optional)
+// and round-to-nearest packed int4 [frames][C] (optional).
+cudaError_t launch_gap(const uint32_t* in, const int8_t* in_s, int64_t frames, int HW, int C, float* out_f32,
+                       uint32_t* out_q, int8_t* out_qs, cudaStream_t stream);
+// gapKernel<__half> semantics: fp16 [frames][C].
+cudaError_t launch_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frames, int HW, int C, __half* out,
+                           cudaStream_t stream);
+
+// A9: batched, time-looped SSM scan. x: F [B*T][D] (row b*T+t); consts: per
+// channel prepared constants; h: [B][E][P] float2 in/out; y: [B*T][E].
+cudaError_t launch_ssm_prepare(const uint32_t* blob, const int8_t* blob_s, int D, int d_state, float* consts,
+                               cudaStream_t stream);
+size_t ssm_consts_floats(int D, int d_state);
+cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
+                            const float* consts, int D, int d_state, float2* h, float* y, int B, int T,
+                            cudaStream_t stream);
+
+// A10: out-projection GEMM y[rows][E] x W_out -> RMSNorm(256-chunk) + bias + act -> fp32 [rows][out].
+cudaError_t launch_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s, const float* bias, int D,
+                           int d_state, int out, int act, int64_t rows, float* o, cudaStream_t stream);
+
+// A13: critic recurrence over T for B sequences; x fp16 [B*T][in].
+cudaError_t launch_critic(const __half* x, const float* w1, const float* wl, const float* w2, int in, int units,
+                          float2* h, float2* h_seq, float* score, int B, int T, cudaStream_t stream);
+
+// A12: Bernoulli action bits, [rows][A] probabilities -> [rows][(A+63)/64] words.
+cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned long long* actions,
+                               cudaStream_t stream);
+
+}  // namespace aic

@@ -1,0 +1,1255 @@
+// C++ layer classes of the inference path and the extern "C" boundary
+// declared in include/aicortex.h.
+//
+// The classes keep the reference's ownership model: a layer owns no memory,
+// reports the bytes it needs, and is bound to caller-owned device memory
+// (ConvLayer ctor/initData, conv_layer.h:45-101; MambaLayer,
+// mamba_layer.h:54-138; Critic, critic.h:58-105). forward() gains batch and
+// sequence extents; the kernels it launches are in k_*.cu.
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+#include "aicortex.h"
+
+namespace aic {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Failure {
+    aic_status code;
+    std::string msg;
+};
+
+[[noreturn]] void fail(aic_status code, const std::string& msg) { throw Failure{code, msg}; }
+void require(bool ok, const std::string& msg)
+{
+    if (!ok) fail(AIC_ERR_INVALID, msg);
+}
+void cuda_ok(cudaError_t e, const char* what)
+{
+    if (e != cudaSuccess) fail(AIC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+bool aligned256(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 255u) == 0; }
+bool is_pow2(int v) { return v > 0 && (v & (v - 1)) == 0; }
+
+template <class F>
+aic_status guarded(F&& f)
+{
+    try {
+        f();
+        return AIC_OK;
+    } catch (const Failure& e) {
+        g_last_error = e.msg;
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return AIC_ERR_INVALID;
+    } catch (...) {
+        g_last_error = "unknown error";
+        return AIC_ERR_INVALID;
+    }
+}
+
+// Sequential 256-byte aligned carve of a caller arena. With base == nullptr it
+// only counts, so sizing and binding share one code path.
+struct Carver {
+    char* base;
+    size_t off = 0;
+    explicit Carver(void* b) : base(static_cast<char*>(b)) {}
+    template <class T>
+    T* take(size_t count)
+    {
+        off = (off + 255) & ~static_cast<size_t>(255);
+        T* p = base ? reinterpret_cast<T*>(base + off) : nullptr;
+        off += count * sizeof(T);
+        return p;
+    }
+    size_t bytes() const { return (off + 255) & ~static_cast<size_t>(255); }
+};
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Host staging of fp32 checkpoint data in mapped pinned memory, which the
+// packer reads directly, as the reference keeps its master weights
+// (uv.h:122, conv_layer.h:80-82). The file is read and checked before any
+// CUDA call, so a missing or short file fails without touching the device.
+struct MappedHost {
+    float* host = nullptr;
+    float* dev = nullptr;
+    explicit MappedHost(const std::vector<float>& src)
+    {
+        cuda_ok(cudaHostAlloc(reinterpret_cast<void**>(&host), src.size() * sizeof(float), cudaHostAllocMapped),
+                "cudaHostAlloc");
+        cuda_ok(cudaHostGetDevicePointer(reinterpret_cast<void**>(&dev), host, 0), "cudaHostGetDevicePointer");
+        std::memcpy(host, src.data(), src.size() * sizeof(float));
+    }
+    ~MappedHost()
+    {
+        if (host) cudaFreeHost(host);
+    }
+    MappedHost(const MappedHost&) = delete;
+    MappedHost& operator=(const MappedHost&) = delete;
+};
+
+// Reads sum(counts) little-endian floats; a missing or short file is an error
+// (the reference reads short files silently, conv_layer.h:37-38).
+std::vector<float> read_floats(const char* path, const std::vector<size_t>& counts)
+{
+    require(path != nullptr, "null path");
+    size_t total = 0;
+    for (size_t c : counts) total += c;
+    std::vector<float> out(total);
+    FILE* f = std::fopen(path, "rb");
+    if (!f) fail(AIC_ERR_IO, std::string("cannot open ") + path);
+    const size_t got = std::fread(out.data(), sizeof(float), total, f);
+    std::fclose(f);
+    if (got != total) fail(AIC_ERR_IO, std::string("short read in ") + path);
+    return out;
+}
+
+std::string join(const char* dir, const char* name)
+{
+    require(dir != nullptr, "null directory");
+    std::string d(dir);
+    if (!d.empty() && d.back() != '/') d.push_back('/');
+    return d + name;
+}
+
+// ---------------------------------------------------------------- ConvLayer
+struct ConvLayer {
+    aic_conv_layer_desc d;
+    bool is_dw;
+    int64_t weight_elems, groups;
+    uint32_t* w = nullptr;
+    int8_t* ws = nullptr;
+    float* bias = nullptr;
+    bool bound = false;
+
+    explicit ConvLayer(const aic_conv_layer_desc& desc) : d(desc)
+    {
+        require(d.in_channels > 0 && d.out_channels > 0 && d.in_channels % 32 == 0 && d.out_channels % 32 == 0,
+                "conv channels must be positive multiples of 32");
+        require(d.kernel_size >= 1 && d.stride >= 1 && d.dim_in >= 1 && d.dim_out >= 1, "bad conv geometry");
+        is_dw = d.kernel_size > 1 && (d.kernel_size & 1) == 1;  // conv_layer.h:49
+        if (is_dw) {
+            if (d.kernel_size != 3 && d.kernel_size != 5 && d.kernel_size != 7)
+                fail(AIC_ERR_UNSUPPORTED, "depthwise kernel size must be 3, 5 or 7");
+            require(d.in_channels == d.out_channels, "depthwise conv needs in == out channels");
+            require(is_pow2(d.dim_out), "depthwise output dimension must be a power of two");
+            require(d.dim_out == (d.dim_in - 1) / d.stride + 1, "depthwise output dimension mismatch");
+        } else if (d.kernel_size == 1) {
+            require(d.stride == 1 && d.dim_in == d.dim_out, "pointwise conv keeps the dimension");
+        } else {
+            if (d.kernel_size != 2 && d.kernel_size != 4) fail(AIC_ERR_UNSUPPORTED, "dense kernel size must be 2 or 4");
+            require(d.stride == d.kernel_size, "dense conv is supported with stride == kernel size");
+            require(is_pow2(d.dim_out) && d.dim_in == d.dim_out * d.stride, "dense conv dimension mismatch");
+        }
+        weight_elems = static_cast<int64_t>(d.in_channels) * d.kernel_size * d.kernel_size * (is_dw ? 1 : d.out_channels);
+        groups = weight_elems >> 5;
+    }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        w = c.take<uint32_t>(groups * 4);
+        ws = c.take<int8_t>(groups);
+        bias = c.take<float>(d.out_channels);
+        return c.bytes();
+    }
+    void check_bound() const
+    {
+        if (!bound) fail(AIC_ERR_STATE, "conv layer parameters not bound");
+    }
+    void load(const float* master, const float* b, cudaStream_t s)
+    {
+        check_bound();
+        require(master != nullptr && b != nullptr, "null weights");
+        cuda_ok(launch_pack_f32(master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s), "pack weights");
+        cuda_ok(cudaMemcpyAsync(bias, b, sizeof(float) * d.out_channels, cudaMemcpyDefault, s), "copy bias");
+    }
+    void load_file(const char* path, cudaStream_t s)
+    {
+        check_bound();
+        MappedHost h(read_floats(path, {static_cast<size_t>(weight_elems), static_cast<size_t>(d.out_channels)}));
+        load(h.dev, h.dev + weight_elems, s);
+        cuda_ok(cudaStreamSynchronize(s), "load sync");
+    }
+    int64_t forward(const uint32_t* in, const int8_t* in_s, uint32_t* out, int8_t* out_s, int64_t frames, cudaStream_t s)
+    {
+        check_bound();
+        if (frames == 0) return 0;
+        require(in && in_s && out && out_s, "null tensor");
+        if (is_dw)
+            cuda_ok(launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+                                   d.dim_in, d.dim_out, s),
+                    "conv_dw");
+        else
+            cuda_ok(launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                          d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s),
+                    "conv_gemm");
+        return 1;
+    }
+};
+
+// ---------------------------------------------------------------- ConvBlock
+struct ConvBlock {
+    aic_conv_block_desc d;
+    std::unique_ptr<ConvLayer> layers[4];
+    int final_stride;
+
+    explicit ConvBlock(const aic_conv_block_desc& desc) : d(desc)
+    {
+        require(d.survival_probability > 0.0f, "survival probability must be positive");
+        final_stride = d.dim_in == d.dim_out ? 1 : d.stride;  // conv_block.h:47
+        // conv_block.h:52-55
+        layers[0].reset(new ConvLayer({d.in_channels, d.in_channels, d.dw_kernel, final_stride, d.dim_in, d.dim_out, 1}));
+        layers[1].reset(new ConvLayer({d.in_channels, d.mid_channels, 1, 1, d.dim_out, d.dim_out, 0}));
+        layers[2].reset(new ConvLayer({d.mid_channels, d.out_channels, 1, 1, d.dim_out, d.dim_out, 1}));
+        layers[3].reset(new ConvLayer({d.in_channels, d.out_channels, final_stride, final_stride, d.dim_in, d.dim_out, 1}));
+    }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        for (auto& l : layers) {
+            char* p = c.take<char>(l->carve(nullptr));
+            l->carve(p);
+            if (base) l->bound = true;
+        }
+        return c.bytes();
+    }
+    int64_t buffer_words(int64_t frames) const
+    {
+        const int cmax = std::max(d.in_channels, std::max(d.mid_channels, d.out_channels));
+        return frames * d.dim_out * d.dim_out * (cmax >> 3);
+    }
+    size_t workspace(int64_t frames, void* base, uint32_t** a, int8_t** as, uint32_t** b, int8_t** bs) const
+    {
+        Carver c(base);
+        const int64_t words = buffer_words(frames);
+        uint32_t* pa = c.take<uint32_t>(words);
+        int8_t* pas = c.take<int8_t>(words / 4);
+        uint32_t* pb = c.take<uint32_t>(words);
+        int8_t* pbs = c.take<int8_t>(words / 4);
+        if (a) { *a = pa; *as = pas; *b = pb; *bs = pbs; }
+        return c.bytes();
+    }
+    int64_t forward(const uint32_t* in, const int8_t* in_s, uint32_t* out, int8_t* out_s, int64_t frames, bool train,
+                    bool survived, void* ws, cudaStream_t s)
+    {
+        if (frames == 0) return 0;
+        require(ws != nullptr && aligned256(ws), "block workspace must be 256-byte aligned");
+        uint32_t *a, *b;
+        int8_t *as, *bs;
+        workspace(frames, ws, &a, &as, &b, &bs);
+        int64_t n = 0;
+        n += layers[0]->forward(in, in_s, a, as, frames, s);
+        n += layers[1]->forward(a, as, b, bs, frames, s);
+        n += layers[2]->forward(b, bs, a, as, frames, s);
+        n += layers[3]->forward(in, in_s, b, bs, frames, s);
+        const float surv_inv = 1.0f / d.survival_probability;
+        const float main_mult = d.residual_factor * (train && survived ? surv_inv : 1.0f);
+        cuda_ok(launch_residual(a, as, b, bs, out, out_s, frames * d.dim_out * d.dim_out, d.out_channels, main_mult,
+                                train && !survived, s),
+                "residual");
+        return n + 1;
+    }
+};
+
+// ---------------------------------------------------------------- MambaLayer
+struct MambaLayer {
+    aic_mamba_layer_desc d;
+    int E, P;
+    int64_t weight_elems, groups;
+    uint32_t* w = nullptr;
+    int8_t* ws = nullptr;
+    float* bias = nullptr;
+    float* consts = nullptr;
+    float2* h = nullptr;
+    int batch_bound = -1;
+    bool bound = false;
+
+    explicit MambaLayer(const aic_mamba_layer_desc& desc) : d(desc)
+    {
+        require(is_pow2(d.d_model) && d.d_model >= 32, "d_model must be a power of two >= 32");
+        if (d.d_state < 32 || d.d_state % 32 != 0)
+            fail(AIC_ERR_UNSUPPORTED, "d_state must be a positive multiple of 32 (reference kernels.h:1089)");
+        if (d.d_state / 32 > 16) fail(AIC_ERR_UNSUPPORTED, "at most 16 states per channel (d_state <= 512)");
+        require(!((d.d_state / 32) & (d.d_state / 32 - 1)), "d_state/32 must be a power of two");
+        require(d.out_channels >= 1 && d.out_channels % 32 == 0, "out channels must be a multiple of 32");
+        require(d.activation >= 0 && d.activation <= 2, "activation must be 0, 1 or 2");
+        E = 2 * d.d_model;
+        P = d.d_state / 32;
+        weight_elems = static_cast<int64_t>(E) * (2 + 32 + 4LL * d.d_state + d.out_channels);  // mamba_layer.h:58
+        groups = weight_elems >> 5;
+    }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        w = c.take<uint32_t>(groups * 4);
+        ws = c.take<int8_t>(groups);
+        bias = c.take<float>(d.out_channels);
+        consts = c.take<float>(ssm_consts_floats(d.d_model, d.d_state));
+        return c.bytes();
+    }
+    size_t state_bytes(int batch) const { return static_cast<size_t>(batch) * E * P * sizeof(float2); }
+    void check_bound() const
+    {
+        if (!bound) fail(AIC_ERR_STATE, "mamba layer parameters not bound");
+    }
+    void load(const float* master, const float* b, cudaStream_t s)
+    {
+        check_bound();
+        require(master != nullptr && b != nullptr, "null weights");
+        cuda_ok(launch_pack_f32(master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s), "pack blob");
+        cuda_ok(cudaMemcpyAsync(bias, b, sizeof(float) * d.out_channels, cudaMemcpyDefault, s), "copy bias");
+        cuda_ok(launch_ssm_prepare(w, ws, d.d_model, d.d_state, consts, s), "ssm prepare");
+    }
+    void load_file(const char* path, cudaStream_t s)
+    {
+        check_bound();
+        MappedHost m(read_floats(path, {static_cast<size_t>(weight_elems), static_cast<size_t>(d.out_channels)}));
+        load(m.dev, m.dev + weight_elems, s);
+        cuda_ok(cudaStreamSynchronize(s), "load sync");
+    }
+    void reset(cudaStream_t s)
+    {
+        if (batch_bound < 0) fail(AIC_ERR_STATE, "mamba state not bound");
+        cuda_ok(cudaMemsetAsync(h, 0, state_bytes(batch_bound), s), "reset state");
+    }
+    size_t workspace_bytes(int64_t rows) const { return ((static_cast<size_t>(rows) * E * sizeof(float)) + 255) & ~size_t(255); }
+    int64_t forward(const uint32_t* in, const int8_t* in_s, float* out, int batch, int seq, void* wsp, cudaStream_t s)
+    {
+        check_bound();
+        if (batch_bound < 0) fail(AIC_ERR_STATE, "mamba state not bound");
+        require(batch == batch_bound, "batch differs from the bound state's batch");
+        require(seq >= 0, "negative sequence length");
+        if (seq == 0 || batch == 0) return 0;
+        require(in && in_s && out && wsp && aligned256(wsp), "null or misaligned tensor");
+        float* y = static_cast<float*>(wsp);
+        cuda_ok(launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, y, batch, seq, s), "ssm scan");
+        cuda_ok(launch_outproj(y, w, ws, bias, d.d_model, d.d_state, d.out_channels, d.activation,
+                               static_cast<int64_t>(batch) * seq, out, s),
+                "outproj");
+        return 2;
+    }
+};
+
+// ---------------------------------------------------------------- MambaBlock
+struct MambaBlock {
+    aic_mamba_block_desc d;
+    std::unique_ptr<MambaLayer> layers[3];
+
+    explicit MambaBlock(const aic_mamba_block_desc& desc) : d(desc)
+    {
+        require(d.survival_probability > 0.0f, "survival probability must be positive");
+        // mamba_block.h:39-41
+        layers[0].reset(new MambaLayer({d.d_model, d.d_state, d.d_model, 1}));
+        layers[1].reset(new MambaLayer({d.d_model, d.d_state, d.d_model, 1}));
+        layers[2].reset(new MambaLayer({d.d_model, d.d_state, d.out_channels, d.activation}));
+    }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        for (auto& l : layers) {
+            char* p = c.take<char>(l->carve(nullptr));
+            l->carve(p);
+            if (base) l->bound = true;
+        }
+        return c.bytes();
+    }
+    size_t state_bytes(int batch) const
+    {
+        Carver c(nullptr);
+        for (auto& l : layers) c.take<char>(l->state_bytes(batch));
+        return c.bytes();
+    }
+    void bind_state(void* base, int batch)
+    {
+        Carver c(base);
+        for (auto& l : layers) {
+            l->h = reinterpret_cast<float2*>(c.take<char>(l->state_bytes(batch)));
+            l->batch_bound = batch;
+        }
+    }
+    size_t workspace(int64_t rows, void* base, float** y, float** o, uint32_t** a, int8_t** as, uint32_t** b,
+                     int8_t** bs) const
+    {
+        Carver c(base);
+        size_t ybytes = 0;
+        for (auto& l : layers) ybytes = std::max(ybytes, l->workspace_bytes(rows));
+        float* py = reinterpret_cast<float*>(c.take<char>(ybytes));
+        float* po = c.take<float>(static_cast<size_t>(rows) * d.d_model);
+        uint32_t* pa = c.take<uint32_t>(static_cast<size_t>(rows) * d.d_model / 8);
+        int8_t* pas = c.take<int8_t>(static_cast<size_t>(rows) * d.d_model / 32);
+        uint32_t* pb = c.take<uint32_t>(static_cast<size_t>(rows) * d.d_model / 8);
+        int8_t* pbs = c.take<int8_t>(static_cast<size_t>(rows) * d.d_model / 32);
+        if (y) { *y = py; *o = po; *a = pa; *as = pas; *b = pb; *bs = pbs; }
+        return c.bytes();
+    }
+    int64_t forward(const uint32_t* in, const int8_t* in_s, float* out, int batch, int seq, bool on_training,
+                    int add_seed, bool survived, void* wsp, cudaStream_t s)
+    {
+        if (batch == 0 || seq == 0) return 0;
+        require(wsp != nullptr && aligned256(wsp), "block workspace must be 256-byte aligned");
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        float *y, *o;
+        uint32_t *a, *b;
+        int8_t *as, *bs;
+        workspace(rows, wsp, &y, &o, &a, &as, &b, &bs);
+        const int64_t n_el = rows * d.d_model, row_groups = d.d_model / 32;
+        int64_t n = 0;
+        // mamba_block.h:60-65
+        n += layers[0]->forward(in, in_s, o, batch, seq, y, s);
+        cuda_ok(launch_pack_f32(o, n_el, a, as, on_training, add_seed, row_groups, s), "requant");
+        const float surv_inv = 1.0f / d.survival_probability;
+        const float main_mult = d.residual_factor * (on_training && survived ? surv_inv : 1.0f);
+        cuda_ok(launch_residual(a, as, in, in_s, b, bs, rows, d.d_model, main_mult, on_training && !survived, s), "residual");
+        // mamba_block.h:66-71
+        n += layers[1]->forward(b, bs, o, batch, seq, y, s);
+        cuda_ok(launch_pack_f32(o, n_el, a, as, on_training, add_seed, row_groups, s), "requant");
+        n += layers[2]->forward(a, as, out, batch, seq, y, s);
+        return n + 3;
+    }
+};
+
+// ---------------------------------------------------------------- Critic
+struct Critic {
+    aic_critic_desc d;
+    float *w1 = nullptr, *w2 = nullptr, *wl = nullptr;
+    float2* h = nullptr;
+    int batch_bound = -1;
+    bool bound = false;
+
+    explicit Critic(const aic_critic_desc& desc) : d(desc)
+    {
+        require(d.in_channels > 0 && d.in_channels % 32 == 0, "critic input channels must be a multiple of 32");
+        require(d.units >= 32 && d.units % 32 == 0 && d.units <= 1024, "critic units must be a multiple of 32 in [32, 1024]");
+        require(d.dim_in >= 1, "bad critic input dimension");
+    }
+    int64_t w1_elems() const { return 2LL * d.in_channels * d.units; }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        w1 = c.take<float>(w1_elems());
+        w2 = c.take<float>(2 * d.units);
+        wl = c.take<float>(w1_elems());
+        return c.bytes();
+    }
+    void check_bound() const
+    {
+        if (!bound) fail(AIC_ERR_STATE, "critic parameters not bound");
+    }
+    void load(const float* a, const float* b, const float* l, cudaStream_t s)
+    {
+        check_bound();
+        require(a && b && l, "null weights");
+        cuda_ok(cudaMemcpyAsync(w1, a, sizeof(float) * w1_elems(), cudaMemcpyDefault, s), "copy w1");
+        cuda_ok(cudaMemcpyAsync(w2, b, sizeof(float) * 2 * d.units, cudaMemcpyDefault, s), "copy w2");
+        cuda_ok(cudaMemcpyAsync(wl, l, sizeof(float) * w1_elems(), cudaMemcpyDefault, s), "copy wl");
+    }
+    void load_file(const char* path, cudaStream_t s)
+    {
+        check_bound();
+        const size_t n1 = static_cast<size_t>(w1_elems()), n2 = 2 * static_cast<size_t>(d.units);
+        MappedHost m(read_floats(path, {n1, n2, n1}));  // critic.h:36-38: W1, W2, Wlambda
+        load(m.dev, m.dev + n1, m.dev + n1 + n2, s);
+        cuda_ok(cudaStreamSynchronize(s), "load sync");
+    }
+    size_t state_bytes(int batch) const { return static_cast<size_t>(batch) * d.units * sizeof(float2); }
+    void reset(cudaStream_t s)
+    {
+        if (batch_bound < 0) fail(AIC_ERR_STATE, "critic state not bound");
+        cuda_ok(cudaMemsetAsync(h, 0, state_bytes(batch_bound), s), "reset critic");
+    }
+    size_t workspace(int64_t rows, void* base, __half** pooled, float2** hseq) const
+    {
+        Carver c(base);
+        __half* p = c.take<__half>(static_cast<size_t>(rows) * d.in_channels);
+        float2* q = c.take<float2>(static_cast<size_t>(rows) * d.units);
+        if (pooled) { *pooled = p; *hseq = q; }
+        return c.bytes();
+    }
+    int64_t forward(const uint32_t* in, const int8_t* in_s, float* score, int batch, int seq, void* wsp, cudaStream_t s)
+    {
+        check_bound();
+        if (batch_bound < 0) fail(AIC_ERR_STATE, "critic state not bound");
+        require(batch == batch_bound, "batch differs from the bound state's batch");
+        if (batch == 0 || seq == 0) return 0;
+        require(in && in_s && score && wsp && aligned256(wsp), "null or misaligned tensor");
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        __half* pooled;
+        float2* hseq;
+        workspace(rows, wsp, &pooled, &hseq);
+        cuda_ok(launch_gap_f16(in, in_s, rows, d.dim_in * d.dim_in, d.in_channels, pooled, s), "critic gap");
+        cuda_ok(launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s), "critic");
+        return 3;
+    }
+    void forward_pooled(const __half* pooled, float* score, int batch, int seq, void* wsp, cudaStream_t s)
+    {
+        check_bound();
+        if (batch_bound < 0) fail(AIC_ERR_STATE, "critic state not bound");
+        require(batch == batch_bound, "batch differs from the bound state's batch");
+        if (batch == 0 || seq == 0) return;
+        require(pooled && score && wsp && aligned256(wsp), "null or misaligned tensor");
+        __half* unused;
+        float2* hseq;
+        workspace(static_cast<int64_t>(batch) * seq, wsp, &unused, &hseq);
+        cuda_ok(launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s), "critic");
+    }
+};
+
+// ---------------------------------------------------------------- Cortex
+struct Cortex {
+    aic_cortex_desc d;
+    std::vector<std::unique_ptr<ConvBlock>> blocks;
+    std::vector<std::unique_ptr<MambaLayer>> units;
+    std::unique_ptr<MambaLayer> actor;
+    std::unique_ptr<Critic> critic;
+    int chunk;
+    int64_t last_launches = 0;
+
+    explicit Cortex(const aic_cortex_desc& desc) : d(desc)
+    {
+        require(d.n_blocks >= 1 && d.n_blocks <= AIC_MAX_BLOCKS, "n_blocks out of range");
+        require(d.planes >= 1 && d.planes <= d.stem_channels && d.stem_channels % 32 == 0, "bad stem planes/channels");
+        require(d.dim >= 1, "bad input dimension");
+        int c = d.stem_channels, dim = d.dim;
+        for (int i = 0; i < d.n_blocks; ++i) {
+            const auto& b = d.blocks[i];
+            require(b.in_channels == c && b.dim_in == dim, "block " + std::to_string(i) + " does not chain");
+            blocks.emplace_back(new ConvBlock(b));
+            c = b.out_channels;
+            dim = b.dim_out;
+        }
+        require(c == d.d_model, "last block's channels must equal d_model");
+        for (int i = 0; i < d.n_units; ++i) units.emplace_back(new MambaLayer({d.d_model, d.d_state, d.d_model, 1}));
+        actor.reset(new MambaLayer({d.d_model, d.d_state, d.actor_out, d.actor_activation}));
+        if (d.critic_units > 0) critic.reset(new Critic({d.d_model, d.critic_units, 1}));
+        chunk = d.chunk_frames > 0 ? d.chunk_frames : 2048;
+    }
+    int final_dim() const { return d.blocks[d.n_blocks - 1].dim_out; }
+    size_t carve(void* base)
+    {
+        Carver c(base);
+        auto put = [&](auto& obj) {
+            char* p = c.take<char>(obj->carve(nullptr));
+            obj->carve(p);
+        };
+        for (auto& b : blocks) put(b);
+        for (auto& u : units) put(u);
+        put(actor);
+        if (critic) put(critic);
+        if (base) {
+            for (auto& b : blocks)
+                for (auto& l : b->layers) l->bound = true;
+            for (auto& u : units) u->bound = true;
+            actor->bound = true;
+            if (critic) critic->bound = true;
+        }
+        return c.bytes();
+    }
+    size_t state(int batch, void* base)
+    {
+        Carver c(base);
+        auto take = [&](float2*& h, int& bound, size_t bytes) {
+            float2* p = reinterpret_cast<float2*>(c.take<char>(bytes));
+            if (base) {
+                h = p;
+                bound = batch;
+            }
+        };
+        for (auto& u : units) take(u->h, u->batch_bound, u->state_bytes(batch));
+        take(actor->h, actor->batch_bound, actor->state_bytes(batch));
+        if (critic) take(critic->h, critic->batch_bound, critic->state_bytes(batch));
+        return c.bytes();
+    }
+    struct Work {
+        uint32_t *stem, *x, *y, *feat, *ua, *ub, *uc;
+        int8_t *stem_s, *x_s, *y_s, *feat_s, *ua_s, *ub_s, *uc_s;
+        void *block_ws, *layer_ws, *critic_ws;
+        float* o;
+    };
+    size_t workspace(int batch, int seq, void* base, Work* w) const
+    {
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        const int64_t ch = std::min<int64_t>(rows, chunk);
+        Carver c(base);
+        Work t{};
+        t.stem = c.take<uint32_t>(ch * d.dim * d.dim * d.stem_channels / 8);
+        t.stem_s = c.take<int8_t>(ch * d.dim * d.dim * d.stem_channels / 32);
+        int64_t act_words = 0, block_ws = 0;
+        for (auto& b : blocks) {
+            act_words = std::max<int64_t>(act_words, ch * b->d.dim_out * b->d.dim_out * b->d.out_channels / 8);
+            block_ws = std::max<int64_t>(block_ws, b->workspace(ch, nullptr, nullptr, nullptr, nullptr, nullptr));
+        }
+        t.x = c.take<uint32_t>(act_words);
+        t.x_s = c.take<int8_t>(act_words / 4);
+        t.y = c.take<uint32_t>(act_words);
+        t.y_s = c.take<int8_t>(act_words / 4);
+        t.block_ws = c.take<char>(block_ws);
+        const int64_t fw = rows * d.d_model / 8;
+        t.feat = c.take<uint32_t>(fw);
+        t.feat_s = c.take<int8_t>(fw / 4);
+        t.ua = c.take<uint32_t>(fw);
+        t.ua_s = c.take<int8_t>(fw / 4);
+        t.ub = c.take<uint32_t>(fw);
+        t.ub_s = c.take<int8_t>(fw / 4);
+        t.uc = c.take<uint32_t>(fw);
+        t.uc_s = c.take<int8_t>(fw / 4);
+        t.o = c.take<float>(rows * d.d_model);
+        size_t lw = actor->workspace_bytes(rows);
+        for (auto& u : units) lw = std::max(lw, u->workspace_bytes(rows));
+        t.layer_ws = c.take<char>(lw);
+        t.critic_ws = critic ? c.take<char>(critic->workspace(rows, nullptr, nullptr, nullptr)) : nullptr;
+        if (w) *w = t;
+        return c.bytes();
+    }
+    void forward(const uint16_t* planes, int batch, int seq, float* actor_out, float* critic_out, uint32_t* features,
+                 int8_t* features_s, void* wsp, cudaStream_t s)
+    {
+        last_launches = 0;
+        if (batch == 0 || seq == 0) return;
+        require(planes && actor_out && wsp && aligned256(wsp), "null or misaligned tensor");
+        Work w;
+        workspace(batch, seq, wsp, &w);
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        uint32_t* feat = features ? features : w.feat;
+        int8_t* feat_s = features ? features_s : w.feat_s;
+        require(feat_s != nullptr, "features exponents missing");
+        const int64_t plane_elems = static_cast<int64_t>(d.planes) * d.dim * d.dim;
+        int64_t n = 0;
+        for (int64_t f0 = 0; f0 < rows; f0 += chunk) {
+            const int64_t fc = std::min<int64_t>(chunk, rows - f0);
+            cuda_ok(launch_stem_pack(reinterpret_cast<const __half*>(planes) + f0 * plane_elems, fc, d.planes,
+                                     d.stem_channels, d.dim, w.stem, w.stem_s, s),
+                    "stem");
+            ++n;
+            const uint32_t* cur = w.stem;
+            const int8_t* cur_s = w.stem_s;
+            for (size_t i = 0; i < blocks.size(); ++i) {
+                uint32_t* dst = (i & 1) ? w.y : w.x;
+                int8_t* dst_s = (i & 1) ? w.y_s : w.x_s;
+                n += blocks[i]->forward(cur, cur_s, dst, dst_s, fc, false, true, w.block_ws, s);
+                cur = dst;
+                cur_s = dst_s;
+            }
+            const int fd = final_dim();
+            cuda_ok(launch_gap(cur, cur_s, fc, fd * fd, d.d_model, nullptr, feat + f0 * d.d_model / 8,
+                               feat_s + f0 * d.d_model / 32, s),
+                    "gap");
+            ++n;
+        }
+        // Mamba trunk: units of layer -> requant -> residual with the unit input.
+        const uint32_t* cur = feat;
+        const int8_t* cur_s = feat_s;
+        uint32_t* bufs[2] = {w.ub, w.uc};
+        int8_t* bufs_s[2] = {w.ub_s, w.uc_s};
+        for (size_t i = 0; i < units.size(); ++i) {
+            n += units[i]->forward(cur, cur_s, w.o, batch, seq, w.layer_ws, s);
+            cuda_ok(launch_pack_f32(w.o, rows * d.d_model, w.ua, w.ua_s, false, 0, 0, s), "unit requant");
+            uint32_t* nxt = bufs[i & 1];
+            int8_t* nxt_s = bufs_s[i & 1];
+            cuda_ok(launch_residual(w.ua, w.ua_s, cur, cur_s, nxt, nxt_s, rows, d.d_model, d.unit_residual_factor, false, s),
+                    "unit residual");
+            n += 2;
+            cur = nxt;
+            cur_s = nxt_s;
+        }
+        n += actor->forward(cur, cur_s, actor_out, batch, seq, w.layer_ws, s);
+        if (critic && critic_out) n += critic->forward(cur, cur_s, critic_out, batch, seq, w.critic_ws, s);
+        last_launches = n;
+    }
+};
+
+template <class T>
+T* handle(void* p, const char* what)
+{
+    if (!p) fail(AIC_ERR_INVALID, std::string("null ") + what + " handle");
+    return static_cast<T*>(p);
+}
+
+}  // namespace
+}  // namespace aic
+
+using namespace aic;
+
+extern "C" {
+
+AIC_API const char* aic_last_error(void) { return g_last_error.c_str(); }
+AIC_API int aic_abi_version(void) { return 1; }
+
+AIC_API aic_status aic_pack_f32(const float* in, int64_t n, uint32_t* out, int8_t* out_s, int stochastic,
+                                int32_t add_idx, void* stream)
+{
+    return guarded([&] {
+        require(n >= 0 && n % 32 == 0, "n must be a non-negative multiple of 32");
+        require(n == 0 || (in && out && out_s), "null tensor");
+        cuda_ok(launch_pack_f32(in, n, out, out_s, stochastic != 0, add_idx, 0, as_stream(stream)), "pack");
+    });
+}
+
+AIC_API aic_status aic_stem_pack(const uint16_t* planes, int64_t frames, int planes_present, int channels, int dim,
+                                 uint32_t* out, int8_t* out_s, void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0 && dim >= 1 && channels > 0 && channels % 32 == 0, "bad stem geometry");
+        require(planes_present >= 0 && planes_present <= channels, "planes_present out of range");
+        require(frames == 0 || (planes && out && out_s), "null tensor");
+        cuda_ok(launch_stem_pack(reinterpret_cast<const __half*>(planes), frames, planes_present, channels, dim, out, out_s,
+                                 as_stream(stream)),
+                "stem");
+    });
+}
+
+AIC_API aic_status aic_residual_add(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res,
+                                    const int8_t* res_s, uint32_t* out, int8_t* out_s, int64_t positions, int channels,
+                                    float main_mult, int skipped, void* stream)
+{
+    return guarded([&] {
+        require(positions >= 0 && channels > 0 && channels % 32 == 0, "bad residual geometry");
+        require(positions == 0 || (res && res_s && out && out_s && (skipped || (main_in && main_s))), "null tensor");
+        cuda_ok(launch_residual(main_in, main_s, res, res_s, out, out_s, positions, channels, main_mult, skipped != 0,
+                                as_stream(stream)),
+                "residual");
+    });
+}
+
+AIC_API aic_status aic_gap(const uint32_t* in, const int8_t* in_s, int64_t frames, int hw, int channels, float* out_f32,
+                           uint32_t* out_q, int8_t* out_qs, void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0 && hw >= 1 && channels > 0 && channels % 32 == 0, "bad gap geometry");
+        require(frames == 0 || (in && in_s), "null tensor");
+        require((out_q == nullptr) == (out_qs == nullptr), "out_q and out_qs go together");
+        cuda_ok(launch_gap(in, in_s, frames, hw, channels, out_f32, out_q, out_qs, as_stream(stream)), "gap");
+    });
+}
+
+AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frames, int hw, int channels,
+                               uint16_t* out, void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0 && hw >= 1 && channels > 0 && channels % 32 == 0, "bad gap geometry");
+        require(frames == 0 || (in && in_s && out), "null tensor");
+        cuda_ok(launch_gap_f16(in, in_s, frames, hw, channels, reinterpret_cast<__half*>(out), as_stream(stream)), "gap");
+    });
+}
+
+AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream)
+{
+    return guarded([&] {
+        require(rows >= 0 && count >= 0, "bad action geometry");
+        require(rows == 0 || count == 0 || (probs && actions), "null tensor");
+        cuda_ok(launch_set_actions(probs, rows, count, reinterpret_cast<unsigned long long*>(actions), as_stream(stream)),
+                "actions");
+    });
+}
+
+// ---- ConvLayer
+AIC_API aic_status aic_conv_layer_create(const aic_conv_layer_desc* desc, aic_conv_layer* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_conv_layer>(new ConvLayer(*desc));
+    });
+}
+AIC_API aic_status aic_conv_layer_sizes(aic_conv_layer l, int64_t* weight_elems, int64_t* bias_elems, size_t* param_bytes)
+{
+    return guarded([&] {
+        auto* c = handle<ConvLayer>(l, "conv layer");
+        if (weight_elems) *weight_elems = c->weight_elems;
+        if (bias_elems) *bias_elems = c->d.out_channels;
+        if (param_bytes) {
+            ConvLayer tmp(*c);
+            *param_bytes = tmp.carve(nullptr);
+        }
+    });
+}
+AIC_API aic_status aic_conv_layer_bind(aic_conv_layer l, void* dev_params)
+{
+    return guarded([&] {
+        auto* c = handle<ConvLayer>(l, "conv layer");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        c->carve(dev_params);
+        c->bound = true;
+    });
+}
+AIC_API aic_status aic_conv_layer_param_ptrs(aic_conv_layer l, uint32_t** weights, int8_t** weight_scales, float** bias)
+{
+    return guarded([&] {
+        auto* c = handle<ConvLayer>(l, "conv layer");
+        c->check_bound();
+        if (weights) *weights = c->w;
+        if (weight_scales) *weight_scales = c->ws;
+        if (bias) *bias = c->bias;
+    });
+}
+AIC_API aic_status aic_conv_layer_load_weights(aic_conv_layer l, const float* master, const float* bias, void* stream)
+{
+    return guarded([&] { handle<ConvLayer>(l, "conv layer")->load(master, bias, as_stream(stream)); });
+}
+AIC_API aic_status aic_conv_layer_load_file_sync(aic_conv_layer l, const char* path, void* stream)
+{
+    return guarded([&] { handle<ConvLayer>(l, "conv layer")->load_file(path, as_stream(stream)); });
+}
+AIC_API aic_status aic_conv_layer_forward(aic_conv_layer l, const uint32_t* in, const int8_t* in_s, uint32_t* out,
+                                          int8_t* out_s, int64_t frames, void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0, "negative frame count");
+        handle<ConvLayer>(l, "conv layer")->forward(in, in_s, out, out_s, frames, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l)
+{
+    return guarded([&] { delete reinterpret_cast<ConvLayer*>(l); });
+}
+
+// ---- ConvBlock
+AIC_API aic_status aic_conv_block_create(const aic_conv_block_desc* desc, aic_conv_block* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_conv_block>(new ConvBlock(*desc));
+    });
+}
+AIC_API aic_status aic_conv_block_layer(aic_conv_block b, int i, aic_conv_layer* out)
+{
+    return guarded([&] {
+        auto* c = handle<ConvBlock>(b, "conv block");
+        require(i >= 0 && i < 4 && out, "layer index out of range");
+        *out = reinterpret_cast<aic_conv_layer>(c->layers[i].get());
+    });
+}
+AIC_API aic_status aic_conv_block_param_bytes(aic_conv_block b, size_t* bytes)
+{
+    return guarded([&] {
+        auto* c = handle<ConvBlock>(b, "conv block");
+        require(bytes != nullptr, "null output");
+        *bytes = c->carve(nullptr);
+    });
+}
+AIC_API aic_status aic_conv_block_bind(aic_conv_block b, void* dev_params)
+{
+    return guarded([&] {
+        auto* c = handle<ConvBlock>(b, "conv block");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        c->carve(dev_params);
+    });
+}
+AIC_API aic_status aic_conv_block_workspace_bytes(aic_conv_block b, int64_t frames, size_t* bytes)
+{
+    return guarded([&] {
+        auto* c = handle<ConvBlock>(b, "conv block");
+        require(bytes && frames >= 0, "bad argument");
+        *bytes = c->workspace(frames, nullptr, nullptr, nullptr, nullptr, nullptr);
+    });
+}
+AIC_API aic_status aic_conv_block_load_dir_sync(aic_conv_block b, const char* dir, void* stream)
+{
+    return guarded([&] {
+        auto* c = handle<ConvBlock>(b, "conv block");
+        static const char* names[4] = {"depthwise_layer.bin", "conv_layer1.bin", "conv_layer2.bin", "residual_layer.bin"};
+        for (int i = 0; i < 4; ++i) c->layers[i]->load_file(join(dir, names[i]).c_str(), as_stream(stream));
+    });
+}
+AIC_API aic_status aic_conv_block_forward(aic_conv_block b, const uint32_t* in, const int8_t* in_s, uint32_t* out,
+                                          int8_t* out_s, int64_t frames, int train_mode, int is_survived, void* workspace,
+                                          void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0, "negative frame count");
+        handle<ConvBlock>(b, "conv block")
+            ->forward(in, in_s, out, out_s, frames, train_mode != 0, is_survived != 0, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_conv_block_destroy(aic_conv_block b)
+{
+    return guarded([&] { delete reinterpret_cast<ConvBlock*>(b); });
+}
+
+// ---- MambaLayer
+AIC_API aic_status aic_mamba_layer_create(const aic_mamba_layer_desc* desc, aic_mamba_layer* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_mamba_layer>(new MambaLayer(*desc));
+    });
+}
+AIC_API aic_status aic_mamba_layer_sizes(aic_mamba_layer l, int64_t* weight_elems, int64_t* bias_elems, size_t* param_bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        if (weight_elems) *weight_elems = m->weight_elems;
+        if (bias_elems) *bias_elems = m->d.out_channels;
+        if (param_bytes) {
+            MambaLayer tmp(*m);
+            *param_bytes = tmp.carve(nullptr);
+        }
+    });
+}
+AIC_API aic_status aic_mamba_layer_bind(aic_mamba_layer l, void* dev_params)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        m->carve(dev_params);
+        m->bound = true;
+    });
+}
+AIC_API aic_status aic_mamba_layer_param_ptrs(aic_mamba_layer l, uint32_t** weights, int8_t** weight_scales, float** bias)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        m->check_bound();
+        if (weights) *weights = m->w;
+        if (weight_scales) *weight_scales = m->ws;
+        if (bias) *bias = m->bias;
+    });
+}
+AIC_API aic_status aic_mamba_layer_load_weights(aic_mamba_layer l, const float* master, const float* bias, void* stream)
+{
+    return guarded([&] { handle<MambaLayer>(l, "mamba layer")->load(master, bias, as_stream(stream)); });
+}
+AIC_API aic_status aic_mamba_layer_load_file_sync(aic_mamba_layer l, const char* path, void* stream)
+{
+    return guarded([&] { handle<MambaLayer>(l, "mamba layer")->load_file(path, as_stream(stream)); });
+}
+AIC_API aic_status aic_mamba_layer_state_bytes(aic_mamba_layer l, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = m->state_bytes(batch);
+    });
+}
+AIC_API aic_status aic_mamba_layer_bind_state(aic_mamba_layer l, void* dev_state, int batch)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(batch >= 0 && (batch == 0 || (dev_state && aligned256(dev_state))), "state must be 256-byte aligned");
+        m->h = static_cast<float2*>(dev_state);
+        m->batch_bound = batch;
+    });
+}
+AIC_API aic_status aic_mamba_layer_reset_state(aic_mamba_layer l, void* stream)
+{
+    return guarded([&] { handle<MambaLayer>(l, "mamba layer")->reset(as_stream(stream)); });
+}
+AIC_API aic_status aic_mamba_layer_workspace_bytes(aic_mamba_layer l, int64_t rows, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(bytes && rows >= 0, "bad argument");
+        *bytes = m->workspace_bytes(rows);
+    });
+}
+AIC_API aic_status aic_mamba_layer_forward(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s, float* out,
+                                           int batch, int seq, void* workspace, void* stream)
+{
+    return guarded([&] {
+        handle<MambaLayer>(l, "mamba layer")->forward(in, in_s, out, batch, seq, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, float* out, int64_t rows, void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        m->check_bound();
+        require(rows >= 0 && (rows == 0 || (y && out)), "bad out-projection arguments");
+        cuda_ok(launch_outproj(y, m->w, m->ws, m->bias, m->d.d_model, m->d.d_state, m->d.out_channels, m->d.activation,
+                               rows, out, as_stream(stream)),
+                "outproj");
+    });
+}
+AIC_API aic_status aic_mamba_layer_destroy(aic_mamba_layer l)
+{
+    return guarded([&] { delete reinterpret_cast<MambaLayer*>(l); });
+}
+
+// ---- MambaBlock
+AIC_API aic_status aic_mamba_block_create(const aic_mamba_block_desc* desc, aic_mamba_block* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_mamba_block>(new MambaBlock(*desc));
+    });
+}
+AIC_API aic_status aic_mamba_block_layer(aic_mamba_block b, int i, aic_mamba_layer* out)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(i >= 0 && i < 3 && out, "layer index out of range");
+        *out = reinterpret_cast<aic_mamba_layer>(m->layers[i].get());
+    });
+}
+AIC_API aic_status aic_mamba_block_param_bytes(aic_mamba_block b, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(bytes != nullptr, "null output");
+        *bytes = m->carve(nullptr);
+    });
+}
+AIC_API aic_status aic_mamba_block_bind(aic_mamba_block b, void* dev_params)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        m->carve(dev_params);
+    });
+}
+AIC_API aic_status aic_mamba_block_state_bytes(aic_mamba_block b, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = m->state_bytes(batch);
+    });
+}
+AIC_API aic_status aic_mamba_block_bind_state(aic_mamba_block b, void* dev_state, int batch)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(batch >= 0 && (batch == 0 || (dev_state && aligned256(dev_state))), "state must be 256-byte aligned");
+        m->bind_state(dev_state, batch);
+    });
+}
+AIC_API aic_status aic_mamba_block_reset_state(aic_mamba_block b, void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        for (auto& l : m->layers) l->reset(as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_block_workspace_bytes(aic_mamba_block b, int64_t rows, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(bytes && rows >= 0, "bad argument");
+        *bytes = m->workspace(rows, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr);
+    });
+}
+AIC_API aic_status aic_mamba_block_load_dir_sync(aic_mamba_block b, const char* dir, void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        static const char* names[3] = {"mamba_strategist.bin", "mamba_tactic.bin", "mamba_executor.bin"};
+        for (int i = 0; i < 3; ++i) m->layers[i]->load_file(join(dir, names[i]).c_str(), as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_block_forward(aic_mamba_block b, const uint32_t* in, const int8_t* in_s, float* out,
+                                           int batch, int seq, int on_training, int add_seed, int is_survived,
+                                           void* workspace, void* stream)
+{
+    return guarded([&] {
+        handle<MambaBlock>(b, "mamba block")
+            ->forward(in, in_s, out, batch, seq, on_training != 0, add_seed, is_survived != 0, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_block_destroy(aic_mamba_block b)
+{
+    return guarded([&] { delete reinterpret_cast<MambaBlock*>(b); });
+}
+
+// ---- Critic
+AIC_API aic_status aic_critic_create(const aic_critic_desc* desc, aic_critic* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_critic>(new Critic(*desc));
+    });
+}
+AIC_API aic_status aic_critic_param_bytes(aic_critic c, size_t* bytes)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(bytes != nullptr, "null output");
+        Critic tmp(*k);
+        *bytes = tmp.carve(nullptr);
+    });
+}
+AIC_API aic_status aic_critic_bind(aic_critic c, void* dev_params)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        k->carve(dev_params);
+        k->bound = true;
+    });
+}
+AIC_API aic_status aic_critic_load_weights(aic_critic c, const float* w1, const float* w2, const float* wl, void* stream)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->load(w1, w2, wl, as_stream(stream)); });
+}
+AIC_API aic_status aic_critic_load_file_sync(aic_critic c, const char* path, void* stream)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->load_file(path, as_stream(stream)); });
+}
+AIC_API aic_status aic_critic_state_bytes(aic_critic c, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = k->state_bytes(batch);
+    });
+}
+AIC_API aic_status aic_critic_bind_state(aic_critic c, void* dev_state, int batch)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(batch >= 0 && (batch == 0 || (dev_state && aligned256(dev_state))), "state must be 256-byte aligned");
+        k->h = static_cast<float2*>(dev_state);
+        k->batch_bound = batch;
+    });
+}
+AIC_API aic_status aic_critic_reset_state(aic_critic c, void* stream)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->reset(as_stream(stream)); });
+}
+AIC_API aic_status aic_critic_workspace_bytes(aic_critic c, int64_t rows, size_t* bytes)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(bytes && rows >= 0, "bad argument");
+        *bytes = k->workspace(rows, nullptr, nullptr, nullptr);
+    });
+}
+AIC_API aic_status aic_critic_forward(aic_critic c, const uint32_t* in, const int8_t* in_s, float* score, int batch,
+                                      int seq, void* workspace, void* stream)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->forward(in, in_s, score, batch, seq, workspace, as_stream(stream)); });
+}
+AIC_API aic_status aic_critic_forward_pooled(aic_critic c, const uint16_t* pooled, float* score, int batch, int seq,
+                                             void* workspace, void* stream)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        k->forward_pooled(reinterpret_cast<const __half*>(pooled), score, batch, seq, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_critic_destroy(aic_critic c)
+{
+    return guarded([&] { delete reinterpret_cast<Critic*>(c); });
+}
+
+// ---- Cortex
+AIC_API aic_status aic_cortex_create(const aic_cortex_desc* desc, aic_cortex* out)
+{
+    return guarded([&] {
+        require(desc && out, "null argument");
+        *out = reinterpret_cast<aic_cortex>(new Cortex(*desc));
+    });
+}
+AIC_API aic_status aic_cortex_block(aic_cortex c, int i, aic_conv_block* out)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(out && i >= 0 && i < static_cast<int>(x->blocks.size()), "block index out of range");
+        *out = reinterpret_cast<aic_conv_block>(x->blocks[i].get());
+    });
+}
+AIC_API aic_status aic_cortex_unit(aic_cortex c, int i, aic_mamba_layer* out)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(out && i >= 0 && i < static_cast<int>(x->units.size()), "unit index out of range");
+        *out = reinterpret_cast<aic_mamba_layer>(x->units[i].get());
+    });
+}
+AIC_API aic_status aic_cortex_actor(aic_cortex c, aic_mamba_layer* out)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(out != nullptr, "null output");
+        *out = reinterpret_cast<aic_mamba_layer>(x->actor.get());
+    });
+}
+AIC_API aic_status aic_cortex_critic(aic_cortex c, aic_critic* out)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(out != nullptr, "null output");
+        *out = reinterpret_cast<aic_critic>(x->critic.get());
+    });
+}
+AIC_API aic_status aic_cortex_param_bytes(aic_cortex c, size_t* bytes)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(bytes != nullptr, "null output");
+        *bytes = x->carve(nullptr);
+    });
+}
+AIC_API aic_status aic_cortex_bind(aic_cortex c, void* dev_params)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(dev_params && aligned256(dev_params), "parameters must be 256-byte aligned");
+        x->carve(dev_params);
+    });
+}
+AIC_API aic_status aic_cortex_state_bytes(aic_cortex c, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = x->state(batch, nullptr);
+    });
+}
+AIC_API aic_status aic_cortex_bind_state(aic_cortex c, void* dev_state, int batch)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(batch >= 0 && dev_state && aligned256(dev_state), "state must be 256-byte aligned");
+        x->state(batch, dev_state);
+    });
+}
+AIC_API aic_status aic_cortex_reset_state(aic_cortex c, void* stream)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        for (auto& u : x->units) u->reset(as_stream(stream));
+        x->actor->reset(as_stream(stream));
+        if (x->critic) x->critic->reset(as_stream(stream));
+    });
+}
+AIC_API aic_status aic_cortex_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(bytes && batch >= 0 && seq >= 0, "bad argument");
+        *bytes = x->workspace(batch, seq, nullptr, nullptr);
+    });
+}
+AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int batch, int seq, float* actor,
+                                      float* critic, uint32_t* features, int8_t* features_s, void* workspace,
+                                      void* stream)
+{
+    return guarded([&] {
+        require(batch >= 0 && seq >= 0, "bad extents");
+        handle<Cortex>(c, "cortex")
+            ->forward(planes, batch, seq, actor, critic, features, features_s, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(launches != nullptr, "null output");
+        *launches = x->last_launches;
+    });
+}
+AIC_API aic_status aic_cortex_destroy(aic_cortex c)
+{
+    return guarded([&] { delete reinterpret_cast<Cortex*>(c); });
+}
+
+}  // extern "C"

@@ -1,0 +1,231 @@
+// Convolution kernels on CUDA cores: the depthwise k x k conv (A5) and the
+// quantized implicit-GEMM conv (A3 dense k2/k4, A4 pointwise) with its fused
+// RMSNorm + bias + SiLU + requant epilogue. Both reproduce the reference's
+// per-output accumulation order, so their results are bit-identical to the
+// reference kernels (AICortex kernels.h:217-282, 514-585, 831-870).
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+
+namespace aic {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Depthwise conv: one thread per (output pixel, word of 8 channels); the four
+// threads of a 32-channel group sit in consecutive lanes and share the absmax
+// through two shuffles. Per channel and tap: fma(x, w, acc[tap & 3]); the four
+// partial sums are folded into the bias in order.
+template <int K>
+__global__ void __launch_bounds__(kThreads) conv_dw_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
+                                                         const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s,
+                                                         const float* __restrict__ bias, uint32_t* __restrict__ out,
+                                                         int8_t* __restrict__ out_s, int64_t total_words, int C, int stride,
+                                                         int Din, int Dout)
+{
+    constexpr int kPad = K >> 1;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    const bool live = t < total_words;
+    const int words = C >> 3, G = C >> 5;
+    const int64_t tt = live ? t : 0;
+    const int j = static_cast<int>(tt % words);
+    const int64_t pix = tt / words;
+    const int hw_out = Dout * Dout;
+    const int64_t frame = pix / hw_out;
+    const int p = static_cast<int>(pix - frame * hw_out);
+    const int g = j >> 2;
+    const int h0 = (p / Dout) * stride - kPad;
+    const int w0 = (p % Dout) * stride - kPad;
+    const int64_t frame_base = frame * Din * Din;
+    float aa[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) aa[a][e] = 0.0f;
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) {
+        const int hi = h0 + k / K, wi = w0 + k % K;
+        const bool valid = hi >= 0 && hi < Din && wi >= 0 && wi < Din;
+        const int64_t sp = frame_base + static_cast<int64_t>(valid ? hi : 0) * Din + (valid ? wi : 0);
+        const uint32_t xw = valid ? in[sp * words + j] : 0u;
+        const float xu = unit_of(valid ? in_s[sp * G + g] : static_cast<int8_t>(0));
+        const uint32_t ww = w[static_cast<int64_t>(k) * words + j];
+        const float wu = unit_of(w_s[static_cast<int64_t>(k) * G + g]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            aa[k & 3][e] = fmaf(static_cast<float>(code_of(xw, e)) * xu, static_cast<float>(code_of(ww, e)) * wu, aa[k & 3][e]);
+    }
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = bias[(j << 3) + e] + (aa[0][e] + aa[1][e] + aa[2][e] + aa[3][e]);
+    int8_t ex;
+    const uint32_t q = quantize_word_x4(v, &ex);
+    if (!live) return;
+    out[t] = q;
+    if ((j & 3) == 0) out_s[pix * G + g] = ex;
+}
+
+// Implicit-GEMM quantized conv on CUDA cores. A CTA owns TP output pixels and
+// one 256-channel chunk (thread = output channel). The TP input rows (all k*k
+// taps) are staged in shared memory and read as broadcasts; each thread
+// streams its own weight row once per tile. Per (pixel, channel) the
+// accumulation is acc[tap & 3] += unit(s_in) * (unit(s_w) * dot) in tap then
+// group order, and the epilogue reduces acc^2 with the reference's
+// warp-butterfly then cross-warp-butterfly tree.
+template <int TP, int KS>
+__global__ void __launch_bounds__(kThreads) conv_gemm_simt_kernel(
+    const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s, const uint32_t* __restrict__ w,
+    const int8_t* __restrict__ w_s, const float* __restrict__ bias, uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
+    int64_t total_pix, int InC, int OutC, int stride, int Din, int Dout, bool act)
+{
+    constexpr int kTaps = KS * KS;
+    extern __shared__ uint4 smem_rows[];  // [TP][kTaps][G] groups, then exponents
+    __shared__ float part[TP][kThreads / 32];
+    __shared__ float total_sq[TP];
+    __shared__ unsigned char tap_ok[TP][kTaps];
+    const int G = InC >> 5;
+    int8_t* smem_exp = reinterpret_cast<int8_t*>(smem_rows + TP * kTaps * G);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int oc = blockIdx.y * kThreads + threadIdx.x;
+    const bool active = oc < OutC;
+    const int64_t pix0 = static_cast<int64_t>(blockIdx.x) * TP;
+    const int pad = KS == stride ? 0 : (KS - 1) >> 1;
+    const int hw_out = Dout * Dout;
+
+    // Stage the input rows.
+    for (int i = threadIdx.x; i < TP * kTaps * G; i += kThreads) {
+        const int pp = i / (kTaps * G);
+        const int k = (i / G) % kTaps;
+        const int g = i % G;
+        const int64_t pix = pix0 + pp;
+        bool ok = pix < total_pix;
+        int64_t sp = 0;
+        if (ok) {
+            const int64_t frame = pix / hw_out;
+            const int p = static_cast<int>(pix - frame * hw_out);
+            const int hi = (p / Dout) * stride - pad + k / KS;
+            const int wi = (p % Dout) * stride - pad + k % KS;
+            ok = hi >= 0 && hi < Din && wi >= 0 && wi < Din;
+            sp = frame * Din * Din + static_cast<int64_t>(hi) * Din + wi;
+        }
+        smem_rows[i] = ok ? reinterpret_cast<const uint4*>(in)[sp * G + g] : make_uint4(0u, 0u, 0u, 0u);
+        smem_exp[i] = ok ? in_s[sp * G + g] : static_cast<int8_t>(0);
+        if (g == 0) tap_ok[pp][k] = ok ? 1 : 0;
+    }
+    __syncthreads();
+
+    float aa[TP][KS == 1 ? 1 : 4];
+#pragma unroll
+    for (int pp = 0; pp < TP; ++pp)
+#pragma unroll
+        for (int a = 0; a < (KS == 1 ? 1 : 4); ++a) aa[pp][a] = 0.0f;
+    if (active) {
+        const uint4* wrow = reinterpret_cast<const uint4*>(w) + static_cast<int64_t>(oc) * kTaps * G;
+        const int8_t* wsrow = w_s + static_cast<int64_t>(oc) * kTaps * G;
+        for (int k = 0; k < kTaps; ++k) {
+            for (int g = 0; g < G; ++g) {
+                const uint4 wv = wrow[k * G + g];
+                const float wu = unit_of(wsrow[k * G + g]);
+#pragma unroll
+                for (int pp = 0; pp < TP; ++pp) {
+                    if (!tap_ok[pp][k]) continue;
+                    const int si = (pp * kTaps + k) * G + g;
+                    const uint4 xv = smem_rows[si];
+                    const int dot = dot8(xv.x, wv.x) + dot8(xv.y, wv.y) + dot8(xv.z, wv.z) + dot8(xv.w, wv.w);
+                    float& acc = aa[pp][KS == 1 ? 0 : (k & 3)];
+                    acc = fmaf(unit_of(smem_exp[si]), wu * static_cast<float>(dot), acc);
+                }
+            }
+        }
+    }
+    float accv[TP];
+#pragma unroll
+    for (int pp = 0; pp < TP; ++pp) {
+        if (KS == 1) accv[pp] = aa[pp][0];
+        else accv[pp] = aa[pp][0] + aa[pp][KS == 1 ? 0 : 1] + aa[pp][KS == 1 ? 0 : 2] + aa[pp][KS == 1 ? 0 : 3];
+        float sq = active ? accv[pp] * accv[pp] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xFFFFFFFFu, sq, o);
+        if (lane == 0) part[pp][warp] = sq;
+    }
+    __syncthreads();
+    for (int pp = warp; pp < TP; pp += kThreads / 32) {
+        float s = lane < kThreads / 32 ? part[pp][lane] : 0.0f;
+#pragma unroll
+        for (int o = (kThreads / 32) >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
+        if (lane == 0) total_sq[pp] = s;
+    }
+    __syncthreads();
+    const float inv_div = __frcp_rn(static_cast<float>(min(OutC, kNormChunk)));
+    const float b = active ? bias[oc] : 0.0f;
+#pragma unroll
+    for (int pp = 0; pp < TP; ++pp) {
+        const int64_t pix = pix0 + pp;
+        float v = fmaf(accv[pp], __frsqrt_rn(fmaf(total_sq[pp], inv_div, kEps)), b);
+        if (act) v = silu_f(v);
+        float amax = fabsf(v);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        const float scale = amax < kEps ? 1.0f : amax;
+        uint32_t q = code_rn(v, kQMax * __frcp_rn(scale)) << ((lane & 7) << 2);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) q |= __shfl_down_sync(0xFFFFFFFFu, q, o);
+        if (active && pix < total_pix) {
+            if ((lane & 7) == 0) out[pix * (OutC >> 3) + (oc >> 3)] = q;
+            if (lane == 0) out_s[pix * (OutC >> 5) + (oc >> 5)] = exponent_of(scale);
+        }
+    }
+}
+
+inline unsigned grid_for(int64_t threads) { return static_cast<unsigned>((threads + kThreads - 1) / kThreads); }
+
+template <int TP, int KS>
+cudaError_t launch_gemm_tp(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                           uint32_t* out, int8_t* out_s, int64_t total_pix, int InC, int OutC, int stride, int Din,
+                           int Dout, bool act, cudaStream_t stream)
+{
+    const int G = InC >> 5;
+    const size_t smem = static_cast<size_t>(TP) * KS * KS * G * (sizeof(uint4) + 1);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(conv_gemm_simt_kernel<TP, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid(static_cast<unsigned>((total_pix + TP - 1) / TP), static_cast<unsigned>((OutC + kThreads - 1) / kThreads));
+    conv_gemm_simt_kernel<TP, KS><<<grid, kThreads, smem, stream>>>(in, in_s, w, w_s, bias, out, out_s, total_pix, InC,
+                                                                   OutC, stride, Din, Dout, act);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                           uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
+                           cudaStream_t stream)
+{
+    const int64_t total = frames * Dout * Dout * (C >> 3);
+    if (total == 0) return cudaSuccess;
+    const unsigned grid = grid_for(total);
+    switch (ksize) {
+        case 3: conv_dw_kernel<3><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
+        case 5: conv_dw_kernel<5><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
+        case 7: conv_dw_kernel<7><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_gemm_simt(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
+                                  const float* bias, uint32_t* out, int8_t* out_s, int64_t frames, int InC, int OutC,
+                                  int ksize, int stride, int Din, int Dout, bool act, cudaStream_t stream)
+{
+    const int64_t total_pix = frames * Dout * Dout;
+    if (total_pix == 0) return cudaSuccess;
+    switch (ksize) {
+        case 1: return launch_gemm_tp<16, 1>(in, in_s, w, w_s, bias, out, out_s, total_pix, InC, OutC, 1, Din, Dout, act, stream);
+        case 2: return launch_gemm_tp<8, 2>(in, in_s, w, w_s, bias, out, out_s, total_pix, InC, OutC, stride, Din, Dout, act, stream);
+        case 4: return launch_gemm_tp<8, 4>(in, in_s, w, w_s, bias, out, out_s, total_pix, InC, OutC, stride, Din, Dout, act, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace aic

@@ -1,0 +1,94 @@
+// Critic head (A13): the gated leaky complex recurrent cell and its scalar
+// read-out (AICortex kernels.h:1685-1778, critic.h:106-116), batched over
+// sequences and looped over time. One warp per (sequence, unit) keeps the
+// unit's complex state in registers across all steps and writes it per step;
+// a second kernel reduces the per-step states to the score with the
+// reference's shuffle-down tree.
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+
+namespace aic {
+namespace {
+
+constexpr int kThreads = 256;
+
+__global__ void __launch_bounds__(kThreads) critic_cell_kernel(const __half* __restrict__ x, const float* __restrict__ w1,
+                                                             const float* __restrict__ wl, int in, int units,
+                                                             float2* __restrict__ h, float2* __restrict__ h_seq, int T)
+{
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
+    const int b = blockIdx.y;
+    if (j >= units) return;
+    float2 hv = h[static_cast<int64_t>(b) * units + j];
+    for (int t = 0; t < T; ++t) {
+        const int64_t row = static_cast<int64_t>(b) * T + t;
+        const __half* xr = x + row * in;
+        float vr = 0.0f, vi = 0.0f, lr = 0.0f, li = 0.0f;
+        for (int c = lane; c < in; c += 32) {
+            const float xf = __half2float(xr[c]);
+            const int64_t i1 = (static_cast<int64_t>(c) * units + j) << 1;
+            const int64_t il = (static_cast<int64_t>(j) * in + c) << 1;
+            vr = fmaf(xf, w1[i1], vr);
+            vi = fmaf(xf, w1[i1 + 1], vi);
+            lr = fmaf(xf, wl[il], lr);
+            li = fmaf(xf, wl[il + 1], li);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            vr += __shfl_down_sync(0xFFFFFFFFu, vr, o);
+            vi += __shfl_down_sync(0xFFFFFFFFu, vi, o);
+            lr += __shfl_down_sync(0xFFFFFFFFu, lr, o);
+            li += __shfl_down_sync(0xFFFFFFFFu, li, o);
+        }
+        if (lane == 0) {
+            const float sr = sigmoid_f(vr), si = sigmoid_f(vi);
+            const float lam = sigmoid_f(sqrtf(fmaf(lr, lr, fmaf(li, li, kEps))));
+            const float dh = 1.0f - lam;
+            const float ar = vr * sr, ai = vi * si;
+            hv = make_float2(fmaf(hv.x, lam, dh * ar), fmaf(hv.y, lam, dh * ai));
+            h_seq[row * units + j] = hv;
+        }
+    }
+    if (lane == 0) h[static_cast<int64_t>(b) * units + j] = hv;
+}
+
+// One CTA of `units` threads per (sequence, step).
+__global__ void critic_score_kernel(const float2* __restrict__ h_seq, const float* __restrict__ w2, int units,
+                                    float* __restrict__ score)
+{
+    __shared__ float warp_sums[32];
+    const int64_t row = blockIdx.x;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    float s = 0.0f;
+    for (int i = threadIdx.x; i < units; i += blockDim.x) {
+        const float2 f = h_seq[row * units + i];
+        s = fmaf(f.x, w2[i << 1], fmaf(f.y, w2[(i << 1) + 1], s));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_down_sync(0xFFFFFFFFu, s, o);
+    if (lane == 0) warp_sums[wid] = s;
+    __syncthreads();
+    if (wid == 0) {
+        float f = lane < nw ? warp_sums[lane] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) f += __shfl_down_sync(0xFFFFFFFFu, f, o);
+        if (lane == 0) score[row] = f;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_critic(const __half* x, const float* w1, const float* wl, const float* w2, int in, int units,
+                          float2* h, float2* h_seq, float* score, int B, int T, cudaStream_t stream)
+{
+    if (B == 0 || T == 0) return cudaSuccess;
+    dim3 grid(static_cast<unsigned>((units + kThreads / 32 - 1) / (kThreads / 32)), static_cast<unsigned>(B));
+    critic_cell_kernel<<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    critic_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), units, 0, stream>>>(h_seq, w2, units, score);
+    return cudaGetLastError();
+}
+
+}  // namespace aic

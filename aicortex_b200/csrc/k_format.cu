@@ -1,0 +1,309 @@
+// Format kernels of the inference path: weight/activation packing (A1), the
+// fp16 stem packer (A2), the per-position residual add (A6), global average
+// pooling (A8) and Bernoulli action sampling (A12). All are HBM-bound integer
+// and byte work, written as coalesced SIMT kernels.
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+
+namespace aic {
+namespace {
+
+constexpr int kThreads = 256;
+
+// Position hash of the reference packer (kernels.h:21-37, device branch): the
+// base is the global thread index, which for the packer is the group index.
+__device__ __forceinline__ uint32_t position_seed(uint32_t tid, int32_t sample)
+{
+    uint32_t s = tid + static_cast<uint32_t>(sample) * 2654435761u;
+    s = (s ^ 61u) ^ (s >> 16);
+    s *= 9u;
+    s ^= s >> 4;
+    s *= 668265261u;
+    s ^= s >> 15;
+    return s == 0u ? 123456789u : s;
+}
+
+// xorshift32 mapped to a float with the reference's factor. The reference
+// writes `(1.0f / 0xFFFFFFFFf)`, where 0xFFFFFFFFf is the integer 2^36-1, so
+// the factor is exactly 2^-36 and the result lies in [0, n/16).
+__device__ __forceinline__ float hashed_uniform(uint32_t seed, float n)
+{
+    seed ^= seed << 13;
+    seed ^= seed >> 17;
+    seed ^= seed << 5;
+    return __uint2float_rn(seed) * (1.0f / 68719476736.0f) * n;
+}
+
+template <bool kStochastic>
+__global__ void __launch_bounds__(kThreads) pack_f32_kernel(const float* __restrict__ in, uint32_t* __restrict__ out,
+                                                          int8_t* __restrict__ out_s, int64_t groups, int32_t add_idx,
+                                                          int64_t row_groups)
+{
+    const int64_t idx = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (idx >= groups) return;
+    float v[32];
+    const float4* src = reinterpret_cast<const float4*>(in + (idx << 5));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 f = src[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    const float scale = amax < kEps ? 1.0f : amax;
+    out_s[idx] = exponent_of(scale);
+    const float inv = kQMax * __frcp_rn(scale);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    if (kStochastic) {
+        const int64_t rel = row_groups > 0 ? idx % row_groups : idx;
+        const uint32_t tid = static_cast<uint32_t>(rel);
+        const uint32_t group_seed = position_seed(tid, static_cast<int32_t>(rel + add_idx));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float scaled = fmaxf(-8.0f, fminf(kQMax, v[i] * inv));
+            const int lo = __float2int_rd(scaled);
+            const float u = hashed_uniform(position_seed(tid, static_cast<int32_t>(group_seed ^ static_cast<uint32_t>(i))), 1.0f);
+            const int q = lo + (u < scaled - __int2float_rd(lo));
+            w[i >> 3] |= (static_cast<uint32_t>(q) & 0xFu) << ((i & 7) << 2);
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn(v[i], inv) << ((i & 7) << 2);
+    }
+    reinterpret_cast<uint4*>(out)[idx] = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// One thread per pixel: reads the present fp16 planes (coalesced along the
+// row), zero-fills the rest of the 32-channel group(s), quantises, writes one
+// 16-byte group per 32 channels.
+__global__ void __launch_bounds__(kThreads) stem_pack_kernel(const __half* __restrict__ planes, int64_t pixels, int hw,
+                                                           int planes_present, int channels, uint32_t* __restrict__ out,
+                                                           int8_t* __restrict__ out_s)
+{
+    const int64_t pix = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (pix >= pixels) return;
+    const int64_t frame = pix / hw;
+    const int64_t sp = pix - frame * hw;
+    const int groups = channels >> 5;
+    for (int g = 0; g < groups; ++g) {
+        float v[32];
+#pragma unroll
+        for (int l = 0; l < 32; ++l) {
+            const int c = (g << 5) + l;
+            v[l] = c < planes_present ? __half2float(planes[(frame * planes_present + c) * hw + sp]) : 0.0f;
+        }
+        uint4 words;
+        int8_t e;
+        quantize_group(v, &words, &e);
+        reinterpret_cast<uint4*>(out)[pix * groups + g] = words;
+        out_s[pix * groups + g] = e;
+    }
+}
+
+// Residual add with one exponent per position. A position is handled by a
+// segment of S lanes (S = next power of two >= C/32, at most 32); each lane
+// walks groups gl, gl+S, ... The values are recomputed in the second pass
+// instead of being kept, which is bit-identical and needs no shared memory.
+template <int S>
+__global__ void __launch_bounds__(kThreads) residual_kernel(const uint32_t* __restrict__ main_in, const int8_t* __restrict__ main_s,
+                                                          const uint32_t* __restrict__ res, const int8_t* __restrict__ res_s,
+                                                          uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
+                                                          int64_t positions, int C, float main_mult, bool skipped)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int64_t pos = warp * (32 / S) + lane / S;
+    const int gl = lane % S;
+    const bool live = pos < positions;
+    const int G = C >> 5;
+    const int64_t pbase = live ? pos : 0;
+    const uint4* mv = reinterpret_cast<const uint4*>(main_in) + pbase * G;
+    const uint4* rv = reinterpret_cast<const uint4*>(res) + pbase * G;
+    float amax = 0.0f;
+    for (int g = gl; live && g < G; g += S) {
+        const float s_res = unit_of(res_s[pbase * G + g]);
+        const float s_in = skipped ? 0.0f : unit_of(main_s[pbase * G + g]) * main_mult;
+        const uint4 a = skipped ? make_uint4(0u, 0u, 0u, 0u) : mv[g];
+        const uint4 b = rv[g];
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float r = fmaf(static_cast<float>(code_of(aw[i], e)), s_in, static_cast<float>(code_of(bw[i], e)) * s_res);
+                amax = fmaxf(amax, fabsf(r));
+            }
+    }
+#pragma unroll
+    for (int o = S >> 1; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+    if (!live) return;
+    const float scale = amax < kEps ? 1.0f : amax;
+    const float inv = kQMax * __frcp_rn(scale);
+    const int8_t e_out = exponent_of(scale);
+    uint4* ov = reinterpret_cast<uint4*>(out) + pos * G;
+    for (int g = gl; g < G; g += S) {
+        const float s_res = unit_of(res_s[pos * G + g]);
+        const float s_in = skipped ? 0.0f : unit_of(main_s[pos * G + g]) * main_mult;
+        const uint4 a = skipped ? make_uint4(0u, 0u, 0u, 0u) : mv[g];
+        const uint4 b = rv[g];
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            w[i] = 0u;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const float r = fmaf(static_cast<float>(code_of(aw[i], e)), s_in, static_cast<float>(code_of(bw[i], e)) * s_res);
+                w[i] |= code_rn(r, inv) << (e << 2);
+            }
+        }
+        ov[g] = make_uint4(w[0], w[1], w[2], w[3]);
+        out_s[pos * G + g] = e_out;
+    }
+}
+
+// Global average pool: one warp per (frame, 32-channel group), lane = channel.
+// Partial sums over blocks of 16 pixels (the reference's per-CTA chunk) are
+// combined in block order, which makes the result deterministic.
+template <bool kHalf>
+__global__ void __launch_bounds__(kThreads) gap_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
+                                                     int64_t frames, int HW, int C, float* __restrict__ out_f32,
+                                                     __half* __restrict__ out_f16, uint32_t* __restrict__ out_q,
+                                                     int8_t* __restrict__ out_qs)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int G = C >> 5;
+    if (warp >= frames * G) return;
+    const int64_t frame = warp / G;
+    const int g = static_cast<int>(warp - frame * G);
+    const int c = (g << 5) + lane;
+    const float inv = __frcp_rn(static_cast<float>(HW));
+    float acc = 0.0f;
+    __half acc_h = __float2half_rn(0.0f);
+    for (int start = 0; start < HW; start += 16) {
+        const int end = min(start + 16, HW);
+        float part = 0.0f;
+        for (int i = start; i < end; ++i) {
+            const int64_t sp = frame * HW + i;
+            const uint32_t w = in[sp * (C >> 3) + (c >> 3)];
+            part = fmaf(static_cast<float>(code_of(w, c & 7)), unit_of(in_s[sp * G + g]), part);
+        }
+        // __fmul_rn keeps the scaled partial separately rounded (as it is when
+        // the reference hands it to atomicAdd) instead of letting the
+        // compiler fuse it into the running sum.
+        if (kHalf) acc_h = __hadd(acc_h, __float2half_rn(__fmul_rn(part, inv)));
+        else acc = __fadd_rn(acc, __fmul_rn(part, inv));
+    }
+    const int64_t oi = frame * C + c;
+    if (kHalf) {
+        out_f16[oi] = acc_h;
+        return;
+    }
+    if (out_f32) out_f32[oi] = acc;
+    if (out_q) {
+        float amax = fabsf(acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+        const float scale = amax < kEps ? 1.0f : amax;
+        uint32_t q = code_rn(acc, kQMax * __frcp_rn(scale)) << ((lane & 7) << 2);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) q |= __shfl_down_sync(0xFFFFFFFFu, q, o);
+        if ((lane & 7) == 0) out_q[frame * (C >> 3) + (g << 2) + (lane >> 3)] = q;
+        if (lane == 0) out_qs[frame * G + g] = exponent_of(scale);
+    }
+}
+
+// Action bits: thread per (row, 64-bit word), bit j set when the position hash
+// of (int(p * 65504) ^ j) maps below p.
+__global__ void __launch_bounds__(kThreads) set_actions_kernel(const float* __restrict__ probs, int64_t rows, int A,
+                                                             unsigned long long* __restrict__ actions)
+{
+    const int words = (A + 63) >> 6;
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (t >= rows * words) return;
+    const int64_t row = t / words;
+    const int wi = static_cast<int>(t - row * words);
+    unsigned long long bits = 0ull;
+    for (int j = wi << 6; j < min(A, (wi + 1) << 6); ++j) {
+        const float p = probs[row * A + j];
+        const int32_t sample = static_cast<int32_t>(p * 65504.0f) ^ j;
+        if (hashed_uniform(position_seed(static_cast<uint32_t>(j), sample), 1.0f) < p) bits |= 1ull << (j & 63);
+    }
+    actions[t] = bits;
+}
+
+inline unsigned grid_for(int64_t threads) { return static_cast<unsigned>((threads + kThreads - 1) / kThreads); }
+
+}  // namespace
+
+cudaError_t launch_pack_f32(const float* in, int64_t n, uint32_t* out, int8_t* out_s, bool stochastic, int32_t add_idx,
+                            int64_t row_groups, cudaStream_t stream)
+{
+    const int64_t groups = n >> 5;
+    if (groups == 0) return cudaSuccess;
+    if (stochastic) pack_f32_kernel<true><<<grid_for(groups), kThreads, 0, stream>>>(in, out, out_s, groups, add_idx, row_groups);
+    else pack_f32_kernel<false><<<grid_for(groups), kThreads, 0, stream>>>(in, out, out_s, groups, add_idx, row_groups);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_stem_pack(const __half* planes, int64_t frames, int planes_present, int channels, int dim,
+                             uint32_t* out, int8_t* out_s, cudaStream_t stream)
+{
+    const int64_t pixels = frames * dim * dim;
+    if (pixels == 0) return cudaSuccess;
+    stem_pack_kernel<<<grid_for(pixels), kThreads, 0, stream>>>(planes, pixels, dim * dim, planes_present, channels, out, out_s);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_residual(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res, const int8_t* res_s,
+                            uint32_t* out, int8_t* out_s, int64_t positions, int C, float main_mult, bool skipped,
+                            cudaStream_t stream)
+{
+    if (positions == 0) return cudaSuccess;
+    const int G = C >> 5;
+    int S = 1;
+    while (S < G && S < 32) S <<= 1;
+    const int64_t warps = (positions + (32 / S) - 1) / (32 / S);
+    const unsigned grid = grid_for(warps * 32);
+#define AIC_RES(SS) residual_kernel<SS><<<grid, kThreads, 0, stream>>>(main_in, main_s, res, res_s, out, out_s, positions, C, main_mult, skipped)
+    switch (S) {
+        case 1: AIC_RES(1); break;
+        case 2: AIC_RES(2); break;
+        case 4: AIC_RES(4); break;
+        case 8: AIC_RES(8); break;
+        case 16: AIC_RES(16); break;
+        default: AIC_RES(32); break;
+    }
+#undef AIC_RES
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gap(const uint32_t* in, const int8_t* in_s, int64_t frames, int HW, int C, float* out_f32,
+                       uint32_t* out_q, int8_t* out_qs, cudaStream_t stream)
+{
+    const int64_t warps = frames * (C >> 5);
+    if (warps == 0) return cudaSuccess;
+    gap_kernel<false><<<grid_for(warps * 32), kThreads, 0, stream>>>(in, in_s, frames, HW, C, out_f32, nullptr, out_q, out_qs);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frames, int HW, int C, __half* out,
+                           cudaStream_t stream)
+{
+    const int64_t warps = frames * (C >> 5);
+    if (warps == 0) return cudaSuccess;
+    gap_kernel<true><<<grid_for(warps * 32), kThreads, 0, stream>>>(in, in_s, frames, HW, C, nullptr, out, nullptr, nullptr);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned long long* actions, cudaStream_t stream)
+{
+    const int64_t n = rows * ((A + 63) >> 6);
+    if (n == 0) return cudaSuccess;
+    set_actions_kernel<<<grid_for(n), kThreads, 0, stream>>>(probs, rows, A, actions);
+    return cudaGetLastError();
+}
+
+}  // namespace aic

@@ -1,0 +1,479 @@
+"""Python mirror of the reference's layer classes over the C ABI.
+
+ConvLayer, ConvBlock, MambaLayer, MambaBlock and Critic keep the reference's
+construction (dimensions in the constructor, weights loaded from fp32 masters
+or the reference's .bin checkpoint files) and forward() signatures, with
+batch and sequence extents added. Device memory (parameters, recurrent state,
+workspace) is allocated here with torch and bound to the C handles; all
+compute runs in libaicortex_b200.so on the caller's current CUDA stream.
+
+Activation tensors use the packed int4 layout of the reference: words as an
+int32 tensor [rows, C // 8] and exponents as an int8 tensor [rows, C // 32].
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from ._lib import call
+
+_ALIGN = 256
+
+
+def _vp(t: Optional[torch.Tensor]) -> Optional[C.c_void_p]:
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream: Optional[torch.cuda.Stream] = None) -> C.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+class _Arena:
+    """A 256-byte aligned device byte buffer owned by torch."""
+
+    def __init__(self, nbytes: int, device: torch.device):
+        self.nbytes = int(nbytes)
+        self.raw = torch.empty(max(self.nbytes, 1) + _ALIGN, dtype=torch.uint8, device=device)
+        self.offset = (-self.raw.data_ptr()) % _ALIGN
+        self.ptr = self.raw.data_ptr() + self.offset
+
+    def view(self, ptr: int, count: int, dtype: torch.dtype) -> torch.Tensor:
+        """Tensor view of `count` elements at device address `ptr` inside the arena."""
+        start = ptr - self.raw.data_ptr()
+        nb = count * torch.tensor([], dtype=dtype).element_size()
+        assert 0 <= start and start + nb <= self.raw.numel(), "view outside arena"
+        return self.raw[start:start + nb].view(dtype)
+
+
+def _size_out() -> C.c_size_t:
+    return C.c_size_t(0)
+
+
+def empty_f(rows: int, channels: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
+    """Uninitialised packed int4 activation tensor pair for rows x channels."""
+    return (torch.empty(rows, channels // 8, dtype=torch.int32, device=device),
+            torch.empty(rows, channels // 32, dtype=torch.int8, device=device))
+
+
+class _Handle:
+    _destroy = ""
+
+    def __init__(self, handle: C.c_void_p, owned: bool):
+        self.h = handle
+        self.owned = owned
+
+    def __del__(self):
+        if getattr(self, "owned", False) and self.h:
+            try:
+                getattr(_lib.lib, self._destroy)(self.h)
+            except Exception:
+                pass
+            self.h = None
+
+
+class ConvLayer(_Handle):
+    """ConvLayer (conv_layer.h): depthwise / dense / pointwise quantized conv."""
+    _destroy = "aic_conv_layer_destroy"
+
+    def __init__(self, in_channels, out_channels, kernel_size, stride, dim_in, dim_out, disable_activation=False,
+                 device="cuda", _handle: Optional[C.c_void_p] = None):
+        self.desc = _lib.ConvLayerDesc(in_channels, out_channels, kernel_size, stride, dim_in, dim_out,
+                                       int(disable_activation))
+        self.device = torch.device(device)
+        if _handle is None:
+            h = C.c_void_p()
+            call("aic_conv_layer_create", C.byref(self.desc), C.byref(h))
+            super().__init__(h, True)
+            self.params = _Arena(self._param_bytes(), self.device)
+            call("aic_conv_layer_bind", self.h, C.c_void_p(self.params.ptr))
+        else:
+            super().__init__(_handle, False)
+            self.params = None
+        we, be = C.c_int64(), C.c_int64()
+        call("aic_conv_layer_sizes", self.h, C.byref(we), C.byref(be), None)
+        self.weight_elems, self.bias_elems = we.value, be.value
+
+    def _param_bytes(self) -> int:
+        nb = _size_out()
+        call("aic_conv_layer_sizes", self.h, None, None, C.byref(nb))
+        return nb.value
+
+    def load_weights(self, master: torch.Tensor, bias: torch.Tensor, stream=None) -> None:
+        assert master.dtype == torch.float32 and master.numel() == self.weight_elems and master.is_contiguous()
+        assert bias.dtype == torch.float32 and bias.numel() == self.bias_elems
+        call("aic_conv_layer_load_weights", self.h, _vp(master), _vp(bias), _stream(stream))
+
+    def load_file(self, path: str, stream=None) -> None:
+        call("aic_conv_layer_load_file_sync", self.h, str(path).encode(), _stream(stream))
+
+    def packed(self, arena: Optional[_Arena] = None):
+        """(words int32, exponents int8, bias fp32) device views of the bound parameters."""
+        arena = arena or self.params
+        w, s, b = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        call("aic_conv_layer_param_ptrs", self.h, C.byref(w), C.byref(s), C.byref(b))
+        g = self.weight_elems // 32
+        return (arena.view(w.value, 4 * g, torch.int32), arena.view(s.value, g, torch.int8),
+                arena.view(b.value, self.bias_elems, torch.float32))
+
+    def forward(self, x, x_s, out, out_s, frames: int, stream=None) -> None:
+        call("aic_conv_layer_forward", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames), _stream(stream))
+
+
+class ConvBlock(_Handle):
+    """ConvBlock (conv_block.h): dw -> pw1 (SiLU) -> pw2, shortcut, residual add."""
+    _destroy = "aic_conv_block_destroy"
+    LAYER_FILES = ("depthwise_layer.bin", "conv_layer1.bin", "conv_layer2.bin", "residual_layer.bin")
+
+    def __init__(self, in_channels, mid_channels, out_channels, stride, dim_in, dim_out, dw_kernel,
+                 survival_probability=1.0, residual_factor=1.0, device="cuda", _handle=None, _arena=None):
+        self.desc = _lib.ConvBlockDesc(in_channels, mid_channels, out_channels, stride, dim_in, dim_out, dw_kernel,
+                                       survival_probability, residual_factor)
+        self.device = torch.device(device)
+        if _handle is None:
+            h = C.c_void_p()
+            call("aic_conv_block_create", C.byref(self.desc), C.byref(h))
+            super().__init__(h, True)
+            nb = _size_out()
+            call("aic_conv_block_param_bytes", self.h, C.byref(nb))
+            self.params = _Arena(nb.value, self.device)
+            call("aic_conv_block_bind", self.h, C.c_void_p(self.params.ptr))
+        else:
+            super().__init__(_handle, False)
+            self.params = _arena
+        stride1 = stride if dim_in != dim_out else 1
+        geo = [(in_channels, in_channels, dw_kernel, stride1, dim_in, dim_out, True),
+               (in_channels, mid_channels, 1, 1, dim_out, dim_out, False),
+               (mid_channels, out_channels, 1, 1, dim_out, dim_out, True),
+               (in_channels, out_channels, stride1, stride1, dim_in, dim_out, True)]
+        self.layers = []
+        for i, g in enumerate(geo):
+            lh = C.c_void_p()
+            call("aic_conv_block_layer", self.h, i, C.byref(lh))
+            layer = ConvLayer(*g, device=device, _handle=lh)
+            layer.params = self.params
+            self.layers.append(layer)
+        self._ws = None
+
+    def workspace(self, frames: int) -> _Arena:
+        nb = _size_out()
+        call("aic_conv_block_workspace_bytes", self.h, int(frames), C.byref(nb))
+        if self._ws is None or self._ws.nbytes < nb.value:
+            self._ws = _Arena(nb.value, self.device)
+        return self._ws
+
+    def load_dir(self, path: str, stream=None) -> None:
+        call("aic_conv_block_load_dir_sync", self.h, str(path).encode(), _stream(stream))
+
+    def forward(self, x, x_s, out, out_s, frames: int, train_mode=False, is_survived=True, stream=None) -> None:
+        ws = self.workspace(frames)
+        call("aic_conv_block_forward", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames), int(train_mode),
+             int(is_survived), C.c_void_p(ws.ptr), _stream(stream))
+
+
+class MambaLayer(_Handle):
+    """MambaLayer (mamba_layer.h): SSM step + out-proj + RMSNorm + bias + activation."""
+    _destroy = "aic_mamba_layer_destroy"
+
+    def __init__(self, d_model, d_state, out_channels, activation, device="cuda", _handle=None, _arena=None):
+        self.desc = _lib.MambaLayerDesc(d_model, d_state, out_channels, activation)
+        self.device = torch.device(device)
+        if _handle is None:
+            h = C.c_void_p()
+            call("aic_mamba_layer_create", C.byref(self.desc), C.byref(h))
+            super().__init__(h, True)
+            nb = _size_out()
+            call("aic_mamba_layer_sizes", self.h, None, None, C.byref(nb))
+            self.params = _Arena(nb.value, self.device)
+            call("aic_mamba_layer_bind", self.h, C.c_void_p(self.params.ptr))
+        else:
+            super().__init__(_handle, False)
+            self.params = _arena
+        we, be = C.c_int64(), C.c_int64()
+        call("aic_mamba_layer_sizes", self.h, C.byref(we), C.byref(be), None)
+        self.weight_elems, self.bias_elems = we.value, be.value
+        self.state = None
+        self.batch = None
+        self._ws = None
+
+    def load_weights(self, master: torch.Tensor, bias: torch.Tensor, stream=None) -> None:
+        assert master.dtype == torch.float32 and master.numel() == self.weight_elems and master.is_contiguous()
+        assert bias.dtype == torch.float32 and bias.numel() == self.bias_elems
+        call("aic_mamba_layer_load_weights", self.h, _vp(master), _vp(bias), _stream(stream))
+
+    def load_file(self, path: str, stream=None) -> None:
+        call("aic_mamba_layer_load_file_sync", self.h, str(path).encode(), _stream(stream))
+
+    def packed(self):
+        w, s, b = C.c_void_p(), C.c_void_p(), C.c_void_p()
+        call("aic_mamba_layer_param_ptrs", self.h, C.byref(w), C.byref(s), C.byref(b))
+        g = self.weight_elems // 32
+        return (self.params.view(w.value, 4 * g, torch.int32), self.params.view(s.value, g, torch.int8),
+                self.params.view(b.value, self.bias_elems, torch.float32))
+
+    def bind_state(self, batch: int, stream=None) -> None:
+        nb = _size_out()
+        call("aic_mamba_layer_state_bytes", self.h, int(batch), C.byref(nb))
+        self.state = _Arena(nb.value, self.device)
+        self.batch = int(batch)
+        call("aic_mamba_layer_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
+        self.reset(stream)
+
+    def state_tensor(self) -> torch.Tensor:
+        """Recurrent state view [batch, 2*d_model, d_state // 32, 2] fp32."""
+        E, Pn = 2 * self.desc.d_model, self.desc.d_state // 32
+        n = self.batch * E * Pn * 2
+        return self.state.view(self.state.ptr, n, torch.float32).view(self.batch, E, Pn, 2)
+
+    def reset(self, stream=None) -> None:
+        call("aic_mamba_layer_reset_state", self.h, _stream(stream))
+
+    def workspace(self, rows: int) -> _Arena:
+        nb = _size_out()
+        call("aic_mamba_layer_workspace_bytes", self.h, int(rows), C.byref(nb))
+        if self._ws is None or self._ws.nbytes < nb.value:
+            self._ws = _Arena(nb.value, self.device)
+        return self._ws
+
+    def outproj(self, y: torch.Tensor, out: torch.Tensor, rows: int, stream=None) -> None:
+        call("aic_mamba_layer_outproj", self.h, _vp(y), _vp(out), int(rows), _stream(stream))
+
+    def forward(self, x, x_s, out, batch: int, seq: int, stream=None) -> None:
+        ws = self.workspace(batch * seq)
+        call("aic_mamba_layer_forward", self.h, _vp(x), _vp(x_s), _vp(out), int(batch), int(seq), C.c_void_p(ws.ptr),
+             _stream(stream))
+
+
+class MambaBlock(_Handle):
+    """MambaBlock (mamba_block.h): strategist -> requant -> residual -> tactic -> requant -> executor."""
+    _destroy = "aic_mamba_block_destroy"
+    LAYER_FILES = ("mamba_strategist.bin", "mamba_tactic.bin", "mamba_executor.bin")
+
+    def __init__(self, d_model, d_state, out_channels, activation=2, survival_probability=1.0, residual_factor=1.0,
+                 device="cuda"):
+        self.desc = _lib.MambaBlockDesc(d_model, d_state, out_channels, activation, survival_probability,
+                                        residual_factor)
+        self.device = torch.device(device)
+        h = C.c_void_p()
+        call("aic_mamba_block_create", C.byref(self.desc), C.byref(h))
+        super().__init__(h, True)
+        nb = _size_out()
+        call("aic_mamba_block_param_bytes", self.h, C.byref(nb))
+        self.params = _Arena(nb.value, self.device)
+        call("aic_mamba_block_bind", self.h, C.c_void_p(self.params.ptr))
+        outs = (d_model, d_model, out_channels)
+        acts = (1, 1, activation)
+        self.layers = []
+        for i in range(3):
+            lh = C.c_void_p()
+            call("aic_mamba_block_layer", self.h, i, C.byref(lh))
+            self.layers.append(MambaLayer(d_model, d_state, outs[i], acts[i], device=device, _handle=lh,
+                                          _arena=self.params))
+        self.state = None
+        self.batch = None
+        self._ws = None
+
+    def bind_state(self, batch: int, stream=None) -> None:
+        nb = _size_out()
+        call("aic_mamba_block_state_bytes", self.h, int(batch), C.byref(nb))
+        self.state = _Arena(nb.value, self.device)
+        self.batch = int(batch)
+        call("aic_mamba_block_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
+        self.reset(stream)
+
+    def reset(self, stream=None) -> None:
+        call("aic_mamba_block_reset_state", self.h, _stream(stream))
+
+    def load_dir(self, path: str, stream=None) -> None:
+        call("aic_mamba_block_load_dir_sync", self.h, str(path).encode(), _stream(stream))
+
+    def forward(self, x, x_s, out, batch: int, seq: int, on_training=False, add_seed=0, is_survived=True,
+                stream=None) -> None:
+        nb = _size_out()
+        call("aic_mamba_block_workspace_bytes", self.h, int(batch * seq), C.byref(nb))
+        if self._ws is None or self._ws.nbytes < nb.value:
+            self._ws = _Arena(nb.value, self.device)
+        call("aic_mamba_block_forward", self.h, _vp(x), _vp(x_s), _vp(out), int(batch), int(seq), int(on_training),
+             int(add_seed), int(is_survived), C.c_void_p(self._ws.ptr), _stream(stream))
+
+
+class Critic(_Handle):
+    """Critic (critic.h): pooled fp16 features -> gated leaky complex cell -> score."""
+    _destroy = "aic_critic_destroy"
+
+    def __init__(self, in_channels, units, dim_in, device="cuda", _handle=None, _arena=None):
+        self.desc = _lib.CriticDesc(in_channels, units, dim_in)
+        self.device = torch.device(device)
+        if _handle is None:
+            h = C.c_void_p()
+            call("aic_critic_create", C.byref(self.desc), C.byref(h))
+            super().__init__(h, True)
+            nb = _size_out()
+            call("aic_critic_param_bytes", self.h, C.byref(nb))
+            self.params = _Arena(nb.value, self.device)
+            call("aic_critic_bind", self.h, C.c_void_p(self.params.ptr))
+        else:
+            super().__init__(_handle, False)
+            self.params = _arena
+        self.state = None
+        self.batch = None
+        self._ws = None
+
+    def load_weights(self, w1: torch.Tensor, w2: torch.Tensor, wl: torch.Tensor, stream=None) -> None:
+        call("aic_critic_load_weights", self.h, _vp(w1), _vp(w2), _vp(wl), _stream(stream))
+
+    def load_file(self, path: str, stream=None) -> None:
+        call("aic_critic_load_file_sync", self.h, str(path).encode(), _stream(stream))
+
+    def bind_state(self, batch: int, stream=None) -> None:
+        nb = _size_out()
+        call("aic_critic_state_bytes", self.h, int(batch), C.byref(nb))
+        self.state = _Arena(nb.value, self.device)
+        self.batch = int(batch)
+        call("aic_critic_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
+        self.reset(stream)
+
+    def reset(self, stream=None) -> None:
+        call("aic_critic_reset_state", self.h, _stream(stream))
+
+    def _workspace(self, rows: int) -> _Arena:
+        nb = _size_out()
+        call("aic_critic_workspace_bytes", self.h, int(rows), C.byref(nb))
+        if self._ws is None or self._ws.nbytes < nb.value:
+            self._ws = _Arena(nb.value, self.device)
+        return self._ws
+
+    def forward_pooled(self, pooled: torch.Tensor, score, batch: int, seq: int, stream=None) -> None:
+        assert pooled.dtype == torch.float16
+        self._workspace(batch * seq)
+        call("aic_critic_forward_pooled", self.h, _vp(pooled), _vp(score), int(batch), int(seq),
+             C.c_void_p(self._ws.ptr), _stream(stream))
+
+    def forward(self, x, x_s, score, batch: int, seq: int, stream=None) -> None:
+        self._workspace(batch * seq)
+        call("aic_critic_forward", self.h, _vp(x), _vp(x_s), _vp(score), int(batch), int(seq),
+             C.c_void_p(self._ws.ptr), _stream(stream))
+
+
+class Cortex(_Handle):
+    """Full forward: stem -> conv blocks -> GAP -> Mamba units -> actor (+ critic)."""
+    _destroy = "aic_cortex_destroy"
+
+    def __init__(self, desc: _lib.CortexDesc, device="cuda"):
+        self.desc = desc
+        self.device = torch.device(device)
+        h = C.c_void_p()
+        call("aic_cortex_create", C.byref(self.desc), C.byref(h))
+        super().__init__(h, True)
+        nb = _size_out()
+        call("aic_cortex_param_bytes", self.h, C.byref(nb))
+        self.params = _Arena(nb.value, self.device)
+        call("aic_cortex_bind", self.h, C.c_void_p(self.params.ptr))
+        self.blocks = []
+        for i in range(desc.n_blocks):
+            bh = C.c_void_p()
+            call("aic_cortex_block", self.h, i, C.byref(bh))
+            b = desc.blocks[i]
+            self.blocks.append(ConvBlock(b.in_channels, b.mid_channels, b.out_channels, b.stride, b.dim_in, b.dim_out,
+                                         b.dw_kernel, b.survival_probability, b.residual_factor, device=device,
+                                         _handle=bh, _arena=self.params))
+        self.units = []
+        for i in range(desc.n_units):
+            uh = C.c_void_p()
+            call("aic_cortex_unit", self.h, i, C.byref(uh))
+            self.units.append(MambaLayer(desc.d_model, desc.d_state, desc.d_model, 1, device=device, _handle=uh,
+                                         _arena=self.params))
+        ah = C.c_void_p()
+        call("aic_cortex_actor", self.h, C.byref(ah))
+        self.actor = MambaLayer(desc.d_model, desc.d_state, desc.actor_out, desc.actor_activation, device=device,
+                                _handle=ah, _arena=self.params)
+        self.critic = None
+        if desc.critic_units > 0:
+            ch = C.c_void_p()
+            call("aic_cortex_critic", self.h, C.byref(ch))
+            self.critic = Critic(desc.d_model, desc.critic_units, 1, device=device, _handle=ch, _arena=self.params)
+        self.state = None
+        self.batch = None
+        self._ws = None
+
+    def bind_state(self, batch: int, stream=None) -> None:
+        nb = _size_out()
+        call("aic_cortex_state_bytes", self.h, int(batch), C.byref(nb))
+        self.state = _Arena(nb.value, self.device)
+        self.batch = int(batch)
+        call("aic_cortex_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
+        self.reset(stream)
+
+    def reset(self, stream=None) -> None:
+        call("aic_cortex_reset_state", self.h, _stream(stream))
+
+    def workspace_bytes(self, batch: int, seq: int) -> int:
+        nb = _size_out()
+        call("aic_cortex_workspace_bytes", self.h, int(batch), int(seq), C.byref(nb))
+        return nb.value
+
+    def forward(self, planes: torch.Tensor, batch: int, seq: int, actor_out: torch.Tensor,
+                critic_out: Optional[torch.Tensor] = None, features: Optional[Sequence[torch.Tensor]] = None,
+                stream=None) -> int:
+        """Runs the forward; returns the number of kernel launches issued."""
+        assert planes.dtype == torch.float16 and planes.is_contiguous()
+        nb = self.workspace_bytes(batch, seq)
+        if self._ws is None or self._ws.nbytes < nb:
+            self._ws = _Arena(nb, self.device)
+        fw, fs = (features if features is not None else (None, None))
+        call("aic_cortex_forward", self.h, _vp(planes), int(batch), int(seq), _vp(actor_out), _vp(critic_out),
+             _vp(fw), _vp(fs), C.c_void_p(self._ws.ptr), _stream(stream))
+        n = C.c_int64()
+        call("aic_cortex_last_launches", self.h, C.byref(n))
+        return n.value
+
+
+def pack_f32(x: torch.Tensor, stochastic=False, add_idx=0, stream=None):
+    """quantizeKernel on a float32 device tensor (numel % 32 == 0)."""
+    assert x.dtype == torch.float32 and x.is_contiguous() and x.numel() % 32 == 0
+    g = x.numel() // 32
+    w = torch.empty(4 * g, dtype=torch.int32, device=x.device)
+    s = torch.empty(g, dtype=torch.int8, device=x.device)
+    call("aic_pack_f32", _vp(x), x.numel(), _vp(w), _vp(s), int(stochastic), int(add_idx), _stream(stream))
+    return w, s
+
+
+def stem_pack(planes: torch.Tensor, channels: int, stream=None):
+    """quantizeNCHWtoNHWCKernel over frames: planes fp16 [frames, P, dim, dim]."""
+    assert planes.dtype == torch.float16 and planes.is_contiguous() and planes.dim() == 4
+    f, p, dim, _ = planes.shape
+    w, s = empty_f(f * dim * dim, channels, planes.device)
+    call("aic_stem_pack", _vp(planes), f, p, channels, dim, _vp(w), _vp(s), _stream(stream))
+    return w, s
+
+
+def residual_add(main_w, main_s, res_w, res_s, positions, channels, main_mult=1.0, skipped=False, stream=None):
+    w, s = empty_f(positions, channels, res_w.device)
+    call("aic_residual_add", _vp(main_w), _vp(main_s), _vp(res_w), _vp(res_s), _vp(w), _vp(s), int(positions),
+         int(channels), float(main_mult), int(skipped), _stream(stream))
+    return w, s
+
+
+def gap(x_w, x_s, frames, hw, channels, quantize=True, stream=None):
+    out = torch.empty(frames, channels, dtype=torch.float32, device=x_w.device)
+    qw, qs = empty_f(frames, channels, x_w.device) if quantize else (None, None)
+    call("aic_gap", _vp(x_w), _vp(x_s), int(frames), int(hw), int(channels), _vp(out), _vp(qw), _vp(qs),
+         _stream(stream))
+    return out, qw, qs
+
+
+def gap_f16(x_w, x_s, frames, hw, channels, stream=None):
+    out = torch.empty(frames, channels, dtype=torch.float16, device=x_w.device)
+    call("aic_gap_f16", _vp(x_w), _vp(x_s), int(frames), int(hw), int(channels), _vp(out), _stream(stream))
+    return out
+
+
+def set_actions(probs: torch.Tensor, stream=None) -> torch.Tensor:
+    assert probs.dtype == torch.float32 and probs.dim() == 2 and probs.is_contiguous()
+    rows, count = probs.shape
+    out = torch.empty(rows, (count + 63) // 64, dtype=torch.int64, device=probs.device)
+    call("aic_set_actions", _vp(probs), rows, count, _vp(out), _stream(stream))
+    return out

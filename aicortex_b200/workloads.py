@@ -1,0 +1,126 @@
+"""Seeded synthetic workloads for the five benchmark configurations.
+
+The reference ships no datasets, checkpoints or golden data; every input and
+weight here is generated from a seed with numpy's PCG64. Shapes follow the
+configurations restated in the reference's own semantics:
+
+  cfg1  one Mamba unit (layer D=256 -> requant -> residual), B=1, T=64
+  cfg2  conv feature stack: 3x128x128 fp16 planes -> stem (32 ch) -> 4 ConvBlocks
+        (dw 3x3 s2, 32->64->128->256->256, mid = 2*out) -> global average pool
+  cfg3  full cortex forward: cfg2 stack -> 4 Mamba units (D=256) -> actor
+        (out 64, identity) and critic (128 complex units), B=256, T=128
+  cfg4  one Mamba layer D=1024, B=32, T=8192
+  cfg5  cfg3 architecture at B=4096, T=256
+
+"d_state = 16" in the configurations means 16 complex states per channel. The
+reference's SSM gives channel ch the states (ch & 31) + 32c, c < d_state/32,
+of its row, so 16 states per channel is the reference's d_state = 512.
+Weights: value = q8 * scale with q8 ~ U{-127..127} and one scale ~ U(0.001,
+0.01) per output row; biases ~ U(-0.1, 0.1); A_re = log(1 + c) for the c-th
+state of a channel (A = -(c+1) after the reference's -exp), A_im = 0.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+STATES_PER_CHANNEL = 16
+D_STATE = 32 * STATES_PER_CHANNEL
+
+
+def _rows(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    q8 = rng.integers(-127, 128, size=(rows, cols)).astype(np.float32)
+    scale = rng.uniform(0.001, 0.01, size=(rows, 1)).astype(np.float32)
+    return (q8 * scale).astype(np.float32)
+
+
+def conv_weights(rng: np.random.Generator, in_c: int, out_c: int, k: int, depthwise: bool) -> np.ndarray:
+    """fp32 master weights: [out][k*k][in] (dense/pointwise) or [k*k][C] (depthwise)."""
+    if depthwise:
+        return np.ascontiguousarray(_rows(rng, in_c, k * k).T).reshape(-1)
+    return _rows(rng, out_c, k * k * in_c).reshape(-1)
+
+
+def bias(rng: np.random.Generator, n: int) -> np.ndarray:
+    return rng.uniform(-0.1, 0.1, size=n).astype(np.float32)
+
+
+def mamba_blob(rng: np.random.Generator, d_model: int, d_state: int, out: int, a_im: float | None = 0.0) -> np.ndarray:
+    """fp32 master blob [W_delta | B_mimo | C_re | C_im | A_re | A_im | D | W_out] (mamba_layer.h:58)."""
+    E, N = 2 * d_model, d_state
+    wd = _rows(rng, 1, E).reshape(-1)
+    bm = _rows(rng, E, 32).reshape(-1)
+    cre = _rows(rng, E, N).reshape(-1)
+    cim = _rows(rng, E, N).reshape(-1)
+    are = np.tile(np.log1p(np.arange(N, dtype=np.float32) // 32).astype(np.float32), E)
+    if a_im is None:
+        aim = rng.uniform(-1.0, 1.0, size=E * N).astype(np.float32)
+    else:
+        aim = np.full(E * N, a_im, dtype=np.float32)
+    dd = _rows(rng, 1, E).reshape(-1)
+    wout = _rows(rng, out, E).reshape(-1)
+    blob = np.concatenate([wd, bm, cre, cim, are, aim, dd, wout]).astype(np.float32)
+    assert blob.size == E * (34 + 4 * N + out)
+    return blob
+
+
+def critic_weights(rng: np.random.Generator, in_c: int, units: int):
+    a = np.sqrt(2.0 / in_c)
+    w1 = rng.uniform(-a, a, size=in_c * units * 2).astype(np.float32)
+    w2 = rng.uniform(-np.sqrt(1.0 / units), np.sqrt(1.0 / units), size=units * 2).astype(np.float32)
+    wl = rng.uniform(-0.1, 0.1, size=units * in_c * 2).astype(np.float32)
+    return w1, w2, wl
+
+
+def planes_u01(rng: np.random.Generator, frames: int, planes: int = 3, dim: int = 128) -> np.ndarray:
+    """fp16 input planes [frames][planes][dim][dim] from U(0, 1)."""
+    return rng.random(size=(frames, planes, dim, dim), dtype=np.float32).astype(np.float16)
+
+
+# ---- stack geometry -------------------------------------------------------
+
+def cfg2_blocks(dim: int = 128):
+    """(in, mid, out, stride, dim_in, dim_out, dw_k) of the cfg2 conv stack."""
+    chans = [32, 64, 128, 256, 256]
+    out = []
+    d = dim
+    for i in range(4):
+        cin, cout = chans[i], chans[i + 1]
+        out.append((cin, 2 * cout, cout, 2, d, d // 2, 3))
+        d //= 2
+    return out
+
+
+def cortex_desc(batch_chunk: int = 2048, n_units: int = 4, d_model: int = 256, d_state: int = D_STATE,
+                actor_out: int = 64, critic_units: int = 128, dim: int = 128):
+    """CortexDesc of the cfg3/cfg5 architecture."""
+    from ._lib import ConvBlockDesc, CortexDesc
+    d = CortexDesc()
+    d.planes, d.stem_channels, d.dim = 3, 32, dim
+    blocks = cfg2_blocks(dim)
+    d.n_blocks = len(blocks)
+    for i, (cin, mid, cout, s, di, do, k) in enumerate(blocks):
+        d.blocks[i] = ConvBlockDesc(cin, mid, cout, s, di, do, k, 1.0, 1.0)
+    d.d_model, d.d_state, d.n_units = d_model, d_state, n_units
+    d.unit_residual_factor = 1.0
+    d.actor_out, d.actor_activation = actor_out, 0
+    d.critic_units = critic_units
+    d.chunk_frames = batch_chunk
+    return d
+
+
+def cortex_weights(seed: int, n_units: int = 4, d_model: int = 256, d_state: int = D_STATE, actor_out: int = 64,
+                   critic_units: int = 128, dim: int = 128):
+    """All fp32 master weights of the cfg3 architecture, in forward order."""
+    rng = np.random.default_rng(seed)
+    blocks = []
+    for (cin, mid, cout, s, di, do, k) in cfg2_blocks(dim):
+        blocks.append([
+            (conv_weights(rng, cin, cin, k, True), bias(rng, cin)),
+            (conv_weights(rng, cin, mid, 1, False), bias(rng, mid)),
+            (conv_weights(rng, mid, cout, 1, False), bias(rng, cout)),
+            (conv_weights(rng, cin, cout, s, False), bias(rng, cout)),
+        ])
+    units = [(mamba_blob(rng, d_model, d_state, d_model), bias(rng, d_model)) for _ in range(n_units)]
+    actor = (mamba_blob(rng, d_model, d_state, actor_out), bias(rng, actor_out))
+    critic = critic_weights(rng, d_model, critic_units)
+    return {"blocks": blocks, "units": units, "actor": actor, "critic": critic}

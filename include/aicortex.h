@@ -1,0 +1,300 @@
+/*
+ * aicortex.h -- C ABI of the B200 (sm_100a) implementation of the AICortex
+ * inference hot path: quantized conv/residual feature stack -> recurrent
+ * complex-diagonal SSM ("Mamba") layers -> actor and critic heads.
+ *
+ * The ABI mirrors the reference's layer classes and their two-phase
+ * construction (a constructor that reports byte counts, then initData()
+ * binding views into caller-owned arenas, then forward()), plus the
+ * reference's extern "C" opaque-state idiom (create / init / run / free in
+ * ca.cu:68-136 and cs.cu:75-136). Every reference forward() gains a batch
+ * dimension (independent environments) and a sequence dimension (successive
+ * calls of the reference, state carried between them); batch = seq = 1 is
+ * exactly one reference call.
+ *
+ * Rules:
+ *  - Functions never throw; they return an aic_status and leave a message for
+ *    aic_last_error() (thread-local).
+ *  - Tensor arguments are plain device pointers (device memory, or mapped
+ *    pinned host memory where noted), borrowed for the duration of the call.
+ *    Streams are cudaStream_t passed as void* (NULL = legacy default stream).
+ *  - Handles allocate no device memory: the caller queries the bytes needed,
+ *    allocates them and binds them (parameters once, recurrent state per batch
+ *    size, workspace per call). Every bound pointer must be 256-byte aligned.
+ *  - All launches are asynchronous on the given stream; nothing synchronises
+ *    except the functions whose name ends in _sync.
+ *  - One handle is used by one host thread / stream at a time.
+ *
+ * Packed int4 format ("F", reference kernels.h:56-85): a group is 32 signed
+ * 4-bit codes in four little-endian u32 words (code i in word i>>3, bits
+ * 4*(i&7)) and one int8 exponent s; the value of code q is
+ * q * max(2^s/7, 2^-13). Activations are NHWC: pixel p, group g -> words
+ * [p*C/8 + 4g .. 4g+3], exponent [p*C/32 + g]. Frames are stacked along the
+ * pixel axis; a sequence tensor's row for (env b, step t) is b*seq + t.
+ */
+#ifndef AICORTEX_H
+#define AICORTEX_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define AIC_API __attribute__((visibility("default")))
+#else
+#define AIC_API
+#endif
+
+typedef int aic_status;
+#define AIC_OK 0
+#define AIC_ERR_INVALID 1     /* bad argument, shape or alignment */
+#define AIC_ERR_UNSUPPORTED 2 /* configuration the reference does not support either */
+#define AIC_ERR_CUDA 3        /* CUDA launch/runtime error */
+#define AIC_ERR_STATE 4       /* handle not bound / state not bound */
+#define AIC_ERR_IO 5          /* checkpoint file missing, short or unreadable */
+
+AIC_API const char* aic_last_error(void);
+AIC_API int aic_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Stateless format kernels
+ * ---------------------------------------------------------------------- */
+
+/* quantizeKernel<float, !stochastic> (reference kernels.h:116-145), as used by
+ * ConvLayer/MambaLayer weight packing (conv_layer.h:98, mamba_layer.h:137:
+ * stochastic, add_idx = n) and by MambaBlock's activation requant
+ * (mamba_block.h:64,70: round-to-nearest, add_idx ignored). n % 32 == 0. */
+AIC_API aic_status aic_pack_f32(const float* in, int64_t n, uint32_t* out, int8_t* out_s, int stochastic,
+                                int32_t add_idx, void* stream);
+
+/* quantizeNCHWtoNHWCKernel<half> (kernels.h:146-195, cortex.h:294-295) over a
+ * batch: fp16 planes [frames][planes_present][dim][dim]; channels
+ * planes_present..channels-1 are zero (the reference zero-fills its capture
+ * buffer, cortex.h:291). Output F [frames*dim*dim][channels]. */
+AIC_API aic_status aic_stem_pack(const uint16_t* planes, int64_t frames, int planes_present, int channels, int dim,
+                                 uint32_t* out, int8_t* out_s, void* stream);
+
+/* residualAddFwdKernel (kernels.h:989-1055, conv_block.h:80-81,
+ * mamba_block.h:65): out = requant(main * main_mult + res) with one exponent
+ * per position; main is ignored when skipped != 0. */
+AIC_API aic_status aic_residual_add(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res,
+                                    const int8_t* res_s, uint32_t* out, int8_t* out_s, int64_t positions, int channels,
+                                    float main_mult, int skipped, void* stream);
+
+/* gapKernel<float> (kernels.h:1653-1684): mean over hw pixels of each frame ->
+ * fp32 [frames][C] (out_f32 may be NULL) and/or its round-to-nearest F
+ * requant [frames][C] (out_q/out_qs may be NULL). */
+AIC_API aic_status aic_gap(const uint32_t* in, const int8_t* in_s, int64_t frames, int hw, int channels, float* out_f32,
+                           uint32_t* out_q, int8_t* out_qs, void* stream);
+/* gapKernel<__half> on a zeroed pool (critic.h:108-111): fp16 bits [frames][C]. */
+AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frames, int hw, int channels,
+                               uint16_t* out, void* stream);
+
+/* setActionsKernel (kernels.h:1473-1485, cortex.h:371-372): per row of
+ * `count` probabilities, Bernoulli bits into [rows][(count+63)/64] words. */
+AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream);
+
+/* ------------------------------------------------------------------------
+ * ConvLayer (conv_layer.h): depthwise (odd k>1), dense (k = 2, 4; stride = k)
+ * or pointwise (k = 1) quantized conv with fused RMSNorm(256-channel chunks)
+ * + bias (+SiLU) + int4 requant.
+ * ---------------------------------------------------------------------- */
+typedef struct aic_conv_layer_t* aic_conv_layer;
+typedef struct {
+    int in_channels, out_channels, kernel_size, stride, dim_in, dim_out;
+    int disable_activation; /* reference ctor argument is_activation_disabled */
+} aic_conv_layer_desc;
+
+/* ConvLayer ctor (conv_layer.h:45-63). */
+AIC_API aic_status aic_conv_layer_create(const aic_conv_layer_desc* desc, aic_conv_layer* out);
+/* Byte count the ctor adds to total_mem_main_device (conv_layer.h:59), plus
+ * this implementation's tensor-core copy of the weights. */
+AIC_API aic_status aic_conv_layer_sizes(aic_conv_layer l, int64_t* weight_elems, int64_t* bias_elems,
+                                        size_t* param_bytes);
+/* initData arena carve (conv_layer.h:64-77). */
+AIC_API aic_status aic_conv_layer_bind(aic_conv_layer l, void* dev_params);
+AIC_API aic_status aic_conv_layer_param_ptrs(aic_conv_layer l, uint32_t** weights, int8_t** weight_scales,
+                                             float** bias);
+/* loadFromFile's device half (conv_layer.h:31-44): fp32 master weights
+ * ([out][k*k][in], or [k*k][C] for depthwise) and bias, device-accessible;
+ * packs with the reference's stochastic packer, bit-exact. */
+AIC_API aic_status aic_conv_layer_load_weights(aic_conv_layer l, const float* master, const float* bias,
+                                               void* stream);
+/* ConvLayer::loadFromFile (conv_layer.h:31-44): raw little-endian fp32
+ * master weights then fp32 bias. Host-side file read + pack. */
+AIC_API aic_status aic_conv_layer_load_file_sync(aic_conv_layer l, const char* path, void* stream);
+/* ConvLayer::forward (conv_layer.h:102-149) over `frames` frames. */
+AIC_API aic_status aic_conv_layer_forward(aic_conv_layer l, const uint32_t* in, const int8_t* in_s, uint32_t* out,
+                                          int8_t* out_s, int64_t frames, void* stream);
+AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l);
+
+/* ------------------------------------------------------------------------
+ * ConvBlock (conv_block.h): dw k x k -> pw1 (SiLU) -> pw2, shortcut (1x1 or
+ * 2x2/s2), residual add scaled by residual_factor.
+ * ---------------------------------------------------------------------- */
+typedef struct aic_conv_block_t* aic_conv_block;
+typedef struct {
+    int in_channels, mid_channels, out_channels, stride, dim_in, dim_out, dw_kernel;
+    float survival_probability, residual_factor;
+} aic_conv_block_desc;
+
+AIC_API aic_status aic_conv_block_create(const aic_conv_block_desc* desc, aic_conv_block* out);
+/* sub-layer i: 0 depthwise, 1 conv_layer1, 2 conv_layer2, 3 residual_layer (conv_block.h:18-21). */
+AIC_API aic_status aic_conv_block_layer(aic_conv_block b, int i, aic_conv_layer* out);
+AIC_API aic_status aic_conv_block_param_bytes(aic_conv_block b, size_t* bytes);
+AIC_API aic_status aic_conv_block_bind(aic_conv_block b, void* dev_params);
+/* Ping-pong buffers a/b (conv_block.h:63-66) for `frames` frames. */
+AIC_API aic_status aic_conv_block_workspace_bytes(aic_conv_block b, int64_t frames, size_t* bytes);
+/* ConvBlock::loadFromFile (conv_block.h:23-29): <dir>/{depthwise_layer,conv_layer1,conv_layer2,residual_layer}.bin */
+AIC_API aic_status aic_conv_block_load_dir_sync(aic_conv_block b, const char* dir, void* stream);
+/* ConvBlock::forward (conv_block.h:74-82). train_mode/is_survived select the
+ * stochastic-depth scaling of the main branch exactly as the reference. */
+AIC_API aic_status aic_conv_block_forward(aic_conv_block b, const uint32_t* in, const int8_t* in_s, uint32_t* out,
+                                          int8_t* out_s, int64_t frames, int train_mode, int is_survived,
+                                          void* workspace, void* stream);
+AIC_API aic_status aic_conv_block_destroy(aic_conv_block b);
+
+/* ------------------------------------------------------------------------
+ * MambaLayer (mamba_layer.h): recurrent complex-diagonal SSM step + out-proj
+ * + RMSNorm(256-chunks) + bias + activation (0 id, 1 SiLU, 2 sigmoid).
+ * d_model must be a power of two >= 32 (the reference indexes ch & (D-1));
+ * d_state a multiple of 32; channel ch owns the d_state/32 states
+ * (ch & 31) + 32c of its row, as the reference kernel does.
+ * ---------------------------------------------------------------------- */
+typedef struct aic_mamba_layer_t* aic_mamba_layer;
+typedef struct {
+    int d_model, d_state, out_channels, activation;
+} aic_mamba_layer_desc;
+
+AIC_API aic_status aic_mamba_layer_create(const aic_mamba_layer_desc* desc, aic_mamba_layer* out);
+/* weight_elems = 2*d_model*(34 + 4*d_state + out) (mamba_layer.h:58). */
+AIC_API aic_status aic_mamba_layer_sizes(aic_mamba_layer l, int64_t* weight_elems, int64_t* bias_elems,
+                                         size_t* param_bytes);
+AIC_API aic_status aic_mamba_layer_bind(aic_mamba_layer l, void* dev_params);
+AIC_API aic_status aic_mamba_layer_param_ptrs(aic_mamba_layer l, uint32_t** weights, int8_t** weight_scales,
+                                              float** bias);
+/* fp32 master blob [W_delta | B_mimo | C_re | C_im | A_re | A_im | D | W_out]
+ * (kernels.h:1084-1089) + bias; packs bit-exactly (mamba_layer.h:137). */
+AIC_API aic_status aic_mamba_layer_load_weights(aic_mamba_layer l, const float* master, const float* bias,
+                                                void* stream);
+AIC_API aic_status aic_mamba_layer_load_file_sync(aic_mamba_layer l, const char* path, void* stream);
+/* Recurrent state h: [batch][2*d_model][d_state/32] complex fp32 (the active
+ * entries of the reference's h_states, mamba_layer.h:90-92). */
+AIC_API aic_status aic_mamba_layer_state_bytes(aic_mamba_layer l, int batch, size_t* bytes);
+AIC_API aic_status aic_mamba_layer_bind_state(aic_mamba_layer l, void* dev_state, int batch);
+/* MambaLayer::reset (mamba_layer.h:171-177). */
+AIC_API aic_status aic_mamba_layer_reset_state(aic_mamba_layer l, void* stream);
+/* y_ssm [rows][2*d_model] fp32 (mamba_layer.h:93-95). */
+AIC_API aic_status aic_mamba_layer_workspace_bytes(aic_mamba_layer l, int64_t rows, size_t* bytes);
+/* MambaLayer::forward (mamba_layer.h:139-146) for `seq` successive steps of
+ * `batch` sequences: in F [batch*seq][d_model], out fp32 [batch*seq][out]. */
+AIC_API aic_status aic_mamba_layer_forward(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s, float* out,
+                                           int batch, int seq, void* workspace, void* stream);
+/* The out-projection alone (mambaSSMFwdOutProjKernel, kernels.h:1188-1259):
+ * y_ssm fp32 [rows][2*d_model] -> out fp32 [rows][out]. */
+AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, float* out, int64_t rows, void* stream);
+AIC_API aic_status aic_mamba_layer_destroy(aic_mamba_layer l);
+
+/* ------------------------------------------------------------------------
+ * MambaBlock (mamba_block.h): strategist (SiLU) -> requant -> residual with
+ * the block input -> tactic (SiLU) -> requant -> executor (activation).
+ * ---------------------------------------------------------------------- */
+typedef struct aic_mamba_block_t* aic_mamba_block;
+typedef struct {
+    int d_model, d_state, out_channels, activation;
+    float survival_probability, residual_factor;
+} aic_mamba_block_desc;
+
+AIC_API aic_status aic_mamba_block_create(const aic_mamba_block_desc* desc, aic_mamba_block* out);
+/* layer i: 0 strategist, 1 tactic, 2 executor (mamba_block.h:18-20). */
+AIC_API aic_status aic_mamba_block_layer(aic_mamba_block b, int i, aic_mamba_layer* out);
+AIC_API aic_status aic_mamba_block_param_bytes(aic_mamba_block b, size_t* bytes);
+AIC_API aic_status aic_mamba_block_bind(aic_mamba_block b, void* dev_params);
+AIC_API aic_status aic_mamba_block_state_bytes(aic_mamba_block b, int batch, size_t* bytes);
+AIC_API aic_status aic_mamba_block_bind_state(aic_mamba_block b, void* dev_state, int batch);
+AIC_API aic_status aic_mamba_block_reset_state(aic_mamba_block b, void* stream);
+AIC_API aic_status aic_mamba_block_workspace_bytes(aic_mamba_block b, int64_t rows, size_t* bytes);
+/* MambaBlock::loadFromFile (mamba_block.h:23-27): <dir>/mamba_{strategist,tactic,executor}.bin */
+AIC_API aic_status aic_mamba_block_load_dir_sync(aic_mamba_block b, const char* dir, void* stream);
+/* MambaBlock::forward (mamba_block.h:58-72): in F [batch*seq][d_model] ->
+ * out fp32 [batch*seq][out]. on_training selects the stochastic requant with
+ * add_seed, as in the reference. */
+AIC_API aic_status aic_mamba_block_forward(aic_mamba_block b, const uint32_t* in, const int8_t* in_s, float* out,
+                                           int batch, int seq, int on_training, int add_seed, int is_survived,
+                                           void* workspace, void* stream);
+AIC_API aic_status aic_mamba_block_destroy(aic_mamba_block b);
+
+/* ------------------------------------------------------------------------
+ * Critic (critic.h): global average pool of an F frame (fp16) -> gated leaky
+ * complex recurrent cell (`units` complex units, fp32 weights) -> scalar.
+ * ---------------------------------------------------------------------- */
+typedef struct aic_critic_t* aic_critic;
+typedef struct {
+    int in_channels, units, dim_in; /* reference ctor: out_channels = 2*units */
+} aic_critic_desc;
+
+AIC_API aic_status aic_critic_create(const aic_critic_desc* desc, aic_critic* out);
+AIC_API aic_status aic_critic_param_bytes(aic_critic c, size_t* bytes);
+AIC_API aic_status aic_critic_bind(aic_critic c, void* dev_params);
+/* W1 [in][units][2], W2 [units][2], Wlambda [units][in][2], fp32 (critic.h:36-38). */
+AIC_API aic_status aic_critic_load_weights(aic_critic c, const float* w1, const float* w2, const float* wl,
+                                           void* stream);
+AIC_API aic_status aic_critic_load_file_sync(aic_critic c, const char* path, void* stream);
+AIC_API aic_status aic_critic_state_bytes(aic_critic c, int batch, size_t* bytes);
+AIC_API aic_status aic_critic_bind_state(aic_critic c, void* dev_state, int batch);
+AIC_API aic_status aic_critic_reset_state(aic_critic c, void* stream);
+AIC_API aic_status aic_critic_workspace_bytes(aic_critic c, int64_t rows, size_t* bytes);
+/* Critic::forward (critic.h:106-116) for `seq` steps of `batch` sequences:
+ * in F [batch*seq][dim_in*dim_in][in], score fp32 [batch*seq]. */
+AIC_API aic_status aic_critic_forward(aic_critic c, const uint32_t* in, const int8_t* in_s, float* score, int batch,
+                                      int seq, void* workspace, void* stream);
+/* criticFwd1Kernel + criticFwd2Kernel on already pooled fp16 features
+ * [batch*seq][in] (critic.h:112-114 after the pooling step). */
+AIC_API aic_status aic_critic_forward_pooled(aic_critic c, const uint16_t* pooled, float* score, int batch, int seq,
+                                             void* workspace, void* stream);
+AIC_API aic_status aic_critic_destroy(aic_critic c);
+
+/* ------------------------------------------------------------------------
+ * Cortex forward (cortex.h:281-303 composition): stem pack -> conv blocks ->
+ * global average pool -> requant -> Mamba units (layer + requant + residual)
+ * -> actor layer, and the critic on the trunk output.
+ * ---------------------------------------------------------------------- */
+typedef struct aic_cortex_t* aic_cortex;
+#define AIC_MAX_BLOCKS 16
+typedef struct {
+    int planes, stem_channels, dim;          /* input fp16 planes, stem channels, input H = W */
+    int n_blocks;
+    aic_conv_block_desc blocks[AIC_MAX_BLOCKS];
+    int d_model, d_state, n_units;           /* Mamba trunk: n_units x (layer D->D SiLU + requant + residual) */
+    float unit_residual_factor;
+    int actor_out, actor_activation;         /* actor MambaLayer D -> actor_out */
+    int critic_units;                        /* 0 = no critic */
+    int chunk_frames;                        /* frames per conv-stack pass (0 = 2048) */
+} aic_cortex_desc;
+
+AIC_API aic_status aic_cortex_create(const aic_cortex_desc* desc, aic_cortex* out);
+AIC_API aic_status aic_cortex_block(aic_cortex c, int i, aic_conv_block* out);
+AIC_API aic_status aic_cortex_unit(aic_cortex c, int i, aic_mamba_layer* out);
+AIC_API aic_status aic_cortex_actor(aic_cortex c, aic_mamba_layer* out);
+AIC_API aic_status aic_cortex_critic(aic_cortex c, aic_critic* out);
+AIC_API aic_status aic_cortex_param_bytes(aic_cortex c, size_t* bytes);
+AIC_API aic_status aic_cortex_bind(aic_cortex c, void* dev_params);
+AIC_API aic_status aic_cortex_state_bytes(aic_cortex c, int batch, size_t* bytes);
+AIC_API aic_status aic_cortex_bind_state(aic_cortex c, void* dev_state, int batch);
+AIC_API aic_status aic_cortex_reset_state(aic_cortex c, void* stream);
+AIC_API aic_status aic_cortex_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes);
+/* planes fp16 [batch*seq][planes][dim][dim]; actor fp32 [batch*seq][actor_out];
+ * critic fp32 [batch*seq] (may be NULL); features (optional) F [batch*seq][d_model]. */
+AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int batch, int seq, float* actor,
+                                      float* critic, uint32_t* features, int8_t* features_s, void* workspace,
+                                      void* stream);
+/* Number of kernel launches the last aic_cortex_forward issued. */
+AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches);
+AIC_API aic_status aic_cortex_destroy(aic_cortex c);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AICORTEX_H */

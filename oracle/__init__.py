@@ -1,0 +1,227 @@
+"""CPU oracle of the AICortex inference hot path -- TEST INFRASTRUCTURE ONLY.
+
+numpy front-end over oracle/_build/liboracle.so (oracle/aic_oracle.c, a
+plain-C restatement of the reference kernels) plus the layer/block
+compositions of the reference headers. Only tests/, __graft_entry__.smoke()
+and bench.py's CPU legs import this package; it is the checker, never the
+thing measured as the product.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "liboracle.so"
+
+
+def build() -> Path:
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+    return LIB_PATH
+
+
+def _load() -> C.CDLL:
+    if not LIB_PATH.exists():
+        build()
+    lib = C.CDLL(str(LIB_PATH))
+    P, I64, I32, F = C.c_void_p, C.c_int64, C.c_int, C.c_float
+    sigs = {
+        "orc_unique_seed": ([C.c_uint32, C.c_int32], C.c_uint32),
+        "orc_uniform": ([C.c_uint32, F], F),
+        "orc_quantize_scale": ([F], C.c_int8),
+        "orc_dequantize_scale": ([C.c_int8], F),
+        "orc_pack_f32": ([P, I64, P, P, I32, C.c_int32], None),
+        "orc_stem_pack": ([P, I64, I32, I32, I32, P, P], None),
+        "orc_conv_pw": ([P, P, P, P, P, P, P, I64, I32, I32, I32], None),
+        "orc_conv_dense": ([P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32, I32, I32], None),
+        "orc_conv_dw": ([P, P, P, P, P, P, P, I64, I32, I32, I32, I32, I32], None),
+        "orc_residual": ([P, P, P, P, P, P, I64, I32, F, I32], None),
+        "orc_gap_f32": ([P, P, I64, I32, I32, P], None),
+        "orc_gap_f16": ([P, P, I64, I32, I32, P], None),
+        "orc_mamba_blob_elems": ([I32, I32, I32], I64),
+        "orc_ssm_scan": ([P, P, P, P, I32, I32, I32, P, P, I32, I32], None),
+        "orc_outproj": ([P, P, P, P, I32, I32, I32, I32, I64, P], None),
+        "orc_critic": ([P, P, P, P, I32, I32, P, P, I32, I32], None),
+        "orc_set_actions": ([P, I64, I32, P], None),
+        "orc_num_threads": ([], I32),
+    }
+    for name, (args, res) in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    return lib
+
+
+lib = _load()
+
+
+def _p(a: np.ndarray) -> C.c_void_p:
+    assert a.flags["C_CONTIGUOUS"]
+    return C.c_void_p(a.ctypes.data)
+
+
+def num_threads() -> int:
+    return lib.orc_num_threads()
+
+
+def pack_f32(x: np.ndarray, stochastic: bool = False, add_idx: int = 0):
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    g = x.size // 32
+    w = np.zeros(4 * g, dtype=np.uint32)
+    s = np.zeros(g, dtype=np.int8)
+    lib.orc_pack_f32(_p(x), x.size, _p(w), _p(s), int(stochastic), int(add_idx))
+    return w, s
+
+
+def stem_pack(planes_f16: np.ndarray, channels: int = 32):
+    planes = np.ascontiguousarray(planes_f16, dtype=np.float16)
+    f, p, dim, _ = planes.shape
+    w = np.zeros((f * dim * dim, channels // 8), dtype=np.uint32)
+    s = np.zeros((f * dim * dim, channels // 32), dtype=np.int8)
+    lib.orc_stem_pack(_p(planes.view(np.uint16)), f, p, channels, dim, _p(w), _p(s))
+    return w, s
+
+
+def conv(x_w, x_s, w_w, w_s, bias, frames, in_c, out_c, k, stride, d_in, d_out, act):
+    """ConvLayer::forward dispatch (conv_layer.h:102-149)."""
+    depthwise = k > 1 and k % 2 == 1
+    out_w = np.zeros((frames * d_out * d_out, out_c // 8), dtype=np.uint32)
+    out_s = np.zeros((frames * d_out * d_out, out_c // 32), dtype=np.int8)
+    args = [_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
+            _p(np.ascontiguousarray(w_w, np.uint32)), _p(np.ascontiguousarray(w_s, np.int8)),
+            _p(np.ascontiguousarray(bias, np.float32)), _p(out_w), _p(out_s)]
+    if depthwise:
+        lib.orc_conv_dw(*args, frames, in_c, k, stride, d_in, d_out)
+    elif k == 1:
+        lib.orc_conv_pw(*args, frames * d_out * d_out, in_c, out_c, int(act))
+    else:
+        lib.orc_conv_dense(*args, frames, in_c, out_c, k, stride, d_in, d_out, int(act))
+    return out_w, out_s
+
+
+def residual(main_w, main_s, res_w, res_s, positions, channels, main_mult=1.0, skipped=False):
+    out_w = np.zeros((positions, channels // 8), dtype=np.uint32)
+    out_s = np.zeros((positions, channels // 32), dtype=np.int8)
+    lib.orc_residual(_p(np.ascontiguousarray(main_w, np.uint32)), _p(np.ascontiguousarray(main_s, np.int8)),
+                     _p(np.ascontiguousarray(res_w, np.uint32)), _p(np.ascontiguousarray(res_s, np.int8)),
+                     _p(out_w), _p(out_s), positions, channels, float(main_mult), int(skipped))
+    return out_w, out_s
+
+
+def gap_f32(x_w, x_s, frames, hw, channels):
+    out = np.zeros((frames, channels), dtype=np.float32)
+    lib.orc_gap_f32(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)), frames, hw,
+                    channels, _p(out))
+    return out
+
+
+def gap_f16(x_w, x_s, frames, hw, channels):
+    out = np.zeros((frames, channels), dtype=np.uint16)
+    lib.orc_gap_f16(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)), frames, hw,
+                    channels, _p(out))
+    return out.view(np.float16)
+
+
+def ssm_scan(x_w, x_s, blob_w, blob_s, d_model, d_state, out, h, B, T):
+    """Returns y [B*T][2*d_model]; h [B][E][d_state/32][2] is updated in place."""
+    E = 2 * d_model
+    y = np.zeros((B * T, E), dtype=np.float32)
+    assert h.dtype == np.float32 and h.flags["C_CONTIGUOUS"]
+    lib.orc_ssm_scan(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
+                     _p(np.ascontiguousarray(blob_w, np.uint32)), _p(np.ascontiguousarray(blob_s, np.int8)),
+                     d_model, d_state, out, _p(h), _p(y), B, T)
+    return y
+
+
+def outproj(y, blob_w, blob_s, bias, d_model, d_state, out, act):
+    y = np.ascontiguousarray(y, np.float32)
+    rows = y.shape[0]
+    o = np.zeros((rows, out), dtype=np.float32)
+    lib.orc_outproj(_p(y), _p(np.ascontiguousarray(blob_w, np.uint32)), _p(np.ascontiguousarray(blob_s, np.int8)),
+                    _p(np.ascontiguousarray(bias, np.float32)), d_model, d_state, out, act, rows, _p(o))
+    return o
+
+
+def critic(x_f16, w1, wl, w2, in_c, units, h, B, T):
+    score = np.zeros(B * T, dtype=np.float32)
+    x = np.ascontiguousarray(x_f16, np.float16)
+    lib.orc_critic(_p(x.view(np.uint16)), _p(np.ascontiguousarray(w1, np.float32)),
+                   _p(np.ascontiguousarray(wl, np.float32)), _p(np.ascontiguousarray(w2, np.float32)), in_c, units,
+                   _p(h), _p(score), B, T)
+    return score
+
+
+def set_actions(probs):
+    probs = np.ascontiguousarray(probs, np.float32)
+    rows, count = probs.shape
+    out = np.zeros((rows, (count + 63) // 64), dtype=np.uint64)
+    lib.orc_set_actions(_p(probs), rows, count, _p(out))
+    return out
+
+
+# ---- compositions ---------------------------------------------------------
+
+class MambaLayerRef:
+    """MambaLayer (mamba_layer.h) on the CPU: packed blob, compact state."""
+
+    def __init__(self, d_model, d_state, out, act, blob_master, bias, batch):
+        self.d_model, self.d_state, self.out, self.act = d_model, d_state, out, act
+        self.w, self.s = pack_f32(blob_master, stochastic=True, add_idx=blob_master.size)
+        self.bias = np.ascontiguousarray(bias, np.float32)
+        self.h = np.zeros((batch, 2 * d_model, d_state // 32, 2), dtype=np.float32)
+
+    def forward(self, x_w, x_s, B, T):
+        y = ssm_scan(x_w, x_s, self.w, self.s, self.d_model, self.d_state, self.out, self.h, B, T)
+        return outproj(y, self.w, self.s, self.bias, self.d_model, self.d_state, self.out, self.act)
+
+
+def conv_block(x_w, x_s, layers, frames, geo, main_mult=1.0, skipped=False):
+    """ConvBlock::forward (conv_block.h:74-82). layers: 4 x (words, exps, bias)."""
+    cin, mid, cout, stride, d_in, d_out, k = geo
+    s1 = stride if d_in != d_out else 1
+    a = conv(x_w, x_s, *layers[0], frames, cin, cin, k, s1, d_in, d_out, 0)
+    b = conv(*a, *layers[1], frames, cin, mid, 1, 1, d_out, d_out, 1)
+    a = conv(*b, *layers[2], frames, mid, cout, 1, 1, d_out, d_out, 0)
+    sc = conv(x_w, x_s, *layers[3], frames, cin, cout, s1, s1, d_in, d_out, 0)
+    return residual(a[0], a[1], sc[0], sc[1], frames * d_out * d_out, cout, main_mult, skipped)
+
+
+def pack_conv_layer(master, bias):
+    w, s = pack_f32(master, stochastic=True, add_idx=master.size)
+    return w, s, np.ascontiguousarray(bias, np.float32)
+
+
+def cortex_forward(weights: dict, planes_f16: np.ndarray, B: int, T: int, blocks_geo, d_model: int, d_state: int,
+                   actor_out: int, critic_units: int, stem_channels: int = 32):
+    """The cortex forward composition on the CPU: stem pack -> ConvBlocks ->
+    GAP -> requant -> units (MambaLayer + requant + residual) -> actor, and the
+    critic on the trunk output (cortex.h:281-303, conv_block.h:74-82,
+    mamba_block.h:60-65, critic.h:106-116). Returns (actor [B*T][actor_out],
+    critic [B*T], features (words, exps))."""
+    frames = B * T
+    xw, xs = stem_pack(planes_f16, stem_channels)
+    for geo, layers in zip(blocks_geo, weights["blocks"]):
+        packed = [pack_conv_layer(m, b) for (m, b) in layers]
+        xw, xs = conv_block(xw, xs, packed, frames, geo)
+    fd = blocks_geo[-1][5]
+    pooled = gap_f32(xw, xs, frames, fd * fd, d_model)
+    fw, fs = pack_f32(pooled)
+    cur = (fw.reshape(frames, -1), fs.reshape(frames, -1))
+    feats = cur
+    for blob, bias in weights["units"]:
+        layer = MambaLayerRef(d_model, d_state, d_model, 1, blob, bias, B)
+        o = layer.forward(cur[0], cur[1], B, T)
+        qw, qs = pack_f32(o)
+        cur = residual(qw, qs, cur[0], cur[1], frames, d_model, 1.0, False)
+    actor_layer = MambaLayerRef(d_model, d_state, actor_out, 0, *weights["actor"], B)
+    actor = actor_layer.forward(cur[0], cur[1], B, T)
+    score = None
+    if critic_units:
+        w1, w2, wl = weights["critic"]
+        pooled_h = gap_f16(cur[0], cur[1], frames, 1, d_model)
+        h = np.zeros((B, critic_units, 2), dtype=np.float32)
+        score = critic(pooled_h, w1, wl, w2, d_model, critic_units, h, B, T)
+    return actor, score, feats

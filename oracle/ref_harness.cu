@@ -1,0 +1,141 @@
+// Reference-kernel harness -- TEST INFRASTRUCTURE ONLY.
+//
+// Compiled by oracle/build_ref.sh against the reference's own kernels.h (and
+// the uv.h / device_constants.h / base_constants.h it pulls in), with the
+// reference build flags (-O3 --use_fast_math --extended-lambda), into
+// oracle/_ref/libaicref_D<d_model>_N<d_state>.so. Each entry point launches
+// one reference kernel with exactly the launch geometry the reference layer
+// classes use (file:line cited per function) on raw device pointers, so the
+// golden-vector generator (tests/golden/make_golden.py) can drive the
+// reference kernels one at a time. Nothing in the product links this.
+//
+// The Mamba kernels read d_model / d_inner / d_state from compile-time
+// constants (kernels.h:1080-1089), which is why one library is built per
+// (d_model, d_state) pair.
+#include "kernels.h"
+
+#define AICREF_API extern "C" __attribute__((visibility("default")))
+
+static int aicref_status() { return (int)cudaGetLastError(); }
+
+AICREF_API int aicref_d_model() { return final_channels; }
+AICREF_API int aicref_d_state() { return mamba_d_state; }
+
+// conv_layer.h:98 / mamba_layer.h:137 (weights, stochastic, add_idx = n) and
+// mamba_block.h:64,70 (activations, round-to-nearest, add_idx = 0).
+AICREF_API int aicref_quantize_f32(const float* in, uint32_t* out, int8_t* scales, int n, int stochastic, int add_idx)
+{
+    const int groups = n >> 5;
+    const int grid = (groups + gpu_block_threads - 1) / gpu_block_threads;
+    if (stochastic) quantizeKernel<float, false><<<grid, gpu_block_threads>>>(in, out, scales, n, add_idx);
+    else quantizeKernel<float, true><<<grid, gpu_block_threads>>>(in, out, scales, n, add_idx);
+    return aicref_status();
+}
+
+// cortex.h:294-295: one fp16 NCHW frame [channels][dim][dim] -> NHWC int4.
+AICREF_API int aicref_stem(const __half* in, uint32_t* out, int8_t* out_s, int dim, int channels)
+{
+    dim3 grid((dim + 31) >> 5, dim, channels >> 5);
+    quantizeNCHWtoNHWCKernel<__half><<<grid, gpu_block_threads>>>(in, out, out_s, dim, channels, 0);
+    return aicref_status();
+}
+
+// conv_layer.h:145-147 (one frame of `positions` pixels).
+AICREF_API int aicref_conv_pw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                              uint32_t* out, int8_t* out_s, int positions, int InC, int OutC, int act)
+{
+    dim3 grid(positions, (OutC + gpu_block_threads - 1) / gpu_block_threads);
+    if (act) convPointwiseFwdKernel<false><<<grid, gpu_block_threads>>>(in, w, in_s, w_s, bias, out, out_s, InC, OutC);
+    else convPointwiseFwdKernel<true><<<grid, gpu_block_threads>>>(in, w, in_s, w_s, bias, out, out_s, InC, OutC);
+    return aicref_status();
+}
+
+// conv_layer.h:118-142 (one frame).
+AICREF_API int aicref_conv_dense(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                                 uint32_t* out, int8_t* out_s, int InC, int OutC, int ksize, int stride, int Din, int Dout, int act)
+{
+    dim3 grid(Dout * Dout, (OutC + gpu_block_threads - 1) / gpu_block_threads);
+#define AICREF_DENSE(NOACT, K) convDenseFwdKernel<NOACT, K><<<grid, gpu_block_threads>>>(in, w, in_s, w_s, bias, out, out_s, InC, OutC, Din, Dout, stride)
+    if (ksize == 2) { if (act) AICREF_DENSE(false, 2); else AICREF_DENSE(true, 2); }
+    else if (ksize == 4) { if (act) AICREF_DENSE(false, 4); else AICREF_DENSE(true, 4); }
+    else return -1;
+#undef AICREF_DENSE
+    return aicref_status();
+}
+
+// conv_layer.h:104-116 (one frame).
+AICREF_API int aicref_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                              uint32_t* out, int8_t* out_s, int C, int ksize, int stride, int Din, int Dout)
+{
+    dim3 grid(Dout * Dout, (C + gpu_block_threads - 1) / gpu_block_threads);
+#define AICREF_DW(K) convDepthwiseFwdKernel<K><<<grid, gpu_block_threads>>>(in, w, in_s, w_s, bias, out, out_s, C, Din, Dout, stride)
+    if (ksize == 3) AICREF_DW(3);
+    else if (ksize == 5) AICREF_DW(5);
+    else if (ksize == 7) AICREF_DW(7);
+    else return -1;
+#undef AICREF_DW
+    return aicref_status();
+}
+
+// conv_block.h:80-81 (dim x dim positions) and mamba_block.h:65 (dim = 1).
+AICREF_API int aicref_residual(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res, const int8_t* res_s,
+                               uint32_t* out, int8_t* out_s, int C, int dim, float survival_prob_inv, int skipped, float residual_factor)
+{
+    dim3 grid(dim, dim);
+    residualAddFwdKernel<><<<grid, gpu_block_threads, C * sizeof(float)>>>(main_in, main_s, res, res_s, out, out_s, C, dim,
+                                                                         survival_prob_inv, skipped != 0, residual_factor);
+    return aicref_status();
+}
+
+// critic.h:108-111; the caller zeroes `pooled` (critic.h:108).
+AICREF_API int aicref_gap_f32(const uint32_t* in, const int8_t* in_s, float* pooled, int spatial, int C)
+{
+    dim3 grid(((C >> 5) + gpu_block_threads - 1) / gpu_block_threads, (spatial + 15) >> 4);
+    gapKernel<float><<<grid, gpu_block_threads>>>(in, in_s, pooled, spatial, C);
+    return aicref_status();
+}
+AICREF_API int aicref_gap_f16(const uint32_t* in, const int8_t* in_s, __half* pooled, int spatial, int C)
+{
+    dim3 grid(((C >> 5) + gpu_block_threads - 1) / gpu_block_threads, (spatial + 15) >> 4);
+    gapKernel<__half><<<grid, gpu_block_threads>>>(in, in_s, pooled, spatial, C);
+    return aicref_status();
+}
+
+// mamba_layer.h:141 -- one time step of one sequence. h/trace buffers are
+// [d_inner][d_state] complex; y is [d_inner].
+AICREF_API int aicref_ssm_step(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, float2* h,
+                               float2* tr_a, float2* tr_b, float2* tr_d, float* y)
+{
+    mambaSSMFwdStateKernel<><<<mamba_d_inner / gpu_block_threads, gpu_block_threads>>>(in, in_s, w, w_s, h, tr_a, tr_b, tr_d, y);
+    return aicref_status();
+}
+
+// mamba_layer.h:142-145.
+AICREF_API int aicref_outproj(const float* y, const uint32_t* w, const int8_t* w_s, const float* bias, float* out, int OutC, int act)
+{
+    const int grid = (OutC + gpu_block_threads - 1) / gpu_block_threads;
+    if (act == 0) mambaSSMFwdOutProjKernel<0><<<grid, gpu_block_threads>>>(y, w, w_s, bias, out, OutC);
+    else if (act == 1) mambaSSMFwdOutProjKernel<1><<<grid, gpu_block_threads>>>(y, w, w_s, bias, out, OutC);
+    else mambaSSMFwdOutProjKernel<2><<<grid, gpu_block_threads>>>(y, w, w_s, bias, out, OutC);
+    return aicref_status();
+}
+
+// critic.h:112-114 -- one time step; units complex units, `in` fp16 inputs.
+AICREF_API int aicref_critic(const __half* pooled, const float* w1, const float* wl, const float* w2, float* h,
+                             float* trace_w1, float* trace_l, float* score, int units, int in)
+{
+    criticFwd1Kernel<__half><<<((units << 5) + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(
+        pooled, w1, wl, h, trace_w1, trace_l, units, in);
+    criticFwd2Kernel<><<<1, units>>>(h, w2, score, units);
+    return aicref_status();
+}
+
+// cortex.h:371-372 -- `actions` must be zeroed by the caller.
+AICREF_API int aicref_set_actions(const float* probs, unsigned long long* actions, int count)
+{
+    setActionsKernel<float><<<(count + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(
+        probs, reinterpret_cast<action_type*>(actions), count);
+    return aicref_status();
+}
+
+AICREF_API int aicref_sync() { return (int)cudaDeviceSynchronize(); }

@@ -1,0 +1,11 @@
+/* Force-included before the reference headers when the reference kernels are
+ * compiled on Linux (oracle/build_ref.sh). glibc >= 2.38 declares the C23
+ * functions fmaximum/fminimum, which collide with the reference's float
+ * constants of the same names; renaming them here keeps every use consistent.
+ * TEST INFRASTRUCTURE ONLY. */
+#pragma once
+#include <cmath>
+#include <cstdio>
+#define fmaximum aic_ref_fmaximum
+#define fminimum aic_ref_fminimum
+namespace std { using ::sqrtf; }

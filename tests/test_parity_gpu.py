@@ -1,0 +1,257 @@
+"""GPU parity of the product kernels (through the C ABI) against
+  (a) golden fixtures produced by the reference's own CUDA kernels
+      (tests/golden/*.npz, tests/golden/make_golden.py), and
+  (b) the CPU oracle (oracle/) on seeded batched inputs.
+
+Tolerances: packing, unpacking and every integer/byte output are compared
+bit-exactly. Activations in the packed int4 format are compared as codes plus
+exponents; a code may flip by one only where the fp32 value sits on a rounding
+boundary, which the fast-math intrinsics (GPU) and libm (oracle) resolve
+differently, so flips are bounded by a rate. fp32 outputs are compared with
+max-abs error <= 1e-3 relative to the tensor's max magnitude (the tolerance
+of the task), and tighter where the computation is order-identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+import aicortex_b200 as A
+from aicortex_b200 import fmt, workloads as W
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda")
+RTOL = 1e-3
+
+
+def t(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+
+
+def h(x):
+    torch.cuda.synchronize()
+    return x.cpu().numpy()
+
+
+def u32(x):
+    return np.ascontiguousarray(h(x) if isinstance(x, torch.Tensor) else x).view(np.uint32)
+
+
+def assert_f_close(w_a, s_a, w_b, s_b, flip_rate=2e-3, what=""):
+    """Packed int4 tensors agree: exponents equal, codes equal except rare +-1 flips."""
+    ca, cb = fmt.codes(u32(w_a).reshape(-1)), fmt.codes(u32(w_b).reshape(-1))
+    sa, sb = np.asarray(s_a).reshape(-1), np.asarray(s_b).reshape(-1)
+    exp_mismatch = np.mean(sa != sb)
+    diff = np.abs(ca.astype(np.int32) - cb.astype(np.int32))
+    assert exp_mismatch <= flip_rate, f"{what}: exponent mismatch rate {exp_mismatch}"
+    same_exp = np.repeat(sa == sb, 32)
+    assert diff[same_exp].max(initial=0) <= 1, f"{what}: code differs by {diff.max()}"
+    assert np.mean(diff > 0) <= flip_rate, f"{what}: flip rate {np.mean(diff > 0)}"
+
+
+def assert_f_equal(w_a, s_a, w_b, s_b, what=""):
+    wa, wb = u32(w_a).reshape(-1), u32(w_b).reshape(-1)
+    sa, sb = np.asarray(s_a).reshape(-1), np.asarray(s_b).reshape(-1)
+    assert np.array_equal(sa, sb), f"{what}: {np.sum(sa != sb)} exponents differ"
+    assert np.array_equal(wa, wb), f"{what}: {np.sum(wa != wb)} words differ"
+
+
+def assert_close(a, b, rtol=RTOL, what=""):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    assert np.isfinite(a).all() and np.isfinite(b).all(), what
+    scale = max(np.abs(b).max(), 1e-30)
+    err = np.abs(a - b).max() / scale
+    assert err <= rtol, f"{what}: max-abs error {err:.3e} (relative to max {scale:.3e})"
+
+
+# ------------------------------------------------------------ golden fixtures
+
+def test_golden_pack(golden):
+    g = golden("pack")
+    w, s = A.pack_f32(t(g["master"]), stochastic=True, add_idx=g["master"].size)
+    assert_f_equal(w, h(s), g["w"], g["s"], "stochastic weight pack")
+    w, s = A.pack_f32(t(g["acts"]))
+    assert_f_equal(w, h(s), g["acts_w"], g["acts_s"], "round-to-nearest pack")
+
+
+def test_golden_stem(golden):
+    g = golden("stem")
+    planes = t(g["planes"][None])
+    w, s = A.stem_pack(planes, int(g["channels"]))
+    assert_f_equal(w, h(s), g["w"], g["s"], "stem")
+
+
+CONV_CASES = ["pw_64_128_silu", "pw_128_64", "pw_64_512_silu", "pw_96_96", "dense_k2_64_128", "dense_k4_32_64",
+              "dense_k2_160_288", "dw_k3_s2_64", "dw_k5_s1_32", "dw_k7_s2_96"]
+
+
+@pytest.mark.parametrize("case", CONV_CASES)
+def test_golden_conv(golden, case):
+    g = golden(f"conv_{case}")
+    cin, cout, k, st, din, dout, act = (int(v) for v in g["geo"])
+    layer = A.ConvLayer(cin, cout, k, st, din, dout, disable_activation=not act)
+    layer.load_weights(t(g["master"]), t(g["bias"]))
+    pw, ps, pb = layer.packed()
+    assert_f_equal(pw, h(ps), g["w"], g["s"], f"{case} weights")
+    ow, os_ = A.empty_f(dout * dout, cout)
+    layer.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
+    assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=1e-3, what=case)
+
+
+@pytest.mark.parametrize("name", ["res_160", "res_mamba_256"])
+def test_golden_residual(golden, name):
+    g = golden(name)
+    ch = int(g["channels"])
+    pos = g["main_w"].shape[0]
+    w, s = A.residual_add(t(g["main_w"]), t(g["main_s"]), t(g["res_w"]), t(g["res_s"]), pos, ch,
+                          main_mult=float(g["rf"]))
+    assert_f_equal(w, h(s), g["out_w"], g["out_s"], name)
+
+
+def test_golden_gap(golden):
+    g = golden("gap")
+    out, qw, qs = A.gap(t(g["x_w"]), t(g["x_s"]), 1, 64, 256)
+    # the reference adds its 16-pixel partial sums with atomics in arrival order
+    assert_close(h(out)[0], g["out"], rtol=1e-6, what="gap f32")
+    oh = A.gap_f16(t(g["c_w"]), t(g["c_s"]), 1, 16, 32)
+    assert np.abs(h(oh).astype(np.float32)[0] - g["c_out"].astype(np.float32)).max() <= \
+        np.abs(g["c_out"].astype(np.float32)).max() * 2e-3
+
+
+@pytest.mark.parametrize("n", [32, 128, 512])
+def test_golden_ssm(golden, n):
+    g = golden(f"ssm_N{n}")
+    D, E, T = 256, 512, g["y"].shape[0]
+    layer = A.MambaLayer(D, n, D, 1)
+    layer.load_weights(t(g["blob"]), t(np.zeros(D, np.float32)))
+    pw, ps, _ = layer.packed()
+    assert_f_equal(pw, h(ps), g["blob_w"], g["blob_s"], "blob pack")
+    layer.bind_state(1)
+    out = torch.empty(T, D, dtype=torch.float32, device=DEV)
+    layer.forward(t(g["x_w"]), t(g["x_s"]), out, 1, T)
+    y = h(layer.workspace(T).view(layer.workspace(T).ptr, T * E, torch.float32)).reshape(T, E)
+    np.testing.assert_array_equal(y, g["y"], err_msg="scan output")
+    # compact state == the active entries (ch & 31) + 32c of the reference's rows
+    st = h(layer.state_tensor())[0]
+    lane = np.arange(E) % 32
+    ref_h = np.stack([g["h"][np.arange(E), lane + 32 * c] for c in range(n // 32)], axis=1)
+    np.testing.assert_array_equal(st, ref_h, err_msg="state")
+    for out_c, act in ((256, 1), (64, 0), (256, 2)):
+        op = A.MambaLayer(D, n, out_c, act)
+        op.load_weights(t(g[f"op{out_c}_{act}_blob"]), t(g["bias"][:out_c]))
+        o = torch.empty(1, out_c, dtype=torch.float32, device=DEV)
+        op.outproj(t(g["yin"][None]), o, 1)
+        np.testing.assert_array_equal(h(o)[0], g[f"op{out_c}_{act}_out"], err_msg=f"outproj {out_c}/{act}")
+
+
+def test_golden_mamba_block(golden):
+    g = golden("mamba_block_N128")
+    T = g["out"].shape[0]
+    blk = A.MambaBlock(256, 128, 128, activation=2)
+    for i in range(3):
+        blk.layers[i].load_weights(t(g[f"blob{i}"]), t(g[f"bias{i}"]))
+    blk.bind_state(1)
+    out = torch.empty(T, 128, dtype=torch.float32, device=DEV)
+    blk.forward(t(g["x_w"]), t(g["x_s"]), out, 1, T)
+    np.testing.assert_array_equal(h(out), g["out"])
+
+
+def test_golden_conv_block(golden):
+    g = golden("conv_block")
+    cin, mid, cout, st, din, dout, k = (int(v) for v in g["geo"])
+    blk = A.ConvBlock(cin, mid, cout, st, din, dout, k, 1.0, float(g["rf"]))
+    for i in range(4):
+        blk.layers[i].load_weights(t(g[f"m{i}"]), t(g[f"b{i}"]))
+    ow, os_ = A.empty_f(dout * dout, cout)
+    blk.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
+    assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=1e-3, what="conv block")
+
+
+def test_golden_critic(golden):
+    g = golden("critic")
+    T = g["x"].shape[0]
+    c = A.Critic(32, 128, 1)
+    c.load_weights(t(g["w1"]), t(g["w2"]), t(g["wl"]))
+    c.bind_state(1)
+    score = torch.empty(T, dtype=torch.float32, device=DEV)
+    c.forward_pooled(t(g["x"]), score, 1, T)
+    np.testing.assert_array_equal(h(score), g["score"])
+
+
+def test_golden_actions(golden):
+    g = golden("actions")
+    words = A.set_actions(t(g["probs"][None]))
+    np.testing.assert_array_equal(h(words)[0].view(np.uint64), g["words"])
+
+
+# ------------------------------------------------------- batched vs. oracle
+
+def test_batched_convs_vs_oracle():
+    import oracle as O
+    rng = np.random.default_rng(7)
+    frames = 3
+    for (cin, cout, k, st, din, dout, act) in [(32, 64, 3, 2, 16, 8, 0), (64, 128, 1, 1, 8, 8, 1),
+                                               (64, 128, 2, 2, 16, 8, 0), (32, 64, 4, 4, 32, 8, 0)]:
+        dw = k > 1 and k % 2 == 1
+        m, b = W.conv_weights(rng, cin, cout, k, dw), W.bias(rng, cout)
+        x = rng.standard_normal((frames * din * din, cin)).astype(np.float32)
+        xw, xs = O.pack_f32(x)
+        xw, xs = xw.reshape(frames * din * din, -1), xs.reshape(frames * din * din, -1)
+        ow_ref, os_ref = O.conv(xw, xs, *O.pack_conv_layer(m, b), frames, cin, cout, k, st, din, dout, act)
+        layer = A.ConvLayer(cin, cout, k, st, din, dout, disable_activation=not act)
+        layer.load_weights(t(m), t(b))
+        ow, os_ = A.empty_f(frames * dout * dout, cout)
+        layer.forward(t(xw.view(np.int32)), t(xs), ow, os_, frames)
+        assert_f_close(ow, h(os_), ow_ref, os_ref, flip_rate=1e-3, what=f"conv k{k} {cin}->{cout}")
+
+
+def test_batched_scan_vs_oracle():
+    import oracle as O
+    rng = np.random.default_rng(8)
+    D, N, B, T = 64, 128, 3, 21
+    blob, bias = W.mamba_blob(rng, D, N, 96, a_im=None), W.bias(rng, 96)
+    ref = O.MambaLayerRef(D, N, 96, 1, blob, bias, B)
+    x = rng.standard_normal((B * T, D)).astype(np.float32)
+    xw, xs = O.pack_f32(x)
+    xw, xs = xw.reshape(B * T, -1), xs.reshape(B * T, -1)
+    o_ref = ref.forward(xw, xs, B, T)
+    layer = A.MambaLayer(D, N, 96, 1)
+    layer.load_weights(t(blob), t(bias))
+    layer.bind_state(B)
+    out = torch.empty(B * T, 96, dtype=torch.float32, device=DEV)
+    layer.forward(t(xw.view(np.int32)), t(xs), out, B, T)
+    assert_close(h(out), o_ref, rtol=1e-4, what="batched mamba layer")
+    assert_close(h(layer.state_tensor()), ref.h, rtol=1e-4, what="batched state")
+    # continuing from the carried state equals one longer call
+    out2 = torch.empty(B * T, 96, dtype=torch.float32, device=DEV)
+    layer.forward(t(xw.view(np.int32)), t(xs), out2, B, T)
+    o_ref2 = ref.forward(xw, xs, B, T)
+    assert_close(h(out2), o_ref2, rtol=1e-4, what="second call with carried state")
+
+
+def test_cortex_small_vs_oracle():
+    import oracle as O
+    B, T, dim = 2, 3, 32
+    desc = W.cortex_desc(batch_chunk=4, d_state=64, critic_units=64, dim=dim)
+    wts = W.cortex_weights(11, d_state=64, critic_units=64, dim=dim)
+    rng = np.random.default_rng(12)
+    planes = W.planes_u01(rng, B * T, 3, dim)
+    cx = A.Cortex(desc)
+    for blk, layers in zip(cx.blocks, wts["blocks"]):
+        for lay, (m, b) in zip(blk.layers, layers):
+            lay.load_weights(t(m), t(b))
+    for u, (m, b) in zip(cx.units, wts["units"]):
+        u.load_weights(t(m), t(b))
+    cx.actor.load_weights(t(wts["actor"][0]), t(wts["actor"][1]))
+    cx.critic.load_weights(*(t(a) for a in wts["critic"]))
+    cx.bind_state(B)
+    actor = torch.empty(B * T, 64, dtype=torch.float32, device=DEV)
+    critic = torch.empty(B * T, dtype=torch.float32, device=DEV)
+    fw, fs = A.empty_f(B * T, 256)
+    n = cx.forward(t(planes), B, T, actor, critic, features=(fw, fs))
+    assert n > 20
+    geo = W.cfg2_blocks(dim)
+    a_ref, c_ref, (frw, frs) = O.cortex_forward(wts, planes, B, T, geo, 256, 64, 64, 64)
+    assert_f_close(fw, h(fs), frw, frs, flip_rate=5e-3, what="features")
+    assert_close(h(actor), a_ref, rtol=2e-2, what="actor logits")
+    assert_close(h(critic), c_ref, rtol=2e-2, what="critic")
