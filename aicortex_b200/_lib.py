@@ -136,7 +136,14 @@ _SIGS = {
     "aic_cortex_reset_state": [P, P],
     "aic_cortex_workspace_bytes": [P, I32, I32, SZ],
     "aic_cortex_forward": [P, P, I32, I32, P, P, P, P, P, P],
+    "aic_cortex_host_workspace_bytes": [P, I32, I32, SZ],
+    "aic_cortex_forward_host": [P, P, I32, I32, P, P, P, P],
     "aic_cortex_last_launches": [P, PI64],
+    "aic_cortex_profile_enable": [P, I32],
+    "aic_cortex_profile_count": [P, C.POINTER(C.c_int)],
+    "aic_cortex_profile_get": [P, I32, C.c_char_p, C.POINTER(C.c_double), PI64, C.POINTER(C.c_double),
+                               C.POINTER(C.c_double)],
+    "aic_cortex_profile_reset": [P],
     "aic_cortex_destroy": [P],
 }
 

@@ -115,6 +115,89 @@ std::vector<float> read_floats(const char* path, const std::vector<size_t>& coun
     return out;
 }
 
+// Per-launch-site CUDA-event timing. Each traced launch is bracketed by two
+// events on its own stream; collect() waits for them and accumulates the
+// elapsed time, the launch count and the algorithmic work of the site.
+struct Profiler {
+    struct Site {
+        std::string name;
+        double ms = 0.0, flops = 0.0, bytes = 0.0;
+        int64_t launches = 0;
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending;
+    };
+    bool enabled = false;
+    std::vector<Site> sites;
+    std::vector<cudaEvent_t> pool;
+
+    ~Profiler()
+    {
+        for (auto& s : sites)
+            for (auto& p : s.pending) pool.push_back(p.first), pool.push_back(p.second);
+        for (cudaEvent_t e : pool) cudaEventDestroy(e);
+    }
+    cudaEvent_t event()
+    {
+        if (!pool.empty()) {
+            cudaEvent_t e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        cuda_ok(cudaEventCreate(&e), "cudaEventCreate");
+        return e;
+    }
+    Site& site(const std::string& name)
+    {
+        for (auto& s : sites)
+            if (s.name == name) return s;
+        sites.push_back(Site{});
+        sites.back().name = name;
+        return sites.back();
+    }
+    void collect()
+    {
+        for (auto& s : sites) {
+            for (auto& p : s.pending) {
+                cuda_ok(cudaEventSynchronize(p.second), "profile sync");
+                float ms = 0.0f;
+                cuda_ok(cudaEventElapsedTime(&ms, p.first, p.second), "profile elapsed");
+                s.ms += ms;
+                pool.push_back(p.first);
+                pool.push_back(p.second);
+            }
+            s.pending.clear();
+        }
+    }
+    void reset()
+    {
+        collect();
+        sites.clear();
+    }
+};
+
+// Launches through `launch` (returning cudaError_t), traced under `name` when
+// a profiler is attached and enabled.
+template <class F>
+void traced(Profiler* p, const std::string& name, cudaStream_t s, double flops, double bytes, const char* what, F&& launch)
+{
+    if (!p || !p->enabled) {
+        cuda_ok(launch(), what);
+        return;
+    }
+    Profiler::Site& site = p->site(name);
+    cudaEvent_t a = p->event(), b = p->event();
+    cuda_ok(cudaEventRecord(a, s), "profile record");
+    cuda_ok(launch(), what);
+    cuda_ok(cudaEventRecord(b, s), "profile record");
+    site.pending.emplace_back(a, b);
+    site.launches += 1;
+    site.flops += flops;
+    site.bytes += bytes;
+}
+
+// Bytes of `elems` values in the packed int4 format (codes + exponents).
+inline double f_bytes(double elems) { return elems * (0.5 + 1.0 / 32.0); }
+
 std::string join(const char* dir, const char* name)
 {
     require(dir != nullptr, "null directory");
@@ -132,6 +215,8 @@ struct ConvLayer {
     int8_t* ws = nullptr;
     float* bias = nullptr;
     bool bound = false;
+    Profiler* prof = nullptr;
+    std::string tag = "conv";
 
     explicit ConvLayer(const aic_conv_layer_desc& desc) : d(desc)
     {
@@ -186,14 +271,21 @@ struct ConvLayer {
         check_bound();
         if (frames == 0) return 0;
         require(in && in_s && out && out_s, "null tensor");
+        const double pix_in = static_cast<double>(frames) * d.dim_in * d.dim_in;
+        const double pix_out = static_cast<double>(frames) * d.dim_out * d.dim_out;
+        const double ksq = static_cast<double>(d.kernel_size) * d.kernel_size;
+        const double bytes = f_bytes(pix_in * d.in_channels) + f_bytes(pix_out * d.out_channels) +
+                             f_bytes(static_cast<double>(weight_elems)) + 4.0 * d.out_channels;
         if (is_dw)
-            cuda_ok(launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
-                                   d.dim_in, d.dim_out, s),
-                    "conv_dw");
+            traced(prof, tag, s, 2.0 * ksq * d.in_channels * pix_out, bytes, "conv_dw", [&] {
+                return launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+                                      d.dim_in, d.dim_out, s);
+            });
         else
-            cuda_ok(launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
-                                          d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s),
-                    "conv_gemm");
+            traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm", [&] {
+                return launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                             d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s);
+            });
         return 1;
     }
 };
@@ -203,6 +295,19 @@ struct ConvBlock {
     aic_conv_block_desc d;
     std::unique_ptr<ConvLayer> layers[4];
     int final_stride;
+    Profiler* prof = nullptr;
+    std::string tag = "block";
+
+    void attach(Profiler* p, const std::string& t)
+    {
+        prof = p;
+        tag = t;
+        static const char* names[4] = {".dw", ".pw1", ".pw2", ".sc"};
+        for (int i = 0; i < 4; ++i) {
+            layers[i]->prof = p;
+            layers[i]->tag = t + names[i];
+        }
+    }
 
     explicit ConvBlock(const aic_conv_block_desc& desc) : d(desc)
     {
@@ -255,9 +360,11 @@ struct ConvBlock {
         n += layers[3]->forward(in, in_s, b, bs, frames, s);
         const float surv_inv = 1.0f / d.survival_probability;
         const float main_mult = d.residual_factor * (train && survived ? surv_inv : 1.0f);
-        cuda_ok(launch_residual(a, as, b, bs, out, out_s, frames * d.dim_out * d.dim_out, d.out_channels, main_mult,
-                                train && !survived, s),
-                "residual");
+        const int64_t pos = frames * d.dim_out * d.dim_out;
+        traced(prof, tag + ".res", s, 3.0 * pos * d.out_channels, 3.0 * f_bytes(static_cast<double>(pos) * d.out_channels),
+               "residual", [&] {
+                   return launch_residual(a, as, b, bs, out, out_s, pos, d.out_channels, main_mult, train && !survived, s);
+               });
         return n + 1;
     }
 };
@@ -274,6 +381,8 @@ struct MambaLayer {
     float2* h = nullptr;
     int batch_bound = -1;
     bool bound = false;
+    Profiler* prof = nullptr;
+    std::string tag = "mamba";
 
     explicit MambaLayer(const aic_mamba_layer_desc& desc) : d(desc)
     {
@@ -333,10 +442,17 @@ struct MambaLayer {
         if (seq == 0 || batch == 0) return 0;
         require(in && in_s && out && wsp && aligned256(wsp), "null or misaligned tensor");
         float* y = static_cast<float*>(wsp);
-        cuda_ok(launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, y, batch, seq, s), "ssm scan");
-        cuda_ok(launch_outproj(y, w, ws, bias, d.d_model, d.d_state, d.out_channels, d.activation,
-                               static_cast<int64_t>(batch) * seq, out, s),
-                "outproj");
+        const double rows = static_cast<double>(batch) * seq;
+        // per (row, channel): 31 flops per state plus ~15 (kernels.h:1126-1176)
+        traced(prof, tag + ".scan", s, rows * E * (31.0 * P + 15.0),
+               f_bytes(rows * d.d_model) + 4.0 * rows * E + 2.0 * batch * E * P * 8.0 + E * P * 16.0, "ssm scan",
+               [&] { return launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, y, batch, seq, s); });
+        traced(prof, tag + ".outproj", s, 2.0 * rows * E * d.out_channels,
+               4.0 * rows * E + f_bytes(static_cast<double>(E) * d.out_channels) + 4.0 * rows * d.out_channels, "outproj",
+               [&] {
+                   return launch_outproj(y, w, ws, bias, d.d_model, d.d_state, d.out_channels, d.activation,
+                                         static_cast<int64_t>(batch) * seq, out, s);
+               });
         return 2;
     }
 };
@@ -426,6 +542,8 @@ struct Critic {
     float2* h = nullptr;
     int batch_bound = -1;
     bool bound = false;
+    Profiler* prof = nullptr;
+    std::string tag = "critic";
 
     explicit Critic(const aic_critic_desc& desc) : d(desc)
     {
@@ -487,8 +605,12 @@ struct Critic {
         __half* pooled;
         float2* hseq;
         workspace(rows, wsp, &pooled, &hseq);
-        cuda_ok(launch_gap_f16(in, in_s, rows, d.dim_in * d.dim_in, d.in_channels, pooled, s), "critic gap");
-        cuda_ok(launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s), "critic");
+        const double hw = static_cast<double>(d.dim_in) * d.dim_in;
+        traced(prof, tag + ".gap", s, rows * hw * d.in_channels, f_bytes(rows * hw * d.in_channels) + 2.0 * rows * d.in_channels,
+               "critic gap", [&] { return launch_gap_f16(in, in_s, rows, d.dim_in * d.dim_in, d.in_channels, pooled, s); });
+        traced(prof, tag + ".cell", s, 8.0 * rows * d.units * d.in_channels,
+               2.0 * rows * d.in_channels + 16.0 * d.units * d.in_channels + 16.0 * rows * d.units + 4.0 * rows, "critic",
+               [&] { return launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s); });
         return 3;
     }
     void forward_pooled(const __half* pooled, float* score, int batch, int seq, void* wsp, cudaStream_t s)
@@ -533,6 +655,7 @@ struct Cortex {
         actor.reset(new MambaLayer({d.d_model, d.d_state, d.actor_out, d.actor_activation}));
         if (d.critic_units > 0) critic.reset(new Critic({d.d_model, d.critic_units, 1}));
         chunk = d.chunk_frames > 0 ? d.chunk_frames : 2048;
+        attach_profiler();
     }
     int final_dim() const { return d.blocks[d.n_blocks - 1].dim_out; }
     size_t carve(void* base)
@@ -611,25 +734,95 @@ struct Cortex {
         if (w) *w = t;
         return c.bytes();
     }
-    void forward(const uint16_t* planes, int batch, int seq, float* actor_out, float* critic_out, uint32_t* features,
-                 int8_t* features_s, void* wsp, cudaStream_t s)
+    int64_t plane_elems() const { return static_cast<int64_t>(d.planes) * d.dim * d.dim; }
+
+    // Host-mode extras after the device workspace: two staging buffers for the
+    // input planes of one chunk each, and device copies of the outputs.
+    size_t host_workspace(int batch, int seq, void* base, Work* w, __half** stage, float** actor_dev,
+                          float** critic_dev) const
     {
-        last_launches = 0;
-        if (batch == 0 || seq == 0) return;
-        require(planes && actor_out && wsp && aligned256(wsp), "null or misaligned tensor");
-        Work w;
-        workspace(batch, seq, wsp, &w);
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        const int64_t ch = std::min<int64_t>(rows, chunk);
+        Carver c(base);
+        void* dev = c.take<char>(workspace(batch, seq, nullptr, nullptr));
+        __half* s0 = c.take<__half>(ch * plane_elems());
+        __half* s1 = c.take<__half>(ch * plane_elems());
+        float* a = c.take<float>(rows * d.actor_out);
+        float* k = c.take<float>(rows);
+        if (base) {
+            workspace(batch, seq, dev, w);
+            stage[0] = s0;
+            stage[1] = s1;
+            *actor_dev = a;
+            *critic_dev = k;
+        }
+        return c.bytes();
+    }
+
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_ready[2] = {nullptr, nullptr}, ev_free[2] = {nullptr, nullptr};
+    Profiler prof;
+
+    ~Cortex()
+    {
+        for (int i = 0; i < 2; ++i) {
+            if (ev_ready[i]) cudaEventDestroy(ev_ready[i]);
+            if (ev_free[i]) cudaEventDestroy(ev_free[i]);
+        }
+        if (copy_stream) cudaStreamDestroy(copy_stream);
+    }
+    void attach_profiler()
+    {
+        for (size_t i = 0; i < blocks.size(); ++i) blocks[i]->attach(&prof, "b" + std::to_string(i));
+        for (size_t i = 0; i < units.size(); ++i) {
+            units[i]->prof = &prof;
+            units[i]->tag = "u" + std::to_string(i);
+        }
+        actor->prof = &prof;
+        actor->tag = "actor";
+        if (critic) critic->prof = &prof;
+    }
+
+    // Shared body of the device- and host-buffer forwards. With `host_planes`
+    // set, chunk i is copied into stage[i & 1] on copy_stream while chunk i-1
+    // runs; the stem kernel of chunk i waits for that copy, and the copy of
+    // chunk i+2 waits for that stem kernel.
+    void run(const __half* dev_planes, const __half* host_planes, __half* const* stage, int batch, int seq,
+             float* actor_out, float* critic_out, uint32_t* features, int8_t* features_s, const Work& w, cudaStream_t s)
+    {
         const int64_t rows = static_cast<int64_t>(batch) * seq;
         uint32_t* feat = features ? features : w.feat;
         int8_t* feat_s = features ? features_s : w.feat_s;
         require(feat_s != nullptr, "features exponents missing");
-        const int64_t plane_elems = static_cast<int64_t>(d.planes) * d.dim * d.dim;
+        const int64_t pe = plane_elems();
+        if (host_planes) {
+            if (!copy_stream) cuda_ok(cudaStreamCreateWithFlags(&copy_stream, cudaStreamNonBlocking), "copy stream");
+            for (int i = 0; i < 2; ++i) {
+                if (!ev_ready[i]) cuda_ok(cudaEventCreateWithFlags(&ev_ready[i], cudaEventDisableTiming), "event");
+                if (!ev_free[i]) cuda_ok(cudaEventCreateWithFlags(&ev_free[i], cudaEventDisableTiming), "event");
+            }
+            // the staging buffers are free once everything queued before this call has run
+            for (int i = 0; i < 2; ++i) cuda_ok(cudaEventRecord(ev_free[i], s), "event record");
+        }
         int64_t n = 0;
-        for (int64_t f0 = 0; f0 < rows; f0 += chunk) {
+        int64_t ci = 0;
+        for (int64_t f0 = 0; f0 < rows; f0 += chunk, ++ci) {
             const int64_t fc = std::min<int64_t>(chunk, rows - f0);
-            cuda_ok(launch_stem_pack(reinterpret_cast<const __half*>(planes) + f0 * plane_elems, fc, d.planes,
-                                     d.stem_channels, d.dim, w.stem, w.stem_s, s),
-                    "stem");
+            const __half* src = dev_planes ? dev_planes + f0 * pe : nullptr;
+            if (host_planes) {
+                const int b = static_cast<int>(ci & 1);
+                cuda_ok(cudaStreamWaitEvent(copy_stream, ev_free[b], 0), "wait free");
+                cuda_ok(cudaMemcpyAsync(stage[b], host_planes + f0 * pe, sizeof(__half) * fc * pe, cudaMemcpyHostToDevice,
+                                        copy_stream),
+                        "planes H2D");
+                cuda_ok(cudaEventRecord(ev_ready[b], copy_stream), "event record");
+                cuda_ok(cudaStreamWaitEvent(s, ev_ready[b], 0), "wait ready");
+                src = stage[b];
+            }
+            const double pix = static_cast<double>(fc) * d.dim * d.dim;
+            traced(&prof, "stem", s, pix * d.stem_channels, pix * d.planes * 2.0 + f_bytes(pix * d.stem_channels), "stem",
+                   [&] { return launch_stem_pack(src, fc, d.planes, d.stem_channels, d.dim, w.stem, w.stem_s, s); });
+            if (host_planes) cuda_ok(cudaEventRecord(ev_free[ci & 1], s), "event record");
             ++n;
             const uint32_t* cur = w.stem;
             const int8_t* cur_s = w.stem_s;
@@ -641,9 +834,11 @@ struct Cortex {
                 cur_s = dst_s;
             }
             const int fd = final_dim();
-            cuda_ok(launch_gap(cur, cur_s, fc, fd * fd, d.d_model, nullptr, feat + f0 * d.d_model / 8,
-                               feat_s + f0 * d.d_model / 32, s),
-                    "gap");
+            const double gp = static_cast<double>(fc) * fd * fd * d.d_model;
+            traced(&prof, "gap", s, gp, f_bytes(gp) + f_bytes(static_cast<double>(fc) * d.d_model), "gap", [&] {
+                return launch_gap(cur, cur_s, fc, fd * fd, d.d_model, nullptr, feat + f0 * d.d_model / 8,
+                                  feat_s + f0 * d.d_model / 32, s);
+            });
             ++n;
         }
         // Mamba trunk: units of layer -> requant -> residual with the unit input.
@@ -651,13 +846,18 @@ struct Cortex {
         const int8_t* cur_s = feat_s;
         uint32_t* bufs[2] = {w.ub, w.uc};
         int8_t* bufs_s[2] = {w.ub_s, w.uc_s};
+        const double el = static_cast<double>(rows) * d.d_model;
         for (size_t i = 0; i < units.size(); ++i) {
+            const std::string tag = "u" + std::to_string(i);
             n += units[i]->forward(cur, cur_s, w.o, batch, seq, w.layer_ws, s);
-            cuda_ok(launch_pack_f32(w.o, rows * d.d_model, w.ua, w.ua_s, false, 0, 0, s), "unit requant");
+            traced(&prof, tag + ".requant", s, 3.0 * el, 4.0 * el + f_bytes(el), "unit requant",
+                   [&] { return launch_pack_f32(w.o, rows * d.d_model, w.ua, w.ua_s, false, 0, 0, s); });
             uint32_t* nxt = bufs[i & 1];
             int8_t* nxt_s = bufs_s[i & 1];
-            cuda_ok(launch_residual(w.ua, w.ua_s, cur, cur_s, nxt, nxt_s, rows, d.d_model, d.unit_residual_factor, false, s),
-                    "unit residual");
+            traced(&prof, tag + ".res", s, 3.0 * el, 3.0 * f_bytes(el), "unit residual", [&] {
+                return launch_residual(w.ua, w.ua_s, cur, cur_s, nxt, nxt_s, rows, d.d_model, d.unit_residual_factor,
+                                       false, s);
+            });
             n += 2;
             cur = nxt;
             cur_s = nxt_s;
@@ -665,6 +865,38 @@ struct Cortex {
         n += actor->forward(cur, cur_s, actor_out, batch, seq, w.layer_ws, s);
         if (critic && critic_out) n += critic->forward(cur, cur_s, critic_out, batch, seq, w.critic_ws, s);
         last_launches = n;
+    }
+
+    void forward(const uint16_t* planes, int batch, int seq, float* actor_out, float* critic_out, uint32_t* features,
+                 int8_t* features_s, void* wsp, cudaStream_t s)
+    {
+        last_launches = 0;
+        if (batch == 0 || seq == 0) return;
+        require(planes && actor_out && wsp && aligned256(wsp), "null or misaligned tensor");
+        Work w;
+        workspace(batch, seq, wsp, &w);
+        run(reinterpret_cast<const __half*>(planes), nullptr, nullptr, batch, seq, actor_out, critic_out, features,
+            features_s, w, s);
+    }
+
+    void forward_host(const uint16_t* planes_host, int batch, int seq, float* actor_host, float* critic_host, void* wsp,
+                      cudaStream_t s)
+    {
+        last_launches = 0;
+        if (batch == 0 || seq == 0) return;
+        require(planes_host && actor_host && wsp && aligned256(wsp), "null or misaligned buffer");
+        Work w;
+        __half* stage[2];
+        float *actor_dev, *critic_dev;
+        host_workspace(batch, seq, wsp, &w, stage, &actor_dev, &critic_dev);
+        const bool want_critic = critic && critic_host;
+        run(nullptr, reinterpret_cast<const __half*>(planes_host), stage, batch, seq, actor_dev,
+            want_critic ? critic_dev : nullptr, nullptr, nullptr, w, s);
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        cuda_ok(cudaMemcpyAsync(actor_host, actor_dev, sizeof(float) * rows * d.actor_out, cudaMemcpyDeviceToHost, s),
+                "actor D2H");
+        if (want_critic)
+            cuda_ok(cudaMemcpyAsync(critic_host, critic_dev, sizeof(float) * rows, cudaMemcpyDeviceToHost, s), "critic D2H");
     }
 };
 
@@ -1238,6 +1470,59 @@ AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int 
         handle<Cortex>(c, "cortex")
             ->forward(planes, batch, seq, actor, critic, features, features_s, workspace, as_stream(stream));
     });
+}
+AIC_API aic_status aic_cortex_host_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(bytes && batch >= 0 && seq >= 0, "bad argument");
+        *bytes = x->host_workspace(batch, seq, nullptr, nullptr, nullptr, nullptr, nullptr);
+    });
+}
+AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_host, int batch, int seq,
+                                           float* actor_host, float* critic_host, void* workspace, void* stream)
+{
+    return guarded([&] {
+        require(batch >= 0 && seq >= 0, "bad extents");
+        handle<Cortex>(c, "cortex")->forward_host(planes_host, batch, seq, actor_host, critic_host, workspace,
+                                                  as_stream(stream));
+    });
+}
+AIC_API aic_status aic_cortex_profile_enable(aic_cortex c, int enable)
+{
+    return guarded([&] { handle<Cortex>(c, "cortex")->prof.enabled = enable != 0; });
+}
+AIC_API aic_status aic_cortex_profile_count(aic_cortex c, int* sites)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        require(sites != nullptr, "null output");
+        x->prof.collect();
+        *sites = static_cast<int>(x->prof.sites.size());
+    });
+}
+AIC_API aic_status aic_cortex_profile_get(aic_cortex c, int site, char name[32], double* total_ms, int64_t* launches,
+                                          double* flops_per_launch, double* bytes_per_launch)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        x->prof.collect();
+        require(site >= 0 && site < static_cast<int>(x->prof.sites.size()), "site index out of range");
+        const auto& s = x->prof.sites[site];
+        if (name) {
+            std::strncpy(name, s.name.c_str(), 31);
+            name[31] = '\0';
+        }
+        if (total_ms) *total_ms = s.ms;
+        if (launches) *launches = s.launches;
+        const double n = s.launches > 0 ? static_cast<double>(s.launches) : 1.0;
+        if (flops_per_launch) *flops_per_launch = s.flops / n;
+        if (bytes_per_launch) *bytes_per_launch = s.bytes / n;
+    });
+}
+AIC_API aic_status aic_cortex_profile_reset(aic_cortex c)
+{
+    return guarded([&] { handle<Cortex>(c, "cortex")->prof.reset(); });
 }
 AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches)
 {

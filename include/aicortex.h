@@ -290,8 +290,27 @@ AIC_API aic_status aic_cortex_workspace_bytes(aic_cortex c, int batch, int seq, 
 AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int batch, int seq, float* actor,
                                       float* critic, uint32_t* features, int8_t* features_s, void* workspace,
                                       void* stream);
-/* Number of kernel launches the last aic_cortex_forward issued. */
+/* Host-buffer variant for callers holding the frames in pinned host memory:
+ * planes_host [batch*seq][planes][dim][dim] fp16 is copied chunk by chunk on
+ * an internal copy stream, overlapped with the conv stack of the previous
+ * chunk; actor_host / critic_host (pinned, critic may be NULL) receive the
+ * outputs. Needs aic_cortex_host_workspace_bytes of workspace. Returns once
+ * the work is queued; synchronise `stream` before reading the outputs. */
+AIC_API aic_status aic_cortex_host_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes);
+AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_host, int batch, int seq,
+                                           float* actor_host, float* critic_host, void* workspace, void* stream);
+/* Number of kernel launches the last forward issued. */
 AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches);
+/* Per-launch-site CUDA-event timing (tracing). When enabled, every kernel
+ * launch of a forward is bracketed by events on its stream; collecting waits
+ * for them. Sites are named like "b0.pw1" (block 0, first pointwise conv),
+ * "u2.scan", "actor.outproj". flops/bytes are the algorithmic work and the
+ * minimum HBM traffic of ONE launch of the site. */
+AIC_API aic_status aic_cortex_profile_enable(aic_cortex c, int enable);
+AIC_API aic_status aic_cortex_profile_count(aic_cortex c, int* sites);
+AIC_API aic_status aic_cortex_profile_get(aic_cortex c, int site, char name[32], double* total_ms, int64_t* launches,
+                                          double* flops_per_launch, double* bytes_per_launch);
+AIC_API aic_status aic_cortex_profile_reset(aic_cortex c);
 AIC_API aic_status aic_cortex_destroy(aic_cortex c);
 
 #ifdef __cplusplus

@@ -1,15 +1,18 @@
 """Generates the golden fixtures in tests/golden/ by running the REFERENCE's own
 CUDA kernels (AICortex kernels.h, compiled for sm_100a by oracle/build_ref.sh
-into oracle/_ref/libaicref_D<d_model>_N<d_state>.so) on seeded inputs.
+into oracle/_ref/libaicref_D<d_model>_N<d_state>.so) on the seeded inputs of
+golden_specs.py.
 
 Needs a GPU and the oracle/_ref libraries; run it on a B200 box:
 
     python tests/golden/make_golden.py [out_dir]
 
-Each fixture is an .npz holding the inputs and the reference outputs of one
-kernel (or one reference composition), small enough to commit. The reference
-kernels are launched with the launch geometry of the reference layer classes
-(see oracle/ref_harness.cu) on the legacy default stream.
+A fixture (.npz) stores the packed activations fed to the reference kernels,
+the reference outputs, and sha256 digests of the regenerated fp32 masters and
+of the reference-packed weights (masters are regenerated from the specs by the
+tests instead of being stored). Reference kernels are launched with the launch
+geometry of the reference layer classes (oracle/ref_harness.cu) on the legacy
+default stream; every device buffer stays referenced until its kernel ends.
 """
 from __future__ import annotations
 
@@ -20,14 +23,15 @@ from pathlib import Path
 import numpy as np
 import torch
 
-ROOT = Path(__file__).resolve().parents[2]
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
-from aicortex_b200 import workloads as W  # noqa: E402
+sys.path.insert(0, str(HERE))
+import golden_specs as S  # noqa: E402
 
 REF_DIR = ROOT / "oracle" / "_ref"
-OUT = Path(sys.argv[1]) if len(sys.argv) > 1 else Path(__file__).resolve().parent
+OUT = Path(sys.argv[1]) if len(sys.argv) > 1 else HERE
 DEV = torch.device("cuda")
-
 _libs: dict = {}
 
 
@@ -38,20 +42,22 @@ def ref(d_model: int = 256, d_state: int = 128) -> C.CDLL:
     return _libs[key]
 
 
-def dev(a: np.ndarray) -> torch.Tensor:
-    return torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+class Dev:
+    """Holds every device tensor it hands out, so none is freed (and its
+    memory reused by the caching allocator) while a kernel may still use it."""
 
+    def __init__(self):
+        self.keep = []
 
-def zeros(n: int, dtype) -> torch.Tensor:
-    return torch.zeros(n, dtype=dtype, device=DEV)
+    def put(self, a: np.ndarray) -> C.c_void_p:
+        t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
+        self.keep.append(t)
+        return C.c_void_p(t.data_ptr())
 
-
-def vp(t: torch.Tensor) -> C.c_void_p:
-    return C.c_void_p(t.data_ptr())
-
-
-def host(t: torch.Tensor) -> np.ndarray:
-    return t.cpu().numpy()
+    def zeros(self, n: int, dtype) -> tuple[torch.Tensor, C.c_void_p]:
+        t = torch.zeros(n, dtype=dtype, device=DEV)
+        self.keep.append(t)
+        return t, C.c_void_p(t.data_ptr())
 
 
 def run(lib, name, *args):
@@ -66,23 +72,28 @@ def run(lib, name, *args):
         raise RuntimeError(f"{name} sync status {st}")
 
 
+def u32(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().numpy().view(np.uint32)
+
+
 def quantize(lib, x: np.ndarray, stochastic: bool, add_idx: int):
+    d = Dev()
     x = np.ascontiguousarray(x, np.float32).reshape(-1)
-    xi = dev(x)
-    w = zeros(x.size // 8, torch.int32)
-    s = zeros(x.size // 32, torch.int8)
-    run(lib, "aicref_quantize_f32", vp(xi), vp(w), vp(s), C.c_int(x.size), C.c_int(int(stochastic)), C.c_int(add_idx))
-    return host(w).view(np.uint32), host(s)
+    px = d.put(x)
+    w, pw = d.zeros(x.size // 8, torch.int32)
+    s, ps = d.zeros(x.size // 32, torch.int8)
+    run(lib, "aicref_quantize_f32", px, pw, ps, C.c_int(x.size), C.c_int(int(stochastic)), C.c_int(add_idx))
+    return u32(w), s.cpu().numpy()
 
 
 def pack_weights(lib, master: np.ndarray):
     return quantize(lib, master, True, master.size)
 
 
-def act_f(lib, rng, rows: int, channels: int, scale: float = 1.0):
-    x = (rng.standard_normal((rows, channels)) * scale).astype(np.float32)
+def act_f(lib, x: np.ndarray):
+    rows, ch = x.shape
     w, s = quantize(lib, x, False, 0)
-    return w.reshape(rows, channels // 8), s.reshape(rows, channels // 32)
+    return w.reshape(rows, ch // 8), s.reshape(rows, ch // 32)
 
 
 def save(name: str, **arrays):
@@ -91,211 +102,188 @@ def save(name: str, **arrays):
     print("wrote", name)
 
 
-def f_out(rows, channels):
-    return zeros(rows * channels // 8, torch.int32), zeros(rows * channels // 32, torch.int8)
-
-
 def gen_pack(lib):
-    rng = np.random.default_rng(100)
-    master = W.conv_weights(rng, 64, 128, 1, False)
+    master, acts = S.pack_master()
     w, s = pack_weights(lib, master)
-    acts = (rng.standard_normal(4096) * 3).astype(np.float32)
-    acts[:32] = 0.0            # an all-zero group (absmax < eps -> scale 1)
-    acts[32:64] *= 1e-4        # a tiny group (clamped dequantisation)
     aw, as_ = quantize(lib, acts, False, 0)
-    save("pack", master=master, w=w, s=s, acts=acts, acts_w=aw, acts_s=as_)
+    save("pack", master_sha=S.sha(master), w=w, s=s, acts_sha=S.sha(acts), acts_w=aw, acts_s=as_)
 
 
 def gen_stem(lib):
-    rng = np.random.default_rng(101)
-    dim, ch = 64, 32
+    d = Dev()
+    planes3 = S.stem_case()
+    dim, ch = planes3.shape[1], 32
     planes = np.zeros((ch, dim, dim), dtype=np.float16)
-    planes[:3] = rng.random((3, dim, dim), dtype=np.float32).astype(np.float16)
-    w, s = f_out(dim * dim, ch)
-    run(lib, "aicref_stem", vp(dev(planes)), vp(w), vp(s), C.c_int(dim), C.c_int(ch))
-    save("stem", planes=planes[:3], channels=np.int32(ch), w=host(w).view(np.uint32), s=host(s))
+    planes[:3] = planes3
+    w, pw = d.zeros(dim * dim * ch // 8, torch.int32)
+    s, ps = d.zeros(dim * dim * ch // 32, torch.int8)
+    run(lib, "aicref_stem", d.put(planes), pw, ps, C.c_int(dim), C.c_int(ch))
+    save("stem", planes_sha=S.sha(planes3), w=u32(w), s=s.cpu().numpy())
 
 
 def gen_conv(lib):
-    rng = np.random.default_rng(102)
-    cases = [  # (name, in, out, k, stride, din, dout, act)
-        ("pw_64_128_silu", 64, 128, 1, 1, 16, 16, 1),
-        ("pw_128_64", 128, 64, 1, 1, 16, 16, 0),
-        ("pw_64_512_silu", 64, 512, 1, 1, 8, 8, 1),
-        ("pw_96_96", 96, 96, 1, 1, 8, 8, 0),
-        ("dense_k2_64_128", 64, 128, 2, 2, 16, 8, 0),
-        ("dense_k4_32_64", 32, 64, 4, 4, 32, 8, 0),
-        ("dense_k2_160_288", 160, 288, 2, 2, 8, 4, 0),
-        ("dw_k3_s2_64", 64, 64, 3, 2, 16, 8, 0),
-        ("dw_k5_s1_32", 32, 32, 5, 1, 8, 8, 0),
-        ("dw_k7_s2_96", 96, 96, 7, 2, 16, 8, 0),
-    ]
-    for name, cin, cout, k, st, din, dout, act in cases:
+    for name, (cin, cout, k, st, din, dout, act) in S.CONV_CASES.items():
+        d = Dev()
+        master, bias, x = S.conv_case(name)
         dw = k > 1 and k % 2 == 1
-        master = W.conv_weights(rng, cin, cout, k, dw)
-        bias = W.bias(rng, cout)
         ww, ws = pack_weights(lib, master)
-        xw, xs = act_f(lib, rng, din * din, cin)
-        ow, os_ = f_out(dout * dout, cout)
-        args = [vp(dev(xw)), vp(dev(xs)), vp(dev(ww)), vp(dev(ws)), vp(dev(bias)), vp(ow), vp(os_)]
+        xw, xs = act_f(lib, x)
+        ow, pow_ = d.zeros(dout * dout * cout // 8, torch.int32)
+        os_, pos = d.zeros(dout * dout * cout // 32, torch.int8)
+        args = [d.put(xw), d.put(xs), d.put(ww), d.put(ws), d.put(bias), pow_, pos]
         if dw:
             run(lib, "aicref_conv_dw", *args, *map(C.c_int, (cin, k, st, din, dout)))
         elif k == 1:
             run(lib, "aicref_conv_pw", *args, *map(C.c_int, (din * din, cin, cout, act)))
         else:
             run(lib, "aicref_conv_dense", *args, *map(C.c_int, (cin, cout, k, st, din, dout, act)))
-        save(f"conv_{name}", master=master, bias=bias, w=ww, s=ws, x_w=xw, x_s=xs,
-             geo=np.array([cin, cout, k, st, din, dout, act], np.int32),
-             out_w=host(ow).view(np.uint32), out_s=host(os_))
+        save(f"conv_{name}", master_sha=S.sha(master), bias_sha=S.sha(bias), w_sha=S.sha(ww), s_sha=S.sha(ws),
+             x_w=xw, x_s=xs, out_w=u32(ow), out_s=os_.cpu().numpy())
 
 
 def gen_residual(lib):
-    rng = np.random.default_rng(103)
-    for name, pos, ch, dim, rf in (("res_160", 64, 160, 8, 0.625), ("res_mamba_256", 1, 256, 1, 1.0)):
-        mw, ms = act_f(lib, rng, pos, ch)
-        rw, rs = act_f(lib, rng, pos, ch, 0.5)
-        ow, os_ = f_out(pos, ch)
-        run(lib, "aicref_residual", vp(dev(mw)), vp(dev(ms)), vp(dev(rw)), vp(dev(rs)), vp(ow), vp(os_), C.c_int(ch),
-            C.c_int(dim), C.c_float(1.0), C.c_int(0), C.c_float(rf))
-        save(name, main_w=mw, main_s=ms, res_w=rw, res_s=rs, channels=np.int32(ch), rf=np.float32(rf),
-             out_w=host(ow).view(np.uint32), out_s=host(os_))
+    for name, (pos, ch, dim, rf) in S.RES_CASES.items():
+        d = Dev()
+        m, r = S.residual_case(name)
+        mw, ms = act_f(lib, m)
+        rw, rs = act_f(lib, r)
+        ow, pow_ = d.zeros(pos * ch // 8, torch.int32)
+        os_, pos_ = d.zeros(pos * ch // 32, torch.int8)
+        run(lib, "aicref_residual", d.put(mw), d.put(ms), d.put(rw), d.put(rs), pow_, pos_, C.c_int(ch), C.c_int(dim),
+            C.c_float(1.0), C.c_int(0), C.c_float(rf))
+        save(name, main_w=mw, main_s=ms, res_w=rw, res_s=rs, out_w=u32(ow), out_s=os_.cpu().numpy())
 
 
 def gen_gap(lib):
-    rng = np.random.default_rng(104)
-    xw, xs = act_f(lib, rng, 64, 256)
-    pooled = zeros(256, torch.float32)
-    run(lib, "aicref_gap_f32", vp(dev(xw)), vp(dev(xs)), vp(pooled), C.c_int(64), C.c_int(256))
-    cw, cs = act_f(lib, rng, 16, 32)
-    pooled_h = zeros(32, torch.float16)
-    run(lib, "aicref_gap_f16", vp(dev(cw)), vp(dev(cs)), vp(pooled_h), C.c_int(16), C.c_int(32))
-    save("gap", x_w=xw, x_s=xs, out=host(pooled), c_w=cw, c_s=cs, c_out=host(pooled_h))
+    d = Dev()
+    x, c = S.gap_case()
+    xw, xs = act_f(lib, x)
+    cw, cs = act_f(lib, c)
+    pooled, pp = d.zeros(256, torch.float32)
+    run(lib, "aicref_gap_f32", d.put(xw), d.put(xs), pp, C.c_int(64), C.c_int(256))
+    pooled_h, ph = d.zeros(32, torch.float16)
+    run(lib, "aicref_gap_f16", d.put(cw), d.put(cs), ph, C.c_int(16), C.c_int(32))
+    save("gap", x_w=xw, x_s=xs, out=pooled.cpu().numpy(), c_w=cw, c_s=cs, c_out=pooled_h.cpu().numpy())
 
 
 def gen_ssm(d_state: int):
-    lib = ref(256, d_state)
-    rng = np.random.default_rng(105 + d_state)
-    D, T = 256, 8
-    E = 2 * D
-    blob = W.mamba_blob(rng, D, d_state, D, a_im=None)
+    lib = ref(S.SSM_D, d_state)
+    d = Dev()
+    blob, x = S.ssm_case(d_state)
+    E = 2 * S.SSM_D
     bw, bs = pack_weights(lib, blob)
-    bwd, bsd = dev(bw), dev(bs)
-    h = zeros(E * d_state * 2, torch.float32)
-    tr = [zeros(E * d_state * 2, torch.float32) for _ in range(3)]
-    y = zeros(E, torch.float32)
-    xw, xs = act_f(lib, rng, T, D)
+    pbw, pbs = d.put(bw), d.put(bs)
+    h, ph = d.zeros(E * d_state * 2, torch.float32)
+    trs = [d.zeros(E * d_state * 2, torch.float32)[1] for _ in range(3)]
+    y, py = d.zeros(E, torch.float32)
+    xw, xs = act_f(lib, x)
     ys = []
-    for t in range(T):
-        run(lib, "aicref_ssm_step", vp(dev(xw[t])), vp(dev(xs[t])), vp(bwd), vp(bsd), vp(h), vp(tr[0]), vp(tr[1]),
-            vp(tr[2]), vp(y))
-        ys.append(host(y).copy())
-    outs = {}
-    bias = W.bias(rng, 512)
-    yin = (rng.standard_normal(E) * 2).astype(np.float32)
-    for out_c, act in ((256, 1), (64, 0), (256, 2)):
-        blob_o = W.mamba_blob(rng, D, d_state, out_c, a_im=None)
+    for t in range(S.SSM_T):
+        run(lib, "aicref_ssm_step", d.put(xw[t]), d.put(xs[t]), pbw, pbs, ph, *trs, py)
+        ys.append(y.cpu().numpy().copy())
+    hv = h.cpu().numpy().reshape(E, d_state, 2)
+    lane = np.arange(E) % 32
+    h_active = np.stack([hv[np.arange(E), lane + 32 * c] for c in range(d_state // 32)], axis=1)
+    extra = {}
+    for out_c, act in S.OUTPROJ_CASES:
+        blob_o, bias_o, yin = S.outproj_case(d_state, out_c, act)
         ow_, os__ = pack_weights(lib, blob_o)
-        o = zeros(out_c, torch.float32)
-        run(lib, "aicref_outproj", vp(dev(yin)), vp(dev(ow_)), vp(dev(os__)), vp(dev(bias[:out_c])), vp(o),
-            C.c_int(out_c), C.c_int(act))
-        outs[f"op{out_c}_{act}_blob"] = blob_o
-        outs[f"op{out_c}_{act}_out"] = host(o)
-    save(f"ssm_N{d_state}", blob=blob, blob_w=bw, blob_s=bs, x_w=xw, x_s=xs, y=np.stack(ys),
-         h=host(h).reshape(E, d_state, 2), yin=yin, bias=bias, **outs)
+        o, po = d.zeros(out_c, torch.float32)
+        run(lib, "aicref_outproj", d.put(yin), d.put(ow_), d.put(os__), d.put(bias_o), po, C.c_int(out_c), C.c_int(act))
+        extra[f"op{out_c}_{act}_sha"] = S.sha(blob_o)
+        extra[f"op{out_c}_{act}_out"] = o.cpu().numpy()
+    save(f"ssm_N{d_state}", blob_sha=S.sha(blob), w_sha=S.sha(bw), s_sha=S.sha(bs), x_w=xw, x_s=xs, y=np.stack(ys),
+         h=h_active, **extra)
 
 
 def gen_mamba_block():
-    """MambaBlock::forward (mamba_block.h:58-72, inference) for T steps, d_state 128."""
-    lib = ref(256, 128)
-    rng = np.random.default_rng(106)
-    D, N, T, OUT = 256, 128, 6, 128
-    E = 2 * D
-    blobs = [W.mamba_blob(rng, D, N, D, a_im=None), W.mamba_blob(rng, D, N, D, a_im=None),
-             W.mamba_blob(rng, D, N, OUT, a_im=None)]
-    biases = [W.bias(rng, D), W.bias(rng, D), W.bias(rng, OUT)]
-    packed = [tuple(dev(a) for a in pack_weights(lib, b)) for b in blobs]
-    outs_c = (D, D, OUT)
+    """MambaBlock::forward (mamba_block.h:58-72, inference) for T steps."""
+    lib = ref(S.MB_D, S.MB_N)
+    d = Dev()
+    blobs, biases, x = S.mamba_block_case()
+    D, N, E = S.MB_D, S.MB_N, 2 * S.MB_D
+    packed = [tuple(d.put(a) for a in pack_weights(lib, b)) for b in blobs]
+    pbias = [d.put(b) for b in biases]
+    outs_c = (D, D, S.MB_OUT)
     acts = (1, 1, 2)
-    st = [[zeros(E * N * 2, torch.float32) for _ in range(4)] for _ in range(3)]
-    y = zeros(E, torch.float32)
-    o = [zeros(c, torch.float32) for c in outs_c]
-    aw, as_ = f_out(1, D)
-    bw, bs = f_out(1, D)
-    xw, xs = act_f(lib, rng, T, D)
+    st = [[d.zeros(E * N * 2, torch.float32)[1] for _ in range(4)] for _ in range(3)]
+    _, py = d.zeros(E, torch.float32)
+    o = [d.zeros(c, torch.float32) for c in outs_c]
+    _, paw = d.zeros(D // 8, torch.int32)
+    _, pas = d.zeros(D // 32, torch.int8)
+    _, pbw = d.zeros(D // 8, torch.int32)
+    _, pbs = d.zeros(D // 32, torch.int8)
+    xw, xs = act_f(lib, x)
     res = []
 
     def layer(i, inw, ins):
-        run(lib, "aicref_ssm_step", vp(inw), vp(ins), vp(packed[i][0]), vp(packed[i][1]), *[vp(t) for t in st[i]], vp(y))
-        run(lib, "aicref_outproj", vp(y), vp(packed[i][0]), vp(packed[i][1]), vp(dev(biases[i])), vp(o[i]),
-            C.c_int(outs_c[i]), C.c_int(acts[i]))
+        run(lib, "aicref_ssm_step", inw, ins, packed[i][0], packed[i][1], *st[i], py)
+        run(lib, "aicref_outproj", py, packed[i][0], packed[i][1], pbias[i], o[i][1], C.c_int(outs_c[i]),
+            C.c_int(acts[i]))
 
-    for t in range(T):
-        xin_w, xin_s = dev(xw[t]), dev(xs[t])
+    for t in range(S.MB_T):
+        xin_w, xin_s = d.put(xw[t]), d.put(xs[t])
         layer(0, xin_w, xin_s)
-        run(lib, "aicref_quantize_f32", vp(o[0]), vp(aw), vp(as_), C.c_int(D), C.c_int(0), C.c_int(0))
-        run(lib, "aicref_residual", vp(aw), vp(as_), vp(xin_w), vp(xin_s), vp(bw), vp(bs), C.c_int(D), C.c_int(1),
-            C.c_float(1.0), C.c_int(0), C.c_float(1.0))
-        layer(1, bw, bs)
-        run(lib, "aicref_quantize_f32", vp(o[1]), vp(aw), vp(as_), C.c_int(D), C.c_int(0), C.c_int(0))
-        layer(2, aw, as_)
-        res.append(host(o[2]).copy())
-    save("mamba_block_N128", blob0=blobs[0], blob1=blobs[1], blob2=blobs[2], bias0=biases[0], bias1=biases[1],
-         bias2=biases[2], x_w=xw, x_s=xs, out=np.stack(res))
+        run(lib, "aicref_quantize_f32", o[0][1], paw, pas, C.c_int(D), C.c_int(0), C.c_int(0))
+        run(lib, "aicref_residual", paw, pas, xin_w, xin_s, pbw, pbs, C.c_int(D), C.c_int(1), C.c_float(1.0),
+            C.c_int(0), C.c_float(1.0))
+        layer(1, pbw, pbs)
+        run(lib, "aicref_quantize_f32", o[1][1], paw, pas, C.c_int(D), C.c_int(0), C.c_int(0))
+        layer(2, paw, pas)
+        res.append(o[2][0].cpu().numpy().copy())
+    save("mamba_block_N128", blob_sha=np.array([S.sha(b) for b in blobs]), x_w=xw, x_s=xs, out=np.stack(res))
 
 
 def gen_conv_block(lib):
     """ConvBlock::forward (conv_block.h:74-82, inference) on one frame."""
-    rng = np.random.default_rng(107)
-    cin, mid, cout, st, din, dout, k = 64, 256, 128, 2, 32, 16, 3
-    masters, biases, packed = [], [], []
-    geo = [(cin, cin, k, True), (cin, mid, 1, False), (mid, cout, 1, False), (cin, cout, 2, False)]
-    for (a, b, kk, dw) in geo:
-        m = W.conv_weights(rng, a, b, kk, dw)
-        bi = W.bias(rng, b)
-        masters.append(m)
-        biases.append(bi)
-        packed.append(tuple(dev(x) for x in pack_weights(lib, m)) + (dev(bi),))
-    xw, xs = act_f(lib, rng, din * din, cin)
-    xwd, xsd = dev(xw), dev(xs)
-    a_w, a_s = f_out(dout * dout, mid)
-    b_w, b_s = f_out(dout * dout, mid)
-    o_w, o_s = f_out(dout * dout, cout)
-    run(lib, "aicref_conv_dw", vp(xwd), vp(xsd), *map(vp, packed[0]), vp(a_w), vp(a_s), *map(C.c_int, (cin, k, st, din, dout)))
-    run(lib, "aicref_conv_pw", vp(a_w), vp(a_s), *map(vp, packed[1]), vp(b_w), vp(b_s), *map(C.c_int, (dout * dout, cin, mid, 1)))
-    run(lib, "aicref_conv_pw", vp(b_w), vp(b_s), *map(vp, packed[2]), vp(a_w), vp(a_s), *map(C.c_int, (dout * dout, mid, cout, 0)))
-    run(lib, "aicref_conv_dense", vp(xwd), vp(xsd), *map(vp, packed[3]), vp(b_w), vp(b_s), *map(C.c_int, (cin, cout, 2, 2, din, dout, 0)))
-    run(lib, "aicref_residual", vp(a_w), vp(a_s), vp(b_w), vp(b_s), vp(o_w), vp(o_s), C.c_int(cout), C.c_int(dout),
-        C.c_float(1.0), C.c_int(0), C.c_float(0.75))
-    save("conv_block", **{f"m{i}": m for i, m in enumerate(masters)}, **{f"b{i}": b for i, b in enumerate(biases)},
-         x_w=xw, x_s=xs, geo=np.array([cin, mid, cout, st, din, dout, k], np.int32), rf=np.float32(0.75),
-         out_w=host(o_w).view(np.uint32), out_s=host(o_s))
+    d = Dev()
+    masters, biases, x = S.conv_block_case()
+    cin, mid, cout, st, din, dout, k = S.CB_GEO
+    packed = []
+    for m, b in zip(masters, biases):
+        w, s = pack_weights(lib, m)
+        packed.append((d.put(w), d.put(s), d.put(b)))
+    xw, xs = act_f(lib, x)
+    pxw, pxs = d.put(xw), d.put(xs)
+    _, paw = d.zeros(dout * dout * mid // 8, torch.int32)
+    _, pas = d.zeros(dout * dout * mid // 32, torch.int8)
+    _, pbw = d.zeros(dout * dout * mid // 8, torch.int32)
+    _, pbs = d.zeros(dout * dout * mid // 32, torch.int8)
+    ow, pow_ = d.zeros(dout * dout * cout // 8, torch.int32)
+    os_, pos = d.zeros(dout * dout * cout // 32, torch.int8)
+    run(lib, "aicref_conv_dw", pxw, pxs, *packed[0], paw, pas, *map(C.c_int, (cin, k, st, din, dout)))
+    run(lib, "aicref_conv_pw", paw, pas, *packed[1], pbw, pbs, *map(C.c_int, (dout * dout, cin, mid, 1)))
+    run(lib, "aicref_conv_pw", pbw, pbs, *packed[2], paw, pas, *map(C.c_int, (dout * dout, mid, cout, 0)))
+    run(lib, "aicref_conv_dense", pxw, pxs, *packed[3], pbw, pbs, *map(C.c_int, (cin, cout, 2, 2, din, dout, 0)))
+    run(lib, "aicref_residual", paw, pas, pbw, pbs, pow_, pos, C.c_int(cout), C.c_int(dout), C.c_float(1.0),
+        C.c_int(0), C.c_float(S.CB_RF))
+    save("conv_block", master_sha=np.array([S.sha(m) for m in masters]), x_w=xw, x_s=xs, out_w=u32(ow),
+         out_s=os_.cpu().numpy())
 
 
 def gen_critic(lib):
-    rng = np.random.default_rng(108)
-    cin, units, T = 32, 128, 5
-    w1, w2, wl = W.critic_weights(rng, cin, units)
-    h = zeros(2 * units, torch.float32)
-    tw1 = zeros(cin * units * 2, torch.float32)
-    tl = zeros(cin * units * 2, torch.float32)
-    score = zeros(1, torch.float32)
-    x = (rng.standard_normal((T, cin)) * 0.5).astype(np.float16)
+    d = Dev()
+    w1, w2, wl, x = S.critic_case()
+    T, cin, units = x.shape[0], 32, 128
+    h, ph = d.zeros(2 * units, torch.float32)
+    _, ptw = d.zeros(cin * units * 2, torch.float32)
+    _, ptl = d.zeros(cin * units * 2, torch.float32)
+    score, psc = d.zeros(1, torch.float32)
+    pw1, pw2, pwl = d.put(w1), d.put(w2), d.put(wl)
     scores = []
-    w1d, w2d, wld = dev(w1), dev(w2), dev(wl)
     for t in range(T):
-        run(lib, "aicref_critic", vp(dev(x[t])), vp(w1d), vp(wld), vp(w2d), vp(h), vp(tw1), vp(tl), vp(score),
-            C.c_int(units), C.c_int(cin))
-        scores.append(float(host(score)[0]))
-    save("critic", w1=w1, w2=w2, wl=wl, x=x, score=np.array(scores, np.float32), h=host(h))
+        run(lib, "aicref_critic", d.put(x[t]), pw1, pwl, pw2, ph, ptw, ptl, psc, C.c_int(units), C.c_int(cin))
+        scores.append(float(score.cpu().numpy()[0]))
+    save("critic", w_sha=np.array([S.sha(w1), S.sha(w2), S.sha(wl), S.sha(x)]), score=np.array(scores, np.float32),
+         h=h.cpu().numpy())
 
 
 def gen_actions(lib):
-    rng = np.random.default_rng(109)
-    probs = rng.random(98).astype(np.float32)
-    probs[:8] = rng.random(8).astype(np.float32) * 0.06
-    acts = torch.zeros(2, dtype=torch.int64, device=DEV)
-    run(lib, "aicref_set_actions", vp(dev(probs)), vp(acts), C.c_int(98))
-    save("actions", probs=probs, words=host(acts).view(np.uint64))
+    d = Dev()
+    probs = S.actions_case()
+    acts, pa = d.zeros(2, torch.int64)
+    run(lib, "aicref_set_actions", d.put(probs), pa, C.c_int(98))
+    save("actions", probs_sha=S.sha(probs), words=acts.cpu().numpy().view(np.uint64))
 
 
 def main():
