@@ -66,6 +66,7 @@ PP = C.POINTER(C.c_void_p)
 
 # name -> argtypes (restype is always aic_status = int)
 _SIGS = {
+    "aic_device_error_sync": [C.POINTER(C.c_int)],
     "aic_pack_f32": [P, I64, P, P, I32, I32, P],
     "aic_stem_pack": [P, I64, I32, I32, I32, P, P, P],
     "aic_residual_add": [P, P, P, P, P, P, I64, I32, F32, I32, P],
@@ -79,6 +80,7 @@ _SIGS = {
     "aic_conv_layer_load_weights": [P, P, P, P],
     "aic_conv_layer_load_file_sync": [P, C.c_char_p, P],
     "aic_conv_layer_forward": [P, P, P, P, P, I64, P],
+    "aic_conv_layer_forward_exact": [P, P, P, P, P, I64, P],
     "aic_conv_layer_destroy": [P],
     "aic_conv_block_create": [C.POINTER(ConvBlockDesc), PP],
     "aic_conv_block_layer": [P, I32, PP],

@@ -33,6 +33,18 @@ cudaError_t launch_conv_gemm_simt(const uint32_t* in, const int8_t* in_s, const 
                                   const float* bias, uint32_t* out, int8_t* out_s, int64_t frames, int InC,
                                   int OutC, int ksize, int stride, int Din, int Dout, bool act, cudaStream_t stream);
 
+// A3/A4 on the tensor cores (tcgen05, TMEM accumulator) with the same fused
+// epilogue. Weights come as swizzled bf16 images built by launch_build_wimg.
+size_t conv_tc_wimg_bytes(int in_c, int out_c, int ksize);
+cudaError_t launch_build_wimg(const uint32_t* w, const int8_t* w_s, int in_c, int out_c, int ksize, uint8_t* img,
+                              cudaStream_t stream);
+cudaError_t launch_conv_gemm_tc(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
+                                uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize, int din,
+                                int dout, bool act, int* err, cudaStream_t stream);
+
+// Device-side error word written by kernels whose bounded waits time out.
+int* device_error_word();
+
 // A6: out = requant(q_main * s_main * main_mult + q_res * s_res), one exponent per position.
 cudaError_t launch_residual(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res, const int8_t* res_s,
                             uint32_t* out, int8_t* out_s, int64_t positions, int C, float main_mult, bool skipped,

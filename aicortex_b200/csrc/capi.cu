@@ -240,17 +240,26 @@ struct ConvLayer {
         weight_elems = static_cast<int64_t>(d.in_channels) * d.kernel_size * d.kernel_size * (is_dw ? 1 : d.out_channels);
         groups = weight_elems >> 5;
     }
+    uint8_t* wimg = nullptr;  // tensor-core weight images (dense/pointwise only)
+
     size_t carve(void* base)
     {
         Carver c(base);
         w = c.take<uint32_t>(groups * 4);
         ws = c.take<int8_t>(groups);
         bias = c.take<float>(d.out_channels);
+        wimg = is_dw ? nullptr : c.take<uint8_t>(conv_tc_wimg_bytes(d.in_channels, d.out_channels, d.kernel_size));
         return c.bytes();
     }
     void check_bound() const
     {
         if (!bound) fail(AIC_ERR_STATE, "conv layer parameters not bound");
+    }
+    // After the packed weights change: derive the tensor-core images.
+    void prepare(cudaStream_t s)
+    {
+        if (!is_dw)
+            cuda_ok(launch_build_wimg(w, ws, d.in_channels, d.out_channels, d.kernel_size, wimg, s), "weight images");
     }
     void load(const float* master, const float* b, cudaStream_t s)
     {
@@ -258,6 +267,23 @@ struct ConvLayer {
         require(master != nullptr && b != nullptr, "null weights");
         cuda_ok(launch_pack_f32(master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s), "pack weights");
         cuda_ok(cudaMemcpyAsync(bias, b, sizeof(float) * d.out_channels, cudaMemcpyDefault, s), "copy bias");
+        prepare(s);
+    }
+    // Reference accumulation order on CUDA cores (bit-exact with the reference kernels).
+    void forward_exact(const uint32_t* in, const int8_t* in_s, uint32_t* out, int8_t* out_s, int64_t frames,
+                       cudaStream_t s)
+    {
+        check_bound();
+        if (frames == 0) return;
+        require(in && in_s && out && out_s, "null tensor");
+        if (is_dw)
+            cuda_ok(launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+                                   d.dim_in, d.dim_out, s),
+                    "conv_dw");
+        else
+            cuda_ok(launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                          d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s),
+                    "conv_gemm_simt");
     }
     void load_file(const char* path, cudaStream_t s)
     {
@@ -283,8 +309,9 @@ struct ConvLayer {
             });
         else
             traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm", [&] {
-                return launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
-                                             d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s);
+                return launch_conv_gemm_tc(in, in_s, wimg, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                           d.kernel_size, d.dim_in, d.dim_out, !d.disable_activation,
+                                           device_error_word(), s);
             });
         return 1;
     }
@@ -917,6 +944,21 @@ extern "C" {
 AIC_API const char* aic_last_error(void) { return g_last_error.c_str(); }
 AIC_API int aic_abi_version(void) { return 1; }
 
+AIC_API aic_status aic_device_error_sync(int* code)
+{
+    return guarded([&] {
+        require(code != nullptr, "null output");
+        cuda_ok(cudaDeviceSynchronize(), "device synchronize");
+        int* word = device_error_word();
+        if (!word) fail(AIC_ERR_CUDA, "device error word unavailable");
+        int v = 0;
+        cuda_ok(cudaMemcpy(&v, word, sizeof(int), cudaMemcpyDeviceToHost), "read error word");
+        const int zero = 0;
+        cuda_ok(cudaMemcpy(word, &zero, sizeof(int), cudaMemcpyHostToDevice), "clear error word");
+        *code = v;
+    });
+}
+
 AIC_API aic_status aic_pack_f32(const float* in, int64_t n, uint32_t* out, int8_t* out_s, int stochastic,
                                 int32_t add_idx, void* stream)
 {
@@ -1037,6 +1079,14 @@ AIC_API aic_status aic_conv_layer_forward(aic_conv_layer l, const uint32_t* in, 
     return guarded([&] {
         require(frames >= 0, "negative frame count");
         handle<ConvLayer>(l, "conv layer")->forward(in, in_s, out, out_s, frames, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_conv_layer_forward_exact(aic_conv_layer l, const uint32_t* in, const int8_t* in_s,
+                                                uint32_t* out, int8_t* out_s, int64_t frames, void* stream)
+{
+    return guarded([&] {
+        require(frames >= 0, "negative frame count");
+        handle<ConvLayer>(l, "conv layer")->forward_exact(in, in_s, out, out_s, frames, as_stream(stream));
     });
 }
 AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l)

@@ -1,0 +1,426 @@
+// Quantized conv (pointwise k=1, dense k=2/4 with stride k) as an implicit
+// GEMM on the 5th-generation tensor cores (tcgen05.mma, accumulator in TMEM),
+// with the RMSNorm(256-chunk) + bias (+SiLU) + int4 requant epilogue fused.
+//
+// Numerics. A packed int4 code q with exponent s stands for q * max(2^s/7,
+// 2^-13) (AICortex kernels.h:69). Both operands are staged in shared memory as
+// bf16 values q * F(s), F(s) = 2^s for s >= -10 and 7 * 2^-13 below (where the
+// reference's dequantisation clamps), which bf16 represents exactly (|q*7| <
+// 2^6). Every product is therefore exact, the tensor core accumulates in fp32,
+// and the epilogue multiplies by fl(1/7)^2. The result equals the reference's
+// sum over groups of unit(s_in) * unit(s_w) * dot up to fp32 summation order.
+//
+// Structure of one CTA (128 threads, one 128-pixel x up-to-256-channel tile):
+//   - thread t converts pixel row t of the A tile for each 64-wide K stage from
+//     the packed activations (im2col on the fly for the dense convs) into a
+//     128B-swizzled K-major bf16 tile;
+//   - the B tile (weights) is a pre-swizzled bf16 image built at weight-load
+//     time, fetched per stage with one cp.async.bulk into the same layout;
+//   - thread 0 issues four tcgen05.mma (M128 x N x K16) per stage and commits
+//     to the stage's mbarrier; stages are double-buffered;
+//   - after the last stage each warp reads its 32 TMEM lanes (= 32 pixel rows)
+//     with tcgen05.ld and each thread normalises, activates and packs its own
+//     row: the 256-channel RMSNorm and the 32-channel requant need no
+//     cross-thread reduction.
+// All mbarrier waits are bounded; on timeout the kernel records an error code
+// in *err, skips the remaining work, waits (bounded) for its own outstanding
+// operations and releases its TMEM before returning.
+#include <cuda_bf16.h>
+
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+
+namespace aic {
+namespace {
+
+constexpr int kBM = 128;          // pixel rows per tile (= TMEM lanes)
+constexpr int kBK = 64;           // K elements per stage (128 bytes of bf16)
+constexpr int kStages = 2;        // smem pipeline depth
+constexpr int kThreads = 128;
+constexpr int kTileA = kBM * kBK * 2;          // 16 KB
+constexpr int kMaxN = 256;
+constexpr int kTileBMax = kMaxN * kBK * 2;     // 32 KB
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+struct TcParams {
+    const uint32_t* in;
+    const int8_t* in_s;
+    const uint8_t* wimg;
+    const float* bias;
+    uint32_t* out;
+    int8_t* out_s;
+    int64_t rows;
+    int in_c, out_c, ksize, din, dout, stages, act;
+    int* err;
+};
+
+// ---- PTX wrappers ---------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p)
+{
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait; returns false (and records `code`) when the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code)
+{
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if (i > 256) __nanosleep(128);
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t cols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(cols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols));
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row atoms of 1024 B.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);        // start address
+    d |= static_cast<uint64_t>(1u) << 16;                      // leading byte offset (unused for SW128 K-major)
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;              // stride byte offset: next 8-row atom
+    d |= static_cast<uint64_t>(1u) << 46;                      // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(2u) << 61;                      // layout: SWIZZLE_128B
+    return d;
+}
+
+// kind::f16 instruction descriptor: bf16 x bf16 -> f32, both K-major, M = 128.
+__host__ __device__ constexpr uint32_t instr_desc(int n)
+{
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- int4 -> bf16 staging ----------------------------------------------------
+
+// bf16 factor F(s): 2^s where the reference's unit is 2^s/7, 7*2^-13 where it
+// clamps to 2^-13.
+__device__ __forceinline__ float stage_factor(int8_t s) { return s >= -10 ? exp2f(static_cast<float>(s)) : 7.0f * kEps; }
+
+// 8 codes of `word` -> 4 bf16x2 words holding (code j, code j+4) * f. The
+// nibble pair (n_j, n_j+4) lands in the two halves as 0x43.. | (n ^ 8), i.e.
+// the bf16 value 128 + q + 8; one fma with (f, -136 f) leaves q * f exactly.
+// A and B use the same K permutation, so the dot products are unchanged.
+__device__ __forceinline__ uint4 unpack_word(uint32_t word, __nv_bfloat162 f, __nv_bfloat162 c)
+{
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        uint32_t x = ((word >> (4 * j)) & 0x000F000Fu) ^ 0x43084308u;
+        __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&x);
+        v = __hfma2(v, f, c);
+        o[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Writes one 32-element group (4 chunks of 16 B) of a K-major SW128 row.
+__device__ __forceinline__ void stage_group(uint8_t* tile, int row, int group_in_stage, uint4 words, int8_t s)
+{
+    const float f = stage_factor(s);
+    const __nv_bfloat162 fv = __floats2bfloat162_rn(f, f);
+    const __nv_bfloat162 cv = __floats2bfloat162_rn(-136.0f * f, -136.0f * f);
+    uint8_t* rowp = tile + (row >> 3) * 1024 + (row & 7) * 128;
+    const uint32_t w[4] = {words.x, words.y, words.z, words.w};
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+        const int chunk = (group_in_stage << 2) + cl;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = unpack_word(w[cl], fv, cv);
+    }
+}
+
+__device__ __forceinline__ void stage_zero(uint8_t* tile, int row, int group_in_stage)
+{
+    uint8_t* rowp = tile + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+        const int chunk = (group_in_stage << 2) + cl;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// Input pixel of output row r for tap `tap` (stride == ksize, no padding).
+__device__ __forceinline__ int64_t tap_pixel(int64_t r, int tap, int ksize, int din, int dout)
+{
+    if (ksize == 1) return r;
+    const int64_t hw = static_cast<int64_t>(dout) * dout;
+    const int64_t frame = r / hw;
+    const int p = static_cast<int>(r - frame * hw);
+    const int hi = (p / dout) * ksize + tap / ksize;
+    const int wi = (p % dout) * ksize + tap % ksize;
+    return frame * din * din + static_cast<int64_t>(hi) * din + wi;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) conv_gemm_tc_kernel(TcParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned tiles (swizzle atoms), then barriers.
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int chunk_idx = blockIdx.y;
+    const int n0 = chunk_idx * kMaxN;
+    const int n_cta = min(kMaxN, p.out_c - n0);
+    const int tile_b = n_cta * kBK * 2;
+    uint8_t* a_tiles = base;
+    uint8_t* b_tiles = base + kStages * kTileA;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(b_tiles + kStages * kTileBMax);
+    // bars[0..S): B full, bars[S..2S): stage free, bars[2S]: accumulator ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const uint32_t tmem_cols = n_cta <= 32 ? 32u : n_cta <= 64 ? 64u : n_cta <= 128 ? 128u : 256u;
+    if (tid == 0) {
+        for (int i = 0; i < 2 * kStages + 1; ++i) mbar_init(smem_addr(&bars[i]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+    const int64_t row = m0 + tid;
+    const bool row_ok = row < p.rows;
+    const int G = p.in_c >> 5;
+    const int GK = G * p.ksize * p.ksize;
+    const uint8_t* wimg = p.wimg + (static_cast<int64_t>(n0) * p.stages * kBK * 2);
+    const uint32_t idesc = instr_desc(n_cta);
+
+    for (int s = 0; s < p.stages; ++s) {
+        const int buf = s % kStages;
+        const uint32_t use = static_cast<uint32_t>(s / kStages);
+        uint8_t* a_tile = a_tiles + buf * kTileA;
+        uint8_t* b_tile = b_tiles + buf * kTileBMax;
+        if (use > 0 && !*abort_flag) {
+            if (!mbar_wait(smem_addr(&bars[kStages + buf]), (use - 1) & 1u, p.err, 1)) *abort_flag = 1;
+        }
+        __syncthreads();
+        if (*abort_flag) break;
+        if (tid == 0) {
+            mbar_expect_tx(smem_addr(&bars[buf]), static_cast<uint32_t>(tile_b));
+            bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(s) * tile_b, static_cast<uint32_t>(tile_b),
+                     smem_addr(&bars[buf]));
+        }
+#pragma unroll
+        for (int gl = 0; gl < 2; ++gl) {
+            const int gk = 2 * s + gl;
+            if (row_ok && gk < GK) {
+                const int tap = gk / G, g = gk - tap * G;
+                const int64_t pix = tap_pixel(row, tap, p.ksize, p.din, p.dout);
+                const uint4 words = reinterpret_cast<const uint4*>(p.in)[pix * G + g];
+                stage_group(a_tile, tid, gl, words, p.in_s[pix * G + g]);
+            } else {
+                stage_zero(a_tile, tid, gl);
+            }
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            if (mbar_wait(smem_addr(&bars[buf]), use & 1u, p.err, 2)) {
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_tile);
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)
+                    mma_bf16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
+                             (s > 0 || j > 0) ? 1u : 0u);
+                mma_commit(smem_addr(&bars[kStages + buf]));
+            } else {
+                *abort_flag = 1;
+            }
+        }
+    }
+    if (tid == 0) mma_commit(smem_addr(&bars[2 * kStages]));
+    __syncthreads();
+    const bool acc_ok = mbar_wait(smem_addr(&bars[2 * kStages]), 0u, p.err, 3);
+    tc_fence_after();
+    if (acc_ok && !*abort_flag) {
+        const float inv49 = (1.0f / kQMax) * (1.0f / kQMax);
+        const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+        float sumsq = 0.0f;
+        for (int c0 = 0; c0 < n_cta; c0 += 32) {
+            float v[32];
+            tmem_ld32(taddr + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float a = v[i] * inv49;
+                sumsq = fmaf(a, a, sumsq);
+            }
+        }
+        const float inv_rms = __frsqrt_rn(fmaf(sumsq, inv_div, kEps));
+        const int groups_out = p.out_c >> 5;
+        for (int c0 = 0; c0 < n_cta; c0 += 32) {
+            float v[32];
+            tmem_ld32(taddr + c0, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                float x = fmaf(v[i] * inv49, inv_rms, __ldg(p.bias + n0 + c0 + i));
+                v[i] = p.act ? silu_f(x) : x;
+            }
+            uint4 words;
+            int8_t e;
+            quantize_group(v, &words, &e);
+            if (row_ok) {
+                const int64_t gi = row * groups_out + ((n0 + c0) >> 5);
+                reinterpret_cast<uint4*>(p.out)[gi] = words;
+                p.out_s[gi] = e;
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, tmem_cols);
+}
+
+// Builds the per-(chunk, stage) swizzled bf16 images of the weights from the
+// packed int4 rows [out_c][ksize^2 * in_c]. One thread per (out channel,
+// 32-element group slot of the padded K).
+__global__ void build_wimg_kernel(const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s, int out_c, int gk_total,
+                                  int stages, uint8_t* __restrict__ img)
+{
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int slots = 2 * stages;
+    if (t >= static_cast<int64_t>(out_c) * slots) return;
+    const int n = static_cast<int>(t / slots);
+    const int gk = static_cast<int>(t % slots);
+    const int chunk = n / kMaxN, nl = n % kMaxN;
+    const int n_chunk = min(kMaxN, out_c - chunk * kMaxN);
+    const int s = gk >> 1, gl = gk & 1;
+    uint8_t* tile = img + (static_cast<int64_t>(chunk) * kMaxN * stages + static_cast<int64_t>(s) * n_chunk) * kBK * 2;
+    if (gk < gk_total) {
+        const int64_t gi = static_cast<int64_t>(n) * gk_total + gk;
+        stage_group(tile, nl, gl, reinterpret_cast<const uint4*>(w)[gi], w_s[gi]);
+    } else {
+        stage_zero(tile, nl, gl);
+    }
+}
+
+__device__ int g_device_error;
+
+}  // namespace
+
+// Address of the device error word of the current device (looked up per
+// call: the symbol has one instance per device).
+int* device_error_word()
+{
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    return static_cast<int*>(p);
+}
+
+size_t conv_tc_wimg_bytes(int in_c, int out_c, int ksize)
+{
+    const int gk_total = (in_c >> 5) * ksize * ksize;
+    const int stages = (gk_total + 1) / 2;
+    return static_cast<size_t>(out_c) * stages * kBK * 2;
+}
+
+cudaError_t launch_build_wimg(const uint32_t* w, const int8_t* w_s, int in_c, int out_c, int ksize, uint8_t* img,
+                              cudaStream_t stream)
+{
+    const int gk_total = (in_c >> 5) * ksize * ksize;
+    const int stages = (gk_total + 1) / 2;
+    const int64_t n = static_cast<int64_t>(out_c) * 2 * stages;
+    build_wimg_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(w, w_s, out_c, gk_total, stages, img);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_gemm_tc(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
+                                uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize, int din,
+                                int dout, bool act, int* err, cudaStream_t stream)
+{
+    const int64_t rows = frames * dout * dout;
+    if (rows == 0) return cudaSuccess;
+    TcParams p;
+    p.in = in; p.in_s = in_s; p.wimg = wimg; p.bias = bias; p.out = out; p.out_s = out_s;
+    p.rows = rows; p.in_c = in_c; p.out_c = out_c; p.ksize = ksize; p.din = din; p.dout = dout;
+    p.stages = ((in_c >> 5) * ksize * ksize + 1) / 2;
+    p.act = act ? 1 : 0;
+    p.err = err;
+    const size_t smem = 1024 + kStages * (kTileA + kTileBMax) + (2 * kStages + 1) * 8 + 16;
+    cudaError_t e = cudaFuncSetAttribute(conv_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    dim3 grid(static_cast<unsigned>((rows + kBM - 1) / kBM), static_cast<unsigned>((out_c + kMaxN - 1) / kMaxN));
+    conv_gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace aic

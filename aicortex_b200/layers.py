@@ -122,6 +122,11 @@ class ConvLayer(_Handle):
     def forward(self, x, x_s, out, out_s, frames: int, stream=None) -> None:
         call("aic_conv_layer_forward", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames), _stream(stream))
 
+    def forward_exact(self, x, x_s, out, out_s, frames: int, stream=None) -> None:
+        """Reference accumulation order on CUDA cores (bit-exact with the reference)."""
+        call("aic_conv_layer_forward_exact", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames),
+             _stream(stream))
+
 
 class ConvBlock(_Handle):
     """ConvBlock (conv_block.h): dw -> pw1 (SiLU) -> pw2, shortcut, residual add."""

@@ -57,6 +57,10 @@ typedef int aic_status;
 
 AIC_API const char* aic_last_error(void);
 AIC_API int aic_abi_version(void);
+/* Synchronises the current device and reads (and clears) the device error
+ * word that kernels set when a bounded wait on the tensor-core pipeline times
+ * out (the kernel then abandons its tile and returns). *code = 0: no error. */
+AIC_API aic_status aic_device_error_sync(int* code);
 
 /* ------------------------------------------------------------------------
  * Stateless format kernels
@@ -128,6 +132,12 @@ AIC_API aic_status aic_conv_layer_load_file_sync(aic_conv_layer l, const char* p
 /* ConvLayer::forward (conv_layer.h:102-149) over `frames` frames. */
 AIC_API aic_status aic_conv_layer_forward(aic_conv_layer l, const uint32_t* in, const int8_t* in_s, uint32_t* out,
                                           int8_t* out_s, int64_t frames, void* stream);
+/* The same conv on CUDA cores in the reference kernels' exact accumulation
+ * order (convPointwiseFwdKernel / convDenseFwdKernel / convDepthwiseFwdKernel):
+ * bit-identical to the reference, slower than aic_conv_layer_forward, whose
+ * tensor-core sums differ in fp32 summation order only. */
+AIC_API aic_status aic_conv_layer_forward_exact(aic_conv_layer l, const uint32_t* in, const int8_t* in_s,
+                                                uint32_t* out, int8_t* out_s, int64_t frames, void* stream);
 AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l);
 
 /* ------------------------------------------------------------------------

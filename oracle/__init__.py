@@ -194,34 +194,60 @@ def pack_conv_layer(master, bias):
     return w, s, np.ascontiguousarray(bias, np.float32)
 
 
-def cortex_forward(weights: dict, planes_f16: np.ndarray, B: int, T: int, blocks_geo, d_model: int, d_state: int,
-                   actor_out: int, critic_units: int, stem_channels: int = 32):
+class CortexRef:
     """The cortex forward composition on the CPU: stem pack -> ConvBlocks ->
     GAP -> requant -> units (MambaLayer + requant + residual) -> actor, and the
     critic on the trunk output (cortex.h:281-303, conv_block.h:74-82,
-    mamba_block.h:60-65, critic.h:106-116). Returns (actor [B*T][actor_out],
-    critic [B*T], features (words, exps))."""
-    frames = B * T
-    xw, xs = stem_pack(planes_f16, stem_channels)
-    for geo, layers in zip(blocks_geo, weights["blocks"]):
-        packed = [pack_conv_layer(m, b) for (m, b) in layers]
-        xw, xs = conv_block(xw, xs, packed, frames, geo)
-    fd = blocks_geo[-1][5]
-    pooled = gap_f32(xw, xs, frames, fd * fd, d_model)
-    fw, fs = pack_f32(pooled)
-    cur = (fw.reshape(frames, -1), fs.reshape(frames, -1))
-    feats = cur
-    for blob, bias in weights["units"]:
-        layer = MambaLayerRef(d_model, d_state, d_model, 1, blob, bias, B)
-        o = layer.forward(cur[0], cur[1], B, T)
-        qw, qs = pack_f32(o)
-        cur = residual(qw, qs, cur[0], cur[1], frames, d_model, 1.0, False)
-    actor_layer = MambaLayerRef(d_model, d_state, actor_out, 0, *weights["actor"], B)
-    actor = actor_layer.forward(cur[0], cur[1], B, T)
-    score = None
-    if critic_units:
-        w1, w2, wl = weights["critic"]
-        pooled_h = gap_f16(cur[0], cur[1], frames, 1, d_model)
-        h = np.zeros((B, critic_units, 2), dtype=np.float32)
-        score = critic(pooled_h, w1, wl, w2, d_model, critic_units, h, B, T)
-    return actor, score, feats
+    mamba_block.h:60-65, critic.h:106-116). Weights are packed once at
+    construction, as the reference does at load time."""
+
+    def __init__(self, weights: dict, blocks_geo, d_model: int, d_state: int, actor_out: int, critic_units: int,
+                 stem_channels: int = 32):
+        self.geo = list(blocks_geo)
+        self.d_model, self.d_state, self.actor_out = d_model, d_state, actor_out
+        self.critic_units, self.stem_channels = critic_units, stem_channels
+        self.blocks = [[pack_conv_layer(m, b) for (m, b) in layers] for layers in weights["blocks"]]
+        self.units = [(pack_f32(blob, True, blob.size), np.ascontiguousarray(bias, np.float32))
+                      for blob, bias in weights["units"]]
+        blob, bias = weights["actor"]
+        self.actor = (pack_f32(blob, True, blob.size), np.ascontiguousarray(bias, np.float32))
+        self.critic_w = weights["critic"]
+
+    def _layer(self, packed, out, act, B):
+        (w, s), bias = packed
+        ref = MambaLayerRef.__new__(MambaLayerRef)
+        ref.d_model, ref.d_state, ref.out, ref.act = self.d_model, self.d_state, out, act
+        ref.w, ref.s, ref.bias = w, s, bias
+        ref.h = np.zeros((B, 2 * self.d_model, self.d_state // 32, 2), dtype=np.float32)
+        return ref
+
+    def forward(self, planes_f16: np.ndarray, B: int, T: int):
+        """Returns (actor [B*T][actor_out], critic [B*T] or None, features (words, exps))."""
+        frames = B * T
+        xw, xs = stem_pack(planes_f16, self.stem_channels)
+        for geo, packed in zip(self.geo, self.blocks):
+            xw, xs = conv_block(xw, xs, packed, frames, geo)
+        fd = self.geo[-1][5]
+        pooled = gap_f32(xw, xs, frames, fd * fd, self.d_model)
+        fw, fs = pack_f32(pooled)
+        cur = (fw.reshape(frames, -1), fs.reshape(frames, -1))
+        feats = cur
+        for packed in self.units:
+            o = self._layer(packed, self.d_model, 1, B).forward(cur[0], cur[1], B, T)
+            qw, qs = pack_f32(o)
+            cur = residual(qw, qs, cur[0], cur[1], frames, self.d_model, 1.0, False)
+        actor = self._layer(self.actor, self.actor_out, 0, B).forward(cur[0], cur[1], B, T)
+        score = None
+        if self.critic_units:
+            w1, w2, wl = self.critic_w
+            pooled_h = gap_f16(cur[0], cur[1], frames, 1, self.d_model)
+            h = np.zeros((B, self.critic_units, 2), dtype=np.float32)
+            score = critic(pooled_h, w1, wl, w2, self.d_model, self.critic_units, h, B, T)
+        return actor, score, feats
+
+
+def cortex_forward(weights: dict, planes_f16: np.ndarray, B: int, T: int, blocks_geo, d_model: int, d_state: int,
+                   actor_out: int, critic_units: int, stem_channels: int = 32):
+    """One-shot CortexRef(...).forward(...)."""
+    return CortexRef(weights, blocks_geo, d_model, d_state, actor_out, critic_units, stem_channels).forward(
+        planes_f16, B, T)
