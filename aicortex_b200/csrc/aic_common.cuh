@@ -82,6 +82,16 @@ __device__ __forceinline__ uint32_t quantize_word_x4(const float (&v)[8], int8_t
     return w;
 }
 
+// The same code as code_rn for finite v without a float->int conversion: the
+// clamped value plus 1.5 * 2^23 is rounded to nearest even by the add, and the
+// low four mantissa bits are then the two's-complement code.
+// (rn(clamp(x)) == clamp(rn(x)) because rounding is monotonic.)
+__device__ __forceinline__ uint32_t code_rn_fast(float v, float inv)
+{
+    const float y = fminf(fmaxf(v * inv, -8.0f), 7.0f);
+    return __float_as_uint(y + 12582912.0f) & 0xFu;
+}
+
 // Quantise 32 values held by one thread into 4 words + exponent.
 __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* words, int8_t* exp_out)
 {
@@ -92,7 +102,7 @@ __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* word
     const float inv = kQMax * __frcp_rn(scale);
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn(v[i], inv) << ((i & 7) << 2);
+    for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn_fast(v[i], inv) << ((i & 7) << 2);
     *words = make_uint4(w[0], w[1], w[2], w[3]);
     *exp_out = exponent_of(scale);
 }

@@ -10,18 +10,21 @@
 // and the epilogue multiplies by fl(1/7)^2. The result equals the reference's
 // sum over groups of unit(s_in) * unit(s_w) * dot up to fp32 summation order.
 //
-// Structure of one CTA (128 threads, one 128-pixel x up-to-256-channel tile):
-//   - thread t converts pixel row t of the A tile for each 64-wide K stage from
-//     the packed activations (im2col on the fly for the dense convs) into a
-//     128B-swizzled K-major bf16 tile;
+// Structure of one CTA (256 threads, one 128-pixel x up-to-256-channel tile):
+//   - for each 64-wide K stage, thread t converts group (t >> 7) of pixel row
+//     (t & 127) of the A tile from the packed activations (im2col on the fly
+//     for the dense convs) into a 128B-swizzled K-major bf16 tile;
 //   - the B tile (weights) is a pre-swizzled bf16 image built at weight-load
 //     time, fetched per stage with one cp.async.bulk into the same layout;
 //   - thread 0 issues four tcgen05.mma (M128 x N x K16) per stage and commits
 //     to the stage's mbarrier; stages are double-buffered;
-//   - after the last stage each warp reads its 32 TMEM lanes (= 32 pixel rows)
-//     with tcgen05.ld and each thread normalises, activates and packs its own
-//     row: the 256-channel RMSNorm and the 32-channel requant need no
-//     cross-thread reduction.
+//   - after the last stage warp w reads TMEM lanes 32*(w&3).. (its 32 pixel
+//     rows) with tcgen05.ld; the two warpgroups take alternate 32-channel
+//     groups, exchange the rows' sums of squares once through shared memory,
+//     and each thread normalises, activates and packs whole 32-channel groups
+//     of its own row, so the requant needs no cross-thread reduction.
+// Shared memory is sized per launch (1-2 stages, B tile of the layer's width)
+// so 2-4 CTAs share an SM, never more than its 512 TMEM columns can hold.
 // All mbarrier waits are bounded; on timeout the kernel records an error code
 // in *err, skips the remaining work, waits (bounded) for its own outstanding
 // operations and releases its TMEM before returning.
@@ -36,7 +39,7 @@ namespace {
 constexpr int kBM = 128;          // pixel rows per tile (= TMEM lanes)
 constexpr int kBK = 64;           // K elements per stage (128 bytes of bf16)
 constexpr int kStages = 2;        // smem pipeline depth
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kTileA = kBM * kBK * 2;          // 16 KB
 constexpr int kMaxN = 256;
 constexpr int kTileBMax = kMaxN * kBK * 2;     // 32 KB
@@ -51,6 +54,7 @@ struct TcParams {
     int8_t* out_s;
     int64_t rows;
     int in_c, out_c, ksize, din, dout, stages, act;
+    int smem_stages, n_max;
     int* err;
 };
 
@@ -226,26 +230,30 @@ __device__ __forceinline__ int64_t tap_pixel(int64_t r, int tap, int ksize, int 
     return frame * din * din + static_cast<int64_t>(hi) * din + wi;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) conv_gemm_tc_kernel(TcParams p)
+__global__ void __launch_bounds__(kThreads, 4) conv_gemm_tc_kernel(TcParams p)
 {
     extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned tiles (swizzle atoms), then barriers.
+    // 1024-byte aligned tiles (swizzle atoms), then bias, row partial sums, barriers.
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int chunk_idx = blockIdx.y;
-    const int n0 = chunk_idx * kMaxN;
+    const int nst = p.smem_stages;
+    const int n0 = blockIdx.y * kMaxN;
     const int n_cta = min(kMaxN, p.out_c - n0);
     const int tile_b = n_cta * kBK * 2;
+    const int tile_b_max = p.n_max * kBK * 2;
     uint8_t* a_tiles = base;
-    uint8_t* b_tiles = base + kStages * kTileA;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(b_tiles + kStages * kTileBMax);
-    // bars[0..S): B full, bars[S..2S): stage free, bars[2S]: accumulator ready
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 1);
+    uint8_t* b_tiles = base + nst * kTileA;
+    float* bias_s = reinterpret_cast<float*>(b_tiles + nst * tile_b_max);
+    float* part = bias_s + kMaxN;  // [2][kBM] partial sums of squares
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 2 * kBM);
+    // bars[0..nst): B full, bars[nst..2nst): stage free, bars[2nst]: accumulator ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * nst + 1);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t tmem_cols = n_cta <= 32 ? 32u : n_cta <= 64 ? 64u : n_cta <= 128 ? 128u : 256u;
+    if (tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
     if (tid == 0) {
-        for (int i = 0; i < 2 * kStages + 1; ++i) mbar_init(smem_addr(&bars[i]), 1);
+        for (int i = 0; i < 2 * nst + 1; ++i) mbar_init(smem_addr(&bars[i]), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -256,20 +264,22 @@ __global__ void __launch_bounds__(kThreads, 1) conv_gemm_tc_kernel(TcParams p)
     const uint32_t tmem = *tmem_slot;
 
     const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
-    const int64_t row = m0 + tid;
-    const bool row_ok = row < p.rows;
+    // producer role: one (row, group-of-stage) per thread
+    const int prow = tid & (kBM - 1), pg = tid >> 7;
+    const int64_t prow_g = m0 + prow;
+    const bool prow_ok = prow_g < p.rows;
     const int G = p.in_c >> 5;
     const int GK = G * p.ksize * p.ksize;
     const uint8_t* wimg = p.wimg + (static_cast<int64_t>(n0) * p.stages * kBK * 2);
     const uint32_t idesc = instr_desc(n_cta);
 
     for (int s = 0; s < p.stages; ++s) {
-        const int buf = s % kStages;
-        const uint32_t use = static_cast<uint32_t>(s / kStages);
+        const int buf = s % nst;
+        const uint32_t use = static_cast<uint32_t>(s / nst);
         uint8_t* a_tile = a_tiles + buf * kTileA;
-        uint8_t* b_tile = b_tiles + buf * kTileBMax;
+        uint8_t* b_tile = b_tiles + buf * tile_b_max;
         if (use > 0 && !*abort_flag) {
-            if (!mbar_wait(smem_addr(&bars[kStages + buf]), (use - 1) & 1u, p.err, 1)) *abort_flag = 1;
+            if (!mbar_wait(smem_addr(&bars[nst + buf]), (use - 1) & 1u, p.err, 1)) *abort_flag = 1;
         }
         __syncthreads();
         if (*abort_flag) break;
@@ -278,17 +288,14 @@ __global__ void __launch_bounds__(kThreads, 1) conv_gemm_tc_kernel(TcParams p)
             bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(s) * tile_b, static_cast<uint32_t>(tile_b),
                      smem_addr(&bars[buf]));
         }
-#pragma unroll
-        for (int gl = 0; gl < 2; ++gl) {
-            const int gk = 2 * s + gl;
-            if (row_ok && gk < GK) {
-                const int tap = gk / G, g = gk - tap * G;
-                const int64_t pix = tap_pixel(row, tap, p.ksize, p.din, p.dout);
-                const uint4 words = reinterpret_cast<const uint4*>(p.in)[pix * G + g];
-                stage_group(a_tile, tid, gl, words, p.in_s[pix * G + g]);
-            } else {
-                stage_zero(a_tile, tid, gl);
-            }
+        const int gk = 2 * s + pg;
+        if (prow_ok && gk < GK) {
+            const int tap = gk / G, g = gk - tap * G;
+            const int64_t pix = tap_pixel(prow_g, tap, p.ksize, p.din, p.dout);
+            const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
+            stage_group(a_tile, prow, pg, words, __ldg(p.in_s + pix * G + g));
+        } else {
+            stage_zero(a_tile, prow, pg);
         }
         fence_async_smem();
         __syncthreads();
@@ -300,45 +307,61 @@ __global__ void __launch_bounds__(kThreads, 1) conv_gemm_tc_kernel(TcParams p)
                 for (int j = 0; j < kBK / 16; ++j)
                     mma_bf16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
                              (s > 0 || j > 0) ? 1u : 0u);
-                mma_commit(smem_addr(&bars[kStages + buf]));
+                mma_commit(smem_addr(&bars[nst + buf]));
             } else {
                 *abort_flag = 1;
             }
         }
     }
-    if (tid == 0) mma_commit(smem_addr(&bars[2 * kStages]));
-    __syncthreads();
-    const bool acc_ok = mbar_wait(smem_addr(&bars[2 * kStages]), 0u, p.err, 3);
+    if (tid == 0) mma_commit(smem_addr(&bars[2 * nst]));
+    const bool acc_ok = mbar_wait(smem_addr(&bars[2 * nst]), 0u, p.err, 3);
     tc_fence_after();
-    if (acc_ok && !*abort_flag) {
+
+    // Epilogue: warp w reads TMEM lanes 32*(w&3).. (its pixel rows); the two
+    // warpgroups take alternate 32-channel groups and share the row's sum of
+    // squares through shared memory.
+    const int q = warp & 3, half = warp >> 2;
+    const int erow = q * 32 + lane;
+    const int64_t row = m0 + erow;
+    const bool ok = acc_ok && !*abort_flag;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int ngroups = n_cta >> 5;
+    float ss = 0.0f;
+    if (ok) {
+        for (int g = half; g < ngroups; g += 2) {
+            float v[32];
+            tmem_ld32(taddr + 32 * g, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], ss);
+        }
+    }
+    part[half * kBM + erow] = ss;
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (ok) {
         const float inv49 = (1.0f / kQMax) * (1.0f / kQMax);
         const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
-        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-        float sumsq = 0.0f;
-        for (int c0 = 0; c0 < n_cta; c0 += 32) {
-            float v[32];
-            tmem_ld32(taddr + c0, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float a = v[i] * inv49;
-                sumsq = fmaf(a, a, sumsq);
-            }
-        }
-        const float inv_rms = __frsqrt_rn(fmaf(sumsq, inv_div, kEps));
+        const float total = (part[erow] + part[kBM + erow]) * (inv49 * inv49);
+        const float sc = inv49 * __frsqrt_rn(fmaf(total, inv_div, kEps));
         const int groups_out = p.out_c >> 5;
-        for (int c0 = 0; c0 < n_cta; c0 += 32) {
+        for (int g = half; g < ngroups; g += 2) {
             float v[32];
-            tmem_ld32(taddr + c0, v);
+            tmem_ld32(taddr + 32 * g, v);
+            const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * g);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                float x = fmaf(v[i] * inv49, inv_rms, __ldg(p.bias + n0 + c0 + i));
-                v[i] = p.act ? silu_f(x) : x;
+            for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 b = b4[i4];
+                const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float x = fmaf(v[4 * i4 + k], sc, bb[k]);
+                    v[4 * i4 + k] = p.act ? __fdividef(x, 1.0f + __expf(-x)) : x;
+                }
             }
             uint4 words;
             int8_t e;
             quantize_group(v, &words, &e);
-            if (row_ok) {
-                const int64_t gi = row * groups_out + ((n0 + c0) >> 5);
+            if (row < p.rows) {
+                const int64_t gi = row * groups_out + (n0 >> 5) + g;
                 reinterpret_cast<uint4*>(p.out)[gi] = words;
                 p.out_s[gi] = e;
             }
@@ -413,8 +436,18 @@ cudaError_t launch_conv_gemm_tc(const uint32_t* in, const int8_t* in_s, const ui
     p.rows = rows; p.in_c = in_c; p.out_c = out_c; p.ksize = ksize; p.din = din; p.dout = dout;
     p.stages = ((in_c >> 5) * ksize * ksize + 1) / 2;
     p.act = act ? 1 : 0;
+    p.smem_stages = p.stages < kStages ? p.stages : kStages;
+    p.n_max = out_c < kMaxN ? out_c : kMaxN;
     p.err = err;
-    const size_t smem = 1024 + kStages * (kTileA + kTileBMax) + (2 * kStages + 1) * 8 + 16;
+    size_t smem = 1024 + static_cast<size_t>(p.smem_stages) * (kTileA + p.n_max * kBK * 2) + (kMaxN + 2 * kBM) * 4 +
+                  (2 * p.smem_stages + 1) * 8 + 16;
+    // Never let more CTAs share an SM than its 512 TMEM columns can serve:
+    // pad the shared-memory request so the smem limit binds first.
+    const int tmem_cols = p.n_max <= 32 ? 32 : p.n_max <= 64 ? 64 : p.n_max <= 128 ? 128 : 256;
+    const int max_ctas = 512 / tmem_cols;
+    const size_t smem_per_sm = 233472;  // 228 KB
+    const size_t floor_smem = smem_per_sm / (max_ctas + 1) + 1;
+    if (smem < floor_smem) smem = floor_smem;
     cudaError_t e = cudaFuncSetAttribute(conv_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
