@@ -50,6 +50,16 @@ __device__ __forceinline__ uint32_t code_rn(float v, float inv)
     return static_cast<uint32_t>(max(-8, min(7, __float2int_rn(v * inv)))) & 0xFu;
 }
 
+// The same code as code_rn for finite v without a float->int conversion: the
+// clamped value plus 1.5 * 2^23 is rounded to nearest even by the add, and the
+// low four mantissa bits are then the two's-complement code.
+// (rn(clamp(x)) == clamp(rn(x)) because rounding is monotonic.)
+__device__ __forceinline__ uint32_t code_rn_fast(float v, float inv)
+{
+    const float y = fminf(fmaxf(v * inv, -8.0f), 7.0f);
+    return __float_as_uint(y + 12582912.0f) & 0xFu;
+}
+
 // Exact sum over 8 code pairs of qa*qb. Each nibble is moved to the top of
 // its byte (16*q as a signed byte) so one dp4a covers four pairs; the two
 // partial dot products carry a factor 256 that is shifted out exactly.
@@ -58,6 +68,13 @@ __device__ __forceinline__ int dot8(uint32_t a, uint32_t b)
     const int hi = __dp4a(static_cast<int>(a & 0xF0F0F0F0u), static_cast<int>(b & 0xF0F0F0F0u), 0);
     const int lo = __dp4a(static_cast<int>((a << 4) & 0xF0F0F0F0u), static_cast<int>((b << 4) & 0xF0F0F0F0u), hi);
     return lo >> 8;
+}
+
+// Code e (0..7) of a packed word as a float, without a conversion
+// instruction: (n ^ 8) placed in the mantissa of 2^23 gives 2^23 + q + 8.
+__device__ __forceinline__ float code_f(uint32_t w, int e)
+{
+    return __uint_as_float(((w >> (e << 2)) & 0xFu) ^ 0x4B000008u) - 8388616.0f;
 }
 
 __device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(1.0f + __expf(-x)); }
@@ -77,19 +94,9 @@ __device__ __forceinline__ uint32_t quantize_word_x4(const float (&v)[8], int8_t
     const float inv = kQMax * __frcp_rn(scale);
     uint32_t w = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) w |= code_rn(v[i], inv) << (i << 2);
+    for (int i = 0; i < 8; ++i) w |= code_rn_fast(v[i], inv) << (i << 2);
     *exp_out = exponent_of(scale);
     return w;
-}
-
-// The same code as code_rn for finite v without a float->int conversion: the
-// clamped value plus 1.5 * 2^23 is rounded to nearest even by the add, and the
-// low four mantissa bits are then the two's-complement code.
-// (rn(clamp(x)) == clamp(rn(x)) because rounding is monotonic.)
-__device__ __forceinline__ uint32_t code_rn_fast(float v, float inv)
-{
-    const float y = fminf(fmaxf(v * inv, -8.0f), 7.0f);
-    return __float_as_uint(y + 12582912.0f) & 0xFu;
 }
 
 // Quantise 32 values held by one thread into 4 words + exponent.

@@ -22,9 +22,11 @@ cudaError_t launch_stem_pack(const __half* planes, int64_t frames, int planes_pr
                              uint32_t* out, int8_t* out_s, cudaStream_t stream);
 
 // A5: depthwise k x k conv (k in {3,5,7}), stride 1/2, pad k/2, + bias, requant.
-cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
-                           const float* bias, uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize,
-                           int stride, int Din, int Dout, cudaStream_t stream);
+// wf: weights dequantised by launch_dw_weights ([k*k][C] fp32).
+cudaError_t launch_dw_weights(const uint32_t* w, const int8_t* w_s, int64_t n, float* wf, cudaStream_t stream);
+cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
+                           int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
+                           cudaStream_t stream);
 
 // A3/A4 on CUDA cores: quantized conv (pointwise when ksize == 1) with the fused
 // RMSNorm(256-chunk) + bias (+SiLU) + requant epilogue; reproduces the

@@ -241,6 +241,7 @@ struct ConvLayer {
         groups = weight_elems >> 5;
     }
     uint8_t* wimg = nullptr;  // tensor-core weight images (dense/pointwise only)
+    float* wf = nullptr;      // dequantised weights (depthwise only)
 
     size_t carve(void* base)
     {
@@ -249,6 +250,7 @@ struct ConvLayer {
         ws = c.take<int8_t>(groups);
         bias = c.take<float>(d.out_channels);
         wimg = is_dw ? nullptr : c.take<uint8_t>(conv_tc_wimg_bytes(d.in_channels, d.out_channels, d.kernel_size));
+        wf = is_dw ? c.take<float>(weight_elems) : nullptr;
         return c.bytes();
     }
     void check_bound() const
@@ -258,7 +260,9 @@ struct ConvLayer {
     // After the packed weights change: derive the tensor-core images.
     void prepare(cudaStream_t s)
     {
-        if (!is_dw)
+        if (is_dw)
+            cuda_ok(launch_dw_weights(w, ws, weight_elems, wf, s), "depthwise weights");
+        else
             cuda_ok(launch_build_wimg(w, ws, d.in_channels, d.out_channels, d.kernel_size, wimg, s), "weight images");
     }
     void load(const float* master, const float* b, cudaStream_t s)
@@ -277,7 +281,7 @@ struct ConvLayer {
         if (frames == 0) return;
         require(in && in_s && out && out_s, "null tensor");
         if (is_dw)
-            cuda_ok(launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+            cuda_ok(launch_conv_dw(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
                                    d.dim_in, d.dim_out, s),
                     "conv_dw");
         else
@@ -304,7 +308,7 @@ struct ConvLayer {
                              f_bytes(static_cast<double>(weight_elems)) + 4.0 * d.out_channels;
         if (is_dw)
             traced(prof, tag, s, 2.0 * ksq * d.in_channels * pix_out, bytes, "conv_dw", [&] {
-                return launch_conv_dw(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+                return launch_conv_dw(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
                                       d.dim_in, d.dim_out, s);
             });
         else

@@ -13,14 +13,15 @@ constexpr int kThreads = 256;
 
 // Depthwise conv: one thread per (output pixel, word of 8 channels); the four
 // threads of a 32-channel group sit in consecutive lanes and share the absmax
-// through two shuffles. Per channel and tap: fma(x, w, acc[tap & 3]); the four
-// partial sums are folded into the bias in order.
+// through two shuffles. Per channel and tap: fma(x, w, acc[tap & 3]) with
+// x = code * unit(s_in) and w the weight dequantised once at load time
+// (code * unit(s_w), the value the reference recomputes per tap); the four
+// partial sums are folded into the bias in order (kernels.h:848-858).
 template <int K>
 __global__ void __launch_bounds__(kThreads) conv_dw_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
-                                                         const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s,
-                                                         const float* __restrict__ bias, uint32_t* __restrict__ out,
-                                                         int8_t* __restrict__ out_s, int64_t total_words, int C, int stride,
-                                                         int Din, int Dout)
+                                                         const float* __restrict__ wf, const float* __restrict__ bias,
+                                                         uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
+                                                         int64_t total_words, int C, int stride, int Din, int Dout)
 {
     constexpr int kPad = K >> 1;
     const int64_t t = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
@@ -46,22 +47,32 @@ __global__ void __launch_bounds__(kThreads) conv_dw_kernel(const uint32_t* __res
         const int hi = h0 + k / K, wi = w0 + k % K;
         const bool valid = hi >= 0 && hi < Din && wi >= 0 && wi < Din;
         const int64_t sp = frame_base + static_cast<int64_t>(valid ? hi : 0) * Din + (valid ? wi : 0);
-        const uint32_t xw = valid ? in[sp * words + j] : 0u;
-        const float xu = unit_of(valid ? in_s[sp * G + g] : static_cast<int8_t>(0));
-        const uint32_t ww = w[static_cast<int64_t>(k) * words + j];
-        const float wu = unit_of(w_s[static_cast<int64_t>(k) * G + g]);
+        const uint32_t xw = valid ? __ldg(in + sp * words + j) : 0u;
+        const float xu = unit_of(valid ? __ldg(in_s + sp * G + g) : static_cast<int8_t>(0));
+        const float4* wp = reinterpret_cast<const float4*>(wf + static_cast<int64_t>(k) * C + (j << 3));
+        const float4 wa = __ldg(wp), wb = __ldg(wp + 1);
+        const float wv[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e)
-            aa[k & 3][e] = fmaf(static_cast<float>(code_of(xw, e)) * xu, static_cast<float>(code_of(ww, e)) * wu, aa[k & 3][e]);
+        for (int e = 0; e < 8; ++e) aa[k & 3][e] = fmaf(code_f(xw, e) * xu, wv[e], aa[k & 3][e]);
     }
     float v[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) v[e] = bias[(j << 3) + e] + (aa[0][e] + aa[1][e] + aa[2][e] + aa[3][e]);
+    for (int e = 0; e < 8; ++e) v[e] = __ldg(bias + (j << 3) + e) + (aa[0][e] + aa[1][e] + aa[2][e] + aa[3][e]);
     int8_t ex;
     const uint32_t q = quantize_word_x4(v, &ex);
     if (!live) return;
     out[t] = q;
     if ((j & 3) == 0) out_s[pix * G + g] = ex;
+}
+
+// Dequantised depthwise weights: wf[i] = code(i) * unit(s[i / 32]), the value
+// dequantize_scalar produces for every tap (kernels.h:77, 856-857).
+__global__ void dw_weights_kernel(const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s, int64_t n,
+                                  float* __restrict__ wf)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (i >= n) return;
+    wf[i] = static_cast<float>(code_of(w[i >> 3], static_cast<int>(i & 7))) * unit_of(w_s[i >> 5]);
 }
 
 // Implicit-GEMM quantized conv on CUDA cores. A CTA owns TP output pixels and
@@ -198,17 +209,24 @@ cudaError_t launch_gemm_tp(const uint32_t* in, const int8_t* in_s, const uint32_
 
 }  // namespace
 
-cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
-                           uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
+cudaError_t launch_dw_weights(const uint32_t* w, const int8_t* w_s, int64_t n, float* wf, cudaStream_t stream)
+{
+    if (n == 0) return cudaSuccess;
+    dw_weights_kernel<<<grid_for(n), kThreads, 0, stream>>>(w, w_s, n, wf);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
+                           int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
                            cudaStream_t stream)
 {
     const int64_t total = frames * Dout * Dout * (C >> 3);
     if (total == 0) return cudaSuccess;
     const unsigned grid = grid_for(total);
     switch (ksize) {
-        case 3: conv_dw_kernel<3><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
-        case 5: conv_dw_kernel<5><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
-        case 7: conv_dw_kernel<7><<<grid, kThreads, 0, stream>>>(in, in_s, w, w_s, bias, out, out_s, total, C, stride, Din, Dout); break;
+        case 3: conv_dw_kernel<3><<<grid, kThreads, 0, stream>>>(in, in_s, wf, bias, out, out_s, total, C, stride, Din, Dout); break;
+        case 5: conv_dw_kernel<5><<<grid, kThreads, 0, stream>>>(in, in_s, wf, bias, out, out_s, total, C, stride, Din, Dout); break;
+        case 7: conv_dw_kernel<7><<<grid, kThreads, 0, stream>>>(in, in_s, wf, bias, out, out_s, total, C, stride, Din, Dout); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -12,6 +12,9 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// NI = in/32 inputs per lane whose weights stay in registers across all steps
+// (0: any `in`, weights re-read from global memory every step).
+template <int NI>
 __global__ void __launch_bounds__(kThreads) critic_cell_kernel(const __half* __restrict__ x, const float* __restrict__ w1,
                                                              const float* __restrict__ wl, int in, int units,
                                                              float2* __restrict__ h, float2* __restrict__ h_seq, int T)
@@ -20,19 +23,37 @@ __global__ void __launch_bounds__(kThreads) critic_cell_kernel(const __half* __r
     const int j = blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
     const int b = blockIdx.y;
     if (j >= units) return;
+    float2 w1r[NI > 0 ? NI : 1], wlr[NI > 0 ? NI : 1];
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+        const int c = lane + 32 * i;
+        w1r[i] = reinterpret_cast<const float2*>(w1)[static_cast<int64_t>(c) * units + j];
+        wlr[i] = reinterpret_cast<const float2*>(wl)[static_cast<int64_t>(j) * in + c];
+    }
     float2 hv = h[static_cast<int64_t>(b) * units + j];
     for (int t = 0; t < T; ++t) {
         const int64_t row = static_cast<int64_t>(b) * T + t;
         const __half* xr = x + row * in;
         float vr = 0.0f, vi = 0.0f, lr = 0.0f, li = 0.0f;
-        for (int c = lane; c < in; c += 32) {
-            const float xf = __half2float(xr[c]);
-            const int64_t i1 = (static_cast<int64_t>(c) * units + j) << 1;
-            const int64_t il = (static_cast<int64_t>(j) * in + c) << 1;
-            vr = fmaf(xf, w1[i1], vr);
-            vi = fmaf(xf, w1[i1 + 1], vi);
-            lr = fmaf(xf, wl[il], lr);
-            li = fmaf(xf, wl[il + 1], li);
+        if (NI > 0) {
+#pragma unroll
+            for (int i = 0; i < NI; ++i) {
+                const float xf = __half2float(xr[lane + 32 * i]);
+                vr = fmaf(xf, w1r[i].x, vr);
+                vi = fmaf(xf, w1r[i].y, vi);
+                lr = fmaf(xf, wlr[i].x, lr);
+                li = fmaf(xf, wlr[i].y, li);
+            }
+        } else {
+            for (int c = lane; c < in; c += 32) {
+                const float xf = __half2float(xr[c]);
+                const int64_t i1 = (static_cast<int64_t>(c) * units + j) << 1;
+                const int64_t il = (static_cast<int64_t>(j) * in + c) << 1;
+                vr = fmaf(xf, w1[i1], vr);
+                vi = fmaf(xf, w1[i1 + 1], vi);
+                lr = fmaf(xf, wl[il], lr);
+                li = fmaf(xf, wl[il + 1], li);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -84,7 +105,13 @@ cudaError_t launch_critic(const __half* x, const float* w1, const float* wl, con
 {
     if (B == 0 || T == 0) return cudaSuccess;
     dim3 grid(static_cast<unsigned>((units + kThreads / 32 - 1) / (kThreads / 32)), static_cast<unsigned>(B));
-    critic_cell_kernel<<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T);
+    switch (in) {
+        case 32: critic_cell_kernel<1><<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T); break;
+        case 64: critic_cell_kernel<2><<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T); break;
+        case 128: critic_cell_kernel<4><<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T); break;
+        case 256: critic_cell_kernel<8><<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T); break;
+        default: critic_cell_kernel<0><<<grid, kThreads, 0, stream>>>(x, w1, wl, in, units, h, h_seq, T); break;
+    }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     critic_score_kernel<<<static_cast<unsigned>(static_cast<int64_t>(B) * T), units, 0, stream>>>(h_seq, w2, units, score);

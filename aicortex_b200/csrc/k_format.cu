@@ -86,18 +86,19 @@ __global__ void __launch_bounds__(kThreads) stem_pack_kernel(const __half* __res
     const int64_t frame = pix / hw;
     const int64_t sp = pix - frame * hw;
     const int groups = channels >> 5;
+    const __half* src = planes + frame * planes_present * hw + sp;
     for (int g = 0; g < groups; ++g) {
-        float v[32];
-#pragma unroll
-        for (int l = 0; l < 32; ++l) {
-            const int c = (g << 5) + l;
-            v[l] = c < planes_present ? __half2float(planes[(frame * planes_present + c) * hw + sp]) : 0.0f;
-        }
-        uint4 words;
-        int8_t e;
-        quantize_group(v, &words, &e);
-        reinterpret_cast<uint4*>(out)[pix * groups + g] = words;
-        out_s[pix * groups + g] = e;
+        // channels >= planes_present are zero: code 0, and they do not move the absmax
+        const int present = min(32, max(0, planes_present - (g << 5)));
+        float amax = 0.0f;
+        for (int l = 0; l < present; ++l) amax = fmaxf(amax, fabsf(__half2float(src[static_cast<int64_t>((g << 5) + l) * hw])));
+        const float scale = amax < kEps ? 1.0f : amax;
+        const float inv = kQMax * __frcp_rn(scale);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+        for (int l = 0; l < present; ++l)
+            w[l >> 3] |= code_rn_fast(__half2float(src[static_cast<int64_t>((g << 5) + l) * hw]), inv) << ((l & 7) << 2);
+        reinterpret_cast<uint4*>(out)[pix * groups + g] = make_uint4(w[0], w[1], w[2], w[3]);
+        out_s[pix * groups + g] = exponent_of(scale);
     }
 }
 
@@ -120,6 +121,34 @@ __global__ void __launch_bounds__(kThreads) residual_kernel(const uint32_t* __re
     const int64_t pbase = live ? pos : 0;
     const uint4* mv = reinterpret_cast<const uint4*>(main_in) + pbase * G;
     const uint4* rv = reinterpret_cast<const uint4*>(res) + pbase * G;
+    if (G == S) {
+        // One group per lane: keep the 32 values in registers (single pass).
+        float r[32];
+        float amax1 = 0.0f;
+        if (live) {
+            const float s_res = unit_of(res_s[pbase * G + gl]);
+            const float s_in = skipped ? 0.0f : unit_of(main_s[pbase * G + gl]) * main_mult;
+            const uint4 a = skipped ? make_uint4(0u, 0u, 0u, 0u) : mv[gl];
+            const uint4 b = rv[gl];
+            const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                r[i] = fmaf(code_f(aw[i >> 3], i & 7), s_in, code_f(bw[i >> 3], i & 7) * s_res);
+                amax1 = fmaxf(amax1, fabsf(r[i]));
+            }
+        }
+#pragma unroll
+        for (int o = S >> 1; o > 0; o >>= 1) amax1 = fmaxf(amax1, __shfl_xor_sync(0xFFFFFFFFu, amax1, o));
+        if (!live) return;
+        const float scale1 = amax1 < kEps ? 1.0f : amax1;
+        const float inv1 = kQMax * __frcp_rn(scale1);
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn_fast(r[i], inv1) << ((i & 7) << 2);
+        reinterpret_cast<uint4*>(out)[pos * G + gl] = make_uint4(w[0], w[1], w[2], w[3]);
+        out_s[pos * G + gl] = exponent_of(scale1);
+        return;
+    }
     float amax = 0.0f;
     for (int g = gl; live && g < G; g += S) {
         const float s_res = unit_of(res_s[pbase * G + g]);

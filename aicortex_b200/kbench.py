@@ -1,0 +1,100 @@
+"""Per-kernel micro-benchmark: one layer of the inference path on one GPU.
+
+    python -m aicortex_b200.kbench conv --cin 32 --cout 128 --k 1 --dim 64 --frames 2048 --act
+    python -m aicortex_b200.kbench dw --cin 32 --k 3 --stride 2 --dim 128 --frames 2048
+    python -m aicortex_b200.kbench scan --d-model 256 --d-state 512 --batch 256 --seq 128
+
+Times `--iters` launches with CUDA events after `--warmup` launches and prints
+one JSON line with the mean time per launch and the algorithmic throughput
+(the same work counts as the library's per-site tracer). Used for ncu
+captures of a single kernel on a small case.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+
+import numpy as np
+import torch
+
+from . import layers as L
+from . import workloads as W
+
+
+def _time(fn, iters: int, warmup: int) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / max(iters, 1)
+
+
+def _f_bytes(n: float) -> float:
+    return n * (0.5 + 1.0 / 32.0)
+
+
+def main(argv=None) -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kind", choices=["conv", "dw", "scan"])
+    ap.add_argument("--cin", type=int, default=32)
+    ap.add_argument("--cout", type=int, default=128)
+    ap.add_argument("--k", type=int, default=1)
+    ap.add_argument("--stride", type=int, default=1)
+    ap.add_argument("--dim", type=int, default=64, help="input H = W")
+    ap.add_argument("--frames", type=int, default=2048)
+    ap.add_argument("--act", action="store_true")
+    ap.add_argument("--exact", action="store_true", help="reference-order CUDA-core kernel")
+    ap.add_argument("--d-model", type=int, default=256)
+    ap.add_argument("--d-state", type=int, default=512)
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--seq", type=int, default=128)
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda")
+    rng = np.random.default_rng(0)
+
+    def t(x):
+        return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
+
+    if a.kind in ("conv", "dw"):
+        k = a.k
+        depthwise = a.kind == "dw"
+        cout = a.cin if depthwise else a.cout
+        stride = a.stride if depthwise else k
+        dout = (a.dim - 1) // stride + 1 if depthwise else a.dim // k
+        layer = L.ConvLayer(a.cin, cout, k, stride, a.dim, dout, disable_activation=not a.act)
+        layer.load_weights(t(W.conv_weights(rng, a.cin, cout, k, depthwise)), t(W.bias(rng, cout)))
+        x = torch.randn(a.frames * a.dim * a.dim * a.cin, device=dev)
+        xw, xs = L.pack_f32(x)
+        del x
+        ow, os_ = L.empty_f(a.frames * dout * dout, cout, dev)
+        fwd = layer.forward_exact if a.exact else layer.forward
+        ms = _time(lambda: fwd(xw, xs, ow, os_, a.frames), a.iters, a.warmup)
+        rows = a.frames * dout * dout
+        flops = 2.0 * rows * cout * k * k * a.cin if not depthwise else 2.0 * rows * cout * k * k
+        nbytes = _f_bytes(a.frames * a.dim * a.dim * a.cin) + _f_bytes(rows * cout) + _f_bytes(layer.weight_elems)
+    else:
+        E = 2 * a.d_model
+        layer = L.MambaLayer(a.d_model, a.d_state, a.d_model, 1)
+        blob = W.mamba_blob(rng, a.d_model, a.d_state, a.d_model, wd_scale=W.WD_SCALE)
+        layer.load_weights(t(blob), t(W.bias(rng, a.d_model)))
+        layer.bind_state(a.batch)
+        rows = a.batch * a.seq
+        xw, xs = L.pack_f32(torch.randn(rows * a.d_model, device=dev))
+        out = torch.empty(rows, a.d_model, dtype=torch.float32, device=dev)
+        ms = _time(lambda: layer.forward(xw, xs, out, a.batch, a.seq), a.iters, a.warmup)
+        P = a.d_state // 32
+        flops = rows * E * (31.0 * P + 15.0) + 2.0 * rows * E * a.d_model
+        nbytes = _f_bytes(rows * a.d_model) + 8.0 * rows * E + 4.0 * rows * a.d_model
+    print(json.dumps({"kind": a.kind, "ms_per_launch": ms, "tflops": flops / ms / 1e9, "gbs": nbytes / ms / 1e6,
+                      "flops": flops, "bytes": nbytes, "args": vars(a)}))
+
+
+if __name__ == "__main__":
+    main()
