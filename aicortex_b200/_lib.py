@@ -140,6 +140,7 @@ _SIGS = {
     "aic_cortex_forward": [P, P, I32, I32, P, P, P, P, P, P],
     "aic_cortex_host_workspace_bytes": [P, I32, I32, SZ],
     "aic_cortex_forward_host": [P, P, I32, I32, P, P, P, P],
+    "aic_cortex_set_exact": [P, I32],
     "aic_cortex_last_launches": [P, PI64],
     "aic_cortex_profile_enable": [P, I32],
     "aic_cortex_profile_count": [P, C.POINTER(C.c_int)],

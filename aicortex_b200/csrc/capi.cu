@@ -242,6 +242,7 @@ struct ConvLayer {
     }
     uint8_t* wimg = nullptr;  // tensor-core weight images (dense/pointwise only)
     float* wf = nullptr;      // dequantised weights (depthwise only)
+    bool exact = false;       // reference accumulation order on CUDA cores
 
     size_t carve(void* base)
     {
@@ -310,6 +311,11 @@ struct ConvLayer {
             traced(prof, tag, s, 2.0 * ksq * d.in_channels * pix_out, bytes, "conv_dw", [&] {
                 return launch_conv_dw(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
                                       d.dim_in, d.dim_out, s);
+            });
+        else if (exact)
+            traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm_simt", [&] {
+                return launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                             d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s);
             });
         else
             traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm", [&] {
@@ -1540,6 +1546,14 @@ AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_
         require(batch >= 0 && seq >= 0, "bad extents");
         handle<Cortex>(c, "cortex")->forward_host(planes_host, batch, seq, actor_host, critic_host, workspace,
                                                   as_stream(stream));
+    });
+}
+AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact)
+{
+    return guarded([&] {
+        auto* x = handle<Cortex>(c, "cortex");
+        for (auto& b : x->blocks)
+            for (auto& l : b->layers) l->exact = exact != 0;
     });
 }
 AIC_API aic_status aic_cortex_profile_enable(aic_cortex c, int enable)

@@ -10,24 +10,24 @@
 // and the epilogue multiplies by fl(1/7)^2. The result equals the reference's
 // sum over groups of unit(s_in) * unit(s_w) * dot up to fp32 summation order.
 //
-// Structure: a persistent, warp-specialised kernel, one CTA per SM walking
-// tiles of 128 pixel rows x one 256-channel chunk:
-//   - producer warps convert, per 64-wide K stage, the A rows from the packed
-//     activations (im2col on the fly for the dense convs) into a 128B-swizzled
-//     K-major bf16 tile of a multi-stage shared-memory ring; the B stage
-//     (weights) is a pre-swizzled bf16 image built at weight-load time and
-//     fetched with one cp.async.bulk into the same layout;
-//   - one thread issues four tcgen05.mma (M128 x N x K16) per stage into one
-//     of two TMEM accumulators and commits stages and tiles to mbarriers;
-//   - epilogue warps read a finished accumulator with tcgen05.ld (warp w owns
-//     TMEM lanes 32*(w&3)..: its 32 pixel rows; two warpgroups take alternate
-//     32-channel groups and exchange the rows' sums of squares once through
-//     shared memory); each thread normalises, activates and packs whole
-//     32-channel groups of its own row, so the requant needs no cross-thread
-//     reduction. The epilogue of one tile overlaps the main loop of the next.
+// Structure of one CTA (256 threads, one 128-pixel x up-to-256-channel tile):
+//   - for each 64-wide K stage, thread t converts group (t >> 7) of pixel row
+//     (t & 127) of the A tile from the packed activations (im2col on the fly
+//     for the dense convs) into a 128B-swizzled K-major bf16 tile;
+//   - the B tile (weights) is a pre-swizzled bf16 image built at weight-load
+//     time, fetched per stage with one cp.async.bulk into the same layout;
+//   - thread 0 issues four tcgen05.mma (M128 x N x K16) per stage and commits
+//     to the stage's mbarrier; stages are double-buffered;
+//   - after the last stage warp w reads TMEM lanes 32*(w&3).. (its 32 pixel
+//     rows) with tcgen05.ld; the two warpgroups take alternate 32-channel
+//     groups, exchange the rows' sums of squares once through shared memory,
+//     and each thread normalises, activates and packs whole 32-channel groups
+//     of its own row, so the requant needs no cross-thread reduction.
+// Shared memory is sized per launch (1-2 stages, B tile of the layer's width)
+// so 2-4 CTAs share an SM, never more than its 512 TMEM columns can hold.
 // All mbarrier waits are bounded; on timeout the kernel records an error code
-// in *err, every role skips its remaining work, and the TMEM columns are
-// released only after the CTA's last tcgen05.commit has completed.
+// in *err, skips the remaining work, waits (bounded) for its own outstanding
+// operations and releases its TMEM before returning.
 #include <cuda_bf16.h>
 
 #include "aic_common.cuh"
@@ -39,12 +39,7 @@ namespace {
 constexpr int kBM = 128;          // pixel rows per tile (= TMEM lanes)
 constexpr int kBK = 64;           // K elements per stage (128 bytes of bf16)
 constexpr int kStages = 2;        // smem pipeline depth
-constexpr int kProducerWarps = 4;
-constexpr int kProducerThreads = kProducerWarps * 32;
-constexpr int kMmaWarp = 4;
-constexpr int kEpiWarp0 = 5;
-constexpr int kEpiWarps = 8;
-constexpr int kPThreads = (kEpiWarp0 + kEpiWarps) * 32;  // 416
+constexpr int kThreads = 256;
 constexpr int kTileA = kBM * kBK * 2;          // 16 KB
 constexpr int kMaxN = 256;
 constexpr int kTileBMax = kMaxN * kBK * 2;     // 32 KB
@@ -59,7 +54,7 @@ struct TcParams {
     int8_t* out_s;
     int64_t rows;
     int in_c, out_c, ksize, din, dout, stages, act;
-    int smem_stages, n_max, m_tiles, n_chunks;
+    int smem_stages, n_max;
     int* err;
 };
 
@@ -235,218 +230,146 @@ __device__ __forceinline__ int64_t tap_pixel(int64_t r, int tap, int ksize, int 
     return frame * din * din + static_cast<int64_t>(hi) * din + wi;
 }
 
-__device__ __forceinline__ void mbar_expect_tx_noarrive(uint32_t bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar)
-{
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-// Bounded wait that also gives up at once when another role has aborted.
-__device__ __forceinline__ bool role_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err, int code)
-{
-    if (*abort_flag) return false;
-    for (uint32_t i = 0; i < kWaitLimit; ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if (i > 256) {
-            if (*abort_flag) return false;
-            __nanosleep(128);
-        }
-    }
-    atomicCAS(err, 0, code);
-    *abort_flag = 1;
-    return false;
-}
-
-// Persistent, warp-specialised kernel. One CTA per SM walks tiles
-// t = blockIdx.x, blockIdx.x + gridDim.x, ... (tile = 128 pixel rows x one
-// 256-channel chunk). Roles:
-//   warps 0-3   producers: fill the A ring (one pixel row per thread, both
-//               groups of each 64-wide K stage); thread 0 also fetches the B
-//               stage with cp.async.bulk; all 128 arrive on full[slot];
-//   warp  4     allocates TMEM (two accumulators) and, on lane 0, issues the
-//               tcgen05.mma of every stage, committing each stage to
-//               empty[slot] and each finished tile to acc_full[buf];
-//   warps 5-12  epilogue: wait acc_full[buf], read the accumulator, normalise,
-//               activate, requant and store; release acc_empty[buf].
-// The epilogue of tile i overlaps the main loop of tile i+1.
-__global__ void __launch_bounds__(kPThreads, 1) conv_gemm_tc_kernel(TcParams p)
+__global__ void __launch_bounds__(kThreads, 4) conv_gemm_tc_kernel(TcParams p)
 {
     extern __shared__ uint8_t smem_raw[];
+    // 1024-byte aligned tiles (swizzle atoms), then bias, row partial sums, barriers.
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int nst = p.smem_stages;
+    const int n0 = blockIdx.y * kMaxN;
+    const int n_cta = min(kMaxN, p.out_c - n0);
+    const int tile_b = n_cta * kBK * 2;
     const int tile_b_max = p.n_max * kBK * 2;
     uint8_t* a_tiles = base;
     uint8_t* b_tiles = base + nst * kTileA;
-    float* part = reinterpret_cast<float*>(b_tiles + nst * tile_b_max);  // [2 bufs][2 halves][kBM]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 4 * kBM);
-    uint64_t* full = bars;
-    uint64_t* empty = bars + nst;
-    uint64_t* acc_full = bars + 2 * nst;
-    uint64_t* acc_empty = acc_full + 2;
-    uint64_t* final_bar = acc_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_bar + 1);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    float* bias_s = reinterpret_cast<float*>(b_tiles + nst * tile_b_max);
+    float* part = bias_s + kMaxN;  // [2][kBM] partial sums of squares
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 2 * kBM);
+    // bars[0..nst): B full, bars[nst..2nst): stage free, bars[2nst]: accumulator ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * nst + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t acc_cols = p.n_max <= 32 ? 32u : p.n_max <= 64 ? 64u : p.n_max <= 128 ? 128u : 256u;
+    const uint32_t tmem_cols = n_cta <= 32 ? 32u : n_cta <= 64 ? 64u : n_cta <= 128 ? 128u : 256u;
+    if (tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
     if (tid == 0) {
-        for (int i = 0; i < nst; ++i) {
-            mbar_init(smem_addr(&full[i]), kProducerThreads);
-            mbar_init(smem_addr(&empty[i]), 1);
-        }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(smem_addr(&acc_full[i]), 1);
-            mbar_init(smem_addr(&acc_empty[i]), kEpiWarps);
-        }
-        mbar_init(smem_addr(final_bar), 1);
+        for (int i = 0; i < 2 * nst + 1; ++i) mbar_init(smem_addr(&bars[i]), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == kMmaWarp) tmem_alloc(smem_addr(tmem_slot), 2 * acc_cols);
+    if (warp == 0) tmem_alloc(smem_addr(tmem_slot), tmem_cols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int num_tiles = p.m_tiles * p.n_chunks;
+
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+    // producer role: one (row, group-of-stage) per thread
+    const int prow = tid & (kBM - 1), pg = tid >> 7;
+    const int64_t prow_g = m0 + prow;
+    const bool prow_ok = prow_g < p.rows;
     const int G = p.in_c >> 5;
     const int GK = G * p.ksize * p.ksize;
+    const uint8_t* wimg = p.wimg + (static_cast<int64_t>(n0) * p.stages * kBK * 2);
+    const uint32_t idesc = instr_desc(n_cta);
 
-    if (warp < kProducerWarps) {
-        uint32_t gs = 0;
-        for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-            const int m_tile = tile / p.n_chunks, chunk = tile - m_tile * p.n_chunks;
-            const int n0 = chunk * kMaxN;
-            const int tile_b = min(kMaxN, p.out_c - n0) * kBK * 2;
-            const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * p.stages * kBK * 2;
-            const int64_t row = static_cast<int64_t>(m_tile) * kBM + tid;
-            const bool row_ok = row < p.rows;
-            for (int s = 0; s < p.stages; ++s, ++gs) {
-                const int slot = static_cast<int>(gs % nst);
-                const uint32_t r = gs / nst;
-                if (!role_wait(smem_addr(&empty[slot]), (r & 1u) ^ 1u, abort_flag, p.err, 1)) break;
-                uint8_t* a_tile = a_tiles + slot * kTileA;
-                if (tid == 0) {
-                    mbar_expect_tx_noarrive(smem_addr(&full[slot]), static_cast<uint32_t>(tile_b));
-                    bulk_g2s(smem_addr(b_tiles + slot * tile_b_max), wimg + static_cast<int64_t>(s) * tile_b,
-                             static_cast<uint32_t>(tile_b), smem_addr(&full[slot]));
-                }
-#pragma unroll
-                for (int gl = 0; gl < 2; ++gl) {
-                    const int gk = 2 * s + gl;
-                    if (row_ok && gk < GK) {
-                        const int tap = gk / G, g = gk - tap * G;
-                        const int64_t pix = tap_pixel(row, tap, p.ksize, p.din, p.dout);
-                        const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
-                        stage_group(a_tile, tid, gl, words, __ldg(p.in_s + pix * G + g));
-                    } else {
-                        stage_zero(a_tile, tid, gl);
-                    }
-                }
-                fence_async_smem();
-                mbar_arrive(smem_addr(&full[slot]));
-            }
+    for (int s = 0; s < p.stages; ++s) {
+        const int buf = s % nst;
+        const uint32_t use = static_cast<uint32_t>(s / nst);
+        uint8_t* a_tile = a_tiles + buf * kTileA;
+        uint8_t* b_tile = b_tiles + buf * tile_b_max;
+        if (use > 0 && !*abort_flag) {
+            if (!mbar_wait(smem_addr(&bars[nst + buf]), (use - 1) & 1u, p.err, 1)) *abort_flag = 1;
         }
-    } else if (warp == kMmaWarp) {
-        if (lane == 0) {
-            uint32_t gs = 0, i = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++i) {
-                const int chunk = tile % p.n_chunks;
-                const int n_cta = min(kMaxN, p.out_c - chunk * kMaxN);
-                const uint32_t idesc = instr_desc(n_cta);
-                const uint32_t b = i & 1u;
-                if (!role_wait(smem_addr(&acc_empty[b]), ((i >> 1) & 1u) ^ 1u, abort_flag, p.err, 4)) break;
+        __syncthreads();
+        if (*abort_flag) break;
+        if (tid == 0) {
+            mbar_expect_tx(smem_addr(&bars[buf]), static_cast<uint32_t>(tile_b));
+            bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(s) * tile_b, static_cast<uint32_t>(tile_b),
+                     smem_addr(&bars[buf]));
+        }
+        const int gk = 2 * s + pg;
+        if (prow_ok && gk < GK) {
+            const int tap = gk / G, g = gk - tap * G;
+            const int64_t pix = tap_pixel(prow_g, tap, p.ksize, p.din, p.dout);
+            const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
+            stage_group(a_tile, prow, pg, words, __ldg(p.in_s + pix * G + g));
+        } else {
+            stage_zero(a_tile, prow, pg);
+        }
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            if (mbar_wait(smem_addr(&bars[buf]), use & 1u, p.err, 2)) {
                 tc_fence_after();
-                const uint32_t tacc = tmem + b * acc_cols;
-                for (int s = 0; s < p.stages; ++s, ++gs) {
-                    const int slot = static_cast<int>(gs % nst);
-                    if (!role_wait(smem_addr(&full[slot]), (gs / nst) & 1u, abort_flag, p.err, 2)) break;
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_addr(a_tiles + slot * kTileA);
-                    const uint32_t b_addr = smem_addr(b_tiles + slot * tile_b_max);
+                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_tile);
 #pragma unroll
-                    for (int j = 0; j < kBK / 16; ++j)
-                        mma_bf16(tacc, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
-                                 (s > 0 || j > 0) ? 1u : 0u);
-                    mma_commit(smem_addr(&empty[slot]));
-                }
-                mma_commit(smem_addr(&acc_full[b]));
+                for (int j = 0; j < kBK / 16; ++j)
+                    mma_bf16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
+                             (s > 0 || j > 0) ? 1u : 0u);
+                mma_commit(smem_addr(&bars[nst + buf]));
+            } else {
+                *abort_flag = 1;
             }
-            mma_commit(smem_addr(final_bar));
         }
-        __syncwarp();
-    } else {
-        const int q = warp & 3, half = (warp - kEpiWarp0) >> 2;
-        const int erow = q * 32 + lane;
+    }
+    if (tid == 0) mma_commit(smem_addr(&bars[2 * nst]));
+    const bool acc_ok = mbar_wait(smem_addr(&bars[2 * nst]), 0u, p.err, 3);
+    tc_fence_after();
+
+    // Epilogue: warp w reads TMEM lanes 32*(w&3).. (its pixel rows); the two
+    // warpgroups take alternate 32-channel groups and share the row's sum of
+    // squares through shared memory.
+    const int q = warp & 3, half = warp >> 2;
+    const int erow = q * 32 + lane;
+    const int64_t row = m0 + erow;
+    const bool ok = acc_ok && !*abort_flag;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int ngroups = n_cta >> 5;
+    float ss = 0.0f;
+    if (ok) {
+        for (int g = half; g < ngroups; g += 2) {
+            float v[32];
+            tmem_ld32(taddr + 32 * g, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss = fmaf(v[i], v[i], ss);
+        }
+    }
+    part[half * kBM + erow] = ss;
+    asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+    if (ok) {
         const float inv49 = (1.0f / kQMax) * (1.0f / kQMax);
         const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+        const float total = (part[erow] + part[kBM + erow]) * (inv49 * inv49);
+        const float sc = inv49 * __frsqrt_rn(fmaf(total, inv_div, kEps));
         const int groups_out = p.out_c >> 5;
-        uint32_t i = 0;
-        // Every epilogue warp runs the same number of iterations and always
-        // reaches the named barrier, even after an abort (it then skips work).
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++i) {
-            const int m_tile = tile / p.n_chunks, chunk = tile - m_tile * p.n_chunks;
-            const int n0 = chunk * kMaxN;
-            const int ngroups = min(kMaxN, p.out_c - n0) >> 5;
-            const uint32_t b = i & 1u;
-            const bool ok = role_wait(smem_addr(&acc_full[b]), (i >> 1) & 1u, abort_flag, p.err, 3);
-            tc_fence_after();
-            const uint32_t taddr = tmem + b * acc_cols + (static_cast<uint32_t>(q * 32) << 16);
-            float ss = 0.0f;
-            if (ok) {
-                for (int g = half; g < ngroups; g += 2) {
-                    float v[32];
-                    tmem_ld32(taddr + 32 * g, v);
+        for (int g = half; g < ngroups; g += 2) {
+            float v[32];
+            tmem_ld32(taddr + 32 * g, v);
+            const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * g);
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) ss = fmaf(v[k], v[k], ss);
+            for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 b = b4[i4];
+                const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float x = fmaf(v[4 * i4 + k], sc, bb[k]);
+                    v[4 * i4 + k] = p.act ? __fdividef(x, 1.0f + __expf(-x)) : x;
                 }
             }
-            float* pb = part + b * 2 * kBM;
-            pb[half * kBM + erow] = ss;
-            asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
-            if (ok) {
-                const float total = (pb[erow] + pb[kBM + erow]) * (inv49 * inv49);
-                const float sc = inv49 * __frsqrt_rn(fmaf(total, inv_div, kEps));
-                const int64_t row = static_cast<int64_t>(m_tile) * kBM + erow;
-                for (int g = half; g < ngroups; g += 2) {
-                    float v[32];
-                    tmem_ld32(taddr + 32 * g, v);
-                    const float4* b4 = reinterpret_cast<const float4*>(p.bias + n0 + 32 * g);
-#pragma unroll
-                    for (int i4 = 0; i4 < 8; ++i4) {
-                        const float4 bb = __ldg(b4 + i4);
-                        const float bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) {
-                            const float x = fmaf(v[4 * i4 + k], sc, bv[k]);
-                            v[4 * i4 + k] = p.act ? __fdividef(x, 1.0f + __expf(-x)) : x;
-                        }
-                    }
-                    uint4 words;
-                    int8_t e;
-                    quantize_group(v, &words, &e);
-                    if (row < p.rows) {
-                        const int64_t gi = row * groups_out + (n0 >> 5) + g;
-                        reinterpret_cast<uint4*>(p.out)[gi] = words;
-                        p.out_s[gi] = e;
-                    }
-                }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_addr(&acc_empty[b]));
+            uint4 words;
+            int8_t e;
+            quantize_group(v, &words, &e);
+            if (row < p.rows) {
+                const int64_t gi = row * groups_out + (n0 >> 5) + g;
+                reinterpret_cast<uint4*>(p.out)[gi] = words;
+                p.out_s[gi] = e;
             }
         }
     }
+    tc_fence_before();
     __syncthreads();
-    if (warp == kMmaWarp) {
-        // every MMA this CTA issued has completed before the columns are freed
-        role_wait(smem_addr(final_bar), 0u, abort_flag, p.err, 5);
-        tc_fence_after();
-        tmem_dealloc(tmem, 2 * acc_cols);
-    }
+    if (warp == 0) tmem_dealloc(tmem, tmem_cols);
 }
 
 // Builds the per-(chunk, stage) swizzled bf16 images of the weights from the
@@ -508,30 +431,28 @@ cudaError_t launch_conv_gemm_tc(const uint32_t* in, const int8_t* in_s, const ui
 {
     const int64_t rows = frames * dout * dout;
     if (rows == 0) return cudaSuccess;
-    int dev = 0, sms = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
     TcParams p;
     p.in = in; p.in_s = in_s; p.wimg = wimg; p.bias = bias; p.out = out; p.out_s = out_s;
     p.rows = rows; p.in_c = in_c; p.out_c = out_c; p.ksize = ksize; p.din = din; p.dout = dout;
     p.stages = ((in_c >> 5) * ksize * ksize + 1) / 2;
     p.act = act ? 1 : 0;
+    p.smem_stages = p.stages < kStages ? p.stages : kStages;
     p.n_max = out_c < kMaxN ? out_c : kMaxN;
-    p.m_tiles = static_cast<int>((rows + kBM - 1) / kBM);
-    p.n_chunks = (out_c + kMaxN - 1) / kMaxN;
     p.err = err;
-    const int stage_bytes = kTileA + p.n_max * kBK * 2;
-    int nst = (200 * 1024) / stage_bytes;
-    nst = nst < 2 ? 2 : (nst > 8 ? 8 : nst);
-    p.smem_stages = nst;
-    const size_t smem = 1024 + static_cast<size_t>(nst) * stage_bytes + 4 * kBM * 4 + (2 * nst + 5) * 8 + 16;
-    e = cudaFuncSetAttribute(conv_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    size_t smem = 1024 + static_cast<size_t>(p.smem_stages) * (kTileA + p.n_max * kBK * 2) + (kMaxN + 2 * kBM) * 4 +
+                  (2 * p.smem_stages + 1) * 8 + 16;
+    // Never let more CTAs share an SM than its 512 TMEM columns can serve:
+    // pad the shared-memory request so the smem limit binds first.
+    const int tmem_cols = p.n_max <= 32 ? 32 : p.n_max <= 64 ? 64 : p.n_max <= 128 ? 128 : 256;
+    const int max_ctas = 512 / tmem_cols;
+    const size_t smem_per_sm = 233472;  // 228 KB
+    const size_t floor_smem = smem_per_sm / (max_ctas + 1) + 1;
+    if (smem < floor_smem) smem = floor_smem;
+    cudaError_t e = cudaFuncSetAttribute(conv_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_chunks;
-    const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
-    conv_gemm_tc_kernel<<<grid, kPThreads, smem, stream>>>(p);
+    dim3 grid(static_cast<unsigned>((rows + kBM - 1) / kBM), static_cast<unsigned>((out_c + kMaxN - 1) / kMaxN));
+    conv_gemm_tc_kernel<<<grid, kThreads, smem, stream>>>(p);
     return cudaGetLastError();
 }
 

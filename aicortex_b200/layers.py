@@ -415,6 +415,10 @@ class Cortex(_Handle):
     def reset(self, stream=None) -> None:
         call("aic_cortex_reset_state", self.h, _stream(stream))
 
+    def set_exact(self, exact: bool) -> None:
+        """Reference accumulation order for every quantized conv (bit-identical to the reference)."""
+        call("aic_cortex_set_exact", self.h, int(exact))
+
     def workspace_bytes(self, batch: int, seq: int) -> int:
         nb = _size_out()
         call("aic_cortex_workspace_bytes", self.h, int(batch), int(seq), C.byref(nb))

@@ -309,6 +309,10 @@ AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int 
 AIC_API aic_status aic_cortex_host_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes);
 AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_host, int batch, int seq,
                                            float* actor_host, float* critic_host, void* workspace, void* stream);
+/* exact != 0: run every quantized conv in the reference kernels' accumulation
+ * order on CUDA cores (bit-identical to the reference, slower); 0 (default):
+ * tensor cores, whose fp32 sums differ in summation order only. */
+AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact);
 /* Number of kernel launches the last forward issued. */
 AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches);
 /* Per-launch-site CUDA-event timing (tracing). When enabled, every kernel
