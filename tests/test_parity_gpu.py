@@ -292,9 +292,9 @@ def test_cortex_small_vs_oracle():
     assert_close(critic, c_ref, rtol=1e-3, what="critic (reference order)")
     fw2, fs2, actor2, critic2 = outs[False]
     fv, rv = fmt.dequant(fw2, fs2), fmt.dequant(fw, fs)
-    assert np.abs(fv - rv).mean() / np.abs(rv).mean() < 5e-2, "features (tensor cores)"
-    assert_close(actor2, actor, rtol=1e-1, what="actor (tensor cores)")
-    assert_close(critic2, critic, rtol=1e-1, what="critic (tensor cores)")
+    for name, a, r in (("features", fv, rv), ("actor", actor2, actor), ("critic", critic2, critic)):
+        rel = np.abs(a - r).mean() / np.abs(r).mean()
+        assert rel < 5e-2, f"{name} (tensor cores): mean error {rel:.3e} relative to the mean magnitude"
 
 @pytest.mark.parametrize("geo", [
     (64, 128, 1, 1, 24, 24, 1),     # 576 rows: 4 full tiles + a partial one
