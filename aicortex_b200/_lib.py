@@ -102,6 +102,7 @@ _SIGS = {
     "aic_mamba_layer_workspace_bytes": [P, I64, SZ],
     "aic_mamba_layer_forward": [P, P, P, P, I32, I32, P, P],
     "aic_mamba_layer_outproj": [P, P, P, I64, P],
+    "aic_mamba_layer_forward_noalloc": [P, P, P, P, I32, I32, P],
     "aic_mamba_layer_destroy": [P],
     "aic_mamba_block_create": [C.POINTER(MambaBlockDesc), PP],
     "aic_mamba_block_layer": [P, I32, PP],

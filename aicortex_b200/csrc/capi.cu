@@ -11,6 +11,7 @@
 #include <cstring>
 #include <exception>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -944,6 +945,35 @@ T* handle(void* p, const char* what)
     return static_cast<T*>(p);
 }
 
+// ---- fixed scratch for aic_mamba_layer_forward_noalloc ------------------
+// Scratch for callers that cannot allocate device memory themselves: the
+// Mamba layer's per-row SSM output y_ssm lives in this array instead of a
+// caller-provided workspace. One instance per device, resident from the time
+// the library is loaded on that device until the process exits.
+constexpr size_t kNoAllocScratchFloats = size_t(1) << 20;  // 4 MiB: rows * 2 * d_model <= 1,048,576
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+constexpr int kMaxDevices = 64;
+float* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+// Device address of g_noalloc_scratch on the current device. In host code the
+// symbol is only a host-side stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+float* noalloc_scratch()
+{
+    int dev = 0;
+    cuda_ok(cudaGetDevice(&dev), "cudaGetDevice");
+    require(dev >= 0 && dev < kMaxDevices, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        cuda_ok(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(g_noalloc_scratch)");
+        g_noalloc_addr[dev] = static_cast<float*>(p);
+    }
+    return g_noalloc_addr[dev];
+}
+
 }  // namespace
 }  // namespace aic
 
@@ -1259,6 +1289,21 @@ AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, fl
         cuda_ok(launch_outproj(y, m->w, m->ws, m->bias, m->d.d_model, m->d.d_state, m->d.out_channels, m->d.activation,
                                rows, out, as_stream(stream)),
                 "outproj");
+    });
+}
+AIC_API aic_status aic_mamba_layer_forward_noalloc(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s,
+                                                   float* out, int batch, int seq, void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(batch >= 0 && seq >= 0, "bad extents");
+        const size_t need = static_cast<size_t>(batch) * seq * m->E;
+        if (need > kNoAllocScratchFloats)
+            fail(AIC_ERR_INVALID, "aic_mamba_layer_forward_noalloc: batch * seq * 2 * d_model = " + std::to_string(need) +
+                                      " floats exceeds the fixed scratch of " + std::to_string(kNoAllocScratchFloats) +
+                                      " floats (4 MiB); use aic_mamba_layer_forward with a workspace");
+        if (need == 0) return;
+        m->forward(in, in_s, out, batch, seq, noalloc_scratch(), as_stream(stream));
     });
 }
 AIC_API aic_status aic_mamba_layer_destroy(aic_mamba_layer l)

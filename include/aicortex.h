@@ -202,6 +202,22 @@ AIC_API aic_status aic_mamba_layer_workspace_bytes(aic_mamba_layer l, int64_t ro
  * `batch` sequences: in F [batch*seq][d_model], out fp32 [batch*seq][out]. */
 AIC_API aic_status aic_mamba_layer_forward(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s, float* out,
                                            int batch, int seq, void* workspace, void* stream);
+/* aic_mamba_layer_forward without a workspace: no counterpart in the
+ * reference. For callers that cannot allocate device memory themselves, for
+ * example a real-time control loop that must not call cudaMalloc (it can
+ * synchronise the whole device and stall the frame) or a plugin whose host
+ * application owns all device memory through its own allocator. The layer's
+ * y_ssm scratch is a 4 MiB array compiled into the library, one per device,
+ * held from load until process exit; batch * seq * 2 * d_model must not
+ * exceed 1,048,576 floats (AIC_ERR_INVALID otherwise). The first call on a
+ * device looks up that array's device address (cudaGetSymbolAddress); make
+ * that first call before capturing a stream. All calls share the one array:
+ * calls that can overlap on the GPU (different streams, no ordering) race.
+ * The scratch is fully overwritten before it is read, so nothing needs
+ * clearing between calls. Parameters and state are bound as usual; the
+ * caller passes inputs and outputs. */
+AIC_API aic_status aic_mamba_layer_forward_noalloc(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s,
+                                                   float* out, int batch, int seq, void* stream);
 /* The out-projection alone (mambaSSMFwdOutProjKernel, kernels.h:1188-1259):
  * y_ssm fp32 [rows][2*d_model] -> out fp32 [rows][out]. */
 AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, float* out, int64_t rows, void* stream);
