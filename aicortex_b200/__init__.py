@@ -6,8 +6,8 @@ reference's layer classes. Importing the package fails if the library is not
 built: there is no fallback path.
 """
 from ._lib import AicError, lib  # noqa: F401  (fails loudly when the .so is missing)
-from .layers import (ConvBlock, ConvLayer, Cortex, Critic, MambaBlock, MambaLayer, empty_f, gap, gap_f16,  # noqa: F401
-                     pack_f32, residual_add, set_actions, stem_pack)
+from .layers import (ConvBlock, ConvLayer, Cortex, Critic, MambaBlock, MambaLayer, audio_frontend, empty_f,  # noqa: F401
+                     gap, gap_f16, pack_f32, residual_add, set_actions, stem_pack)
 
-__all__ = ["AicError", "ConvBlock", "ConvLayer", "Cortex", "Critic", "MambaBlock", "MambaLayer", "empty_f", "gap",
+__all__ = ["AicError", "ConvBlock", "ConvLayer", "Cortex", "Critic", "MambaBlock", "MambaLayer", "audio_frontend", "empty_f", "gap",
            "gap_f16", "pack_f32", "residual_add", "set_actions", "stem_pack"]

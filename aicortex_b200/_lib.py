@@ -73,6 +73,8 @@ _SIGS = {
     "aic_gap": [P, P, I64, I32, I32, P, P, P, P],
     "aic_gap_f16": [P, P, I64, I32, I32, P, P],
     "aic_set_actions": [P, I64, I32, P, P],
+    "aic_audio_workspace_bytes": [SZ],
+    "aic_audio_frontend": [P, P, I32, I32, P, P],
     "aic_conv_layer_create": [C.POINTER(ConvLayerDesc), PP],
     "aic_conv_layer_sizes": [P, PI64, PI64, SZ],
     "aic_conv_layer_bind": [P, P],

@@ -77,6 +77,13 @@ cudaError_t launch_outproj(const float* y, const uint32_t* blob, const int8_t* b
 cudaError_t launch_critic(const __half* x, const float* w1, const float* wl, const float* w2, int in, int units,
                           float2* h, float2* h_seq, float* score, int B, int T, cudaStream_t stream);
 
+// A14: audio front-end (ca.cu): 2048 int16 PCM samples -> two fp16 planes
+// (|X|/N^2, phase of the 1024x1024 fp16 FFT) resized to dim x dim, written to
+// channels first_channel and first_channel+1 of an fp16 [C][dim][dim] frame.
+size_t audio_workspace_bytes();
+cudaError_t launch_audio_frontend(const short* pcm, __half* frame, int dim, int first_channel, void* workspace,
+                                  cudaStream_t stream);
+
 // A12: Bernoulli action bits, [rows][A] probabilities -> [rows][(A+63)/64] words.
 cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned long long* actions,
                                cudaStream_t stream);

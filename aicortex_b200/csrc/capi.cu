@@ -1056,6 +1056,27 @@ AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t f
     });
 }
 
+AIC_API aic_status aic_audio_workspace_bytes(size_t* bytes)
+{
+    return guarded([&] {
+        require(bytes != nullptr, "null output");
+        *bytes = audio_workspace_bytes();
+    });
+}
+
+AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int dim, int first_channel, void* workspace,
+                                      void* stream)
+{
+    return guarded([&] {
+        require(pcm && frame && workspace && aligned256(workspace), "null or misaligned buffer");
+        require(dim >= 2 && dim <= 1024 && dim % 2 == 0, "dim must be even and at most 1024");
+        require(first_channel >= 0, "bad channel");
+        cuda_ok(launch_audio_frontend(reinterpret_cast<const short*>(pcm), reinterpret_cast<__half*>(frame), dim,
+                                      first_channel, workspace, as_stream(stream)),
+                "audio front-end");
+    });
+}
+
 AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream)
 {
     return guarded([&] {

@@ -486,3 +486,18 @@ def set_actions(probs: torch.Tensor, stream=None) -> torch.Tensor:
     out = torch.empty(rows, (count + 63) // 64, dtype=torch.int64, device=probs.device)
     call("aic_set_actions", _vp(probs), rows, count, _vp(out), _stream(stream))
     return out
+
+
+def audio_frontend(pcm: torch.Tensor, frame: torch.Tensor, first_channel: int = 4, stream=None) -> None:
+    """Audio front-end (ca.cu): 2048 int16 PCM samples -> |FFT| and phase planes
+    written to frame[first_channel] and frame[first_channel + 1] (fp16 [C][dim][dim])."""
+    assert pcm.dtype == torch.int16 and pcm.numel() == 2048 and pcm.is_contiguous()
+    assert frame.dtype == torch.float16 and frame.dim() == 3 and frame.is_contiguous()
+    assert 0 <= first_channel and first_channel + 2 <= frame.shape[0] and frame.shape[1] == frame.shape[2]
+    nb = _size_out()
+    call("aic_audio_workspace_bytes", C.byref(nb))
+    ws = _Arena(nb.value, frame.device)
+    if stream is not None:
+        ws.raw.record_stream(stream)  # the workspace is freed on return while the kernels may still run
+    call("aic_audio_frontend", _vp(pcm), _vp(frame), int(frame.shape[-1]), int(first_channel), C.c_void_p(ws.ptr),
+         _stream(stream))

@@ -96,6 +96,19 @@ AIC_API aic_status aic_gap(const uint32_t* in, const int8_t* in_s, int64_t frame
 AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frames, int hw, int channels,
                                uint16_t* out, void* stream);
 
+/* Audio front-end of the reference's capture path (ca.cu:76-117): 2048 int16
+ * PCM samples (1024 interleaved stereo frames, device memory) -> fp16 ->
+ * bilinear resize to 1024 x 1024 -> 2-D radix-2 fp16 FFT -> |X|/1024^2 and
+ * atan2 planes -> bilinear resize to dim x dim, written to channels
+ * first_channel and first_channel + 1 of an fp16 frame [C][dim][dim] (the
+ * reference uses channels 4 and 5 of its 32-channel stem input, ca.cu:118-125).
+ * The reference's row FFT reads past its input for rows 512..1023 and its
+ * column FFT overwrites its own input; here those reads see zeros and the
+ * column results go to a separate buffer. workspace: aic_audio_workspace_bytes. */
+AIC_API aic_status aic_audio_workspace_bytes(size_t* bytes);
+AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int dim, int first_channel,
+                                      void* workspace, void* stream);
+
 /* setActionsKernel (kernels.h:1473-1485, cortex.h:371-372): per row of
  * `count` probabilities, Bernoulli bits into [rows][(count+63)/64] words. */
 AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream);

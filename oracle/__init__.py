@@ -47,6 +47,10 @@ def _load() -> C.CDLL:
         "orc_critic": ([P, P, P, P, I32, I32, P, P, I32, I32], None),
         "orc_set_actions": ([P, I64, I32, P], None),
         "orc_num_threads": ([], I32),
+        "orc_audio_pcm_to_half": ([P, I32, P], None),
+        "orc_resize_half": ([P, P, I32, I32, I32, I32], None),
+        "orc_fft_rows": ([P, I32, P], None),
+        "orc_fft_cols": ([P, I32, P], None),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -160,6 +164,23 @@ def set_actions(probs):
     out = np.zeros((rows, (count + 63) // 64), dtype=np.uint64)
     lib.orc_set_actions(_p(probs), rows, count, _p(out))
     return out
+
+
+def audio_frontend(pcm: np.ndarray, dim: int = 256, n: int = 1024):
+    """ca.cu:106-113 with the row FFT's out-of-range rows reading zeros and the
+    column FFT out of place. Returns (planes [2][n][n], out [2][dim][dim]) fp16."""
+    pcm = np.ascontiguousarray(pcm, np.int16)
+    h = np.zeros(pcm.size, np.uint16)
+    lib.orc_audio_pcm_to_half(_p(pcm), pcm.size, _p(h))
+    image = np.zeros(2 * n * n, np.uint16)
+    lib.orc_resize_half(_p(h), _p(image), n, 1, n, 1)  # src_h: the 1024-sample buffer (ca.cu:107)
+    rows = np.zeros(2 * n * n, np.uint16)
+    lib.orc_fft_rows(_p(image), n, _p(rows))
+    planes = np.zeros(2 * n * n, np.uint16)
+    lib.orc_fft_cols(_p(rows), n, _p(planes))
+    out = np.zeros(2 * dim * dim, np.uint16)
+    lib.orc_resize_half(_p(planes), _p(out), n, n, dim, 2)
+    return planes.view(np.float16).reshape(2, n, n), out.view(np.float16).reshape(2, dim, dim)
 
 
 # ---- compositions ---------------------------------------------------------

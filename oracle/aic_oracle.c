@@ -713,3 +713,112 @@ void orc_set_actions(const float* probs, int64_t rows, int A, uint64_t* actions)
         }
     }
 }
+
+/* ------------------------------------------------------------------ A14 */
+/* Audio front-end (ca.cu:4-20, 76-117; kernels.h:1420-1459, 1566-1652) in
+ * emulated fp16: every fp16 operation is computed in float (exact for the
+ * product of two halves) and rounded to half, as the GPU does per op. */
+static inline uint16_t orc_hmul(uint16_t a, uint16_t b) { return orc_float_to_half(orc_half_to_float(a) * orc_half_to_float(b)); }
+static inline uint16_t orc_hadd(uint16_t a, uint16_t b) { return orc_float_to_half(orc_half_to_float(a) + orc_half_to_float(b)); }
+static inline uint16_t orc_hsub(uint16_t a, uint16_t b) { return orc_float_to_half(orc_half_to_float(a) - orc_half_to_float(b)); }
+
+void orc_audio_pcm_to_half(const int16_t* pcm, int n, uint16_t* out)
+{
+    const uint16_t inv = orc_float_to_half(1.0f / 32768.0f);
+    for (int i = 0; i < n; ++i) out[i] = orc_hmul(orc_float_to_half((float)pcm[i]), inv);
+}
+
+void orc_resize_half(const uint16_t* src, uint16_t* dst, int src_h, int src_w, int dst_dim, int channels)
+{
+    const float scale = (float)src_w / (float)dst_dim;
+    for (int c = 0; c < channels; ++c) {
+        const uint16_t* s = src + (int64_t)c * src_w * src_h;
+        for (int y = 0; y < dst_dim; ++y) {
+            const float ys = fmaf((float)y + 0.5f, scale, -0.5f);
+            const float fy = floorf(ys);
+            const int y1 = fy > 0.0f ? (int)fy : 0;
+            const float wy = ys - fy;
+            const int r1 = y1 * src_w, r2 = (y1 + 1 < src_h - 1 ? y1 + 1 : src_h - 1) * src_w;
+            for (int x = 0; x < dst_dim; ++x) {
+                const float xs = fmaf((float)x + 0.5f, scale, -0.5f);
+                const float fx = floorf(xs);
+                const float wx = xs - fx;
+                const int x1 = fx > 0.0f ? (int)fx : 0;
+                const int x2 = x1 + 1 < src_w - 1 ? x1 + 1 : src_w - 1;
+                const float v11 = orc_half_to_float(s[r1 + x1]);
+                const float v21 = orc_half_to_float(s[r2 + x1]);
+                const float top = fmaf(wx, orc_half_to_float(s[r1 + x2]) - v11, v11);
+                const float res = fmaf(wy, fmaf(wx, orc_half_to_float(s[r2 + x2]) - v21, v21) - top, top);
+                dst[(int64_t)c * dst_dim * dst_dim + (int64_t)y * dst_dim + x] = orc_float_to_half(res);
+            }
+        }
+    }
+}
+
+/* radix-2 DIT on n complex halves (re, im interleaved), input in natural order */
+static void orc_fft_half(uint16_t* z, int n)
+{
+    int log2n = 0;
+    while ((1 << log2n) < n) ++log2n;
+    uint16_t* t = (uint16_t*)malloc(sizeof(uint16_t) * 2 * n);
+    for (int i = 0; i < n; ++i) {
+        int r = 0;
+        for (int b = 0; b < log2n; ++b) r |= ((i >> b) & 1) << (log2n - 1 - b);
+        t[2 * r] = z[2 * i];
+        t[2 * r + 1] = z[2 * i + 1];
+    }
+    for (int s = 1; s <= log2n; ++s) {
+        const int m = 1 << s, half_m = m >> 1;
+        for (int b = 0; b < n / 2; ++b) {
+            const int local = b % half_m;
+            const int u = b / half_m * m + local, v = u + half_m;
+            const float arg = (-6.2831853f * (float)local) / (float)m;
+            const uint16_t wr = orc_float_to_half(cosf(arg)), wi = orc_float_to_half(sinf(arg));
+            /* complex_mul_half2 (kernels.h:98-102) */
+            const uint16_t ar = t[2 * v], ai = t[2 * v + 1];
+            const uint16_t tr = orc_hsub(orc_hmul(ar, wr), orc_hmul(ai, wi));
+            const uint16_t ti = orc_hadd(orc_hmul(ai, wr), orc_hmul(ar, wi));
+            const uint16_t ur = t[2 * u], ui = t[2 * u + 1];
+            t[2 * u] = orc_hadd(ur, tr);
+            t[2 * u + 1] = orc_hadd(ui, ti);
+            t[2 * v] = orc_hsub(ur, tr);
+            t[2 * v + 1] = orc_hsub(ui, ti);
+        }
+    }
+    memcpy(z, t, sizeof(uint16_t) * 2 * n);
+    free(t);
+}
+
+/* fftRowKernel: row r = complex pairs of in[2nr .. 2nr + 2n) (in holds 2 n^2 halves) */
+void orc_fft_rows(const uint16_t* in, int n, uint16_t* out)
+{
+#pragma omp parallel for schedule(static)
+    for (int r = 0; r < n; ++r) {
+        memcpy(out + (int64_t)r * 2 * n, in + (int64_t)r * 2 * n, sizeof(uint16_t) * 2 * n);
+        orc_fft_half(out + (int64_t)r * 2 * n, n);
+    }
+}
+
+/* fftColumnKernel, out of place: planes [2][n][n] = |X| / n^2, atan2(im, re) */
+void orc_fft_cols(const uint16_t* in, int n, uint16_t* planes)
+{
+    const float norm = 1.0f / ((float)n * (float)n);
+#pragma omp parallel
+    {
+        uint16_t* col = (uint16_t*)malloc(sizeof(uint16_t) * 2 * n);
+#pragma omp for schedule(static)
+        for (int x = 0; x < n; ++x) {
+            for (int r = 0; r < n; ++r) {
+                col[2 * r] = in[((int64_t)r * n + x) * 2];
+                col[2 * r + 1] = in[((int64_t)r * n + x) * 2 + 1];
+            }
+            orc_fft_half(col, n);
+            for (int r = 0; r < n; ++r) {
+                const float re = orc_half_to_float(col[2 * r]), im = orc_half_to_float(col[2 * r + 1]);
+                planes[(int64_t)r * n + x] = orc_float_to_half(sqrtf(fmaf(re, re, im * im)) * norm);
+                planes[(int64_t)n * n + (int64_t)r * n + x] = orc_float_to_half(atan2f(im, re));
+            }
+        }
+        free(col);
+    }
+}

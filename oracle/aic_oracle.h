@@ -104,6 +104,15 @@ void orc_critic(const uint16_t* x, const float* w1, const float* wl,
 void orc_set_actions(const float* probs, int64_t rows, int A,
                      uint64_t* actions);
 
+/* A14: audio front-end (ca.cu:4-20, 76-117; kernels.h:1420-1459, 1566-1652),
+ * fp16 values as IEEE half bits. */
+void orc_audio_pcm_to_half(const int16_t* pcm, int n, uint16_t* out);
+void orc_resize_half(const uint16_t* src, uint16_t* dst, int src_h, int src_w, int dst_dim, int channels);
+/* in: 2 n^2 halves (row r pairs elements 2nr + 2k, +1); out: n x n complex (re, im) */
+void orc_fft_rows(const uint16_t* in, int n, uint16_t* out);
+/* in: n x n complex; planes: [2][n][n] = |X|/n^2, atan2(im, re) */
+void orc_fft_cols(const uint16_t* in, int n, uint16_t* planes);
+
 int orc_num_threads(void);
 
 #ifdef __cplusplus

@@ -1,6 +1,6 @@
 #!/usr/bin/env bash
 # Compiles the reference's own CUDA kernels (AICortex kernels.h and the headers
-# it includes) for sm_100a into oracle/_ref/, one shared library per
+# it includes, and the audio front-end ca.cu) for sm_100a into oracle/_ref/, one shared library per
 # (d_model, d_state) pair, driven by oracle/ref_harness.cu.
 # TEST INFRASTRUCTURE ONLY: the libraries are the golden-vector source for
 # tests/golden/make_golden.py and never part of the product.
@@ -9,7 +9,8 @@
 # base_constants.h, so the four headers the kernels need are copied to a
 # temporary directory outside the repository, the two constants rewritten
 # there, and the copy deleted after the build. A stub <windows.h> replaces the
-# Windows SDK header that kernels.h includes (kernels.h:14) but does not use.
+# Windows SDK header that kernels.h includes (kernels.h:14); it declares only
+# the BYTE and DWORD types named by ca.cu's capture entry point.
 set -euo pipefail
 REF=${AICORTEX_REFERENCE:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
@@ -23,11 +24,12 @@ PAIRS=${AICREF_PAIRS:-"256:32 256:128 256:512"}
 for pair in $PAIRS; do
   D=${pair%%:*}; N=${pair##*:}
   lib="$OUT/libaicref_D${D}_N${N}.so"
-  if [ -f "$lib" ] && [ "$lib" -nt "$HERE/ref_harness.cu" ] && [ "$lib" -nt "$REF/kernels.h" ]; then continue; fi
+  if [ -f "$lib" ] && [ "$lib" -nt "$HERE/ref_harness.cu" ] && [ "$lib" -nt "$REF/kernels.h" ] && [ "$lib" -nt "$0" ]; then continue; fi
   tmp=$(mktemp -d /tmp/aicref.XXXXXX)
-  cp "$REF/kernels.h" "$REF/uv.h" "$REF/device_constants.h" "$REF/base_constants.h" "$tmp/"
+  cp "$REF/kernels.h" "$REF/uv.h" "$REF/device_constants.h" "$REF/base_constants.h" "$REF/ca.cu" "$tmp/"
   sed -i -E "s/final_channels = [0-9]+/final_channels = ${D}/; s/mamba_d_state = [0-9]+/mamba_d_state = ${N}/" "$tmp/base_constants.h"
-  : > "$tmp/windows.h"
+  # the two Windows SDK types ca.cu's capture entry point names (ca.cu:76)
+  printf 'typedef unsigned char BYTE;\ntypedef unsigned long DWORD;\n' > "$tmp/windows.h"
   nvcc -std=c++17 -O3 --use_fast_math --extended-lambda \
        -gencode arch=compute_100a,code=sm_100a -lineinfo \
        -Xcompiler -fPIC -shared \

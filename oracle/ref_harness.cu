@@ -13,6 +13,7 @@
 // constants (kernels.h:1080-1089), which is why one library is built per
 // (d_model, d_state) pair.
 #include "kernels.h"
+#include "ca.cu"  // AudioProcessorOP (ca.cu:4-20)
 
 #define AICREF_API extern "C" __attribute__((visibility("default")))
 
@@ -135,6 +136,37 @@ AICREF_API int aicref_set_actions(const float* probs, unsigned long long* action
 {
     setActionsKernel<float><<<(count + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(
         probs, reinterpret_cast<action_type*>(actions), count);
+    return aicref_status();
+}
+
+// ca.cu:106: 2048 int16 samples -> fp16 through AudioProcessorOP.
+AICREF_API int aicref_audio_convert(const short* pcm, __half* out)
+{
+    AudioProcessorOP op{out, pcm};
+    forEachNUniversalVectorKernel<<<1, gpu_block_threads>>>(op, 2048 >> 3);
+    return aicref_status();
+}
+
+// ca.cu:107,112 launch geometry: 16x16 blocks, two outputs per thread.
+AICREF_API int aicref_resize(const __half* src, __half* dst, int src_h, int src_w, int dst_dim, int channels)
+{
+    dim3 block(16, 16);
+    dim3 grid(dst_dim / (block.x << 1), dst_dim / block.y, channels);
+    resizeKernel<__half><<<grid, block>>>(src, dst, src_h, src_w, dst_dim, channels);
+    return aicref_status();
+}
+
+// ca.cu:108-109 with an input of 2 x 1024 x 1024 halves (rows 512.. read the upper half).
+AICREF_API int aicref_fft_rows(const __half* in, __half2* out)
+{
+    fftRowKernel<1024><<<1024, gpu_block_threads>>>(in, out);
+    return aicref_status();
+}
+
+// ca.cu:110, out of place: out holds 2 x 1024 x 1024 halves (|X|/N^2, phase).
+AICREF_API int aicref_fft_cols(const __half2* in, __half* out)
+{
+    fftColumnKernel<1024><<<1024, gpu_block_threads>>>(in, out);
     return aicref_status();
 }
 

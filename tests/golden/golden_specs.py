@@ -131,3 +131,16 @@ RES_CASES = {"res_160": (64, 160, 8, 0.625), "res_mamba_256": (1, 256, 1, 1.0)}
 def stem_case():
     rng = np.random.default_rng(1100)
     return rng.random((3, 64, 64), dtype=np.float32).astype(np.float16)
+
+
+AUDIO_DIM = 256  # img_resolution of the frames the audio planes are written into
+
+
+def audio_case():
+    """Two 2048-sample int16 windows (1024 stereo frames): a seeded noisy one
+    and one with both extremes of int16 at the samples the front-end reads."""
+    rng = np.random.default_rng(1200)
+    a = np.clip(rng.standard_normal(2048) * 6000, -32768, 32767).astype(np.int16)
+    b = rng.integers(-32768, 32768, 2048).astype(np.int16)
+    b[0], b[1] = -32768, 32767
+    return np.stack([a, b])

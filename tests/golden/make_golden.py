@@ -286,8 +286,33 @@ def gen_actions(lib):
     save("actions", probs_sha=S.sha(probs), words=acts.cpu().numpy().view(np.uint64))
 
 
+def gen_audio(lib):
+    """ca.cu:106-113 one hop window at a time: convert, resize 1024 x 1 -> 1024
+    x 1024, row FFT over a 2 x 1024 x 1024 input with a zero upper half, column
+    FFT into a separate planes buffer, resize both planes to 256 x 256."""
+    n, dim = 1024, S.AUDIO_DIM
+    pcm = S.audio_case()
+    outs, plane_sha = [], []
+    for win in pcm:
+        d = Dev()
+        h, ph = d.zeros(2048, torch.float16)
+        run(lib, "aicref_audio_convert", d.put(win), ph)
+        image, pimg = d.zeros(2 * n * n, torch.float16)
+        run(lib, "aicref_resize", ph, pimg, C.c_int(1024), C.c_int(1), C.c_int(n), C.c_int(1))
+        rows, prows = d.zeros(2 * n * n, torch.float16)
+        run(lib, "aicref_fft_rows", pimg, prows)
+        planes, ppl = d.zeros(2 * n * n, torch.float16)
+        run(lib, "aicref_fft_cols", prows, ppl)
+        out, pout = d.zeros(2 * dim * dim, torch.float16)
+        run(lib, "aicref_resize", ppl, pout, C.c_int(n), C.c_int(n), C.c_int(dim), C.c_int(2))
+        outs.append(out.cpu().numpy().reshape(2, dim, dim))
+        plane_sha.append(S.sha(planes.cpu().numpy()))
+    save("audio", pcm_sha=S.sha(pcm), out=np.stack(outs), planes_sha=np.array(plane_sha))
+
+
 def main():
     lib = ref(256, 128)
+    gen_audio(lib)
     gen_pack(lib)
     gen_stem(lib)
     gen_conv(lib)

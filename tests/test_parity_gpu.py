@@ -202,6 +202,19 @@ def test_golden_actions(golden):
     np.testing.assert_array_equal(h(words)[0].view(np.uint64), g["words"])
 
 
+def test_golden_audio(golden):
+    """A14 bit-exact against the reference kernels; channels other than the two
+    audio planes of the frame stay untouched."""
+    g = golden("audio")
+    dim = S.AUDIO_DIM
+    for i, win in enumerate(S.audio_case()):
+        frame = torch.full((6, dim, dim), 3.0, dtype=torch.float16, device=DEV)
+        A.audio_frontend(t(win), frame, first_channel=4)
+        f = h(frame)
+        np.testing.assert_array_equal(f[4:].view(np.uint16), g["out"][i].view(np.uint16))
+        assert (f[:4] == 3.0).all()
+
+
 # ------------------------------------------------------- batched vs. oracle
 
 def test_batched_convs_vs_oracle():
@@ -257,8 +270,9 @@ def test_cortex_small_vs_oracle():
     shortcut conv's fp32 sum differs from the reference order in the last bits,
     which flips a requant code at a rounding boundary at a rate of ~1e-3 per
     layer (tests above); the flips propagate through the following quantized
-    layers, so end to end the heads are compared with a 1e-1 bound and the
-    mean feature error with 5e-2."""
+    layers, so end to end each output is compared with the reference-order run
+    statistically: mean absolute error below 0.2 of the mean magnitude and a
+    correlation above 0.95."""
     import oracle as O
     B, T, dim = 2, 3, 32
     desc = W.cortex_desc(batch_chunk=4, d_state=64, critic_units=64, dim=dim)
@@ -297,6 +311,7 @@ def test_cortex_small_vs_oracle():
         rel = np.abs(a - r).mean() / np.abs(r).mean()
         corr = np.corrcoef(a, r)[0, 1]
         assert rel < 0.2 and corr > 0.95, f"{name} (tensor cores): mean error {rel:.3e}, correlation {corr:.4f}"
+
 
 @pytest.mark.parametrize("geo", [
     (64, 128, 1, 1, 24, 24, 1),     # 576 rows: 4 full tiles + a partial one
