@@ -17,6 +17,9 @@ AIC_ERR_CUDA = 3
 AIC_ERR_STATE = 4
 AIC_ERR_IO = 5
 AIC_MAX_BLOCKS = 16
+AIC_CONV_ORDERED = 0
+AIC_CONV_FAST = 1
+AIC_CONV_SIMT = 2
 
 
 class AicError(RuntimeError):
@@ -73,6 +76,7 @@ _SIGS = {
     "aic_gap": [P, P, I64, I32, I32, P, P, P, P],
     "aic_gap_f16": [P, P, I64, I32, I32, P, P],
     "aic_set_actions": [P, I64, I32, P, P],
+    "aic_selftest_rcp": [P, P, P],
     "aic_audio_workspace_bytes": [SZ],
     "aic_audio_frontend": [P, P, I32, I32, P, P],
     "aic_conv_layer_create": [C.POINTER(ConvLayerDesc), PP],
@@ -83,6 +87,7 @@ _SIGS = {
     "aic_conv_layer_load_file_sync": [P, C.c_char_p, P],
     "aic_conv_layer_forward": [P, P, P, P, P, I64, P],
     "aic_conv_layer_forward_exact": [P, P, P, P, P, I64, P],
+    "aic_conv_layer_set_mode": [P, I32],
     "aic_conv_layer_destroy": [P],
     "aic_conv_block_create": [C.POINTER(ConvBlockDesc), PP],
     "aic_conv_block_layer": [P, I32, PP],
@@ -144,6 +149,7 @@ _SIGS = {
     "aic_cortex_host_workspace_bytes": [P, I32, I32, SZ],
     "aic_cortex_forward_host": [P, P, I32, I32, P, P, P, P],
     "aic_cortex_set_exact": [P, I32],
+    "aic_cortex_set_conv_mode": [P, I32],
     "aic_cortex_last_launches": [P, PI64],
     "aic_cortex_profile_enable": [P, I32],
     "aic_cortex_profile_count": [P, C.POINTER(C.c_int)],

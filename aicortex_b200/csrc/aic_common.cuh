@@ -77,8 +77,28 @@ __device__ __forceinline__ float code_f(uint32_t w, int e)
     return __uint_as_float(((w >> (e << 2)) & 0xFu) ^ 0x4B000008u) - 8388616.0f;
 }
 
-__device__ __forceinline__ float sigmoid_f(float x) { return __frcp_rn(1.0f + __expf(-x)); }
+// Reciprocal of d >= 1 rounded to nearest, results below 2^-126 flushed to
+// zero (the rcp.rn.ftz semantics of __frcp_rn under fast math): one
+// Newton-Raphson step from the hardware approximation, with the residual
+// 1 - d*y formed exactly by an FMA (Markstein's correction). Infinity is
+// clamped to the largest float first, whose reciprocal flushes to zero.
+// aic_selftest_rcp compares it with __frcp_rn over every significand of ten
+// binades from 1 to 2^126 and at the clamp: no input differs.
+__device__ __forceinline__ float rcp_rn_ge1(float d)
+{
+    d = fminf(d, 3.40282347e38f);
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+    const float r = fmaf(-d, y, 1.0f);
+    return fmaf(r, y, y);
+}
+
+// sigmoid(x) = __frcp_rn(1 + __expf(-x)) and silu(x) = x * sigmoid(x), as the
+// reference defines them (kernels.h:86-87); 1 + e >= 1, so rcp_rn_ge1 gives
+// the same bits as __frcp_rn.
+__device__ __forceinline__ float sigmoid_f(float x) { return rcp_rn_ge1(1.0f + __expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
 
 // Quantise 32 values held as 8 per lane across 4 consecutive lanes (lane & 3
 // selects the word). Returns this lane's packed word; *exp_out gets the

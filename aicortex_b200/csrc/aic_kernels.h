@@ -44,6 +44,21 @@ cudaError_t launch_conv_gemm_tc(const uint32_t* in, const int8_t* in_s, const ui
                                 uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize, int din,
                                 int dout, bool act, int* err, cudaStream_t stream);
 
+// A3/A4 on the tensor cores in the reference's accumulation order (exact
+// integer dots from the MMA, the fp32 fmaf chain over groups on CUDA cores):
+// bit-identical to the reference. ksize 1 or 2 (conv_tc_ord_supported).
+bool conv_tc_ord_supported(int ksize);
+size_t conv_tc_ord_wimg_bytes(int in_c, int out_c, int ksize);
+cudaError_t launch_build_wimg_ord(const uint32_t* w, const int8_t* w_s, int in_c, int out_c, int ksize, uint8_t* img,
+                                  cudaStream_t stream);
+cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
+                                    uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize,
+                                    int din, int dout, bool act, int* err, cudaStream_t stream);
+
+// Compares rcp_rn_ge1 with __frcp_rn over every significand of several
+// binades; *mismatches (zeroed by the caller) counts differing results.
+cudaError_t launch_selftest_rcp(unsigned long long* mismatches, float* first_bad, cudaStream_t stream);
+
 // Device-side error word written by kernels whose bounded waits time out.
 int* device_error_word();
 

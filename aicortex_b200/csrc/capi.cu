@@ -241,9 +241,10 @@ struct ConvLayer {
         weight_elems = static_cast<int64_t>(d.in_channels) * d.kernel_size * d.kernel_size * (is_dw ? 1 : d.out_channels);
         groups = weight_elems >> 5;
     }
-    uint8_t* wimg = nullptr;  // tensor-core weight images (dense/pointwise only)
-    float* wf = nullptr;      // dequantised weights (depthwise only)
-    bool exact = false;       // reference accumulation order on CUDA cores
+    uint8_t* wimg = nullptr;      // tensor-core weight images, AIC_CONV_FAST (dense/pointwise only)
+    uint8_t* wimg_ord = nullptr;  // tensor-core images, AIC_CONV_ORDERED (k = 1, 2)
+    float* wf = nullptr;          // dequantised weights (depthwise only)
+    int mode = AIC_CONV_ORDERED;
 
     size_t carve(void* base)
     {
@@ -252,6 +253,9 @@ struct ConvLayer {
         ws = c.take<int8_t>(groups);
         bias = c.take<float>(d.out_channels);
         wimg = is_dw ? nullptr : c.take<uint8_t>(conv_tc_wimg_bytes(d.in_channels, d.out_channels, d.kernel_size));
+        wimg_ord = is_dw || !conv_tc_ord_supported(d.kernel_size)
+                       ? nullptr
+                       : c.take<uint8_t>(conv_tc_ord_wimg_bytes(d.in_channels, d.out_channels, d.kernel_size));
         wf = is_dw ? c.take<float>(weight_elems) : nullptr;
         return c.bytes();
     }
@@ -266,6 +270,9 @@ struct ConvLayer {
             cuda_ok(launch_dw_weights(w, ws, weight_elems, wf, s), "depthwise weights");
         else
             cuda_ok(launch_build_wimg(w, ws, d.in_channels, d.out_channels, d.kernel_size, wimg, s), "weight images");
+        if (wimg_ord)
+            cuda_ok(launch_build_wimg_ord(w, ws, d.in_channels, d.out_channels, d.kernel_size, wimg_ord, s),
+                    "weight images");
     }
     void load(const float* master, const float* b, cudaStream_t s)
     {
@@ -313,16 +320,22 @@ struct ConvLayer {
                 return launch_conv_dw(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
                                       d.dim_in, d.dim_out, s);
             });
-        else if (exact)
-            traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm_simt", [&] {
-                return launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
-                                             d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s);
-            });
-        else
+        else if (mode == AIC_CONV_FAST)
             traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm", [&] {
                 return launch_conv_gemm_tc(in, in_s, wimg, bias, out, out_s, frames, d.in_channels, d.out_channels,
                                            d.kernel_size, d.dim_in, d.dim_out, !d.disable_activation,
                                            device_error_word(), s);
+            });
+        else if (mode == AIC_CONV_ORDERED && wimg_ord)
+            traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm_ord", [&] {
+                return launch_conv_gemm_tc_ord(in, in_s, wimg_ord, bias, out, out_s, frames, d.in_channels,
+                                               d.out_channels, d.kernel_size, d.dim_in, d.dim_out,
+                                               !d.disable_activation, device_error_word(), s);
+            });
+        else  // AIC_CONV_SIMT, and the 4x4 dense conv in AIC_CONV_ORDERED
+            traced(prof, tag, s, 2.0 * pix_out * d.out_channels * ksq * d.in_channels, bytes, "conv_gemm_simt", [&] {
+                return launch_conv_gemm_simt(in, in_s, w, ws, bias, out, out_s, frames, d.in_channels, d.out_channels,
+                                             d.kernel_size, d.stride, d.dim_in, d.dim_out, !d.disable_activation, s);
             });
         return 1;
     }
@@ -1056,6 +1069,15 @@ AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t f
     });
 }
 
+AIC_API aic_status aic_selftest_rcp(uint64_t* mismatches, float* first_bad, void* stream)
+{
+    return guarded([&] {
+        require(mismatches && first_bad, "null buffer");
+        cuda_ok(launch_selftest_rcp(reinterpret_cast<unsigned long long*>(mismatches), first_bad, as_stream(stream)),
+                "rcp self-test");
+    });
+}
+
 AIC_API aic_status aic_audio_workspace_bytes(size_t* bytes)
 {
     return guarded([&] {
@@ -1148,6 +1170,13 @@ AIC_API aic_status aic_conv_layer_forward_exact(aic_conv_layer l, const uint32_t
     return guarded([&] {
         require(frames >= 0, "negative frame count");
         handle<ConvLayer>(l, "conv layer")->forward_exact(in, in_s, out, out_s, frames, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_conv_layer_set_mode(aic_conv_layer l, int mode)
+{
+    return guarded([&] {
+        require(mode == AIC_CONV_ORDERED || mode == AIC_CONV_FAST || mode == AIC_CONV_SIMT, "unknown conv mode");
+        handle<ConvLayer>(l, "conv layer")->mode = mode;
     });
 }
 AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l)
@@ -1614,13 +1643,18 @@ AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_
                                                   as_stream(stream));
     });
 }
-AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact)
+AIC_API aic_status aic_cortex_set_conv_mode(aic_cortex c, int mode)
 {
     return guarded([&] {
+        require(mode == AIC_CONV_ORDERED || mode == AIC_CONV_FAST || mode == AIC_CONV_SIMT, "unknown conv mode");
         auto* x = handle<Cortex>(c, "cortex");
         for (auto& b : x->blocks)
-            for (auto& l : b->layers) l->exact = exact != 0;
+            for (auto& l : b->layers) l->mode = mode;
     });
+}
+AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact)
+{
+    return aic_cortex_set_conv_mode(c, exact ? AIC_CONV_SIMT : AIC_CONV_ORDERED);
 }
 AIC_API aic_status aic_cortex_profile_enable(aic_cortex c, int enable)
 {

@@ -1,0 +1,482 @@
+// Quantized conv (pointwise k=1, dense k=2 with stride 2) on the 5th-generation
+// tensor cores with the reference's floating-point accumulation order, so the
+// packed outputs are bit-identical to the reference kernels
+// (AICortex kernels.h:217-282 convPointwiseFwdKernel, 514-585
+// convDenseFwdKernel).
+//
+// The reference accumulates, per output (pixel, channel), over taps k and
+// 32-element groups g in order:
+//     acc[k & 3] = fmaf(unit(s_in[k][g]), unit(s_w[k][g]) * dot[k][g], acc[k & 3])
+// where dot is the exact integer dot product of the two groups' codes, and
+// folds the partial sums as ((acc0 + acc1) + acc2) + acc3. The integer dots
+// are what a tensor core computes exactly: with the codes themselves (-8..7,
+// exact in bf16) as operands, a K=32 kind::f16 MMA sums 32 integer products of
+// magnitude <= 64 in fp32, which is exact. So each stage of two groups issues
+// two MMAs per group into a group-private TMEM accumulator, and the CUDA cores
+// run the reference's fmaf chain over the groups, in group order, from those
+// exact dots. Only the chain runs in fp32, exactly as the reference does.
+//
+// Tile: 128 pixel rows x 64 output channels, so a thread's chain state is
+// 32 accumulators (plus 32 for the finished taps of a 2x2 conv) and two CTAs
+// (128 registers per thread) fit on an SM. The RMSNorm spans up to 256 channels, so the CTAs covering
+// one norm chunk form a cluster (2 for 128 channels, 4 for 256) and exchange
+// their rows' per-32-channel sums of squares through distributed shared
+// memory; the sums are then folded with the reference's butterfly tree (32
+// lanes, then 8 warps). Layers with <= 64 output channels use no cluster.
+//
+// Pipeline (256 threads, a run of consecutive row tiles per CTA): the CTA
+// walks one sequence of stages across its tiles. For stage s every thread stages one
+// (row, group) of the A tile from the packed activations (im2col on the fly
+// for k=2) and records unit(s_in); thread 0 fetches the stage's B image
+// (codes as bf16 in the SW128 layout, followed by unit(s_w) of both groups)
+// with one cp.async.bulk and issues the MMAs for stage s; meanwhile all
+// threads run the chain for stage s-1 from TMEM (tcgen05.ld), and after a
+// tile's last stage its epilogue, which so overlaps the next tile's first
+// MMAs. A, B and the per-group accumulators are double buffered. Thread
+// (row r, half h) owns the chain of row r over the tile's 32-channel group h.
+//
+// All mbarrier waits are bounded; on timeout the kernel records an error code
+// in *err, skips the remaining work, still takes part in every CTA and
+// cluster barrier, waits (bounded) for its MMAs and releases its TMEM.
+#include <cuda_bf16.h>
+
+#include "aic_common.cuh"
+#include "aic_kernels.h"
+#include "tc_ptx.cuh"
+
+namespace aic {
+namespace {
+
+using namespace tc;
+
+constexpr int kThreads = 256;
+constexpr int kBK = 64;                   // two 32-element groups per stage
+constexpr int kTileA = kBM * kBK * 2;     // 16 KB of bf16
+constexpr int kNCta = 64;                 // output channels per CTA
+constexpr int kImgRow = kBK * 2 + 2 * 4;  // image bytes per channel per stage: 128 B codes + 2 units
+
+struct OrdParams {
+    const uint32_t* in;
+    const int8_t* in_s;
+    const uint8_t* wimg;
+    const float* bias;
+    uint32_t* out;
+    int8_t* out_s;
+    int64_t rows;
+    int in_c, out_c, din, dout, stages, gk_total, act;
+    int n_max;          // largest channel count of any CTA of the launch
+    int tiles_per_cta;  // consecutive 128-row tiles each CTA column processes
+    int* err;
+};
+
+// Barrier over every thread of the cluster with release/acquire ordering of
+// shared memory (local and distributed).
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Store to the same shared-memory offset in the cluster CTA of rank `peer`.
+__device__ __forceinline__ void st_peer_f32(uint32_t local_addr, uint32_t peer, float v)
+{
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(peer));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+// Lane 0's value of the reference's `v += __shfl_xor_sync(v, o)` for
+// o = 16..1 over the 32 lanes' squares acc[i]^2 (kernels.h:266-267): a
+// pairwise tree with stride halving. The products and sums are separately
+// rounded (no contraction into fma).
+__device__ __forceinline__ float tree_sq32(const float (&a)[32])
+{
+    float t[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) t[i] = __fadd_rn(__fmul_rn(a[i], a[i]), __fmul_rn(a[i + 16], a[i + 16]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < o; ++i) t[i] = __fadd_rn(t[i], t[i + o]);
+    return t[0];
+}
+
+// TMEM columns: per-group accumulators of n channels, double buffered over
+// stages (a single stage needs one buffer, a single group one slot).
+__host__ __device__ inline uint32_t ord_tmem_cols(int n, int stages, int gk_total)
+{
+    const int need = (stages > 1 ? 4 : gk_total > 1 ? 2 : 1) * n;
+    return need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
+}
+
+template <int KS, int CS, bool ACT>
+__global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // CTA y covers channels [n0, n0 + n_cta) of norm chunk y / CS
+    const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
+    const int n_cta = min(kNCta, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
+    const bool live = n_cta > 0;
+    const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
+    uint8_t* a_tiles = base;                       // [2][kTileA]
+    uint8_t* b_tiles = base + 2 * kTileA;          // [2][slot_b]: codes [n][128 B], then units [2][n]
+    float* din_s = reinterpret_cast<float*>(b_tiles + 2 * slot_b);  // [2 buffers][2 groups][kBM] unit(s_in)
+    float* bias_s = din_s + 4 * kBM;               // [kNCta]
+    float* part = bias_s + kNCta;                  // [2 tiles][8][kBM] group sums of squares of the norm chunk
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 16 * kBM);  // 0,1: B full; 2,3: MMAs done; 4: drain
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t ncols = live ? ord_tmem_cols(n_cta, p.stages, p.gk_total) : 0u;
+    for (int i = tid; i < 16 * kBM; i += kThreads) part[i] = 0.0f;
+    if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
+    if (tid == 0) {
+        for (int i = 0; i < 5; ++i) mbar_init(smem_addr(&bars[i]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (live && warp == 0) tmem_alloc(smem_addr(tmem_slot), ncols);
+    tc_fence_before();
+    __syncthreads();
+    if (CS > 1) cluster_sync_all();  // every peer's `part` is initialised before any remote store
+    tc_fence_after();
+    const uint32_t tmem = live ? *tmem_slot : 0u;
+
+    // Row tiles of this CTA: tiles_per_cta consecutive tiles from tile0 (the
+    // same tiles for every CTA of a cluster, which therefore run in lockstep).
+    const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
+    const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
+    const int64_t my_tiles = tile0 < n_tiles ? min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0) : 0;
+    const int S = p.stages;
+    const int64_t total = my_tiles * S;
+
+    const int prow = tid & (kBM - 1), pg = tid >> 7;  // producer: (row, group of the stage)
+    const int G = p.in_c >> 5;
+    const int GK = p.gk_total;
+    const int stage_bytes = n_cta * kImgRow;
+    const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
+    const uint32_t idesc = instr_desc(n_cta);
+    const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+
+    // chain role: row erow (== prow), 32-channel group hw of the tile
+    const int q = warp & 3, hw = warp >> 2;
+    const int erow = q * 32 + lane;
+    const bool has_cols = hw < (n_cta >> 5);
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(32 * hw);
+    float acc[32], sacc[KS == 1 ? 1 : 32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
+
+    // fmaf chain over the groups of global stage gc (stage sc of its tile)
+    auto chain = [&](int64_t gc, int sc) -> bool {
+        const int buf = static_cast<int>(gc & 1);
+        if (!mbar_wait(smem_addr(&bars[2 + buf]), static_cast<uint32_t>(gc >> 1) & 1u, p.err, 12)) return false;
+        tc_fence_after();
+        const float* units = reinterpret_cast<const float*>(b_tiles + buf * slot_b + n_cta * 128);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int gk = 2 * sc + j;
+            if (gk >= GK) break;
+            if (KS == 2 && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+                    acc[i] = 0.0f;
+                }
+            }
+            if (has_cols) {
+                const float du = din_s[(buf * 2 + j) * kBM + erow];
+                const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta + 32 * hw);
+#pragma unroll
+                for (int h16 = 0; h16 < 2; ++h16) {
+                    float pv[16];
+                    tmem_ld16(tl + static_cast<uint32_t>((buf * 2 + j) * n_cta + 16 * h16), pv);
+#pragma unroll
+                    for (int i4 = 0; i4 < 4; ++i4) {
+                        const float4 u = u4[4 * h16 + i4];
+                        const int b = 16 * h16 + 4 * i4;
+                        acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
+                        acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
+                        acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
+                        acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+        return true;
+    };
+
+    // One loop over this CTA's global stages; iteration gs stages and issues
+    // stage gs, then runs the chain of stage gs - 1 and, after a tile's last
+    // stage, its epilogue. Every CTA runs every iteration and every barrier
+    // (work is skipped, not the barriers, after an abort or in an empty CTA).
+    bool ok = true;  // this thread's chain of the current tile completed
+    // producer position (stage sp of local tile tp) and consumer position
+    // (stage sc of local tile tc) advance by one stage per iteration
+    int sp = 0, sc = 0;
+    int64_t tp = 0, tc = 0;
+    const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
+    for (int64_t gs = 0; gs <= total; ++gs) {
+        const int buf = static_cast<int>(gs & 1);
+        __syncthreads();  // stage gs-2's chain is done with this buffer's units and accumulators
+        const bool run = live && !*abort_flag;
+        const bool produce = run && gs < total;
+        uint8_t* a_tile = a_tiles + buf * kTileA;
+        uint8_t* b_tile = b_tiles + buf * slot_b;
+        // with at most two stages per tile, buffer b keeps stage b % S: the weights
+        // are fetched for the first two global stages only
+        const bool fetch_b = S > 2 || gs < 2;
+        if (produce) {
+            if (tid == 0 && fetch_b) {
+                mbar_expect_tx(smem_addr(&bars[buf]), static_cast<uint32_t>(stage_bytes));
+                bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(sp) * stage_bytes,
+                         static_cast<uint32_t>(stage_bytes), smem_addr(&bars[buf]));
+            }
+            const int64_t row_p = (tile0 + tp) * kBM + prow;
+            const int gk = 2 * sp + pg;
+            float du = 0.0f;
+            if (row_p < p.rows && gk < GK) {
+                const int tap = gk / G, g = gk - tap * G;
+                const int64_t pix = tap_pixel_pow2(row_p, tap, KS, lg_din, lg_dout);
+                const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
+                du = unit_of(__ldg(p.in_s + pix * G + g));
+                stage_group_f(a_tile, prow, pg, words, 1.0f);
+            } else {
+                stage_zero(a_tile, prow, pg);
+            }
+            din_s[(buf * 2 + pg) * kBM + prow] = du;
+            fence_async_smem();
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (produce && tid == 0) {
+            if (!fetch_b || mbar_wait(smem_addr(&bars[buf]), static_cast<uint32_t>(gs >> 1) & 1u, p.err, 11)) {
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_tile);
+                // two K16 MMAs per group; a padding group (odd group count) has no
+                // accumulator slot and is skipped
+                const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)
+                    if (j < n_mma)
+                        mma_bf16(tmem + static_cast<uint32_t>((buf * 2 + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
+                                 smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
+                mma_commit(smem_addr(&bars[2 + buf]));
+            } else {
+                *abort_flag = 1;
+            }
+        }
+        if (gs < total && ++sp == S) {
+            sp = 0;
+            ++tp;
+        }
+        if (gs == 0) continue;
+        const int64_t gc = gs - 1;
+        const int sc_now = sc;
+        if (++sc == S) sc = 0;
+        if (run && ok) {
+            if (!chain(gc, sc_now)) {
+                ok = false;
+                *abort_flag = 1;
+            }
+        }
+        if (sc_now != S - 1) continue;
+
+        // Epilogue of local tile tc: fold the taps, square-sum the 32-channel
+        // group, share the sums across the norm chunk, normalise, activate, pack.
+        const int64_t tile = tile0 + tc;
+        float* part_t = part + (tc & 1) * 8 * kBM;
+        ++tc;
+        const bool emit = run && ok && has_cols;
+        if (KS == 2) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+        }
+        if (emit) {
+            const float gs2 = tree_sq32(acc);
+            float* dst = &part_t[(((n0 & (kNormChunk - 1)) >> 5) + hw) * kBM + erow];
+            if (CS > 1) {
+#pragma unroll
+                for (int r = 0; r < CS; ++r) st_peer_f32(smem_addr(dst), static_cast<uint32_t>(r), gs2);
+            } else {
+                *dst = gs2;
+            }
+        }
+        __syncthreads();
+        if (CS > 1) cluster_sync_all();
+        if (emit) {
+            // the reference's cross-warp butterfly over the chunk's 8 group sums (kernels.h:271-276)
+            float w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w8[i] = part_t[i * kBM + erow];
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+                for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
+            const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
+            const int64_t row = tile * kBM + erow;
+            const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * hw);
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 b = b4[i4];
+                const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float x = fmaf(acc[4 * i4 + k], sc_norm, bb[k]);
+                    acc[4 * i4 + k] = ACT ? silu_f(x) : x;
+                }
+            }
+            uint4 words;
+            int8_t e;
+            quantize_group(acc, &words, &e);
+            if (row < p.rows) {
+                const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + hw;
+                reinterpret_cast<uint4*>(p.out)[gi] = words;
+                p.out_s[gi] = e;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+#pragma unroll
+        for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
+    }
+    if (live) {
+        // every MMA this CTA issued has completed before TMEM is released
+        if (tid == 0) mma_commit(smem_addr(&bars[4]));
+        if (warp == 0) mbar_wait(smem_addr(&bars[4]), 0u, p.err, 13);
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_fence_after();
+            tmem_dealloc(tmem, ncols);
+        }
+    }
+}
+
+// Per (64-channel chunk, stage) image: the codes of both groups as bf16 in the
+// SW128 K-major layout ([n][64] elements), then unit(s_w) of group 0 and
+// group 1 ([2][n] fp32). One thread per (output channel, group slot).
+__global__ void build_wimg_ord_kernel(const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s, int out_c,
+                                      int gk_total, int stages, uint8_t* __restrict__ img)
+{
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int slots = 2 * stages;
+    if (t >= static_cast<int64_t>(out_c) * slots) return;
+    const int n = static_cast<int>(t / slots);
+    const int gk = static_cast<int>(t % slots);
+    const int chunk = n / kNCta, nl = n % kNCta;
+    const int n_chunk = min(kNCta, out_c - chunk * kNCta);
+    const int s = gk >> 1, gl = gk & 1;
+    uint8_t* tile = img + (static_cast<int64_t>(chunk) * kNCta * stages + static_cast<int64_t>(s) * n_chunk) * kImgRow;
+    float* units = reinterpret_cast<float*>(tile + n_chunk * 128);
+    if (gk < gk_total) {
+        const int64_t gi = static_cast<int64_t>(n) * gk_total + gk;
+        stage_group_f(tile, nl, gl, reinterpret_cast<const uint4*>(w)[gi], 1.0f);
+        units[gl * n_chunk + nl] = unit_of(w_s[gi]);
+    } else {
+        stage_zero(tile, nl, gl);
+        units[gl * n_chunk + nl] = 0.0f;
+    }
+}
+
+// Clusters of CS CTAs along y cover a norm chunk (chunks along y as well);
+// along x each CTA column takes tiles_per_cta consecutive row tiles.
+template <int KS, int CS>
+cudaError_t launch_ord(const OrdParams& p, size_t smem, unsigned chunks, cudaStream_t stream)
+{
+    auto kern = p.act ? conv_gemm_tc_ord_kernel<KS, CS, true> : conv_gemm_tc_ord_kernel<KS, CS, false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = CS;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CS > 1 ? 1 : 0;
+    const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
+    cfg.gridDim = dim3(static_cast<unsigned>((n_tiles + p.tiles_per_cta - 1) / p.tiles_per_cta), chunks * CS, 1);
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+template <int KS>
+cudaError_t launch_ord_cs(const OrdParams& p, size_t smem, cudaStream_t stream)
+{
+    // CTAs per norm chunk: ceil(min(out_c, 256) / 64) rounded up to 1, 2 or 4
+    const int w = p.out_c < kNormChunk ? p.out_c : kNormChunk;
+    const int cs = w <= kNCta ? 1 : w <= 2 * kNCta ? 2 : 4;
+    const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
+    // Tiles per CTA: amortise the per-CTA set-up while keeping >= ~8 CTAs per
+    // SM's worth of work in the grid (so the scheduler balances the tail).
+    const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
+    const int64_t ctas_per_tile_row = static_cast<int64_t>(chunks) * cs;
+    int64_t t = n_tiles * ctas_per_tile_row / (148 * 8);
+    OrdParams q = p;
+    q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 8 ? 8 : t);
+    if (cs == 1) return launch_ord<KS, 1>(q, smem, chunks, stream);
+    if (cs == 2) return launch_ord<KS, 2>(q, smem, chunks, stream);
+    return launch_ord<KS, 4>(q, smem, chunks, stream);
+}
+
+}  // namespace
+
+bool conv_tc_ord_supported(int ksize) { return ksize == 1 || ksize == 2; }
+
+size_t conv_tc_ord_wimg_bytes(int in_c, int out_c, int ksize)
+{
+    const int gk_total = (in_c >> 5) * ksize * ksize;
+    const int stages = (gk_total + 1) / 2;
+    return static_cast<size_t>(out_c) * stages * kImgRow;
+}
+
+cudaError_t launch_build_wimg_ord(const uint32_t* w, const int8_t* w_s, int in_c, int out_c, int ksize, uint8_t* img,
+                                  cudaStream_t stream)
+{
+    const int gk_total = (in_c >> 5) * ksize * ksize;
+    const int stages = (gk_total + 1) / 2;
+    const int64_t n = static_cast<int64_t>(out_c) * 2 * stages;
+    build_wimg_ord_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(w, w_s, out_c, gk_total, stages,
+                                                                                     img);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
+                                    uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize,
+                                    int din, int dout, bool act, int* err, cudaStream_t stream)
+{
+    if (!conv_tc_ord_supported(ksize)) return cudaErrorInvalidValue;
+    const int64_t rows = frames * dout * dout;
+    if (rows == 0) return cudaSuccess;
+    OrdParams p;
+    p.in = in; p.in_s = in_s; p.wimg = wimg; p.bias = bias; p.out = out; p.out_s = out_s;
+    p.rows = rows; p.in_c = in_c; p.out_c = out_c; p.din = din; p.dout = dout;
+    p.gk_total = (in_c >> 5) * ksize * ksize;
+    p.stages = (p.gk_total + 1) / 2;
+    p.act = act ? 1 : 0;
+    p.n_max = out_c < kNCta ? out_c : kNCta;
+    p.tiles_per_cta = 1;
+    p.err = err;
+    const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
+    size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * static_cast<size_t>(slot_b) +
+                  (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;
+    // Never let more CTAs share an SM than its 512 TMEM columns can serve.
+    const int max_ctas = static_cast<int>(512u / ord_tmem_cols(p.n_max, p.stages, p.gk_total));
+    const size_t smem_per_sm = 233472;  // 228 KB
+    const size_t floor_smem = smem_per_sm / (max_ctas + 1) + 1;
+    if (smem < floor_smem) smem = floor_smem;
+    return ksize == 1 ? launch_ord_cs<1>(p, smem, stream) : launch_ord_cs<2>(p, smem, stream);
+}
+
+}  // namespace aic

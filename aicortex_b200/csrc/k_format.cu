@@ -335,4 +335,34 @@ cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned
     return cudaGetLastError();
 }
 
+namespace {
+// d = (1 + i / 2^23) * 2^e for every i < 2^23 and the exponents below: counts
+// the d where rcp_rn_ge1 and __frcp_rn differ in any bit.
+__constant__ int kRcpExps[10] = {0, 1, 2, 22, 23, 24, 64, 100, 125, 126};
+__global__ void selftest_rcp_kernel(unsigned long long* mismatches, float* first_bad)
+{
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (1u << 23)) return;
+    for (int k = 0; k < 10; ++k) {
+        const float d = __uint_as_float(((127u + kRcpExps[k]) << 23) | i);
+        if (__float_as_uint(rcp_rn_ge1(d)) != __float_as_uint(__frcp_rn(d))) {
+            if (atomicAdd(mismatches, 1ull) == 0ull) *first_bad = d;
+        }
+    }
+    if (i == 0) {  // the clamped top of the range
+        const float top[3] = {3.40282347e38f, __uint_as_float(0x7F800000u), 1.7e38f};
+        for (int k = 0; k < 3; ++k)
+            if (__float_as_uint(rcp_rn_ge1(top[k])) != __float_as_uint(__frcp_rn(top[k]))) {
+                if (atomicAdd(mismatches, 1ull) == 0ull) *first_bad = top[k];
+            }
+    }
+}
+}  // namespace
+
+cudaError_t launch_selftest_rcp(unsigned long long* mismatches, float* first_bad, cudaStream_t stream)
+{
+    selftest_rcp_kernel<<<(1u << 23) / 256, 256, 0, stream>>>(mismatches, first_bad);
+    return cudaGetLastError();
+}
+
 }  // namespace aic

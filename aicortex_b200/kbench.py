@@ -49,6 +49,7 @@ def main(argv=None) -> None:
     ap.add_argument("--frames", type=int, default=2048)
     ap.add_argument("--act", action="store_true")
     ap.add_argument("--exact", action="store_true", help="reference-order CUDA-core kernel")
+    ap.add_argument("--mode", choices=["ordered", "fast", "simt"], default="ordered", help="conv mode")
     ap.add_argument("--d-model", type=int, default=256)
     ap.add_argument("--d-state", type=int, default=512)
     ap.add_argument("--batch", type=int, default=256)
@@ -74,6 +75,7 @@ def main(argv=None) -> None:
         xw, xs = L.pack_f32(x)
         del x
         ow, os_ = L.empty_f(a.frames * dout * dout, cout, dev)
+        layer.set_mode({"ordered": 0, "fast": 1, "simt": 2}[a.mode])
         fwd = layer.forward_exact if a.exact else layer.forward
         ms = _time(lambda: fwd(xw, xs, ow, os_, a.frames), a.iters, a.warmup)
         rows = a.frames * dout * dout

@@ -122,6 +122,11 @@ class ConvLayer(_Handle):
     def forward(self, x, x_s, out, out_s, frames: int, stream=None) -> None:
         call("aic_conv_layer_forward", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames), _stream(stream))
 
+    def set_mode(self, mode: int) -> None:
+        """AIC_CONV_ORDERED (default, tensor cores, reference order), AIC_CONV_FAST
+        (tensor cores, MMA summation order) or AIC_CONV_SIMT (CUDA cores, reference order)."""
+        call("aic_conv_layer_set_mode", self.h, int(mode))
+
     def forward_exact(self, x, x_s, out, out_s, frames: int, stream=None) -> None:
         """Reference accumulation order on CUDA cores (bit-exact with the reference)."""
         call("aic_conv_layer_forward_exact", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames),
@@ -416,8 +421,14 @@ class Cortex(_Handle):
         call("aic_cortex_reset_state", self.h, _stream(stream))
 
     def set_exact(self, exact: bool) -> None:
-        """Reference accumulation order for every quantized conv (bit-identical to the reference)."""
+        """True: every quantized conv on CUDA cores with the reference kernels' structure
+        (AIC_CONV_SIMT); False: the default AIC_CONV_ORDERED. Both are bit-identical to
+        the reference."""
         call("aic_cortex_set_exact", self.h, int(exact))
+
+    def set_conv_mode(self, mode: int) -> None:
+        """AIC_CONV_ORDERED (default), AIC_CONV_FAST or AIC_CONV_SIMT for every conv layer."""
+        call("aic_cortex_set_conv_mode", self.h, int(mode))
 
     def workspace_bytes(self, batch: int, seq: int) -> int:
         nb = _size_out()

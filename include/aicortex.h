@@ -106,6 +106,12 @@ AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t f
  * column FFT overwrites its own input; here those reads see zeros and the
  * column results go to a separate buffer. workspace: aic_audio_workspace_bytes. */
 AIC_API aic_status aic_audio_workspace_bytes(size_t* bytes);
+
+/* Numerics self-test of the library's reciprocal (the sigmoid's 1/(1+e)):
+ * counts, into the device word *mismatches (zeroed by the caller), the inputs
+ * d >= 1 over every significand of ten binades where it differs from the IEEE
+ * round-to-nearest reciprocal __frcp_rn; *first_bad (device) gets one such d. */
+AIC_API aic_status aic_selftest_rcp(uint64_t* mismatches, float* first_bad, void* stream);
 AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int dim, int first_channel,
                                       void* workspace, void* stream);
 
@@ -142,15 +148,29 @@ AIC_API aic_status aic_conv_layer_load_weights(aic_conv_layer l, const float* ma
 /* ConvLayer::loadFromFile (conv_layer.h:31-44): raw little-endian fp32
  * master weights then fp32 bias. Host-side file read + pack. */
 AIC_API aic_status aic_conv_layer_load_file_sync(aic_conv_layer l, const char* path, void* stream);
-/* ConvLayer::forward (conv_layer.h:102-149) over `frames` frames. */
+/* ConvLayer::forward (conv_layer.h:102-149) over `frames` frames, in the
+ * layer's conv mode (aic_conv_layer_set_mode; default AIC_CONV_ORDERED). */
 AIC_API aic_status aic_conv_layer_forward(aic_conv_layer l, const uint32_t* in, const int8_t* in_s, uint32_t* out,
                                           int8_t* out_s, int64_t frames, void* stream);
-/* The same conv on CUDA cores in the reference kernels' exact accumulation
- * order (convPointwiseFwdKernel / convDenseFwdKernel / convDepthwiseFwdKernel):
- * bit-identical to the reference, slower than aic_conv_layer_forward, whose
- * tensor-core sums differ in fp32 summation order only. */
+/* The same conv on CUDA cores with the reference kernels' structure
+ * (convPointwiseFwdKernel / convDenseFwdKernel / convDepthwiseFwdKernel),
+ * whatever the layer's mode: bit-identical to the reference. */
 AIC_API aic_status aic_conv_layer_forward_exact(aic_conv_layer l, const uint32_t* in, const int8_t* in_s,
                                                 uint32_t* out, int8_t* out_s, int64_t frames, void* stream);
+/* Arithmetic of the pointwise and dense convs (depthwise convs always run on
+ * CUDA cores in the reference order):
+ *   AIC_CONV_ORDERED (default) tensor cores compute the exact integer group
+ *       dots; the fp32 accumulation over groups follows the reference order,
+ *       so outputs are bit-identical to the reference (the 4x4 dense conv
+ *       runs as AIC_CONV_SIMT);
+ *   AIC_CONV_FAST  tensor cores accumulate all of K in fp32 in MMA order;
+ *       equal to the reference up to fp32 summation order (a requant code
+ *       flips only where a value sits on a rounding boundary);
+ *   AIC_CONV_SIMT  CUDA cores, reference order (bit-identical). */
+#define AIC_CONV_ORDERED 0
+#define AIC_CONV_FAST 1
+#define AIC_CONV_SIMT 2
+AIC_API aic_status aic_conv_layer_set_mode(aic_conv_layer l, int mode);
 AIC_API aic_status aic_conv_layer_destroy(aic_conv_layer l);
 
 /* ------------------------------------------------------------------------
@@ -338,9 +358,9 @@ AIC_API aic_status aic_cortex_forward(aic_cortex c, const uint16_t* planes, int 
 AIC_API aic_status aic_cortex_host_workspace_bytes(aic_cortex c, int batch, int seq, size_t* bytes);
 AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_host, int batch, int seq,
                                            float* actor_host, float* critic_host, void* workspace, void* stream);
-/* exact != 0: run every quantized conv in the reference kernels' accumulation
- * order on CUDA cores (bit-identical to the reference, slower); 0 (default):
- * tensor cores, whose fp32 sums differ in summation order only. */
+/* Conv mode (AIC_CONV_*) of every conv layer of the cortex. */
+AIC_API aic_status aic_cortex_set_conv_mode(aic_cortex c, int mode);
+/* exact != 0: AIC_CONV_SIMT; 0: AIC_CONV_ORDERED (the default). */
 AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact);
 /* Number of kernel launches the last forward issued. */
 AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches);

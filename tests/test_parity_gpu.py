@@ -108,12 +108,13 @@ def test_golden_conv(golden, case):
     assert S.sha(u32(pw)) == str(g["w_sha"]) and S.sha(h(ps)) == str(g["s_sha"]), "weights differ from the reference pack"
     ow, os_ = A.empty_f(dout * dout, cout)
     layer.forward_exact(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
-    assert_f_equal(ow, h(os_), g["out_w"], g["out_s"], case + " (reference order)")
-    layer.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
-    if k > 1 and k % 2 == 1:
-        assert_f_equal(ow, h(os_), g["out_w"], g["out_s"], case)
-    else:  # tensor-core sums: fp32 summation order differs
-        assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=2e-3, what=case + " (tcgen05)")
+    assert_f_equal(ow, h(os_), g["out_w"], g["out_s"], case + " (CUDA cores)")
+    layer.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)  # default: AIC_CONV_ORDERED
+    assert_f_equal(ow, h(os_), g["out_w"], g["out_s"], case + " (tensor cores, reference order)")
+    if not (k > 1 and k % 2 == 1):
+        layer.set_mode(A.AIC_CONV_FAST)  # fp32 summation order of the MMA
+        layer.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
+        assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=2e-3, what=case + " (tensor cores, fast)")
     assert_no_device_error()
 
 
@@ -180,9 +181,12 @@ def test_golden_conv_block(golden):
         blk.layers[i].load_weights(t(masters[i]), t(biases[i]))
     ow, os_ = A.empty_f(dout * dout, cout)
     blk.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
-    # pw1/pw2/shortcut run on the tensor cores; a code flip in an intermediate
-    # tensor propagates, so the block output is compared with a flip budget
-    assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=5e-3, what="conv block")
+    assert_f_equal(ow, h(os_), g["out_w"], g["out_s"], "conv block")
+    for lay in blk.layers:
+        lay.set_mode(A.AIC_CONV_FAST)
+    blk.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1)
+    # a code flip in an intermediate tensor propagates: flip budget
+    assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=5e-3, what="conv block (fast)")
 
 
 def test_golden_critic(golden):
@@ -263,16 +267,16 @@ def test_batched_scan_vs_oracle():
 def test_cortex_small_vs_oracle():
     """Full forward (stem -> 4 blocks -> GAP -> 4 Mamba units -> actor, critic).
 
-    Reference-order mode: every kernel keeps the reference's arithmetic order,
-    so the only differences from the oracle are libm vs fast-math intrinsics
-    (rare code flips): features, actor and critic within 1e-3.
-    Tensor-core mode (the default and the benchmarked path): a pointwise or
-    shortcut conv's fp32 sum differs from the reference order in the last bits,
-    which flips a requant code at a rounding boundary at a rate of ~1e-3 per
-    layer (tests above); the flips propagate through the following quantized
-    layers, so end to end each output is compared with the reference-order run
-    statistically: mean absolute error below 0.2 of the mean magnitude and a
-    correlation above 0.95."""
+    AIC_CONV_SIMT and AIC_CONV_ORDERED (the default) both keep the reference's
+    arithmetic order in every kernel: they agree bit for bit with each other,
+    and with the oracle up to libm vs fast-math intrinsics (rare code flips):
+    features, actor and critic within 1e-3.
+    AIC_CONV_FAST: a pointwise or shortcut conv's fp32 sum differs from the
+    reference order in the last bits, which flips a requant code at a rounding
+    boundary at a rate of ~1e-4 per layer; the flips propagate through the
+    following quantized layers, so end to end only the pooled features are
+    compared, statistically (mean error below 0.2 of the mean magnitude,
+    correlation above 0.95)."""
     import oracle as O
     B, T, dim = 2, 3, 32
     desc = W.cortex_desc(batch_chunk=4, d_state=64, critic_units=64, dim=dim)
@@ -291,39 +295,44 @@ def test_cortex_small_vs_oracle():
     geo = W.cfg2_blocks(dim)
     a_ref, c_ref, (frw, frs) = O.cortex_forward(wts, planes, B, T, geo, 256, 64, 64, 64)
     outs = {}
-    for exact in (True, False):
-        cx.set_exact(exact)
+    for mode in (A.AIC_CONV_SIMT, A.AIC_CONV_ORDERED, A.AIC_CONV_FAST):
+        cx.set_conv_mode(mode)
         cx.reset()
         actor = torch.empty(B * T, 64, dtype=torch.float32, device=DEV)
         critic = torch.empty(B * T, dtype=torch.float32, device=DEV)
         fw, fs = A.empty_f(B * T, 256)
         n = cx.forward(t(planes), B, T, actor, critic, features=(fw, fs))
         assert n > 20
-        outs[exact] = (u32(fw), h(fs), h(actor), h(critic))
-    fw, fs, actor, critic = outs[True]
+        outs[mode] = (u32(fw), h(fs), h(actor), h(critic))
+    fw, fs, actor, critic = outs[A.AIC_CONV_SIMT]
     assert_f_close(fw, fs, frw, frs, flip_rate=1e-2, what="features (reference order)")
     assert_close(actor, a_ref, rtol=1e-3, what="actor (reference order)")
     assert_close(critic, c_ref, rtol=1e-3, what="critic (reference order)")
-    fw2, fs2, actor2, critic2 = outs[False]
-    fv, rv = fmt.dequant(fw2, fs2), fmt.dequant(fw, fs)
-    for name, a, r in (("features", fv, rv), ("actor", actor2, actor), ("critic", critic2, critic)):
-        a, r = np.asarray(a, np.float64).ravel(), np.asarray(r, np.float64).ravel()
-        rel = np.abs(a - r).mean() / np.abs(r).mean()
-        corr = np.corrcoef(a, r)[0, 1]
-        assert rel < 0.2 and corr > 0.95, f"{name} (tensor cores): mean error {rel:.3e}, correlation {corr:.4f}"
+    for x, y, name in zip(outs[A.AIC_CONV_ORDERED], outs[A.AIC_CONV_SIMT], ("words", "exponents", "actor", "critic")):
+        assert np.array_equal(x, y), f"tensor cores (reference order) vs CUDA cores: {name} differ"
+    fw2, fs2 = outs[A.AIC_CONV_FAST][:2]
+    a, r = fmt.dequant(fw2, fs2).astype(np.float64).ravel(), fmt.dequant(fw, fs).astype(np.float64).ravel()
+    rel = np.abs(a - r).mean() / np.abs(r).mean()
+    corr = np.corrcoef(a, r)[0, 1]
+    assert rel < 0.2 and corr > 0.95, f"features (fast): mean error {rel:.3e}, correlation {corr:.4f}"
+    assert_no_device_error()
 
 
 @pytest.mark.parametrize("geo", [
     (64, 128, 1, 1, 24, 24, 1),     # 576 rows: 4 full tiles + a partial one
-    (256, 512, 1, 1, 16, 16, 1),    # two 256-channel norm chunks
-    (512, 288, 1, 1, 12, 12, 0),    # 8 K stages, chunks of 256 and 32
+    (256, 512, 1, 1, 16, 16, 1),    # two 256-channel norm chunks (two CTA pairs)
+    (512, 288, 1, 1, 12, 12, 0),    # chunks of 256 and 32 (a pair with an empty CTA)
     (32, 64, 1, 1, 16, 16, 0),      # K = 32: one half-filled stage
-    (128, 256, 2, 2, 32, 16, 0),    # shortcut conv 2x2 / stride 2
+    (96, 96, 1, 1, 16, 16, 1),      # 96-channel tile
+    (128, 256, 2, 2, 32, 16, 0),    # shortcut conv 2x2 / stride 2, one CTA pair
     (32, 64, 4, 4, 64, 16, 0),      # patcher conv 4x4 / stride 4
     (160, 96, 2, 2, 16, 8, 1),
+    (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps
+    (32, 64, 2, 2, 32, 16, 1),      # one group per tap
 ])
 def test_tensor_core_conv_vs_reference_order(geo):
-    """tcgen05 conv vs the reference-order CUDA-core kernel on several tiles."""
+    """tcgen05 convs vs the CUDA-core kernel with the reference's structure:
+    AIC_CONV_ORDERED bit-identical, AIC_CONV_FAST within the flip bound."""
     cin, cout, k, st, din, dout, act = geo
     rng = np.random.default_rng(cin * 7 + cout)
     frames = 2
@@ -335,11 +344,14 @@ def test_tensor_core_conv_vs_reference_order(geo):
     rows = frames * dout * dout
     ow, os_ = A.empty_f(rows, cout)
     ew, es = A.empty_f(rows, cout)
-    layer.forward(xw, xs, ow, os_, frames)
     layer.forward_exact(xw, xs, ew, es, frames)
+    layer.forward(xw, xs, ow, os_, frames)
+    assert_f_equal(ow, h(os_), u32(ew), h(es), f"ordered vs CUDA cores {geo}")
+    layer.set_mode(A.AIC_CONV_FAST)
+    layer.forward(xw, xs, ow, os_, frames)
     # fp32 summation order only: a code flips where the value sits within a
     # few ulp of a rounding boundary
-    assert_f_close(ow, h(os_), ew, h(es), flip_rate=1e-4, what=f"tc vs exact {geo}")
+    assert_f_close(ow, h(os_), ew, h(es), flip_rate=1e-4, what=f"fast vs CUDA cores {geo}")
     assert_no_device_error()
 
 
@@ -398,3 +410,14 @@ def test_cortex_forward_is_deterministic():
         outs.append((h(actor), h(critic)))
     np.testing.assert_array_equal(outs[0][0], outs[1][0])
     np.testing.assert_array_equal(outs[0][1], outs[1][1])
+
+
+def test_reciprocal_matches_ieee():
+    """The sigmoid's reciprocal (one FMA Newton step from rcp.approx) equals the
+    IEEE round-to-nearest reciprocal __frcp_rn of the reference for every
+    significand of ten binades from 1 to 2^126, and at the clamped top."""
+    bad = torch.zeros(1, dtype=torch.int64, device=DEV)
+    first = torch.zeros(1, dtype=torch.float32, device=DEV)
+    A._lib.call("aic_selftest_rcp", C.c_void_p(bad.data_ptr()), C.c_void_p(first.data_ptr()),
+                C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert int(h(bad)[0]) == 0, f"{int(h(bad)[0])} mismatches, e.g. d = {float(h(first)[0])!r}"
