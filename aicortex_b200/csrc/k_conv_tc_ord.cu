@@ -147,9 +147,9 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     // same tiles for every CTA of a cluster, which therefore run in lockstep).
     const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
     const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
-    const int64_t my_tiles = tile0 < n_tiles ? min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0) : 0;
+    const int my_tiles = tile0 < n_tiles ? static_cast<int>(min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0)) : 0;
     const int S = p.stages;
-    const int64_t total = my_tiles * S;
+    const int total = my_tiles * S;
 
     const int prow = tid & (kBM - 1), pg = tid >> 7;  // producer: (row, group of the stage)
     const int G = p.in_c >> 5;
@@ -170,30 +170,39 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
     for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
 
+    // Per-buffer addresses of the chain: units of the stage's two groups, unit(s_in)
+    // of this thread's row, and this warp's TMEM accumulator columns.
+    const float* units0 = reinterpret_cast<const float*>(b_tiles + n_cta * 128) + 32 * hw;
+    const float* units1 = reinterpret_cast<const float*>(b_tiles + slot_b + n_cta * 128) + 32 * hw;
+    int ctap_g = 0;  // position within its tap of the next group the chain consumes
+
     // fmaf chain over the groups of global stage gc (stage sc of its tile)
-    auto chain = [&](int64_t gc, int sc) -> bool {
-        const int buf = static_cast<int>(gc & 1);
+    auto chain = [&](int gc, int sc) -> bool {
+        const int buf = gc & 1;
         if (!mbar_wait(smem_addr(&bars[2 + buf]), static_cast<uint32_t>(gc >> 1) & 1u, p.err, 12)) return false;
         tc_fence_after();
-        const float* units = reinterpret_cast<const float*>(b_tiles + buf * slot_b + n_cta * 128);
+        const float* units = buf ? units1 : units0;
+        const float* dins = din_s + buf * 2 * kBM + erow;
+        const uint32_t tb = tl + static_cast<uint32_t>(buf * 2 * n_cta);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int gk = 2 * sc + j;
             if (gk >= GK) break;
-            if (KS == 2 && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
+            if (KS == 2 && gk > 0 && ctap_g == 0) {  // a tap's chain ends: fold it, start the next from 0
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
                     acc[i] = 0.0f;
                 }
             }
+            if (KS == 2 && ++ctap_g == G) ctap_g = 0;
             if (has_cols) {
-                const float du = din_s[(buf * 2 + j) * kBM + erow];
-                const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta + 32 * hw);
+                const float du = dins[j * kBM];
+                const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta);
 #pragma unroll
                 for (int h16 = 0; h16 < 2; ++h16) {
                     float pv[16];
-                    tmem_ld16(tl + static_cast<uint32_t>((buf * 2 + j) * n_cta + 16 * h16), pv);
+                    tmem_ld16(tb + static_cast<uint32_t>(j * n_cta + 16 * h16), pv);
 #pragma unroll
                     for (int i4 = 0; i4 < 4; ++i4) {
                         const float4 u = u4[4 * h16 + i4];
@@ -217,11 +226,28 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     bool ok = true;  // this thread's chain of the current tile completed
     // producer position (stage sp of local tile tp) and consumer position
     // (stage sc of local tile tc) advance by one stage per iteration
-    int sp = 0, sc = 0;
-    int64_t tp = 0, tc = 0;
+    int sp = 0, sc = 0, tp = 0, tc = 0;
     const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
-    for (int64_t gs = 0; gs <= total; ++gs) {
-        const int buf = static_cast<int>(gs & 1);
+    // This thread's A group of the next stage to produce, loaded one stage
+    // ahead so the global-memory latency overlaps the chain and epilogue. Its
+    // tap and position within the tap advance by two groups per stage.
+    const int tap0 = pg >= G ? 1 : 0, g0 = pg - tap0 * G;
+    int p_tap = tap0, p_g = g0;
+    uint4 pf_words = make_uint4(0u, 0u, 0u, 0u);
+    int8_t pf_s = 0;
+    bool pf_ok = false;
+    auto prefetch = [&](int t_local) {
+        const int64_t row = (tile0 + t_local) * kBM + prow;
+        pf_ok = live && row < p.rows && p_tap < KS * KS;
+        if (pf_ok) {
+            const int64_t gi = tap_pixel_pow2(row, p_tap, KS, lg_din, lg_dout) * G + p_g;
+            pf_words = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
+            pf_s = __ldg(p.in_s + gi);
+        }
+    };
+    if (total > 0) prefetch(0);
+    for (int gs = 0; gs <= total; ++gs) {
+        const int buf = gs & 1;
         __syncthreads();  // stage gs-2's chain is done with this buffer's units and accumulators
         const bool run = live && !*abort_flag;
         const bool produce = run && gs < total;
@@ -236,20 +262,30 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
                 bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(sp) * stage_bytes,
                          static_cast<uint32_t>(stage_bytes), smem_addr(&bars[buf]));
             }
-            const int64_t row_p = (tile0 + tp) * kBM + prow;
-            const int gk = 2 * sp + pg;
             float du = 0.0f;
-            if (row_p < p.rows && gk < GK) {
-                const int tap = gk / G, g = gk - tap * G;
-                const int64_t pix = tap_pixel_pow2(row_p, tap, KS, lg_din, lg_dout);
-                const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
-                du = unit_of(__ldg(p.in_s + pix * G + g));
-                stage_group_f(a_tile, prow, pg, words, 1.0f);
+            if (pf_ok) {
+                du = unit_of(pf_s);
+                stage_group_f(a_tile, prow, pg, pf_words, 1.0f);
             } else {
                 stage_zero(a_tile, prow, pg);
             }
             din_s[(buf * 2 + pg) * kBM + prow] = du;
             fence_async_smem();
+            // the stage after this one
+            if (gs + 1 < total) {
+                if (sp + 1 == S) {
+                    p_tap = tap0;
+                    p_g = g0;
+                    prefetch(tp + 1);
+                } else {
+                    p_g += 2;
+                    while (p_g >= G) {
+                        p_g -= G;
+                        ++p_tap;
+                    }
+                    prefetch(tp);
+                }
+            }
         }
         tc_fence_before();
         __syncthreads();
@@ -275,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             ++tp;
         }
         if (gs == 0) continue;
-        const int64_t gc = gs - 1;
+        const int gc = gs - 1;
         const int sc_now = sc;
         if (++sc == S) sc = 0;
         if (run && ok) {
@@ -348,6 +384,232 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         // every MMA this CTA issued has completed before TMEM is released
         if (tid == 0) mma_commit(smem_addr(&bars[4]));
         if (warp == 0) mbar_wait(smem_addr(&bars[4]), 0u, p.err, 13);
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_fence_after();
+            tmem_dealloc(tmem, ncols);
+        }
+    }
+}
+
+// ---- chain at the end: every group's dot products resident in TMEM --------
+//
+// For up to four 32-element groups per output (k^2 * in_c <= 128) all the
+// per-group accumulators of a tile fit in TMEM (groups x width <= 256
+// columns, two CTAs per SM). The stage loop then only stages A and issues
+// MMAs (group g into TMEM slice g), and the epilogue runs the reference's
+// fmaf chain over the groups one 32-channel group of columns at a time, so a
+// thread's chain state is transient: pass 1 folds the chain, square-sums the
+// group and parks the pre-norm sums back in TMEM slice 0; pass 2 normalises,
+// activates and packs. Tiles are 128 rows x W channels, W = 128 for up to two
+// groups and 64 otherwise; the CTAs of one RMSNorm chunk form a cluster as in
+// the streaming kernel. One tile per CTA.
+constexpr int kCaeMaxGroups = 4;
+
+template <int KS, int CS, bool ACT, int W>
+__global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_cae_kernel(OrdParams p)
+{
+    constexpr int kChunks = W / kNCta;  // 64-channel image chunks per CTA
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * W;
+    const int n_cta = min(W, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
+    const bool live = n_cta > 0;
+    const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
+    uint8_t* a_tiles = base;                                    // [2][kTileA]
+    uint8_t* b_codes = base + 2 * kTileA;                       // [S][W][128 B]
+    float* b_units = reinterpret_cast<float*>(b_codes + 2 * W * 128);  // [S][2][W]
+    float* din_s = b_units + 2 * 2 * W;                         // [kCaeMaxGroups][kBM] unit(s_in)
+    float* bias_s = din_s + kCaeMaxGroups * kBM;                // [W]
+    float* part = bias_s + W;                                   // [8][kBM]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 8 * kBM);  // 0: B; 1,2: A slot free; 3: acc ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int need = GK * (n_cta > 0 ? n_cta : 0);
+    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
+    for (int i = tid; i < 8 * kBM; i += kThreads) part[i] = 0.0f;
+    if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
+    if (tid == 0) {
+        for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&bars[i]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (live && warp == 0) tmem_alloc(smem_addr(tmem_slot), ncols);
+    tc_fence_before();
+    __syncthreads();
+    if (CS > 1) cluster_sync_all();  // every peer's `part` is initialised before any remote store
+    tc_fence_after();
+    const uint32_t tmem = live ? *tmem_slot : 0u;
+
+    // All stages' weights, once: per 64-channel chunk the codes, then the units
+    // of group 0 and group 1 (image layout of build_wimg_ord_kernel).
+    if (live && tid == 0) {
+        mbar_expect_tx(smem_addr(&bars[0]), static_cast<uint32_t>(S * n_cta * kImgRow));
+        for (int st = 0; st < S; ++st) {
+            for (int c = 0; c < kChunks; ++c) {
+                const int cn0 = n0 + c * kNCta;
+                const int n_c = min(kNCta, p.out_c - cn0);
+                if (n_c <= 0) break;
+                const uint8_t* img = p.wimg + (static_cast<int64_t>(cn0) * S + static_cast<int64_t>(st) * n_c) * kImgRow;
+                bulk_g2s(smem_addr(b_codes + (st * W + c * kNCta) * 128), img, static_cast<uint32_t>(n_c * 128),
+                         smem_addr(&bars[0]));
+                for (int j = 0; j < 2; ++j)
+                    bulk_g2s(smem_addr(b_units + (st * 2 + j) * W + c * kNCta), img + n_c * 128 + j * n_c * 4,
+                             static_cast<uint32_t>(n_c * 4), smem_addr(&bars[0]));
+            }
+        }
+    }
+
+    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
+    const int prow = tid & (kBM - 1), pg = tid >> 7;
+    const int64_t prow_g = m0 + prow;
+    const bool prow_ok = prow_g < p.rows;
+    const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
+    const uint32_t idesc = instr_desc(n_cta);
+
+    for (int st = 0; live && st < S; ++st) {
+        const int buf = st & 1;
+        uint8_t* a_tile = a_tiles + buf * kTileA;
+        if (st >= 2 && !*abort_flag) {
+            if (!mbar_wait(smem_addr(&bars[1 + buf]), 0u, p.err, 21)) *abort_flag = 1;
+        }
+        __syncthreads();
+        if (*abort_flag) break;
+        const int gk = 2 * st + pg;
+        float du = 0.0f;
+        if (prow_ok && gk < GK) {
+            const int tap = gk / G, g = gk - tap * G;
+            const int64_t pix = tap_pixel_pow2(prow_g, tap, KS, lg_din, lg_dout);
+            const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
+            du = unit_of(__ldg(p.in_s + pix * G + g));
+            stage_group_f(a_tile, prow, pg, words, 1.0f);
+        } else {
+            stage_zero(a_tile, prow, pg);
+        }
+        if (gk < GK) din_s[gk * kBM + prow] = du;
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            if (st > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 22)) {
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_codes + st * W * 128);
+                const int n_mma = 2 * st + 1 < GK ? kBK / 16 : kBK / 32;
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)
+                    if (j < n_mma)
+                        mma_bf16(tmem + static_cast<uint32_t>((2 * st + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
+                                 smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
+                mma_commit(smem_addr(&bars[1 + buf]));
+            } else {
+                *abort_flag = 1;
+            }
+        }
+    }
+    if (live && tid == 0) mma_commit(smem_addr(&bars[3]));
+    __syncthreads();
+    bool ok = live && !*abort_flag;
+    if (live) {
+        if (!mbar_wait(smem_addr(&bars[3]), 0u, p.err, 23)) ok = false;
+        tc_fence_after();
+    }
+
+    // Pass 1: chain, tap fold and square-sum per 32-channel group; the
+    // pre-norm sums go back to TMEM slice 0.
+    const int q = warp & 3, hw = warp >> 2;
+    const int erow = q * 32 + lane;
+    const int ngroups = n_cta >> 5;
+    const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const int gbase = (n0 & (kNormChunk - 1)) >> 5;
+    if (ok) {
+        for (int cg = hw; cg < ngroups; cg += 2) {
+            float acc[32], sacc[KS == 1 ? 1 : 32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
+            for (int g = 0; g < GK; ++g) {
+                if (KS == 2 && g > 0 && g % G == 0) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+                        acc[i] = 0.0f;
+                    }
+                }
+                const float du = din_s[g * kBM + erow];
+                const float4* u4 = reinterpret_cast<const float4*>(b_units + ((g >> 1) * 2 + (g & 1)) * W + 32 * cg);
+#pragma unroll
+                for (int h16 = 0; h16 < 2; ++h16) {
+                    float pv[16];
+                    tmem_ld16(tl + static_cast<uint32_t>(g * n_cta + 32 * cg + 16 * h16), pv);
+#pragma unroll
+                    for (int i4 = 0; i4 < 4; ++i4) {
+                        const float4 u = u4[4 * h16 + i4];
+                        const int b = 16 * h16 + 4 * i4;
+                        acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
+                        acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
+                        acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
+                        acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
+                    }
+                }
+            }
+            if (KS == 2) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+            }
+            const float gs2 = tree_sq32(acc);
+            float* dst = &part[(gbase + cg) * kBM + erow];
+            if (CS > 1) {
+#pragma unroll
+                for (int r = 0; r < CS; ++r) st_peer_f32(smem_addr(dst), static_cast<uint32_t>(r), gs2);
+            } else {
+                *dst = gs2;
+            }
+            tmem_st32(tl + static_cast<uint32_t>(32 * cg), acc);
+        }
+    }
+    __syncthreads();
+    if (CS > 1) cluster_sync_all();
+    // Pass 2: the reference's cross-warp butterfly over the chunk's 8 group
+    // sums (kernels.h:271-276), then bias, activation and requant.
+    if (ok) {
+        float w8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w8[i] = part[i * kBM + erow];
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+            for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
+        const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+        const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
+        const int64_t row = m0 + erow;
+        for (int cg = hw; cg < ngroups; cg += 2) {
+            float v[32];
+            tmem_ld32(tl + static_cast<uint32_t>(32 * cg), v);
+            const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * cg);
+#pragma unroll
+            for (int i4 = 0; i4 < 8; ++i4) {
+                const float4 b = b4[i4];
+                const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float x = fmaf(v[4 * i4 + k], sc_norm, bb[k]);
+                    v[4 * i4 + k] = ACT ? silu_f(x) : x;
+                }
+            }
+            uint4 words;
+            int8_t e;
+            quantize_group(v, &words, &e);
+            if (row < p.rows) {
+                const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + cg;
+                reinterpret_cast<uint4*>(p.out)[gi] = words;
+                p.out_s[gi] = e;
+            }
+        }
+    }
+    if (live) {
         tc_fence_before();
         __syncthreads();
         if (warp == 0) {
@@ -452,6 +714,54 @@ cudaError_t launch_build_wimg_ord(const uint32_t* w, const int8_t* w_s, int in_c
     return cudaGetLastError();
 }
 
+template <int KS, int CS, int W>
+cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
+{
+    auto kern = p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W> : conv_gemm_tc_cae_kernel<KS, CS, false, W>;
+    size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * W * 128 + 2 * 2 * W * 4 +
+                  (kCaeMaxGroups * kBM + W + 8 * kBM) * sizeof(float) + 4 * 8 + 16;
+    // Never let more CTAs share an SM than its 512 TMEM columns can serve.
+    const int need = p.gk_total * (p.out_c < W ? p.out_c : W);
+    const int tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+    const size_t floor_smem = 233472 / (512 / tmem_cols + 1) + 1;
+    if (smem < floor_smem) smem = floor_smem;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = CS;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CS > 1 ? 1 : 0;
+    cfg.gridDim = dim3(static_cast<unsigned>((p.rows + kBM - 1) / kBM), chunks * CS, 1);
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+// Chain-at-end dispatch: W = 128 for up to two groups, else 64; CS CTAs per
+// norm chunk.
+template <int KS>
+cudaError_t launch_cae_w(const OrdParams& p, cudaStream_t stream)
+{
+    const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
+    const int w = p.out_c < kNormChunk ? p.out_c : kNormChunk;
+    if (p.gk_total <= 2) {
+        if (w <= 128) return launch_cae<KS, 1, 128>(p, chunks, stream);
+        return launch_cae<KS, 2, 128>(p, chunks, stream);
+    }
+    if (w <= 64) return launch_cae<KS, 1, 64>(p, chunks, stream);
+    if (w <= 128) return launch_cae<KS, 2, 64>(p, chunks, stream);
+    return launch_cae<KS, 4, 64>(p, chunks, stream);
+}
+
 cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
                                     uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize,
                                     int din, int dout, bool act, int* err, cudaStream_t stream)
@@ -468,6 +778,10 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     p.n_max = out_c < kNCta ? out_c : kNCta;
     p.tiles_per_cta = 1;
     p.err = err;
+    // measured: the chain at the end wins with one or two groups per output,
+    // the streaming kernel from three on
+    if (p.gk_total <= 2)
+        return ksize == 1 ? launch_cae_w<1>(p, stream) : launch_cae_w<2>(p, stream);
     const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * static_cast<size_t>(slot_b) +
                   (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;
