@@ -27,6 +27,11 @@ cudaError_t launch_dw_weights(const uint32_t* w, const int8_t* w_s, int64_t n, f
 cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
                            int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
                            cudaStream_t stream);
+// The same conv with one thread per (output pixel, 8 channels) and no tiling
+// (strides other than 1 and 2; the reference-structure cross-check).
+cudaError_t launch_conv_dw_direct(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias,
+                                  uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din,
+                                  int Dout, cudaStream_t stream);
 
 // A3/A4 on CUDA cores: quantized conv (pointwise when ksize == 1) with the fused
 // RMSNorm(256-chunk) + bias (+SiLU) + requant epilogue; reproduces the

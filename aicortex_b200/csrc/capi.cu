@@ -290,7 +290,7 @@ struct ConvLayer {
         if (frames == 0) return;
         require(in && in_s && out && out_s, "null tensor");
         if (is_dw)
-            cuda_ok(launch_conv_dw(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
+            cuda_ok(launch_conv_dw_direct(in, in_s, wf, bias, out, out_s, frames, d.in_channels, d.kernel_size, d.stride,
                                    d.dim_in, d.dim_out, s),
                     "conv_dw");
         else

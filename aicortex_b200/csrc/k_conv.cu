@@ -65,6 +65,107 @@ __global__ void __launch_bounds__(kThreads) conv_dw_kernel(const uint32_t* __res
     if ((j & 3) == 0) out_s[pix * G + g] = ex;
 }
 
+// Depthwise conv, tiled: a CTA computes an 8 x 8 block of output pixels for
+// one 32-channel group. The input block it reads (with the halo) is staged once
+// in shared memory already dequantised, x = code * unit(s_in) (the value the
+// reference forms per tap), with zeros outside the image (the reference's
+// invalid taps contribute fma(0, w, acc)). Thread (channel quad cq, pixel pp)
+// keeps its 4 channels' k*k weights in registers and runs the reference's
+// per-tap chains acc[tap & 3] for pixels pp and pp + 32, then folds them into
+// the bias in order and packs the 32-channel group across 8 lanes. Pixel
+// quads are stored XOR-swizzled so both the staging stores and the tap loads
+// are bank-conflict free.
+template <int K, int S>
+__global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
+                                                               const float* __restrict__ wf, const float* __restrict__ bias,
+                                                               uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
+                                                               int C, int Din, int Dout, int tiles_x)
+{
+    constexpr int kT = 8, kPad = K >> 1, kHin = (kT - 1) * S + K, kWin = kHin;
+    extern __shared__ float4 xs[];  // [kHin * kWin][8] float4, quad q of pixel i at i * 8 + (q ^ (i & 7))
+    const int G = C >> 5;
+    const int g = blockIdx.y;
+    const int tiles_pf = tiles_x * tiles_x;
+    const int64_t frame = blockIdx.x / tiles_pf;
+    const int tin = static_cast<int>(blockIdx.x - frame * tiles_pf);
+    const int ty = tin / tiles_x, tx = tin - ty * tiles_x;
+    const int oy0 = ty * kT, ox0 = tx * kT;
+    const int iy0 = oy0 * S - kPad, ix0 = ox0 * S - kPad;
+    const int64_t fbase = frame * Din * Din;
+
+    for (int i = threadIdx.x; i < kHin * kWin; i += kThreads) {
+        const int ry = i / kWin, rx = i - ry * kWin;
+        const int iy = iy0 + ry, ix = ix0 + rx;
+        float4* dst = xs + i * 8;
+        const int sw = i & 7;
+        if (iy >= 0 && iy < Din && ix >= 0 && ix < Din) {
+            const int64_t pix = fbase + static_cast<int64_t>(iy) * Din + ix;
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(in) + pix * G + g);
+            const float u = unit_of(__ldg(in_s + pix * G + g));
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                dst[(2 * q) ^ sw] = make_float4(code_f(ww[q], 0) * u, code_f(ww[q], 1) * u, code_f(ww[q], 2) * u,
+                                                code_f(ww[q], 3) * u);
+                dst[(2 * q + 1) ^ sw] = make_float4(code_f(ww[q], 4) * u, code_f(ww[q], 5) * u, code_f(ww[q], 6) * u,
+                                                    code_f(ww[q], 7) * u);
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) dst[q] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+    }
+
+    const int cq = threadIdx.x & 7, pp = threadIdx.x >> 3;
+    const int c0 = (g << 5) + 4 * cq;
+    float4 wk[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) wk[k] = __ldg(reinterpret_cast<const float4*>(wf + static_cast<int64_t>(k) * C + c0));
+    const float4 bv = __ldg(reinterpret_cast<const float4*>(bias + c0));
+    __syncthreads();
+
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+        const int pt = pp + 32 * half;
+        const int oy = pt >> 3, ox = pt & 7;
+        float a[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) a[c][e] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < K * K; ++k) {
+            const int ip = (oy * S + k / K) * kWin + ox * S + k % K;
+            const float4 x = xs[ip * 8 + (cq ^ (ip & 7))];
+            a[k & 3][0] = fmaf(x.x, wk[k].x, a[k & 3][0]);
+            a[k & 3][1] = fmaf(x.y, wk[k].y, a[k & 3][1]);
+            a[k & 3][2] = fmaf(x.z, wk[k].z, a[k & 3][2]);
+            a[k & 3][3] = fmaf(x.w, wk[k].w, a[k & 3][3]);
+        }
+        const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = bb[e] + (a[0][e] + a[1][e] + a[2][e] + a[3][e]);
+        // 32-channel group = 8 lanes (cq 0..7) of this pixel
+        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+        const float scale = amax < kEps ? 1.0f : amax;
+        const float inv = kQMax * __frcp_rn(scale);
+        uint32_t h16 = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) h16 |= code_rn_fast(v[e], inv) << (4 * e);
+        const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, h16, 1);
+        const int oyy = oy0 + oy, oxx = ox0 + ox;
+        if (oyy < Dout && oxx < Dout) {
+            const int64_t opix = frame * Dout * Dout + static_cast<int64_t>(oyy) * Dout + oxx;
+            if ((cq & 1) == 0) out[opix * (C >> 3) + 4 * g + (cq >> 1)] = h16 | (other << 16);
+            if (cq == 0) out_s[opix * G + g] = exponent_of(scale);
+        }
+    }
+}
+
 // Dequantised depthwise weights: wf[i] = code(i) * unit(s[i / 32]), the value
 // dequantize_scalar produces for every tap (kernels.h:77, 856-857).
 __global__ void dw_weights_kernel(const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s, int64_t n,
@@ -216,9 +317,40 @@ cudaError_t launch_dw_weights(const uint32_t* w, const int8_t* w_s, int64_t n, f
     return cudaGetLastError();
 }
 
+template <int K, int S>
+cudaError_t launch_dw_tiled(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
+                            int8_t* out_s, int64_t frames, int C, int Din, int Dout, cudaStream_t stream)
+{
+    constexpr int kHin = 7 * S + K;
+    const size_t smem = static_cast<size_t>(kHin) * kHin * 8 * sizeof(float4);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(conv_dw_tiled_kernel<K, S>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem));
+        if (e != cudaSuccess) return e;
+    }
+    const int tiles_x = (Dout + 7) / 8;
+    const dim3 grid(static_cast<unsigned>(frames * tiles_x * tiles_x), static_cast<unsigned>(C >> 5));
+    conv_dw_tiled_kernel<K, S><<<grid, kThreads, smem, stream>>>(in, in_s, wf, bias, out, out_s, C, Din, Dout, tiles_x);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
                            int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din, int Dout,
                            cudaStream_t stream)
+{
+    if (frames == 0) return cudaSuccess;
+    // 3x3 (the stack's kernel) tiled; larger kernels keep k*k weight quads per
+    // thread only at very high register counts, so they run direct
+    if (ksize == 3 && stride == 1)
+        return launch_dw_tiled<3, 1>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+    if (ksize == 3 && stride == 2)
+        return launch_dw_tiled<3, 2>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+    return launch_conv_dw_direct(in, in_s, wf, bias, out, out_s, frames, C, ksize, stride, Din, Dout, stream);
+}
+
+cudaError_t launch_conv_dw_direct(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias,
+                                  uint32_t* out, int8_t* out_s, int64_t frames, int C, int ksize, int stride, int Din,
+                                  int Dout, cudaStream_t stream)
 {
     const int64_t total = frames * Dout * Dout * (C >> 3);
     if (total == 0) return cudaSuccess;

@@ -170,32 +170,25 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
     for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
 
-    // Per-buffer addresses of the chain: units of the stage's two groups, unit(s_in)
-    // of this thread's row, and this warp's TMEM accumulator columns.
-    const float* units0 = reinterpret_cast<const float*>(b_tiles + n_cta * 128) + 32 * hw;
-    const float* units1 = reinterpret_cast<const float*>(b_tiles + slot_b + n_cta * 128) + 32 * hw;
-    int ctap_g = 0;  // position within its tap of the next group the chain consumes
-
     // fmaf chain over the groups of global stage gc (stage sc of its tile)
     auto chain = [&](int gc, int sc) -> bool {
         const int buf = gc & 1;
         if (!mbar_wait(smem_addr(&bars[2 + buf]), static_cast<uint32_t>(gc >> 1) & 1u, p.err, 12)) return false;
         tc_fence_after();
-        const float* units = buf ? units1 : units0;
+        const float* units = reinterpret_cast<const float*>(b_tiles + buf * slot_b + n_cta * 128) + 32 * hw;
         const float* dins = din_s + buf * 2 * kBM + erow;
         const uint32_t tb = tl + static_cast<uint32_t>(buf * 2 * n_cta);
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             const int gk = 2 * sc + j;
             if (gk >= GK) break;
-            if (KS == 2 && gk > 0 && ctap_g == 0) {  // a tap's chain ends: fold it, start the next from 0
+            if (KS == 2 && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
                     acc[i] = 0.0f;
                 }
             }
-            if (KS == 2 && ++ctap_g == G) ctap_g = 0;
             if (has_cols) {
                 const float du = dins[j * kBM];
                 const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta);
@@ -228,24 +221,27 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     // (stage sc of local tile tc) advance by one stage per iteration
     int sp = 0, sc = 0, tp = 0, tc = 0;
     const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
-    // This thread's A group of the next stage to produce, loaded one stage
-    // ahead so the global-memory latency overlaps the chain and epilogue. Its
-    // tap and position within the tap advance by two groups per stage.
-    const int tap0 = pg >= G ? 1 : 0, g0 = pg - tap0 * G;
-    int p_tap = tap0, p_g = g0;
+    // This thread's A group of the next stage to produce (group gk = 2 * s + pg
+    // of its row's im2col), loaded one stage ahead so the global-memory latency
+    // overlaps the chain and epilogue.
     uint4 pf_words = make_uint4(0u, 0u, 0u, 0u);
     int8_t pf_s = 0;
     bool pf_ok = false;
-    auto prefetch = [&](int t_local) {
+    auto prefetch = [&](int t_local, int s_local) {
         const int64_t row = (tile0 + t_local) * kBM + prow;
-        pf_ok = live && row < p.rows && p_tap < KS * KS;
+        const int gk = 2 * s_local + pg;
+        pf_ok = live && row < p.rows && gk < GK;
         if (pf_ok) {
-            const int64_t gi = tap_pixel_pow2(row, p_tap, KS, lg_din, lg_dout) * G + p_g;
+            int64_t gi = row * G + gk;  // pointwise: the row's own pixel, group gk
+            if (KS == 2) {
+                const int tap = gk / G, g = gk - tap * G;
+                gi = tap_pixel_pow2(row, tap, KS, lg_din, lg_dout) * G + g;
+            }
             pf_words = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
             pf_s = __ldg(p.in_s + gi);
         }
     };
-    if (total > 0) prefetch(0);
+    if (total > 0) prefetch(0, 0);
     for (int gs = 0; gs <= total; ++gs) {
         const int buf = gs & 1;
         __syncthreads();  // stage gs-2's chain is done with this buffer's units and accumulators
@@ -273,18 +269,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             fence_async_smem();
             // the stage after this one
             if (gs + 1 < total) {
-                if (sp + 1 == S) {
-                    p_tap = tap0;
-                    p_g = g0;
-                    prefetch(tp + 1);
-                } else {
-                    p_g += 2;
-                    while (p_g >= G) {
-                        p_g -= G;
-                        ++p_tap;
-                    }
-                    prefetch(tp);
-                }
+                if (sp + 1 == S) prefetch(tp + 1, 0);
+                else prefetch(tp, sp + 1);
             }
         }
         tc_fence_before();
@@ -407,8 +393,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 // the streaming kernel. One tile per CTA.
 constexpr int kCaeMaxGroups = 4;
 
-template <int KS, int CS, bool ACT, int W>
-__global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_cae_kernel(OrdParams p)
+template <int KS, int CS, bool ACT, int W, bool ONE>
+__global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel(OrdParams p)
 {
     constexpr int kChunks = W / kNCta;  // 64-channel image chunks per CTA
     extern __shared__ uint8_t smem_raw[];
@@ -717,7 +703,10 @@ cudaError_t launch_build_wimg_ord(const uint32_t* w, const int8_t* w_s, int in_c
 template <int KS, int CS, int W>
 cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
 {
-    auto kern = p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W> : conv_gemm_tc_cae_kernel<KS, CS, false, W>;
+    // a single group per output (K = 32) leaves room for four CTAs per SM
+    auto kern = p.gk_total == 1
+                    ? (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, true> : conv_gemm_tc_cae_kernel<KS, CS, false, W, true>)
+                    : (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, false> : conv_gemm_tc_cae_kernel<KS, CS, false, W, false>);
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * W * 128 + 2 * 2 * W * 4 +
                   (kCaeMaxGroups * kBM + W + 8 * kBM) * sizeof(float) + 4 * 8 + 16;
     // Never let more CTAs share an SM than its 512 TMEM columns can serve.

@@ -355,6 +355,33 @@ def test_tensor_core_conv_vs_reference_order(geo):
     assert_no_device_error()
 
 
+@pytest.mark.parametrize("geo", [
+    (32, 3, 2, 128, 64),    # the stack's first block, full 8x8 tiles
+    (64, 3, 2, 64, 32),
+    (96, 3, 1, 16, 16),     # stride 1, three groups
+    (256, 3, 2, 16, 8),
+    (32, 3, 2, 8, 4),       # one partial tile
+    (64, 5, 1, 8, 8),       # 5x5 / 7x7 run the direct kernel in both calls
+])
+def test_depthwise_tiled_vs_direct(geo):
+    """Shared-memory tiled depthwise conv (forward) vs the direct kernel
+    (forward_exact): the same per-tap arithmetic, bit-identical."""
+    C, k, st, din, dout = geo
+    rng = np.random.default_rng(C + 7 * din)
+    frames = 3
+    m, b = W.conv_weights(rng, C, C, k, True), W.bias(rng, C)
+    layer = A.ConvLayer(C, C, k, st, din, dout)
+    layer.load_weights(t(m), t(b))
+    x = torch.from_numpy((rng.standard_normal(frames * din * din * C) * 2).astype(np.float32)).to(DEV)
+    xw, xs = A.pack_f32(x)
+    rows = frames * dout * dout
+    ow, os_ = A.empty_f(rows, C)
+    ew, es = A.empty_f(rows, C)
+    layer.forward(xw, xs, ow, os_, frames)
+    layer.forward_exact(xw, xs, ew, es, frames)
+    assert_f_equal(ow, h(os_), ew, h(es), f"depthwise tiled vs direct {geo}")
+
+
 def _small_cortex(B, T, dim=32, chunk=4, seed=31):
     desc = W.cortex_desc(batch_chunk=chunk, d_state=64, critic_units=64, dim=dim)
     wts = W.cortex_weights(seed, d_state=64, critic_units=64, dim=dim)
