@@ -75,6 +75,7 @@ _SIGS = {
     "aic_residual_add": [P, P, P, P, P, P, I64, I32, F32, I32, P],
     "aic_gap": [P, P, I64, I32, I32, P, P, P, P],
     "aic_gap_f16": [P, P, I64, I32, I32, P, P],
+    "aic_screen_frontend": [P, P, I32, I32, I32, C.c_uint32, F32, F32, P],
     "aic_set_actions": [P, I64, I32, P, P],
     "aic_selftest_rcp": [P, P, P],
     "aic_audio_workspace_bytes": [SZ],

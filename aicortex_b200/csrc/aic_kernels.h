@@ -104,6 +104,12 @@ size_t audio_workspace_bytes();
 cudaError_t launch_audio_frontend(const short* pcm, __half* frame, int dim, int first_channel, void* workspace,
                                   cudaStream_t stream);
 
+// F2: screen front-end (cs.cu): BGRA8 [dim*dim] -> fp16 planes B, G, R, A at
+// channels first_channel.. of an fp16 [C][dim][dim] frame; train adds the
+// reference's pixel dropout and brightness/contrast augmentation. dim even.
+cudaError_t launch_screen_frontend(const uint8_t* bgra, __half* frame, int dim, int first_channel, bool train,
+                                   uint32_t frame_seed, float brightness, float contrast, cudaStream_t stream);
+
 // A12: Bernoulli action bits, [rows][A] probabilities -> [rows][(A+63)/64] words.
 cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned long long* actions,
                                cudaStream_t stream);

@@ -1099,6 +1099,19 @@ AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int d
     });
 }
 
+AIC_API aic_status aic_screen_frontend(const uint8_t* bgra, uint16_t* frame, int dim, int first_channel, int train,
+                                      uint32_t frame_seed, float brightness, float contrast, void* stream)
+{
+    return guarded([&] {
+        require(bgra && frame, "null buffer");
+        require(dim >= 2 && dim % 2 == 0, "dim must be even");
+        require(first_channel >= 0, "bad channel");
+        cuda_ok(launch_screen_frontend(bgra, reinterpret_cast<__half*>(frame), dim, first_channel, train != 0, frame_seed,
+                                       brightness, contrast, as_stream(stream)),
+                "screen front-end");
+    });
+}
+
 AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream)
 {
     return guarded([&] {

@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kThreads, 4) conv_gemm_tc_kernel(TcParams p)
 {
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned tiles (swizzle atoms), then bias, row partial sums, barriers.
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
     const int nst = p.smem_stages;
     const int n0 = blockIdx.y * kMaxN;
     const int n_cta = min(kMaxN, p.out_c - n0);

@@ -112,7 +112,7 @@ template <int KS, int CS, bool ACT>
 __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams p)
 {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
     // CTA y covers channels [n0, n0 + n_cta) of norm chunk y / CS
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
     const int n_cta = min(kNCta, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 {
     constexpr int kChunks = W / kNCta;  // 64-channel image chunks per CTA
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * W;
     const int n_cta = min(W, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
     const bool live = n_cta > 0;

@@ -499,6 +499,18 @@ def set_actions(probs: torch.Tensor, stream=None) -> torch.Tensor:
     return out
 
 
+def screen_frontend(bgra: torch.Tensor, frame: torch.Tensor, first_channel: int = 0, train: bool = False,
+                    frame_seed: int = 0, brightness: float = 0.0, contrast: float = 1.0, stream=None) -> None:
+    """Screen front-end (cs.cu): uint8 BGRA [dim, dim, 4] -> fp16 planes B, G, R, A at
+    frame[first_channel : first_channel + 4] (fp16 [C][dim][dim]); train adds the
+    reference's pixel dropout (seeded by frame_seed) and brightness/contrast augmentation."""
+    assert bgra.dtype == torch.uint8 and bgra.is_contiguous() and bgra.numel() == 4 * frame.shape[-1] ** 2
+    assert frame.dtype == torch.float16 and frame.dim() == 3 and frame.is_contiguous()
+    assert 0 <= first_channel and first_channel + 4 <= frame.shape[0] and frame.shape[1] == frame.shape[2]
+    call("aic_screen_frontend", _vp(bgra), _vp(frame), int(frame.shape[-1]), int(first_channel), int(bool(train)),
+         C.c_uint32(frame_seed & 0xFFFFFFFF), float(brightness), float(contrast), _stream(stream))
+
+
 def audio_frontend(pcm: torch.Tensor, frame: torch.Tensor, first_channel: int = 4, stream=None) -> None:
     """Audio front-end (ca.cu): 2048 int16 PCM samples -> |FFT| and phase planes
     written to frame[first_channel] and frame[first_channel + 1] (fp16 [C][dim][dim])."""

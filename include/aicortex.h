@@ -115,6 +115,17 @@ AIC_API aic_status aic_selftest_rcp(uint64_t* mismatches, float* first_bad, void
 AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int dim, int first_channel,
                                       void* workspace, void* stream);
 
+/* Screen front-end (cs.cu:5-45, run_cuda_processing_visual cs.cu:104-123
+ * without the D3D11 texture copy): bgra = dim*dim BGRA8 pixels (device), written
+ * as fp16 planes byte/255 in byte order B, G, R, A to channels first_channel ..
+ * first_channel + 3 of the fp16 frame [C][dim][dim]. train != 0 applies the
+ * reference's training-mode pixel dropout, hashed from frame_seed (the
+ * reference draws it with generateUniqueSeed), and the brightness/contrast
+ * augmentation with the given values (the reference draws them uniformly from
+ * +-0.15 and 1 +- 0.2), all in fp16 arithmetic. dim must be even. */
+AIC_API aic_status aic_screen_frontend(const uint8_t* bgra, uint16_t* frame, int dim, int first_channel, int train,
+                                       uint32_t frame_seed, float brightness, float contrast, void* stream);
+
 /* setActionsKernel (kernels.h:1473-1485, cortex.h:371-372): per row of
  * `count` probabilities, Bernoulli bits into [rows][(count+63)/64] words. */
 AIC_API aic_status aic_set_actions(const float* probs, int64_t rows, int count, uint64_t* actions, void* stream);

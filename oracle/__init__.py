@@ -51,6 +51,7 @@ def _load() -> C.CDLL:
         "orc_resize_half": ([P, P, I32, I32, I32, I32], None),
         "orc_fft_rows": ([P, I32, P], None),
         "orc_fft_cols": ([P, I32, P], None),
+        "orc_screen_frontend": ([P, I32, I32, C.c_uint32, C.c_float, C.c_float, P], None),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -164,6 +165,17 @@ def set_actions(probs):
     out = np.zeros((rows, (count + 63) // 64), dtype=np.uint64)
     lib.orc_set_actions(_p(probs), rows, count, _p(out))
     return out
+
+
+def screen_frontend(bgra: np.ndarray, train: bool = False, frame_seed: int = 0, brightness: float = 0.0,
+                    contrast: float = 1.0) -> np.ndarray:
+    """cs.cu:5-45: uint8 BGRA [H, W, 4] -> fp16 planes [4][H][W] (B, G, R, A)."""
+    bgra = np.ascontiguousarray(bgra, np.uint8)
+    h, w = bgra.shape[:2]
+    out = np.zeros(4 * h * w, np.uint16)
+    lib.orc_screen_frontend(_p(bgra), h * w, int(bool(train)), frame_seed & 0xFFFFFFFF, float(brightness),
+                            float(contrast), _p(out))
+    return out.view(np.float16).reshape(4, h, w)
 
 
 def audio_frontend(pcm: np.ndarray, dim: int = 256, n: int = 1024):

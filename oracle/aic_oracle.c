@@ -822,3 +822,60 @@ void orc_fft_cols(const uint16_t* in, int n, uint16_t* planes)
         free(col);
     }
 }
+
+/* ------------------------------------------------------------------ F2 */
+/* Screen front-end (cs.cu:5-45): kernels.h:38-45 bounded xorshift hash. */
+static uint32_t orc_bounded_hash(uint32_t seed, uint32_t n)
+{
+    seed ^= seed << 13;
+    seed ^= seed >> 17;
+    seed ^= seed << 5;
+    return (uint32_t)(((uint64_t)seed * n) >> 32);
+}
+
+/* A double rounded to the nearest binary16 (ties to even), as fp16 bits. */
+static uint16_t orc_double_to_half(double r)
+{
+    if (r == 0.0) return signbit(r) ? 0x8000u : 0u;
+    int e;
+    frexp(fabs(r), &e);                       /* |r| in [2^(e-1), 2^e) */
+    int ulp_exp = (e - 1) - 10;               /* 11 significant bits */
+    if (ulp_exp < -24) ulp_exp = -24;          /* subnormal spacing */
+    const double n = nearbyint(ldexp(r, -ulp_exp));
+    return orc_float_to_half((float)ldexp(n, ulp_exp));  /* exact in float and half */
+}
+
+/* __hfma: a*b + c with one rounding; exact in double for the operands here
+ * (the products and sums of halves span well under 53 bits). */
+static uint16_t orc_hfma(uint16_t a, uint16_t b, uint16_t c)
+{
+    return orc_double_to_half((double)orc_half_to_float(a) * (double)orc_half_to_float(b) + (double)orc_half_to_float(c));
+}
+
+/* bgra [pixels] (4 bytes each) -> planes [4][pixels] as fp16 bits
+ * (ProcessBgraToRgbOP cs.cu:12-31, AugmentBrightnessContrastOP cs.cu:40-44). */
+void orc_screen_frontend(const uint8_t* bgra, int pixels, int train, uint32_t frame_seed, float brightness,
+                         float contrast, uint16_t* planes)
+{
+    const uint16_t h_half = orc_float_to_half(0.5f), one = orc_float_to_half(1.0f);
+    const uint16_t c = orc_float_to_half(contrast);
+    const uint16_t offset = orc_float_to_half(0.5f + orc_half_to_float(orc_float_to_half(brightness)));
+    for (int idx = 0; idx < pixels; ++idx) {
+        uint8_t px[4] = {bgra[4 * idx], bgra[4 * idx + 1], bgra[4 * idx + 2], bgra[4 * idx + 3]};
+        if (train) {
+            const uint32_t r = orc_bounded_hash(frame_seed ^ (uint32_t)idx, 10000u);
+            if (r < 50u) px[0] = px[1] = px[2] = 0;
+            else if (r < 100u) px[0] = px[1] = px[2] = 255;
+        }
+        for (int ch = 0; ch < 4; ++ch) {
+            uint16_t v = orc_float_to_half((float)px[ch] * (1.0f / 255.0f));
+            if (train) {
+                const uint16_t d = orc_float_to_half(orc_half_to_float(v) - orc_half_to_float(h_half));
+                v = orc_hfma(d, c, offset);
+                if (orc_half_to_float(v) > 1.0f) v = one;  /* __hmin2(., 1) */
+                if (!(orc_half_to_float(v) > 0.0f)) v = 0; /* __hmax2(., +0) */
+            }
+            planes[(int64_t)ch * pixels + idx] = v;
+        }
+    }
+}

@@ -113,6 +113,10 @@ void orc_fft_rows(const uint16_t* in, int n, uint16_t* out);
 /* in: n x n complex; planes: [2][n][n] = |X|/n^2, atan2(im, re) */
 void orc_fft_cols(const uint16_t* in, int n, uint16_t* planes);
 
+/* F2: screen front-end (cs.cu:5-45): bgra [pixels][4] -> fp16 bits [4][pixels]. */
+void orc_screen_frontend(const uint8_t* bgra, int pixels, int train, uint32_t frame_seed, float brightness,
+                         float contrast, uint16_t* planes);
+
 int orc_num_threads(void);
 
 #ifdef __cplusplus

@@ -1,6 +1,7 @@
 #!/usr/bin/env bash
 # Compiles the reference's own CUDA kernels (AICortex kernels.h and the headers
-# it includes, and the audio front-end ca.cu) for sm_100a into oracle/_ref/, one shared library per
+# it includes, the audio front-end ca.cu and the screen front-end's operators
+# from cs.cu) for sm_100a into oracle/_ref/, one shared library per
 # (d_model, d_state) pair, driven by oracle/ref_harness.cu.
 # TEST INFRASTRUCTURE ONLY: the libraries are the golden-vector source for
 # tests/golden/make_golden.py and never part of the product.
@@ -24,9 +25,12 @@ PAIRS=${AICREF_PAIRS:-"256:32 256:128 256:512"}
 for pair in $PAIRS; do
   D=${pair%%:*}; N=${pair##*:}
   lib="$OUT/libaicref_D${D}_N${N}.so"
-  if [ -f "$lib" ] && [ "$lib" -nt "$HERE/ref_harness.cu" ] && [ "$lib" -nt "$REF/kernels.h" ] && [ "$lib" -nt "$0" ]; then continue; fi
+  if [ -f "$lib" ] && [ "$lib" -nt "$HERE/ref_harness.cu" ] && [ "$lib" -nt "$REF/kernels.h" ] && [ "$lib" -nt "$REF/cs.cu" ] && [ "$lib" -nt "$0" ]; then continue; fi
   tmp=$(mktemp -d /tmp/aicref.XXXXXX)
   cp "$REF/kernels.h" "$REF/uv.h" "$REF/device_constants.h" "$REF/base_constants.h" "$REF/ca.cu" "$tmp/"
+  # the screen front-end's two elementwise operators (cs.cu:5-45), cut from
+  # cs.cu without its D3D11 interop part, which cannot build here
+  awk '/^struct ProcessBgraToRgbOP/{on=1} /^struct InternalCudaVisualState/{on=0} on' "$REF/cs.cu" > "$tmp/cs_ops.h"
   sed -i -E "s/final_channels = [0-9]+/final_channels = ${D}/; s/mamba_d_state = [0-9]+/mamba_d_state = ${N}/" "$tmp/base_constants.h"
   # the two Windows SDK types ca.cu's capture entry point names (ca.cu:76)
   printf 'typedef unsigned char BYTE;\ntypedef unsigned long DWORD;\n' > "$tmp/windows.h"

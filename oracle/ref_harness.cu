@@ -13,7 +13,8 @@
 // constants (kernels.h:1080-1089), which is why one library is built per
 // (d_model, d_state) pair.
 #include "kernels.h"
-#include "ca.cu"  // AudioProcessorOP (ca.cu:4-20)
+#include "ca.cu"      // AudioProcessorOP (ca.cu:4-20)
+#include "cs_ops.h"   // ProcessBgraToRgbOP, AugmentBrightnessContrastOP (cs.cu:5-45), cut by build_ref.sh
 
 #define AICREF_API extern "C" __attribute__((visibility("default")))
 
@@ -167,6 +168,29 @@ AICREF_API int aicref_fft_rows(const __half* in, __half2* out)
 AICREF_API int aicref_fft_cols(const __half2* in, __half* out)
 {
     fftColumnKernel<1024><<<1024, gpu_block_threads>>>(in, out);
+    return aicref_status();
+}
+
+template <typename Op>
+__global__ void aicref_elementwise(Op op, int n)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) op(i);
+}
+
+// cs.cu:116: BGRA8 [pixels] -> fp16 planes [4][pixels] (train: pixel dropout seeded by frame_seed).
+AICREF_API int aicref_screen(const uchar4* bgra, __half* out, int pixels, unsigned frame_seed, int train)
+{
+    ProcessBgraToRgbOP op{bgra, out, pixels, frame_seed, train != 0};
+    aicref_elementwise<<<(pixels + 255) / 256, 256>>>(op, pixels);
+    return aicref_status();
+}
+
+// cs.cu:117-122: the augmentation over `pairs` half2 of the planes.
+AICREF_API int aicref_augment(__half2* v, int pairs, float brightness, float contrast)
+{
+    AugmentBrightnessContrastOP op{v, __float2half2_rn(brightness), __float2half2_rn(contrast)};
+    aicref_elementwise<<<(pairs + 255) / 256, 256>>>(op, pairs);
     return aicref_status();
 }
 

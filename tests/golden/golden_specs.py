@@ -144,3 +144,14 @@ def audio_case():
     b = rng.integers(-32768, 32768, 2048).astype(np.int16)
     b[0], b[1] = -32768, 32767
     return np.stack([a, b])
+
+
+SCREEN_DIM = 64
+SCREEN_SEED = 0x9E3779B9          # frame seed of the training-mode case (the reference draws it per frame)
+SCREEN_AUG = (0.0732421875, 1.1484375)  # brightness, contrast (in the reference's +-0.15 and 1 +- 0.2 ranges)
+
+
+def screen_case():
+    """A seeded BGRA8 frame of SCREEN_DIM^2 pixels."""
+    rng = np.random.default_rng(1300)
+    return rng.integers(0, 256, (SCREEN_DIM, SCREEN_DIM, 4), dtype=np.uint8)

@@ -310,8 +310,26 @@ def gen_audio(lib):
     save("audio", pcm_sha=S.sha(pcm), out=np.stack(outs), planes_sha=np.array(plane_sha))
 
 
+def gen_screen(lib):
+    """cs.cu:116-122 on one frame: inference (conversion only) and training
+    (pixel dropout from the frame seed, then the brightness/contrast
+    augmentation over all four planes as half2 pairs)."""
+    bgra = S.screen_case()
+    px = bgra.shape[0] * bgra.shape[1]
+    outs = []
+    for train in (0, 1):
+        d = Dev()
+        out, po = d.zeros(4 * px, torch.float16)
+        run(lib, "aicref_screen", d.put(bgra), po, C.c_int(px), C.c_uint(S.SCREEN_SEED), C.c_int(train))
+        if train:
+            run(lib, "aicref_augment", po, C.c_int(2 * px), C.c_float(S.SCREEN_AUG[0]), C.c_float(S.SCREEN_AUG[1]))
+        outs.append(out.cpu().numpy().reshape(4, bgra.shape[0], bgra.shape[1]))
+    save("screen", bgra_sha=S.sha(bgra), out=np.stack(outs))
+
+
 def main():
     lib = ref(256, 128)
+    gen_screen(lib)
     gen_audio(lib)
     gen_pack(lib)
     gen_stem(lib)

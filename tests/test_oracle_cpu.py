@@ -205,3 +205,13 @@ def test_oracle_audio(golden):
     # __sincosf/atan2f there; both round to fp16, so a handful of values sit
     # one fp16 step apart (measured: 4 of 131072, magnitudes identical).
     assert diff_rate <= 1e-3 and mag_err <= 1e-3 and ph_err <= 2e-3, (diff_rate, mag_err, ph_err)
+
+
+def test_oracle_screen(golden):
+    g = golden("screen")
+    bgra = S.screen_case()
+    assert S.sha(bgra) == str(g["bgra_sha"])
+    plain = O.screen_frontend(bgra)
+    train = O.screen_frontend(bgra, True, S.SCREEN_SEED, *S.SCREEN_AUG)
+    np.testing.assert_array_equal(plain.view(np.uint16), g["out"][0].view(np.uint16))
+    np.testing.assert_array_equal(train.view(np.uint16), g["out"][1].view(np.uint16))

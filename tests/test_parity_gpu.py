@@ -206,6 +206,21 @@ def test_golden_actions(golden):
     np.testing.assert_array_equal(h(words)[0].view(np.uint64), g["words"])
 
 
+def test_golden_screen(golden):
+    """F2 bit-exact against the reference's operators, inference and training
+    mode; channels outside the four planes stay untouched."""
+    g = golden("screen")
+    bgra = S.screen_case()
+    dim = bgra.shape[0]
+    for i, train in enumerate((False, True)):
+        frame = torch.full((6, dim, dim), 3.0, dtype=torch.float16, device=DEV)
+        A.screen_frontend(t(bgra), frame, first_channel=1, train=train, frame_seed=S.SCREEN_SEED,
+                          brightness=S.SCREEN_AUG[0], contrast=S.SCREEN_AUG[1])
+        f = h(frame)
+        np.testing.assert_array_equal(f[1:5].view(np.uint16), g["out"][i].view(np.uint16))
+        assert (f[0] == 3.0).all() and (f[5] == 3.0).all()
+
+
 def test_golden_audio(golden):
     """A14 bit-exact against the reference kernels; channels other than the two
     audio planes of the frame stay untouched."""
