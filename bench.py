@@ -143,6 +143,9 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1
+    # for its workers); read by the OpenMP runtime when the oracle loads
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)))
     import oracle
     from aicortex_b200 import workloads as W
     wts = W.cortex_weights(SEED)
