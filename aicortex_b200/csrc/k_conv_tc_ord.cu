@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 // group and parks the pre-norm sums back in TMEM slice 0; pass 2 normalises,
 // activates and packs. Tiles are 128 rows x W channels, W = 128 for up to two
 // groups and 64 otherwise; the CTAs of one RMSNorm chunk form a cluster as in
-// the streaming kernel. One tile per CTA.
+// the streaming kernel. A run of up to 8 row tiles per CTA.
 constexpr int kCaeMaxGroups = 4;
 
 template <int KS, int CS, bool ACT, int W, bool ONE>
@@ -408,15 +408,15 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     float* b_units = reinterpret_cast<float*>(b_codes + 2 * W * 128);  // [S][2][W]
     float* din_s = b_units + 2 * 2 * W;                         // [kCaeMaxGroups][kBM] unit(s_in)
     float* bias_s = din_s + kCaeMaxGroups * kBM;                // [W]
-    float* part = bias_s + W;                                   // [8][kBM]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 8 * kBM);  // 0: B; 1,2: A slot free; 3: acc ready
+    float* part = bias_s + W;                                   // [2 tiles][8][kBM]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 16 * kBM);  // 0: B; 3: accumulators ready
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int need = GK * (n_cta > 0 ? n_cta : 0);
     const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
-    for (int i = tid; i < 8 * kBM; i += kThreads) part[i] = 0.0f;
+    for (int i = tid; i < 16 * kBM; i += kThreads) part[i] = 0.0f;
     if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
     if (tid == 0) {
         for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&bars[i]), 1);
@@ -449,151 +449,157 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
         }
     }
 
-    const int64_t m0 = static_cast<int64_t>(blockIdx.x) * kBM;
     const int prow = tid & (kBM - 1), pg = tid >> 7;
-    const int64_t prow_g = m0 + prow;
-    const bool prow_ok = prow_g < p.rows;
     const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
-    const uint32_t idesc = instr_desc(n_cta);
-
-    for (int st = 0; live && st < S; ++st) {
-        const int buf = st & 1;
-        uint8_t* a_tile = a_tiles + buf * kTileA;
-        if (st >= 2 && !*abort_flag) {
-            if (!mbar_wait(smem_addr(&bars[1 + buf]), 0u, p.err, 21)) *abort_flag = 1;
-        }
-        __syncthreads();
-        if (*abort_flag) break;
-        const int gk = 2 * st + pg;
-        float du = 0.0f;
-        if (prow_ok && gk < GK) {
-            const int tap = gk / G, g = gk - tap * G;
-            const int64_t pix = tap_pixel_pow2(prow_g, tap, KS, lg_din, lg_dout);
-            const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
-            du = unit_of(__ldg(p.in_s + pix * G + g));
-            stage_group_f(a_tile, prow, pg, words, 1.0f);
-        } else {
-            stage_zero(a_tile, prow, pg);
-        }
-        if (gk < GK) din_s[gk * kBM + prow] = du;
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            if (st > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 22)) {
-                tc_fence_after();
-                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_codes + st * W * 128);
-                const int n_mma = 2 * st + 1 < GK ? kBK / 16 : kBK / 32;
-#pragma unroll
-                for (int j = 0; j < kBK / 16; ++j)
-                    if (j < n_mma)
-                        mma_bf16(tmem + static_cast<uint32_t>((2 * st + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
-                                 smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
-                mma_commit(smem_addr(&bars[1 + buf]));
-            } else {
-                *abort_flag = 1;
-            }
-        }
-    }
-    if (live && tid == 0) mma_commit(smem_addr(&bars[3]));
-    __syncthreads();
-    bool ok = live && !*abort_flag;
-    if (live) {
-        if (!mbar_wait(smem_addr(&bars[3]), 0u, p.err, 23)) ok = false;
-        tc_fence_after();
-    }
-
-    // Pass 1: chain, tap fold and square-sum per 32-channel group; the
-    // pre-norm sums go back to TMEM slice 0.
+    const uint32_t idesc = instr_desc(n_cta > 0 ? n_cta : 32);
     const int q = warp & 3, hw = warp >> 2;
     const int erow = q * 32 + lane;
     const int ngroups = n_cta >> 5;
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const int gbase = (n0 & (kNormChunk - 1)) >> 5;
-    if (ok) {
-        for (int cg = hw; cg < ngroups; cg += 2) {
-            float acc[32], sacc[KS == 1 ? 1 : 32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
-            for (int g = 0; g < GK; ++g) {
-                if (KS == 2 && g > 0 && g % G == 0) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
-                        acc[i] = 0.0f;
-                    }
-                }
-                const float du = din_s[g * kBM + erow];
-                const float4* u4 = reinterpret_cast<const float4*>(b_units + ((g >> 1) * 2 + (g & 1)) * W + 32 * cg);
-#pragma unroll
-                for (int h16 = 0; h16 < 2; ++h16) {
-                    float pv[16];
-                    tmem_ld16(tl + static_cast<uint32_t>(g * n_cta + 32 * cg + 16 * h16), pv);
-#pragma unroll
-                    for (int i4 = 0; i4 < 4; ++i4) {
-                        const float4 u = u4[4 * h16 + i4];
-                        const int b = 16 * h16 + 4 * i4;
-                        acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
-                        acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
-                        acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
-                        acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
-                    }
-                }
-            }
-            if (KS == 2) {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
-            }
-            const float gs2 = tree_sq32(acc);
-            float* dst = &part[(gbase + cg) * kBM + erow];
-            if (CS > 1) {
-#pragma unroll
-                for (int r = 0; r < CS; ++r) st_peer_f32(smem_addr(dst), static_cast<uint32_t>(r), gs2);
+    const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+
+    // A run of consecutive row tiles per CTA (the same for every CTA of a
+    // cluster): the weights are fetched once; each tile's MMAs have completed
+    // (its accumulator barrier) before the next tile restages A and reuses TMEM.
+    const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
+    const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
+    const int my_tiles = tile0 < n_tiles ? static_cast<int>(min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0)) : 0;
+    for (int t = 0; t < my_tiles; ++t) {
+        const int64_t m0 = (tile0 + t) * kBM;
+        const int64_t prow_g = m0 + prow;
+        const bool prow_ok = prow_g < p.rows;
+        for (int st = 0; live && st < S; ++st) {
+            const int buf = st & 1;
+            uint8_t* a_tile = a_tiles + buf * kTileA;
+            __syncthreads();
+            if (*abort_flag) break;
+            const int gk = 2 * st + pg;
+            float du = 0.0f;
+            if (prow_ok && gk < GK) {
+                const int tap = gk / G, g = gk - tap * G;
+                const int64_t pix = tap_pixel_pow2(prow_g, tap, KS, lg_din, lg_dout);
+                const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
+                du = unit_of(__ldg(p.in_s + pix * G + g));
+                stage_group_f(a_tile, prow, pg, words, 1.0f);
             } else {
-                *dst = gs2;
+                stage_zero(a_tile, prow, pg);
             }
-            tmem_st32(tl + static_cast<uint32_t>(32 * cg), acc);
-        }
-    }
-    __syncthreads();
-    if (CS > 1) cluster_sync_all();
-    // Pass 2: the reference's cross-warp butterfly over the chunk's 8 group
-    // sums (kernels.h:271-276), then bias, activation and requant.
-    if (ok) {
-        float w8[8];
+            if (gk < GK) din_s[gk * kBM + prow] = du;
+            fence_async_smem();
+            __syncthreads();
+            if (tid == 0) {
+                if (t > 0 || st > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 22)) {
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_codes + st * W * 128);
+                    const int n_mma = 2 * st + 1 < GK ? kBK / 16 : kBK / 32;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) w8[i] = part[i * kBM + erow];
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1)
-#pragma unroll
-            for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
-        const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
-        const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
-        const int64_t row = m0 + erow;
-        for (int cg = hw; cg < ngroups; cg += 2) {
-            float v[32];
-            tmem_ld32(tl + static_cast<uint32_t>(32 * cg), v);
-            const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * cg);
-#pragma unroll
-            for (int i4 = 0; i4 < 8; ++i4) {
-                const float4 b = b4[i4];
-                const float bb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float x = fmaf(v[4 * i4 + k], sc_norm, bb[k]);
-                    v[4 * i4 + k] = ACT ? silu_f(x) : x;
+                    for (int j = 0; j < kBK / 16; ++j)
+                        if (j < n_mma)
+                            mma_bf16(tmem + static_cast<uint32_t>((2 * st + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
+                                     smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
+                } else {
+                    *abort_flag = 1;
                 }
             }
-            uint4 words;
-            int8_t e;
-            quantize_group(v, &words, &e);
-            if (row < p.rows) {
-                const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + cg;
-                reinterpret_cast<uint4*>(p.out)[gi] = words;
-                p.out_s[gi] = e;
+        }
+        if (live && tid == 0) mma_commit(smem_addr(&bars[3]));
+        __syncthreads();
+        bool ok = live && !*abort_flag;
+        if (live) {
+            if (!mbar_wait(smem_addr(&bars[3]), static_cast<uint32_t>(t & 1), p.err, 23)) ok = false;
+            tc_fence_after();
+        }
+
+        // Pass 1: chain, tap fold and square-sum per 32-channel group; the
+        // pre-norm sums go back to TMEM slice 0.
+        float* part_t = part + (t & 1) * 8 * kBM;
+        if (ok) {
+            for (int cg = hw; cg < ngroups; cg += 2) {
+                float acc[32], sacc[KS == 1 ? 1 : 32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+#pragma unroll
+                for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
+                for (int g = 0; g < GK; ++g) {
+                    if (KS == 2 && g > 0 && g % G == 0) {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) {
+                            sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+                            acc[i] = 0.0f;
+                        }
+                    }
+                    const float du = din_s[g * kBM + erow];
+                    const float4* u4 = reinterpret_cast<const float4*>(b_units + ((g >> 1) * 2 + (g & 1)) * W + 32 * cg);
+#pragma unroll
+                    for (int h16 = 0; h16 < 2; ++h16) {
+                        float pv[16];
+                        tmem_ld16(tl + static_cast<uint32_t>(g * n_cta + 32 * cg + 16 * h16), pv);
+#pragma unroll
+                        for (int i4 = 0; i4 < 4; ++i4) {
+                            const float4 u = u4[4 * h16 + i4];
+                            const int b = 16 * h16 + 4 * i4;
+                            acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
+                            acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
+                            acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
+                            acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
+                        }
+                    }
+                }
+                if (KS == 2) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
+                }
+                const float gs2 = tree_sq32(acc);
+                float* dst = &part_t[(gbase + cg) * kBM + erow];
+                if (CS > 1) {
+#pragma unroll
+                    for (int r = 0; r < CS; ++r) st_peer_f32(smem_addr(dst), static_cast<uint32_t>(r), gs2);
+                } else {
+                    *dst = gs2;
+                }
+                tmem_st32(tl + static_cast<uint32_t>(32 * cg), acc);
             }
         }
+        __syncthreads();
+        if (CS > 1) cluster_sync_all();
+        // Pass 2: the reference's cross-warp butterfly over the chunk's 8 group
+        // sums (kernels.h:271-276), then bias, activation and requant.
+        if (ok) {
+            float w8[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w8[i] = part_t[i * kBM + erow];
+#pragma unroll
+            for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+                for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
+            const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
+            const int64_t row = m0 + erow;
+            for (int cg = hw; cg < ngroups; cg += 2) {
+                float v[32];
+                tmem_ld32(tl + static_cast<uint32_t>(32 * cg), v);
+                const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * cg);
+#pragma unroll
+                for (int i4 = 0; i4 < 8; ++i4) {
+                    const float4 b = b4[i4];
+                    const float bb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float x = fmaf(v[4 * i4 + k], sc_norm, bb[k]);
+                        v[4 * i4 + k] = ACT ? silu_f(x) : x;
+                    }
+                }
+                uint4 words;
+                int8_t e;
+                quantize_group(v, &words, &e);
+                if (row < p.rows) {
+                    const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + cg;
+                    reinterpret_cast<uint4*>(p.out)[gi] = words;
+                    p.out_s[gi] = e;
+                }
+            }
+        }
+        tc_fence_before();  // this tile's TMEM reads precede the next tile's MMAs
     }
     if (live) {
         tc_fence_before();
@@ -708,7 +714,7 @@ cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
                     ? (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, true> : conv_gemm_tc_cae_kernel<KS, CS, false, W, true>)
                     : (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, false> : conv_gemm_tc_cae_kernel<KS, CS, false, W, false>);
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * W * 128 + 2 * 2 * W * 4 +
-                  (kCaeMaxGroups * kBM + W + 8 * kBM) * sizeof(float) + 4 * 8 + 16;
+                  (kCaeMaxGroups * kBM + W + 16 * kBM) * sizeof(float) + 4 * 8 + 16;
     // Never let more CTAs share an SM than its 512 TMEM columns can serve.
     const int need = p.gk_total * (p.out_c < W ? p.out_c : W);
     const int tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
@@ -729,8 +735,14 @@ cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = CS > 1 ? 1 : 0;
-    cfg.gridDim = dim3(static_cast<unsigned>((p.rows + kBM - 1) / kBM), chunks * CS, 1);
-    e = cudaLaunchKernelEx(&cfg, kern, p);
+    // runs of tiles amortise the weight fetch and set-up; with a single group
+    // (four CTAs per SM) one tile per CTA measured slightly faster
+    const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
+    int64_t t = p.gk_total == 1 ? 1 : n_tiles * chunks * CS / (148 * 8);
+    OrdParams q = p;
+    q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 8 ? 8 : t);
+    cfg.gridDim = dim3(static_cast<unsigned>((n_tiles + q.tiles_per_cta - 1) / q.tiles_per_cta), chunks * CS, 1);
+    e = cudaLaunchKernelEx(&cfg, kern, q);
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
@@ -769,8 +781,8 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     p.err = err;
     // measured: the chain at the end wins with one or two groups per output,
     // the streaming kernel from three on
-    if (p.gk_total <= 2)
-        return ksize == 1 ? launch_cae_w<1>(p, stream) : launch_cae_w<2>(p, stream);
+    if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
+        return launch_cae_w<1>(p, stream);
     const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * static_cast<size_t>(slot_b) +
                   (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;
