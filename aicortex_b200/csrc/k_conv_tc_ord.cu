@@ -401,47 +401,49 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     }
 }
 
-// ---- chain at the end: every group's dot products resident in TMEM --------
+// ---- chain at the end: pointwise convs with one or two groups -------------
 //
-// For up to four 32-element groups per output (k^2 * in_c <= 128) all the
-// per-group accumulators of a tile fit in TMEM (groups x width <= 256
-// columns, two CTAs per SM). The stage loop then only stages A and issues
-// MMAs (group g into TMEM slice g), and the epilogue runs the reference's
-// fmaf chain over the groups one 32-channel group of columns at a time, so a
-// thread's chain state is transient: pass 1 folds the chain, square-sums the
-// group and parks the pre-norm sums back in TMEM slice 0; pass 2 normalises,
-// activates and packs. Tiles are 128 rows x W channels, W = 128 for up to two
-// groups and 64 otherwise; the CTAs of one RMSNorm chunk form a cluster as in
-// the streaming kernel. A run of up to 8 row tiles per CTA.
-constexpr int kCaeMaxGroups = 4;
+// With in_c <= 64 the whole K of a tile is one stage of at most two 32-element
+// groups, and every group's dot products stay resident in TMEM (group g in
+// slice g). Per row tile the CTA stages A once and issues the MMAs, and the
+// epilogue then runs the reference's fmaf chain over the groups one 32-channel
+// group of columns at a time, so a thread's chain state is transient: pass 1
+// folds the chain, square-sums the group and parks the pre-norm sums back in
+// TMEM slice 0; pass 2 normalises, activates and packs. Tiles are 128 rows x
+// 128 channels; the two CTAs of a 256-channel RMSNorm chunk form a cluster as
+// in the streaming kernel. The weights of the CTA's channels are fetched once
+// for its run of up to 8 row tiles. Shared memory holds one A tile and one
+// stage of weights (about 45 KB), so with a single group (128 TMEM columns,
+// 64 registers per thread) four CTAs share an SM.
+constexpr int kCaeW = 128;
 
-template <int KS, int CS, bool ACT, int W, bool ONE>
+template <int CS, bool ACT, bool ONE>
 __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel(OrdParams p)
 {
-    constexpr int kChunks = W / kNCta;  // 64-channel image chunks per CTA
+    constexpr int W = kCaeW, kChunks = W / kNCta;  // 64-channel image chunks per CTA
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * W;
     const int n_cta = min(W, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
     const bool live = n_cta > 0;
-    const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
-    uint8_t* a_tiles = base;                                    // [2][kTileA]
-    uint8_t* b_codes = base + 2 * kTileA;                       // [S][W][128 B]
-    float* b_units = reinterpret_cast<float*>(b_codes + 2 * W * 128);  // [S][2][W]
-    float* din_s = b_units + 2 * 2 * W;                         // [kCaeMaxGroups][kBM] unit(s_in)
-    float* bias_s = din_s + kCaeMaxGroups * kBM;                // [W]
-    float* part = bias_s + W;                                   // [2 tiles][8][kBM]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 16 * kBM);  // 0: B; 3: accumulators ready
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+    const int GK = p.gk_total;  // 1 or 2
+    uint8_t* a_tile = base;                                         // [kTileA]
+    uint8_t* b_codes = base + kTileA;                               // [W][128 B]
+    float* b_units = reinterpret_cast<float*>(b_codes + W * 128);  // [2][W]
+    float* din_s = b_units + 2 * W;                                 // [2][kBM] unit(s_in)
+    float* bias_s = din_s + 2 * kBM;                                // [W]
+    float* part = bias_s + W;                                       // [2 tiles][8][kBM]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 16 * kBM);  // 0: B; 1: accumulators ready
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int need = GK * (n_cta > 0 ? n_cta : 0);
-    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : need <= 256 ? 256u : 512u;
+    const uint32_t ncols = need <= 32 ? 32u : need <= 64 ? 64u : need <= 128 ? 128u : 256u;
     for (int i = tid; i < 16 * kBM; i += kThreads) part[i] = 0.0f;
     if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
     if (tid == 0) {
-        for (int i = 0; i < 4; ++i) mbar_init(smem_addr(&bars[i]), 1);
+        for (int i = 0; i < 2; ++i) mbar_init(smem_addr(&bars[i]), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -452,27 +454,23 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     tc_fence_after();
     const uint32_t tmem = live ? *tmem_slot : 0u;
 
-    // All stages' weights, once: per 64-channel chunk the codes, then the units
-    // of group 0 and group 1 (image layout of build_wimg_ord_kernel).
+    // The weights, once: per 64-channel chunk the codes, then the units of
+    // group 0 and group 1 (image layout of build_wimg_ord_kernel, one stage).
     if (live && tid == 0) {
-        mbar_expect_tx(smem_addr(&bars[0]), static_cast<uint32_t>(S * n_cta * kImgRow));
-        for (int st = 0; st < S; ++st) {
-            for (int c = 0; c < kChunks; ++c) {
-                const int cn0 = n0 + c * kNCta;
-                const int n_c = min(kNCta, p.out_c - cn0);
-                if (n_c <= 0) break;
-                const uint8_t* img = p.wimg + (static_cast<int64_t>(cn0) * S + static_cast<int64_t>(st) * n_c) * kImgRow;
-                bulk_g2s(smem_addr(b_codes + (st * W + c * kNCta) * 128), img, static_cast<uint32_t>(n_c * 128),
-                         smem_addr(&bars[0]));
-                for (int j = 0; j < 2; ++j)
-                    bulk_g2s(smem_addr(b_units + (st * 2 + j) * W + c * kNCta), img + n_c * 128 + j * n_c * 4,
-                             static_cast<uint32_t>(n_c * 4), smem_addr(&bars[0]));
-            }
+        mbar_expect_tx(smem_addr(&bars[0]), static_cast<uint32_t>(n_cta * kImgRow));
+        for (int c = 0; c < kChunks; ++c) {
+            const int cn0 = n0 + c * kNCta;
+            const int n_c = min(kNCta, p.out_c - cn0);
+            if (n_c <= 0) break;
+            const uint8_t* img = p.wimg + static_cast<int64_t>(cn0) * kImgRow;
+            bulk_g2s(smem_addr(b_codes + c * kNCta * 128), img, static_cast<uint32_t>(n_c * 128), smem_addr(&bars[0]));
+            for (int j = 0; j < 2; ++j)
+                bulk_g2s(smem_addr(b_units + j * W + c * kNCta), img + n_c * 128 + j * n_c * 4,
+                         static_cast<uint32_t>(n_c * 4), smem_addr(&bars[0]));
         }
     }
 
     const int prow = tid & (kBM - 1), pg = tid >> 7;
-    const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
     const uint32_t idesc = instr_desc(n_cta > 0 ? n_cta : 32);
     const int q = warp & 3, hw = warp >> 2;
     const int erow = q * 32 + lane;
@@ -482,77 +480,63 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
 
     // A run of consecutive row tiles per CTA (the same for every CTA of a
-    // cluster): the weights are fetched once; each tile's MMAs have completed
-    // (its accumulator barrier) before the next tile restages A and reuses TMEM.
+    // cluster); each tile's MMAs have completed (the accumulator barrier)
+    // before the next tile restages A and reuses TMEM.
     const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
     const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
     const int my_tiles = tile0 < n_tiles ? static_cast<int>(min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0)) : 0;
     for (int t = 0; t < my_tiles; ++t) {
         const int64_t m0 = (tile0 + t) * kBM;
         const int64_t prow_g = m0 + prow;
-        const bool prow_ok = prow_g < p.rows;
-        for (int st = 0; live && st < S; ++st) {
-            const int buf = st & 1;
-            uint8_t* a_tile = a_tiles + buf * kTileA;
-            __syncthreads();
-            if (*abort_flag) break;
-            const int gk = 2 * st + pg;
+        __syncthreads();  // the previous tile's chain has read din_s
+        if (live && pg < GK && !*abort_flag) {
             float du = 0.0f;
-            if (prow_ok && gk < GK) {
-                const int tap = gk / G, g = gk - tap * G;
-                const int64_t pix = tap_pixel_pow2(prow_g, tap, KS, lg_din, lg_dout);
-                const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + pix * G + g);
-                du = unit_of(__ldg(p.in_s + pix * G + g));
+            if (prow_g < p.rows) {
+                const int64_t gi = prow_g * GK + pg;  // pointwise: the row's own pixel, group pg
+                const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
+                du = unit_of(__ldg(p.in_s + gi));
                 stage_group_f(a_tile, prow, pg, words, 1.0f);
             } else {
                 stage_zero(a_tile, prow, pg);
             }
-            if (gk < GK) din_s[gk * kBM + prow] = du;
-            fence_async_smem();
-            __syncthreads();
-            if (tid == 0) {
-                if (t > 0 || st > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 22)) {
-                    tc_fence_after();
-                    const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_codes + st * W * 128);
-                    const int n_mma = 2 * st + 1 < GK ? kBK / 16 : kBK / 32;
-#pragma unroll
-                    for (int j = 0; j < kBK / 16; ++j)
-                        if (j < n_mma)
-                            mma_bf16(tmem + static_cast<uint32_t>((2 * st + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
-                                     smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
-                } else {
-                    *abort_flag = 1;
-                }
-            }
+            din_s[pg * kBM + prow] = du;
         }
-        if (live && tid == 0) mma_commit(smem_addr(&bars[3]));
+        fence_async_smem();
+        __syncthreads();
+        if (live && tid == 0) {
+            if (!*abort_flag && (t > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 22))) {
+                tc_fence_after();
+                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_codes);
+                // two K16 MMAs per group; group 1's half of A is not read with one group
+                const int n_mma = GK == 2 ? kBK / 16 : kBK / 32;
+#pragma unroll
+                for (int j = 0; j < kBK / 16; ++j)
+                    if (j < n_mma)
+                        mma_bf16(tmem + static_cast<uint32_t>((j >> 1) * n_cta), smem_desc(a_addr + 32 * j),
+                                 smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
+            } else {
+                *abort_flag = 1;
+            }
+            mma_commit(smem_addr(&bars[1]));  // arrives once the MMAs (if any) complete
+        }
         __syncthreads();
         bool ok = live && !*abort_flag;
         if (live) {
-            if (!mbar_wait(smem_addr(&bars[3]), static_cast<uint32_t>(t & 1), p.err, 23)) ok = false;
+            if (!mbar_wait(smem_addr(&bars[1]), static_cast<uint32_t>(t & 1), p.err, 23)) ok = false;
             tc_fence_after();
         }
 
-        // Pass 1: chain, tap fold and square-sum per 32-channel group; the
-        // pre-norm sums go back to TMEM slice 0.
+        // Pass 1: chain and square-sum per 32-channel group; the pre-norm
+        // sums go back to TMEM slice 0.
         float* part_t = part + (t & 1) * 8 * kBM;
         if (ok) {
             for (int cg = hw; cg < ngroups; cg += 2) {
-                float acc[32], sacc[KS == 1 ? 1 : 32];
+                float acc[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-#pragma unroll
-                for (int i = 0; i < (KS == 1 ? 1 : 32); ++i) sacc[i] = 0.0f;
                 for (int g = 0; g < GK; ++g) {
-                    if (KS == 2 && g > 0 && g % G == 0) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) {
-                            sacc[KS == 1 ? 0 : i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
-                            acc[i] = 0.0f;
-                        }
-                    }
                     const float du = din_s[g * kBM + erow];
-                    const float4* u4 = reinterpret_cast<const float4*>(b_units + ((g >> 1) * 2 + (g & 1)) * W + 32 * cg);
+                    const float4* u4 = reinterpret_cast<const float4*>(b_units + g * W + 32 * cg);
 #pragma unroll
                     for (int h16 = 0; h16 < 2; ++h16) {
                         float pv[16];
@@ -567,10 +551,6 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
                             acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
                         }
                     }
-                }
-                if (KS == 2) {
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[KS == 1 ? 0 : i], acc[i]);
                 }
                 const float gs2 = tree_sq32(acc);
                 float* dst = &part_t[(gbase + cg) * kBM + erow];
@@ -732,18 +712,15 @@ cudaError_t launch_build_wimg_ord(const uint32_t* w, const int8_t* w_s, int in_c
     return cudaGetLastError();
 }
 
-template <int KS, int CS, int W>
+template <int CS, bool ONE>
 cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
 {
-    // a single group per output (K = 32) leaves room for four CTAs per SM
-    auto kern = p.gk_total == 1
-                    ? (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, true> : conv_gemm_tc_cae_kernel<KS, CS, false, W, true>)
-                    : (p.act ? conv_gemm_tc_cae_kernel<KS, CS, true, W, false> : conv_gemm_tc_cae_kernel<KS, CS, false, W, false>);
-    size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * W * 128 + 2 * 2 * W * 4 +
-                  (kCaeMaxGroups * kBM + W + 16 * kBM) * sizeof(float) + 4 * 8 + 16;
+    auto kern = p.act ? conv_gemm_tc_cae_kernel<CS, true, ONE> : conv_gemm_tc_cae_kernel<CS, false, ONE>;
+    size_t smem = 1024 + static_cast<size_t>(kTileA) + kCaeW * 128 + 2 * kCaeW * 4 +
+                  (2 * kBM + kCaeW + 16 * kBM) * sizeof(float) + 2 * 8 + 8;
     // Never let more CTAs share an SM than its 512 TMEM columns can serve.
-    const int need = p.gk_total * (p.out_c < W ? p.out_c : W);
-    const int tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : need <= 256 ? 256 : 512;
+    const int need = p.gk_total * (p.out_c < kCaeW ? p.out_c : kCaeW);
+    const int tmem_cols = need <= 32 ? 32 : need <= 64 ? 64 : need <= 128 ? 128 : 256;
     const size_t floor_smem = 233472 / (512 / tmem_cols + 1) + 1;
     if (smem < floor_smem) smem = floor_smem;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -774,20 +751,14 @@ cudaError_t launch_cae(const OrdParams& p, unsigned chunks, cudaStream_t stream)
     return cudaGetLastError();
 }
 
-// Chain-at-end dispatch: W = 128 for up to two groups, else 64; CS CTAs per
-// norm chunk.
-template <int KS>
-cudaError_t launch_cae_w(const OrdParams& p, cudaStream_t stream)
+// Chain-at-end dispatch (pointwise, one or two groups): one CTA per 128
+// channels, a cluster of two per 256-channel norm chunk.
+cudaError_t launch_cae_pw(const OrdParams& p, cudaStream_t stream)
 {
     const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
-    const int w = p.out_c < kNormChunk ? p.out_c : kNormChunk;
-    if (p.gk_total <= 2) {
-        if (w <= 128) return launch_cae<KS, 1, 128>(p, chunks, stream);
-        return launch_cae<KS, 2, 128>(p, chunks, stream);
-    }
-    if (w <= 64) return launch_cae<KS, 1, 64>(p, chunks, stream);
-    if (w <= 128) return launch_cae<KS, 2, 64>(p, chunks, stream);
-    return launch_cae<KS, 4, 64>(p, chunks, stream);
+    const bool narrow = p.out_c <= kCaeW;
+    if (p.gk_total == 1) return narrow ? launch_cae<1, true>(p, chunks, stream) : launch_cae<2, true>(p, chunks, stream);
+    return narrow ? launch_cae<1, false>(p, chunks, stream) : launch_cae<2, false>(p, chunks, stream);
 }
 
 cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, const uint8_t* wimg, const float* bias,
@@ -809,7 +780,7 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // measured: the chain at the end wins with one or two groups per output,
     // the streaming kernel from three on
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
-        return launch_cae_w<1>(p, stream);
+        return launch_cae_pw(p, stream);
     const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * static_cast<size_t>(slot_b) +
                   (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;
