@@ -99,6 +99,24 @@ __device__ __forceinline__ float rcp_rn_ge1(float d)
 __device__ __forceinline__ float sigmoid_f(float x) { return rcp_rn_ge1(1.0f + __expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
 
+// ---- packed fp32 pairs (the sm_100 two-lane FFMA/FADD/FMUL) -----------------
+// Each component of __ffma2_rn / __fadd2_rn / __fmul2_rn is rounded exactly as
+// the scalar __fmaf_rn / __fadd_rn / __fmul_rn, so two independent
+// per-channel chains run as one instruction stream and keep the scalar bits.
+__device__ __forceinline__ float2 dup2(float a) { return make_float2(a, a); }
+
+// silu_f of both components (the same operations, the arithmetic paired).
+__device__ __forceinline__ float2 silu2(float2 x)
+{
+    const float2 d = __fadd2_rn(dup2(1.0f), make_float2(__expf(-x.x), __expf(-x.y)));
+    const float2 dc = make_float2(fminf(d.x, 3.40282347e38f), fminf(d.y, 3.40282347e38f));
+    float2 y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y.x) : "f"(dc.x));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y.y) : "f"(dc.y));
+    const float2 r = __ffma2_rn(make_float2(-dc.x, -dc.y), y, dup2(1.0f));
+    return __fmul2_rn(x, __ffma2_rn(r, y, y));
+}
+
 
 // Quantise 32 values held as 8 per lane across 4 consecutive lanes (lane & 3
 // selects the word). Returns this lane's packed word; *exp_out gets the
@@ -130,6 +148,27 @@ __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* word
     uint32_t w[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn_fast(v[i], inv) << ((i & 7) << 2);
+    *words = make_uint4(w[0], w[1], w[2], w[3]);
+    *exp_out = exponent_of(scale);
+}
+
+// quantize_group over 32 values held as 16 pairs (value 2i + j in v[i].j).
+__device__ __forceinline__ void quantize_group2(const float2 (&v)[16], uint4* words, int8_t* exp_out)
+{
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
+    const float scale = amax < kEps ? 1.0f : amax;
+    const float2 inv = dup2(kQMax * __frcp_rn(scale));
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        float2 y = __fmul2_rn(v[i], inv);
+        y = make_float2(fminf(fmaxf(y.x, -8.0f), 7.0f), fminf(fmaxf(y.y, -8.0f), 7.0f));
+        y = __fadd2_rn(y, dup2(12582912.0f));  // code_rn_fast of both
+        const uint32_t two = (__float_as_uint(y.x) & 0xFu) | ((__float_as_uint(y.y) & 0xFu) << 4);
+        w[i >> 2] |= two << ((i & 3) << 3);
+    }
     *words = make_uint4(w[0], w[1], w[2], w[3]);
     *exp_out = exponent_of(scale);
 }

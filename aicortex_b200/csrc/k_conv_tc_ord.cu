@@ -100,6 +100,20 @@ __device__ __forceinline__ float tree_sq32(const float (&a)[32])
     return t[0];
 }
 
+// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j): the
+// same tree, two lanes of it per instruction.
+__device__ __forceinline__ float tree_sq32x2(const float2 (&a)[16])
+{
+    float2 t[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t[i] = __fadd2_rn(__fmul2_rn(a[i], a[i]), __fmul2_rn(a[i + 8], a[i + 8]));
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < o; ++i) t[i] = __fadd2_rn(t[i], t[i + o]);
+    return __fadd_rn(t[0].x, t[0].y);
+}
+
 // TMEM columns: per-group accumulators of n channels, double buffered over
 // stages (a single stage needs one buffer, a single group one slot).
 __host__ __device__ inline uint32_t ord_tmem_cols(int n, int stages, int gk_total)
@@ -169,11 +183,11 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     const bool has_cols = hw < (n_cta >> 5);
     const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(32 * hw);
     constexpr bool kFold = KS == 2 && !G1;  // finished taps kept apart from the running chain
-    float acc[32], sacc[kFold ? 32 : 1];
+    float2 acc[16], sacc[kFold ? 16 : 1];  // channel pairs
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 16; ++i) acc[i] = dup2(0.0f);
 #pragma unroll
-    for (int i = 0; i < (kFold ? 32 : 1); ++i) sacc[i] = 0.0f;
+    for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
 
     // fmaf chain over the groups of global stage gc (stage sc of its tile)
     auto chain = [&](int gc, int sc) -> bool {
@@ -189,13 +203,13 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             if (gk >= GK) break;
             if (kFold && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    sacc[kFold ? i : 0] = __fadd_rn(sacc[kFold ? i : 0], acc[i]);
-                    acc[i] = 0.0f;
+                for (int i = 0; i < 16; ++i) {
+                    sacc[kFold ? i : 0] = __fadd2_rn(sacc[kFold ? i : 0], acc[i]);
+                    acc[i] = dup2(0.0f);
                 }
             }
-            if (G1 && has_cols) {
-                const float du = dins[j * kBM];
+            if (has_cols) {
+                const float2 du = dup2(dins[j * kBM]);
                 const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta);
 #pragma unroll
                 for (int h16 = 0; h16 < 2; ++h16) {
@@ -204,28 +218,16 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
                     for (int i4 = 0; i4 < 4; ++i4) {
                         const float4 u = u4[4 * h16 + i4];
-                        const int b = 16 * h16 + 4 * i4;
-                        acc[b + 0] = __fadd_rn(acc[b + 0], __fmul_rn(du, __fmul_rn(u.x, pv[4 * i4 + 0])));
-                        acc[b + 1] = __fadd_rn(acc[b + 1], __fmul_rn(du, __fmul_rn(u.y, pv[4 * i4 + 1])));
-                        acc[b + 2] = __fadd_rn(acc[b + 2], __fmul_rn(du, __fmul_rn(u.z, pv[4 * i4 + 2])));
-                        acc[b + 3] = __fadd_rn(acc[b + 3], __fmul_rn(du, __fmul_rn(u.w, pv[4 * i4 + 3])));
-                    }
-                }
-            } else if (has_cols) {
-                const float du = dins[j * kBM];
-                const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta);
-#pragma unroll
-                for (int h16 = 0; h16 < 2; ++h16) {
-                    float pv[16];
-                    tmem_ld16(tb + static_cast<uint32_t>(j * n_cta + 16 * h16), pv);
-#pragma unroll
-                    for (int i4 = 0; i4 < 4; ++i4) {
-                        const float4 u = u4[4 * h16 + i4];
-                        const int b = 16 * h16 + 4 * i4;
-                        acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
-                        acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
-                        acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
-                        acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
+                        const int b = 8 * h16 + 2 * i4;
+                        const float2 p0 = __fmul2_rn(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1]));
+                        const float2 p1 = __fmul2_rn(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3]));
+                        if (G1) {
+                            acc[b] = __fadd2_rn(acc[b], __fmul2_rn(du, p0));
+                            acc[b + 1] = __fadd2_rn(acc[b + 1], __fmul2_rn(du, p1));
+                        } else {
+                            acc[b] = __ffma2_rn(du, p0, acc[b]);
+                            acc[b + 1] = __ffma2_rn(du, p1, acc[b + 1]);
+                        }
                     }
                 }
             }
@@ -338,10 +340,10 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         const bool emit = run && ok && has_cols;
         if (kFold) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[i] = __fadd_rn(sacc[kFold ? i : 0], acc[i]);
+            for (int i = 0; i < 16; ++i) acc[i] = __fadd2_rn(sacc[kFold ? i : 0], acc[i]);
         }
         if (emit) {
-            const float gs2 = tree_sq32(acc);
+            const float gs2 = tree_sq32x2(acc);
             float* dst = &part_t[(((n0 & (kNormChunk - 1)) >> 5) + hw) * kBM + erow];
             if (CS > 1) {
 #pragma unroll
@@ -363,20 +365,21 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
                 for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
             const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
             const int64_t row = tile * kBM + erow;
+            const float2 sc2 = dup2(sc_norm);
             const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * hw);
 #pragma unroll
             for (int i4 = 0; i4 < 8; ++i4) {
                 const float4 b = b4[i4];
-                const float bb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float x = fmaf(acc[4 * i4 + k], sc_norm, bb[k]);
-                    acc[4 * i4 + k] = ACT ? silu_f(x) : x;
+                acc[2 * i4] = __ffma2_rn(acc[2 * i4], sc2, make_float2(b.x, b.y));
+                acc[2 * i4 + 1] = __ffma2_rn(acc[2 * i4 + 1], sc2, make_float2(b.z, b.w));
+                if (ACT) {
+                    acc[2 * i4] = silu2(acc[2 * i4]);
+                    acc[2 * i4 + 1] = silu2(acc[2 * i4 + 1]);
                 }
             }
             uint4 words;
             int8_t e;
-            quantize_group(acc, &words, &e);
+            quantize_group2(acc, &words, &e);
             if (row < p.rows) {
                 const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + hw;
                 reinterpret_cast<uint4*>(p.out)[gi] = words;
@@ -384,9 +387,9 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < 16; ++i) acc[i] = dup2(0.0f);
 #pragma unroll
-        for (int i = 0; i < (kFold ? 32 : 1); ++i) sacc[i] = 0.0f;
+        for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
     }
     if (live) {
         // every MMA this CTA issued has completed before TMEM is released
@@ -531,11 +534,11 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
         float* part_t = part + (t & 1) * 8 * kBM;
         if (ok) {
             for (int cg = hw; cg < ngroups; cg += 2) {
-                float acc[32];
+                float2 acc[16];  // channel pairs
 #pragma unroll
-                for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+                for (int i = 0; i < 16; ++i) acc[i] = dup2(0.0f);
                 for (int g = 0; g < GK; ++g) {
-                    const float du = din_s[g * kBM + erow];
+                    const float2 du = dup2(din_s[g * kBM + erow]);
                     const float4* u4 = reinterpret_cast<const float4*>(b_units + g * W + 32 * cg);
 #pragma unroll
                     for (int h16 = 0; h16 < 2; ++h16) {
@@ -544,15 +547,15 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 #pragma unroll
                         for (int i4 = 0; i4 < 4; ++i4) {
                             const float4 u = u4[4 * h16 + i4];
-                            const int b = 16 * h16 + 4 * i4;
-                            acc[b + 0] = fmaf(du, __fmul_rn(u.x, pv[4 * i4 + 0]), acc[b + 0]);
-                            acc[b + 1] = fmaf(du, __fmul_rn(u.y, pv[4 * i4 + 1]), acc[b + 1]);
-                            acc[b + 2] = fmaf(du, __fmul_rn(u.z, pv[4 * i4 + 2]), acc[b + 2]);
-                            acc[b + 3] = fmaf(du, __fmul_rn(u.w, pv[4 * i4 + 3]), acc[b + 3]);
+                            const int b = 8 * h16 + 2 * i4;
+                            acc[b] = __ffma2_rn(du, __fmul2_rn(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1])),
+                                                acc[b]);
+                            acc[b + 1] = __ffma2_rn(
+                                du, __fmul2_rn(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3])), acc[b + 1]);
                         }
                     }
                 }
-                const float gs2 = tree_sq32(acc);
+                const float gs2 = tree_sq32x2(acc);
                 float* dst = &part_t[(gbase + cg) * kBM + erow];
                 if (CS > 1) {
 #pragma unroll
@@ -577,23 +580,25 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
                 for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
             const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
             const int64_t row = m0 + erow;
+            const float2 sc2 = dup2(sc_norm);
             for (int cg = hw; cg < ngroups; cg += 2) {
                 float v[32];
                 tmem_ld32(tl + static_cast<uint32_t>(32 * cg), v);
                 const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * cg);
+                float2 x[16];
 #pragma unroll
                 for (int i4 = 0; i4 < 8; ++i4) {
                     const float4 b = b4[i4];
-                    const float bb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float x = fmaf(v[4 * i4 + k], sc_norm, bb[k]);
-                        v[4 * i4 + k] = ACT ? silu_f(x) : x;
+                    x[2 * i4] = __ffma2_rn(make_float2(v[4 * i4], v[4 * i4 + 1]), sc2, make_float2(b.x, b.y));
+                    x[2 * i4 + 1] = __ffma2_rn(make_float2(v[4 * i4 + 2], v[4 * i4 + 3]), sc2, make_float2(b.z, b.w));
+                    if (ACT) {
+                        x[2 * i4] = silu2(x[2 * i4]);
+                        x[2 * i4 + 1] = silu2(x[2 * i4 + 1]);
                     }
                 }
                 uint4 words;
                 int8_t e;
-                quantize_group(v, &words, &e);
+                quantize_group2(x, &words, &e);
                 if (row < p.rows) {
                     const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + cg;
                     reinterpret_cast<uint4*>(p.out)[gi] = words;

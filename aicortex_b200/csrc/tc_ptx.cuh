@@ -168,6 +168,17 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
         : "memory");
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
+// tmem_st32 of 32 values held as 16 pairs (value 2i + j in v[i].j)
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 (&v)[16])
+{
+    float f[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        f[2 * i] = v[i].x;
+        f[2 * i + 1] = v[i].y;
+    }
+    tmem_st32(taddr, f);
+}
 
 // ---- int4 -> bf16 staging ----------------------------------------------------
 
