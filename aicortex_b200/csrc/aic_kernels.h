@@ -60,7 +60,7 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
                                     uint32_t* out, int8_t* out_s, int64_t frames, int in_c, int out_c, int ksize,
                                     int din, int dout, bool act, int* err, cudaStream_t stream);
 
-// Compares rcp_rn_ge1 with __frcp_rn over every significand of several
+// Compares rcp_rn_pos with __frcp_rn over every significand of several
 // binades; *mismatches (zeroed by the caller) counts differing results.
 cudaError_t launch_selftest_rcp(unsigned long long* mismatches, float* first_bad, cudaStream_t stream);
 

@@ -102,14 +102,23 @@ __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t*
         if (iy >= 0 && iy < Din && ix >= 0 && ix < Din) {
             const int64_t pix = fbase + static_cast<int64_t>(iy) * Din + ix;
             const uint4 w = __ldg(reinterpret_cast<const uint4*>(in) + pix * G + g);
-            const float u = unit_of(__ldg(in_s + pix * G + g));
+            const float2 u = dup2(unit_of(__ldg(in_s + pix * G + g)));
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                dst[(2 * q) ^ sw] = make_float4(code_f(ww[q], 0) * u, code_f(ww[q], 1) * u, code_f(ww[q], 2) * u,
-                                                code_f(ww[q], 3) * u);
-                dst[(2 * q + 1) ^ sw] = make_float4(code_f(ww[q], 4) * u, code_f(ww[q], 5) * u, code_f(ww[q], 6) * u,
-                                                    code_f(ww[q], 7) * u);
+                // byte j of lo / hi: code 2j / 2j + 1 of the word as n ^ 8; each
+                // is placed in the mantissa of 2^23 (0x4B0000bb = 2^23 + q + 8)
+                const uint32_t lo = (ww[q] & 0x0F0F0F0Fu) ^ 0x08080808u;
+                const uint32_t hi = ((ww[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+                float2 x[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float2 c = make_float2(__uint_as_float(__byte_perm(lo, 0x4B000000u, 0x7440u | j)),
+                                                 __uint_as_float(__byte_perm(hi, 0x4B000000u, 0x7440u | j)));
+                    x[j] = mul2(add2(c, dup2(-8388616.0f)), u);  // code * unit(s_in)
+                }
+                dst[(2 * q) ^ sw] = make_float4(x[0].x, x[0].y, x[1].x, x[1].y);
+                dst[(2 * q + 1) ^ sw] = make_float4(x[2].x, x[2].y, x[3].x, x[3].y);
             }
         } else {
 #pragma unroll
@@ -119,46 +128,75 @@ __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t*
 
     const int cq = threadIdx.x & 7, pp = threadIdx.x >> 3;
     const int c0 = (g << 5) + 4 * cq;
-    float4 wk[K * K];
+    float2 wk[K * K][2];  // channel pairs (4cq, 4cq + 1), (4cq + 2, 4cq + 3)
 #pragma unroll
-    for (int k = 0; k < K * K; ++k) wk[k] = __ldg(reinterpret_cast<const float4*>(wf + static_cast<int64_t>(k) * C + c0));
+    for (int k = 0; k < K * K; ++k) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(wf + static_cast<int64_t>(k) * C + c0));
+        wk[k][0] = make_float2(w.x, w.y);
+        wk[k][1] = make_float2(w.z, w.w);
+    }
     const float4 bv = __ldg(reinterpret_cast<const float4*>(bias + c0));
+    const float2 b01 = make_float2(bv.x, bv.y), b23 = make_float2(bv.z, bv.w);
+    // Thread (cq, pp) computes output pixels (oy + 4h, ox), h < TH / 4. Its
+    // tap k reads input pixel ip0 + 4 h S kWin + (k / K) kWin + k % K; S kWin
+    // is even, so 4 h S kWin is a multiple of 8 and the swizzled quad position
+    // of every tap is the same for all h: the offsets are computed once.
+    static_assert((S * kWin) % 2 == 0, "the swizzle phase must repeat every 4 output rows");
+    const int oy = pp >> 3, ox = pp & 7;
+    const int ip0 = oy * S * kWin + ox * S;
+    int off[K * K];
+#pragma unroll
+    for (int k = 0; k < K * K; ++k) {
+        const int ip = ip0 + (k / K) * kWin + k % K;
+        off[k] = ip * 8 + (cq ^ (ip & 7));
+    }
     __syncthreads();
 
 #pragma unroll
-    for (int half = 0; half < TH / 4; ++half) {
-        const int pt = pp + 32 * half;
-        const int oy = pt >> 3, ox = pt & 7;
-        float a[4][4];
+    for (int h = 0; h < TH / 4; ++h) {
+        const float4* xh = xs + h * 4 * S * kWin * 8;
+        float2 a[4][2];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) a[c][e] = 0.0f;
+        for (int t = 0; t < 4; ++t) a[t][0] = a[t][1] = dup2(0.0f);
 #pragma unroll
         for (int k = 0; k < K * K; ++k) {
-            const int ip = (oy * S + k / K) * kWin + ox * S + k % K;
-            const float4 x = xs[ip * 8 + (cq ^ (ip & 7))];
-            a[k & 3][0] = fmaf(x.x, wk[k].x, a[k & 3][0]);
-            a[k & 3][1] = fmaf(x.y, wk[k].y, a[k & 3][1]);
-            a[k & 3][2] = fmaf(x.z, wk[k].z, a[k & 3][2]);
-            a[k & 3][3] = fmaf(x.w, wk[k].w, a[k & 3][3]);
+            const float4 x = xh[off[k]];
+            a[k & 3][0] = fma2(make_float2(x.x, x.y), wk[k][0], a[k & 3][0]);
+            a[k & 3][1] = fma2(make_float2(x.z, x.w), wk[k][1], a[k & 3][1]);
         }
-        const float bb[4] = {bv.x, bv.y, bv.z, bv.w};
-        float v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = bb[e] + (a[0][e] + a[1][e] + a[2][e] + a[3][e]);
-        // 32-channel group = 8 lanes (cq 0..7) of this pixel
-        float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
-        const float scale = amax < kEps ? 1.0f : amax;
-        const float inv = kQMax * __frcp_rn(scale);
-        uint32_t h16 = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) h16 |= code_rn_fast(v[e], inv) << (4 * e);
+        const float2 v0 = add2(b01, add2(add2(add2(a[0][0], a[1][0]), a[2][0]), a[3][0]));
+        const float2 v1 = add2(b23, add2(add2(add2(a[0][1], a[1][1]), a[2][1]), a[3][1]));
+        // 32-channel group = 8 lanes (cq 0..7) of this pixel; requant as
+        // quantize_group2 does (a warp whose groups are all finite skips the
+        // clamps; any NaN or infinity sends the warp through the reference's
+        // sequence)
+        float amax = amax_nan(amax_nan(amax_nan(amax_nan(0.0f, v0.x), v0.y), v1.x), v1.y);
+        amax = max_nan(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+        amax = max_nan(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+        amax = max_nan(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 4));
+        float scale;
+        uint32_t h16;
+        if (__any_sync(0xFFFFFFFFu, !is_finite_amax(amax))) {
+            float a = fmaxf(fmaxf(fmaxf(butterfly_start(), fabsf(v0.x)), fabsf(v0.y)), fmaxf(fabsf(v1.x), fabsf(v1.y)));
+            a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 1));
+            a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 2));
+            a = fmaxf(a, __shfl_xor_sync(0xFFFFFFFFu, a, 4));
+            scale = a < kEps ? 1.0f : a;
+            const float inv = kQMax * rcp_rn_pos(scale);
+            h16 = code_rn(v0.x, inv) | (code_rn(v0.y, inv) << 4) | (code_rn(v1.x, inv) << 8) | (code_rn(v1.y, inv) << 12);
+        } else {
+            scale = amax < kEps ? 1.0f : amax;
+            const float inv = kQMax * rcp_rn_pos(scale);
+            // bits 0x4B400000 + q_i -> nibbles, as pack8_magic does for 8 codes
+            // (scalar: the product is rounded before the add)
+            uint32_t h = magic_bits(__fmul_rn(v1.y, inv));
+            h = (h << 4) + magic_bits(__fmul_rn(v1.x, inv));
+            h = (h << 4) + magic_bits(__fmul_rn(v0.y, inv));
+            h = (h << 4) + magic_bits(__fmul_rn(v0.x, inv));
+            h16 = ((h - 0x4B3FFFF8u * 0x1111u) ^ 0x8888u) & 0xFFFFu;
+        }
         const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, h16, 1);
-        const int oyy = oy0 + oy, oxx = ox0 + ox;
+        const int oyy = oy0 + oy + 4 * h, oxx = ox0 + ox;
         if (oyy < Dout && oxx < Dout) {
             const int64_t opix = frame * Dout * Dout + static_cast<int64_t>(oyy) * Dout + oxx;
             if ((cq & 1) == 0) out[opix * (C >> 3) + 4 * g + (cq >> 1)] = h16 | (other << 16);

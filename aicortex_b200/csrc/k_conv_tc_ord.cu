@@ -100,18 +100,17 @@ __device__ __forceinline__ float tree_sq32(const float (&a)[32])
     return t[0];
 }
 
-// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j): the
-// same tree, two lanes of it per instruction.
+// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j), in
+// scalar arithmetic (a square feeding a sum must not be fused).
 __device__ __forceinline__ float tree_sq32x2(const float2 (&a)[16])
 {
-    float2 t[8];
+    float f[32];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t[i] = __fadd2_rn(__fmul2_rn(a[i], a[i]), __fmul2_rn(a[i + 8], a[i + 8]));
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < o; ++i) t[i] = __fadd2_rn(t[i], t[i + o]);
-    return __fadd_rn(t[0].x, t[0].y);
+    for (int i = 0; i < 16; ++i) {
+        f[2 * i] = a[i].x;
+        f[2 * i + 1] = a[i].y;
+    }
+    return tree_sq32(f);
 }
 
 // TMEM columns: per-group accumulators of n channels, double buffered over
@@ -204,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             if (kFold && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    sacc[kFold ? i : 0] = __fadd2_rn(sacc[kFold ? i : 0], acc[i]);
+                    sacc[kFold ? i : 0] = add2(sacc[kFold ? i : 0], acc[i]);
                     acc[i] = dup2(0.0f);
                 }
             }
@@ -219,14 +218,16 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
                     for (int i4 = 0; i4 < 4; ++i4) {
                         const float4 u = u4[4 * h16 + i4];
                         const int b = 8 * h16 + 2 * i4;
-                        const float2 p0 = __fmul2_rn(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1]));
-                        const float2 p1 = __fmul2_rn(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3]));
-                        if (G1) {
-                            acc[b] = __fadd2_rn(acc[b], __fmul2_rn(du, p0));
-                            acc[b + 1] = __fadd2_rn(acc[b + 1], __fmul2_rn(du, p1));
+                        const float2 p0 = mul2(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1]));
+                        const float2 p1 = mul2(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3]));
+                        if (G1) {  // scalar: the product is rounded before the add
+                            acc[b].x = __fadd_rn(acc[b].x, __fmul_rn(du.x, p0.x));
+                            acc[b].y = __fadd_rn(acc[b].y, __fmul_rn(du.y, p0.y));
+                            acc[b + 1].x = __fadd_rn(acc[b + 1].x, __fmul_rn(du.x, p1.x));
+                            acc[b + 1].y = __fadd_rn(acc[b + 1].y, __fmul_rn(du.y, p1.y));
                         } else {
-                            acc[b] = __ffma2_rn(du, p0, acc[b]);
-                            acc[b + 1] = __ffma2_rn(du, p1, acc[b + 1]);
+                            acc[b] = fma2(du, p0, acc[b]);
+                            acc[b + 1] = fma2(du, p1, acc[b + 1]);
                         }
                     }
                 }
@@ -302,15 +303,16 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         if (produce && tid == 0) {
             if (!fetch_b || mbar_wait(smem_addr(&bars[buf]), static_cast<uint32_t>(gs >> 1) & 1u, p.err, 11)) {
                 tc_fence_after();
-                const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_tile);
+                // K16 steps advance the SW128 descriptors by 32 bytes (2 in the address field)
+                const uint64_t da = smem_desc(smem_addr(a_tile)), db = smem_desc(smem_addr(b_tile));
                 // two K16 MMAs per group; a padding group (odd group count) has no
                 // accumulator slot and is skipped
                 const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j)
                     if (j < n_mma)
-                        mma_bf16(tmem + static_cast<uint32_t>((buf * 2 + (j >> 1)) * n_cta), smem_desc(a_addr + 32 * j),
-                                 smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
+                        mma_bf16(tmem + static_cast<uint32_t>((buf * 2 + (j >> 1)) * n_cta), da + 2 * j, db + 2 * j, idesc,
+                                 static_cast<uint32_t>(j & 1));
                 mma_commit(smem_addr(&bars[2 + buf]));
             } else {
                 *abort_flag = 1;
@@ -340,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         const bool emit = run && ok && has_cols;
         if (kFold) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = __fadd2_rn(sacc[kFold ? i : 0], acc[i]);
+            for (int i = 0; i < 16; ++i) acc[i] = add2(sacc[kFold ? i : 0], acc[i]);
         }
         if (emit) {
             const float gs2 = tree_sq32x2(acc);
@@ -370,8 +372,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
             for (int i4 = 0; i4 < 8; ++i4) {
                 const float4 b = b4[i4];
-                acc[2 * i4] = __ffma2_rn(acc[2 * i4], sc2, make_float2(b.x, b.y));
-                acc[2 * i4 + 1] = __ffma2_rn(acc[2 * i4 + 1], sc2, make_float2(b.z, b.w));
+                acc[2 * i4] = fma2(acc[2 * i4], sc2, make_float2(b.x, b.y));
+                acc[2 * i4 + 1] = fma2(acc[2 * i4 + 1], sc2, make_float2(b.z, b.w));
                 if (ACT) {
                     acc[2 * i4] = silu2(acc[2 * i4]);
                     acc[2 * i4 + 1] = silu2(acc[2 * i4 + 1]);
@@ -548,10 +550,10 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
                         for (int i4 = 0; i4 < 4; ++i4) {
                             const float4 u = u4[4 * h16 + i4];
                             const int b = 8 * h16 + 2 * i4;
-                            acc[b] = __ffma2_rn(du, __fmul2_rn(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1])),
+                            acc[b] = fma2(du, mul2(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1])),
                                                 acc[b]);
-                            acc[b + 1] = __ffma2_rn(
-                                du, __fmul2_rn(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3])), acc[b + 1]);
+                            acc[b + 1] = fma2(
+                                du, mul2(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3])), acc[b + 1]);
                         }
                     }
                 }
@@ -589,8 +591,8 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 #pragma unroll
                 for (int i4 = 0; i4 < 8; ++i4) {
                     const float4 b = b4[i4];
-                    x[2 * i4] = __ffma2_rn(make_float2(v[4 * i4], v[4 * i4 + 1]), sc2, make_float2(b.x, b.y));
-                    x[2 * i4 + 1] = __ffma2_rn(make_float2(v[4 * i4 + 2], v[4 * i4 + 3]), sc2, make_float2(b.z, b.w));
+                    x[2 * i4] = fma2(make_float2(v[4 * i4], v[4 * i4 + 1]), sc2, make_float2(b.x, b.y));
+                    x[2 * i4 + 1] = fma2(make_float2(v[4 * i4 + 2], v[4 * i4 + 3]), sc2, make_float2(b.z, b.w));
                     if (ACT) {
                         x[2 * i4] = silu2(x[2 * i4]);
                         x[2 * i4 + 1] = silu2(x[2 * i4 + 1]);

@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(kThreads) pack_f32_kernel(const float* __restr
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
     const float scale = amax < kEps ? 1.0f : amax;
     out_s[idx] = exponent_of(scale);
-    const float inv = kQMax * __frcp_rn(scale);
+    const float inv = kQMax * rcp_rn_pos(scale);
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     if (kStochastic) {
         const int64_t rel = row_groups > 0 ? idx % row_groups : idx;
@@ -90,13 +90,14 @@ __global__ void __launch_bounds__(kThreads) stem_pack_kernel(const __half* __res
     for (int g = 0; g < groups; ++g) {
         // channels >= planes_present are zero: code 0, and they do not move the absmax
         const int present = min(32, max(0, planes_present - (g << 5)));
-        float amax = 0.0f;
+        // the reference's butterfly over 32 lanes, padding lanes holding 0
+        float amax = present < 32 ? 0.0f : butterfly_start();
         for (int l = 0; l < present; ++l) amax = fmaxf(amax, fabsf(__half2float(src[static_cast<int64_t>((g << 5) + l) * hw])));
         const float scale = amax < kEps ? 1.0f : amax;
-        const float inv = kQMax * __frcp_rn(scale);
+        const float inv = kQMax * rcp_rn_pos(scale);
         uint32_t w[4] = {0u, 0u, 0u, 0u};
         for (int l = 0; l < present; ++l)
-            w[l >> 3] |= code_rn_fast(__half2float(src[static_cast<int64_t>((g << 5) + l) * hw]), inv) << ((l & 7) << 2);
+            w[l >> 3] |= code_rn(__half2float(src[static_cast<int64_t>((g << 5) + l) * hw]), inv) << ((l & 7) << 2);
         reinterpret_cast<uint4*>(out)[pix * groups + g] = make_uint4(w[0], w[1], w[2], w[3]);
         out_s[pix * groups + g] = exponent_of(scale);
     }
@@ -120,7 +121,8 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
     uint32_t packed_s = 0;
     for (int g = 0; g < groups; ++g) {
         const int present = min(32, max(0, planes_present - (g << 5)));
-        float amax[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float a0 = present < 32 ? 0.0f : butterfly_start();  // as stem_pack_kernel
+        float amax[4] = {a0, a0, a0, a0};
         for (int l = 0; l < present; ++l) {
             const uint2 v = __ldg(reinterpret_cast<const uint2*>(src + static_cast<int64_t>((g << 5) + l) * hw));
             const __half2 h01 = *reinterpret_cast<const __half2*>(&v.x), h23 = *reinterpret_cast<const __half2*>(&v.y);
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const float scale = amax[k] < kEps ? 1.0f : amax[k];
-            inv[k] = kQMax * __frcp_rn(scale);
+            inv[k] = kQMax * rcp_rn_pos(scale);
             ex[k] = exponent_of(scale);
         }
         uint32_t w[4][4] = {};
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
             const __half2 h01 = *reinterpret_cast<const __half2*>(&v.x), h23 = *reinterpret_cast<const __half2*>(&v.y);
             const float x[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) w[k][l >> 3] |= code_rn_fast(x[k], inv[k]) << ((l & 7) << 2);
+            for (int k = 0; k < 4; ++k) w[k][l >> 3] |= code_rn(x[k], inv[k]) << ((l & 7) << 2);
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) ov[k * groups + g] = make_uint4(w[k][0], w[k][1], w[k][2], w[k][3]);
@@ -181,7 +183,7 @@ __global__ void __launch_bounds__(kThreads) residual_kernel(const uint32_t* __re
     if (G == S) {
         // One group per lane: keep the 32 values in registers (single pass).
         float r[32];
-        float amax1 = 0.0f;
+        float amax1 = 0.0f, amaxn = 0.0f;  // the reference's absmax, and one that keeps a NaN
         if (live) {
             const float s_res = unit_of(res_s[pbase * G + gl]);
             const float s_in = skipped ? 0.0f : unit_of(main_s[pbase * G + gl]) * main_mult;
@@ -192,16 +194,30 @@ __global__ void __launch_bounds__(kThreads) residual_kernel(const uint32_t* __re
             for (int i = 0; i < 32; ++i) {
                 r[i] = fmaf(code_f(aw[i >> 3], i & 7), s_in, code_f(bw[i >> 3], i & 7) * s_res);
                 amax1 = fmaxf(amax1, fabsf(r[i]));
+                amaxn = amax_nan(amaxn, r[i]);
             }
         }
 #pragma unroll
-        for (int o = S >> 1; o > 0; o >>= 1) amax1 = fmaxf(amax1, __shfl_xor_sync(0xFFFFFFFFu, amax1, o));
+        for (int o = S >> 1; o > 0; o >>= 1) {
+            amax1 = fmaxf(amax1, __shfl_xor_sync(0xFFFFFFFFu, amax1, o));
+            amaxn = max_nan(amaxn, __shfl_xor_sync(0xFFFFFFFFu, amaxn, o));
+        }
         if (!live) return;
         const float scale1 = amax1 < kEps ? 1.0f : amax1;
-        const float inv1 = kQMax * __frcp_rn(scale1);
+        const float inv1 = kQMax * rcp_rn_pos(scale1);
         uint32_t w[4] = {0u, 0u, 0u, 0u};
+        if (is_finite_amax(amaxn)) {  // no NaN or infinity in the group: rn without the clamp (aic_common.cuh)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn_fast(r[i], inv1) << ((i & 7) << 2);
+            for (int q = 0; q < 4; ++q) {
+                uint32_t z[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) z[i] = magic_bits(__fmul_rn(r[8 * q + i], inv1));
+                w[q] = pack8_magic(z);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn(r[i], inv1) << ((i & 7) << 2);
+        }
         reinterpret_cast<uint4*>(out)[pos * G + gl] = make_uint4(w[0], w[1], w[2], w[3]);
         out_s[pos * G + gl] = exponent_of(scale1);
         return;
@@ -225,7 +241,7 @@ __global__ void __launch_bounds__(kThreads) residual_kernel(const uint32_t* __re
     for (int o = S >> 1; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
     if (!live) return;
     const float scale = amax < kEps ? 1.0f : amax;
-    const float inv = kQMax * __frcp_rn(scale);
+    const float inv = kQMax * rcp_rn_pos(scale);
     const int8_t e_out = exponent_of(scale);
     uint4* ov = reinterpret_cast<uint4*>(out) + pos * G;
     for (int g = gl; g < G; g += S) {
@@ -293,7 +309,7 @@ __global__ void __launch_bounds__(kThreads) gap_kernel(const uint32_t* __restric
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
         const float scale = amax < kEps ? 1.0f : amax;
-        uint32_t q = code_rn(acc, kQMax * __frcp_rn(scale)) << ((lane & 7) << 2);
+        uint32_t q = code_rn(acc, kQMax * rcp_rn_pos(scale)) << ((lane & 7) << 2);
 #pragma unroll
         for (int o = 4; o > 0; o >>= 1) q |= __shfl_down_sync(0xFFFFFFFFu, q, o);
         if ((lane & 7) == 0) out_q[frame * (C >> 3) + (g << 2) + (lane >> 3)] = q;
@@ -400,22 +416,22 @@ cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned
 
 namespace {
 // d = (1 + i / 2^23) * 2^e for every i < 2^23 and the exponents below: counts
-// the d where rcp_rn_ge1 and __frcp_rn differ in any bit.
-__constant__ int kRcpExps[10] = {0, 1, 2, 22, 23, 24, 64, 100, 125, 126};
+// the d where rcp_rn_pos and __frcp_rn differ in any bit.
+__constant__ int kRcpExps[13] = {-13, -7, -1, 0, 1, 2, 22, 23, 24, 64, 100, 125, 126};
 __global__ void selftest_rcp_kernel(unsigned long long* mismatches, float* first_bad)
 {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (1u << 23)) return;
-    for (int k = 0; k < 10; ++k) {
-        const float d = __uint_as_float(((127u + kRcpExps[k]) << 23) | i);
-        if (__float_as_uint(rcp_rn_ge1(d)) != __float_as_uint(__frcp_rn(d))) {
+    for (int k = 0; k < 13; ++k) {
+        const float d = __uint_as_float((static_cast<uint32_t>(127 + kRcpExps[k]) << 23) | i);
+        if (__float_as_uint(rcp_rn_pos(d)) != __float_as_uint(__frcp_rn(d))) {
             if (atomicAdd(mismatches, 1ull) == 0ull) *first_bad = d;
         }
     }
     if (i == 0) {  // the clamped top of the range
         const float top[3] = {3.40282347e38f, __uint_as_float(0x7F800000u), 1.7e38f};
         for (int k = 0; k < 3; ++k)
-            if (__float_as_uint(rcp_rn_ge1(top[k])) != __float_as_uint(__frcp_rn(top[k]))) {
+            if (__float_as_uint(rcp_rn_pos(top[k])) != __float_as_uint(__frcp_rn(top[k]))) {
                 if (atomicAdd(mismatches, 1ull) == 0ull) *first_bad = top[k];
             }
     }

@@ -11,7 +11,8 @@ namespace aic {
 namespace tc {
 
 constexpr int kBM = 128;                 // pixel rows per tile (= TMEM lanes)
-constexpr uint32_t kWaitLimit = 1u << 22; // bounded mbarrier polls (~0.5 s with back-off)
+constexpr uint32_t kWaitLimit = 1u << 22;          // mbarrier polls before a wait gives up
+constexpr uint64_t kWaitNs = 1000000000ull;         // ... or this many nanoseconds, whichever is first
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p)
 {
@@ -28,25 +29,38 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// One poll of the phase with parity `parity`. The suspend-time hint lets the
+// hardware park the thread (up to ~20 us) until the phase completes instead of
+// returning at once, so a waiting warp issues few instructions.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(20000u)
         : "memory");
     return ok != 0;
 }
 
-// Bounded wait; returns false (and records `code`) when the phase never completes.
+__device__ __forceinline__ uint64_t global_ns()
+{
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Bounded wait: at most kWaitLimit polls and about kWaitNs nanoseconds;
+// returns false (and records `code`) when the phase never completes.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code)
 {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
     for (uint32_t i = 0; i < kWaitLimit; ++i) {
         if (mbar_try(bar, parity)) return true;
-        if (i > 256) __nanosleep(128);
+        if (global_ns() - t0 > kWaitNs) break;
     }
     atomicCAS(err, 0, code);
     return false;

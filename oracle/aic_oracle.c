@@ -95,11 +95,15 @@ static inline float orc_rsqrt(float x) { return (float)(1.0 / sqrt((double)x)); 
 static inline float orc_sigmoid(float x) { return orc_rcp(1.0f + expf(-x)); }     /* kernels.h:86 */
 static inline float orc_silu(float x) { return x * orc_sigmoid(x); }              /* kernels.h:87 */
 
-/* kernels.h:70: clamp(rn(v * inv), -8, 7) & 0xF */
+/* kernels.h:70: clamp(__float2int_rn(v * inv), -8, 7) & 0xF. The GPU
+   conversion (cvt.rni.s32.f32) gives 0 for a NaN and saturates infinities;
+   clamping before the conversion gives the same code (rounding is monotonic)
+   and keeps the C conversion defined. */
 static inline uint32_t orc_q_rn(float v, float inv)
 {
-    int q = (int)rintf(v * inv);
-    q = q < -8 ? -8 : (q > 7 ? 7 : q);
+    const float p = v * inv;
+    if (p != p) return 0u;
+    const int q = (int)rintf(fmaxf(-8.0f, fminf(7.0f, p)));
     return (uint32_t)q & 0xFu;
 }
 
@@ -226,7 +230,7 @@ void orc_stem_pack(const uint16_t* planes, int64_t frames, int planes_present,
         const int64_t f = fp / hw, sp = fp % hw;
         for (int g = 0; g < groups; ++g) {
             float v[32];
-            float amax = 0.0f;
+            float amax = NAN; /* the reference reduces |v| by a lane butterfly: NaN only if every value is */
             for (int l = 0; l < 32; ++l) {
                 const int c = (g << 5) + l;
                 v[l] = c < planes_present ? orc_half_to_float(planes[(f * planes_present + c) * hw + sp]) : 0.0f;
@@ -263,7 +267,7 @@ static void orc_conv_epilogue(const float* acc, const float* bias, int OutC, int
         const float inv_rms = orc_rsqrt(fmaf(block_sq, inv_div, ORC_EPS));
         for (int base = c0; base < c0 + ORC_CPB && base < OutC; base += 32) {
             float v[32];
-            float amax = 0.0f;
+            float amax = NAN; /* the reference reduces |v| by a lane butterfly: NaN only if every value is */
             for (int l = 0; l < 32; ++l) {
                 float a = fmaf(acc[base + l], inv_rms, bias[base + l]);
                 if (act) a = orc_silu(a);
@@ -368,7 +372,7 @@ void orc_conv_dw(const uint32_t* in, const int8_t* in_s, const uint32_t* w,
         const int w0 = (p & (Dout - 1)) * stride - pad;
         for (int g = 0; g < G; ++g) {
             float v[32];
-            float amax = 0.0f;
+            float amax = NAN; /* the reference reduces |v| by a lane butterfly: NaN only if every value is */
             for (int l = 0; l < 32; ++l) {
                 const int c = (g << 5) + l;
                 float a = bias[c];

@@ -371,6 +371,46 @@ def test_tensor_core_conv_vs_reference_order(geo):
 
 
 @pytest.mark.parametrize("geo", [
+    (32, 128, 1, 1, 8, 8, 1),    # chain at the end, one group
+    (64, 128, 1, 1, 8, 8, 0),    # chain at the end, two groups
+    (512, 256, 1, 1, 4, 4, 0),   # streaming, 16 groups, clusters of 4
+    (32, 64, 2, 2, 16, 8, 1),    # 2x2, one group per tap
+    (128, 256, 2, 2, 8, 4, 0),   # 2x2, four groups per tap
+    (32, 32, 3, 2, 16, 8, 0),    # depthwise 3x3 / 2 (tiled and direct kernels)
+])
+def test_conv_overflow_vs_oracle(geo):
+    """Activations and weights near the top of the exponent range: the chains
+    overflow to +-inf, the RMSNorm of an infinite row is 0, and inf * 0 or
+    inf - inf leave NaN in the groups. The reference's requant skips a NaN in
+    the absmax and codes it 0 (the int conversion of a NaN); every kernel must
+    agree bit for bit, and with the oracle."""
+    import oracle as O
+    cin, cout, k, st, din, dout, act = geo
+    dw = k > 1 and k % 2 == 1
+    rng = np.random.default_rng(cin + 3 * cout + k)
+    frames = 2
+    m, b = W.conv_weights(rng, cin, cout, k, dw) * np.float32(1e30), W.bias(rng, cout)
+    x = (rng.standard_normal((frames * din * din, cin)) * 1e30).astype(np.float32)
+    xw, xs = O.pack_f32(x)
+    xw, xs = xw.reshape(frames * din * din, -1), xs.reshape(frames * din * din, -1)
+    ow_ref, os_ref = O.conv(xw, xs, *O.pack_conv_layer(m, b), frames, cin, cout, k, st, din, dout, act)
+    layer = A.ConvLayer(cin, cout, k, st, din, dout, disable_activation=not act)
+    layer.load_weights(t(m), t(b))
+    rows = frames * dout * dout
+    ow, os_ = A.empty_f(rows, cout)
+    ew, es = A.empty_f(rows, cout)
+    layer.forward(t(xw.view(np.int32)), t(xs), ow, os_, frames)
+    layer.forward_exact(t(xw.view(np.int32)), t(xs), ew, es, frames)
+    assert_f_equal(ow, h(os_), u32(ew), h(es), f"tensor cores / tiled vs CUDA cores / direct {geo}")
+    zeros = float((u32(ew).view(np.uint8) == 0).mean())
+    assert zeros > 0.05, f"the case should produce NaN groups (zero bytes {zeros:.3f})"
+    # the oracle's rsqrt and exp are correctly rounded host functions: a few
+    # finite values may flip, never the NaN positions
+    assert_f_close(ew, h(es), ow_ref, os_ref, flip_rate=1e-3, what=f"overflow conv vs oracle {geo}")
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("geo", [
     (32, 3, 2, 128, 64),    # the stack's first block, full 8x8 tiles
     (64, 3, 2, 64, 32),
     (96, 3, 1, 16, 16),     # stride 1, three groups
@@ -455,9 +495,10 @@ def test_cortex_forward_is_deterministic():
 
 
 def test_reciprocal_matches_ieee():
-    """The sigmoid's reciprocal (one FMA Newton step from rcp.approx) equals the
-    IEEE round-to-nearest reciprocal __frcp_rn of the reference for every
-    significand of ten binades from 1 to 2^126, and at the clamped top."""
+    """The reciprocal of the sigmoid and the quantisers (one FMA Newton step
+    from rcp.approx) equals the IEEE round-to-nearest reciprocal __frcp_rn of
+    the reference for every significand of thirteen binades from 2^-13 (the
+    smallest quantiser scale) to 2^126, and at the clamped top."""
     bad = torch.zeros(1, dtype=torch.int64, device=DEV)
     first = torch.zeros(1, dtype=torch.float32, device=DEV)
     A._lib.call("aic_selftest_rcp", C.c_void_p(bad.data_ptr()), C.c_void_p(first.data_ptr()),
