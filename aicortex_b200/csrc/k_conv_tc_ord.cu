@@ -252,21 +252,44 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     uint4 pf_words = make_uint4(0u, 0u, 0u, 0u);
     int8_t pf_s = 0;
     bool pf_ok = false;
-    auto prefetch = [&](int t_local, int s_local) {
+    // Per producer tile: the group base of the row's input pixel (pointwise) or
+    // of the top-left pixel of its 2x2 window; within the tile the im2col
+    // position (tap, group g) of group gk = 2 s + pg advances by two groups per
+    // stage, so a stage costs one small offset and no division.
+    const uint4* pf_base = reinterpret_cast<const uint4*>(p.in);
+    const int8_t* pf_sbase = p.in_s;
+    bool pf_row_ok = false;
+    int pf_tap = 0, pf_g = 0;
+    auto start_tile = [&](int t_local) {
         const int64_t row = (tile0 + t_local) * kBM + prow;
-        const int gk = 2 * s_local + pg;
-        pf_ok = live && row < p.rows && gk < GK;
-        if (pf_ok) {
-            int64_t gi = row * G + gk;  // pointwise: the row's own pixel, group gk
-            if (KS == 2) {
-                const int tap = gk / G, g = gk - tap * G;
-                gi = tap_pixel_pow2(row, tap, KS, lg_din, lg_dout) * G + g;
-            }
-            pf_words = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
-            pf_s = __ldg(p.in_s + gi);
+        pf_row_ok = live && row < p.rows;
+        const int64_t pix0 = KS == 2 ? (pf_row_ok ? tap_pixel_pow2(row, 0, KS, lg_din, lg_dout) : 0) : row;
+        pf_base = reinterpret_cast<const uint4*>(p.in) + pix0 * G;
+        pf_sbase = p.in_s + pix0 * G;
+        pf_tap = 0;
+        pf_g = pg;
+        while (pf_g >= G) {  // G == 1: group 1 is tap 1
+            pf_g -= G;
+            ++pf_tap;
         }
     };
-    if (total > 0) prefetch(0, 0);
+    auto prefetch = [&](int s_local) {  // stage s_local of the current producer tile
+        pf_ok = pf_row_ok && 2 * s_local + pg < GK;
+        if (pf_ok) {
+            const int off = (KS == 2 ? (((pf_tap >> 1) << lg_din) + (pf_tap & 1)) * G : 0) + pf_g;
+            pf_words = __ldg(pf_base + off);
+            pf_s = __ldg(pf_sbase + off);
+        }
+        pf_g += 2;
+        while (pf_g >= G) {
+            pf_g -= G;
+            ++pf_tap;
+        }
+    };
+    if (total > 0) {
+        start_tile(0);
+        prefetch(0);
+    }
     for (int gs = 0; gs <= total; ++gs) {
         const int buf = gs & 1;
         __syncthreads();  // stage gs-2's chain is done with this buffer's units and accumulators
@@ -294,8 +317,12 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             fence_async_smem();
             // the stage after this one
             if (gs + 1 < total) {
-                if (sp + 1 == S) prefetch(tp + 1, 0);
-                else prefetch(tp, sp + 1);
+                if (sp + 1 == S) {
+                    start_tile(tp + 1);
+                    prefetch(0);
+                } else {
+                    prefetch(sp + 1);
+                }
             }
         }
         tc_fence_before();
