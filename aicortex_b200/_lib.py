@@ -106,6 +106,8 @@ _SIGS = {
     "aic_mamba_layer_load_file_sync": [P, C.c_char_p, P],
     "aic_mamba_layer_state_bytes": [P, I32, SZ],
     "aic_mamba_layer_bind_state": [P, P, I32],
+    "aic_mamba_layer_trace_bytes": [P, I32, P],
+    "aic_mamba_layer_bind_traces": [P, P, I32],
     "aic_mamba_layer_reset_state": [P, P],
     "aic_mamba_layer_workspace_bytes": [P, I64, SZ],
     "aic_mamba_layer_forward": [P, P, P, P, I32, I32, P, P],
@@ -118,6 +120,8 @@ _SIGS = {
     "aic_mamba_block_bind": [P, P],
     "aic_mamba_block_state_bytes": [P, I32, SZ],
     "aic_mamba_block_bind_state": [P, P, I32],
+    "aic_mamba_block_trace_bytes": [P, I32, P],
+    "aic_mamba_block_bind_traces": [P, P, I32],
     "aic_mamba_block_reset_state": [P, P],
     "aic_mamba_block_workspace_bytes": [P, I64, SZ],
     "aic_mamba_block_load_dir_sync": [P, C.c_char_p, P],
@@ -130,6 +134,8 @@ _SIGS = {
     "aic_critic_load_file_sync": [P, C.c_char_p, P],
     "aic_critic_state_bytes": [P, I32, SZ],
     "aic_critic_bind_state": [P, P, I32],
+    "aic_critic_trace_bytes": [P, I32, P],
+    "aic_critic_bind_traces": [P, P, I32],
     "aic_critic_reset_state": [P, P],
     "aic_critic_workspace_bytes": [P, I64, SZ],
     "aic_critic_forward": [P, P, P, P, I32, I32, P, P],

@@ -85,17 +85,22 @@ cudaError_t launch_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t frame
 cudaError_t launch_ssm_prepare(const uint32_t* blob, const int8_t* blob_s, int D, int d_state, float* consts,
                                cudaStream_t stream);
 size_t ssm_consts_floats(int D, int d_state);
+// traces: nullptr, or trace_A | trace_B | trace_Delta [3][B][E][d_state/32]
+// complex, advanced with the state (training-mode forward, kernels.h:1158-1170).
 cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
-                            const float* consts, int D, int d_state, float2* h, float* y, int B, int T,
+                            const float* consts, int D, int d_state, float2* h, float2* traces, float* y, int B, int T,
                             cudaStream_t stream);
 
 // A10: out-projection GEMM y[rows][E] x W_out -> RMSNorm(256-chunk) + bias + act -> fp32 [rows][out].
 cudaError_t launch_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s, const float* bias, int D,
                            int d_state, int out, int act, int64_t rows, float* o, cudaStream_t stream);
 
-// A13: critic recurrence over T for B sequences; x fp16 [B*T][in].
+// A13: critic recurrence over T for B sequences; x fp16 [B*T][in]. trace_w1
+// [B][in][units] and trace_l [B][units][in] complex: nullptr, or the
+// training-mode eligibility traces, advanced in place (kernels.h:1731-1751).
 cudaError_t launch_critic(const __half* x, const float* w1, const float* wl, const float* w2, int in, int units,
-                          float2* h, float2* h_seq, float* score, int B, int T, cudaStream_t stream);
+                          float2* h, float2* h_seq, float2* trace_w1, float2* trace_l, float* score, int B, int T,
+                          cudaStream_t stream);
 
 // A14: audio front-end (ca.cu): 2048 int16 PCM samples -> two fp16 planes
 // (|X|/N^2, phase of the 1024x1024 fp16 FFT) resized to dim x dim, written to

@@ -430,6 +430,7 @@ struct MambaLayer {
     float* bias = nullptr;
     float* consts = nullptr;
     float2* h = nullptr;
+    float2* traces = nullptr;  // trace_A | trace_B | trace_Delta [3][batch][E][P]; null: inference forward
     int batch_bound = -1;
     bool bound = false;
     Profiler* prof = nullptr;
@@ -482,6 +483,8 @@ struct MambaLayer {
     {
         if (batch_bound < 0) fail(AIC_ERR_STATE, "mamba state not bound");
         cuda_ok(cudaMemsetAsync(h, 0, state_bytes(batch_bound), s), "reset state");
+        // mamba_layer.h:171-177 zeroes the traces with the state
+        if (traces) cuda_ok(cudaMemsetAsync(traces, 0, 3 * state_bytes(batch_bound), s), "reset traces");
     }
     size_t workspace_bytes(int64_t rows) const { return ((static_cast<size_t>(rows) * E * sizeof(float)) + 255) & ~size_t(255); }
     int64_t forward(const uint32_t* in, const int8_t* in_s, float* out, int batch, int seq, void* wsp, cudaStream_t s)
@@ -497,7 +500,7 @@ struct MambaLayer {
         // per (row, channel): 31 flops per state plus ~15 (kernels.h:1126-1176)
         traced(prof, tag + ".scan", s, rows * E * (31.0 * P + 15.0),
                f_bytes(rows * d.d_model) + 4.0 * rows * E + 2.0 * batch * E * P * 8.0 + E * P * 16.0, "ssm scan",
-               [&] { return launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, y, batch, seq, s); });
+               [&] { return launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, traces, y, batch, seq, s); });
         traced(prof, tag + ".outproj", s, 2.0 * rows * E * d.out_channels,
                4.0 * rows * E + f_bytes(static_cast<double>(E) * d.out_channels) + 4.0 * rows * d.out_channels, "outproj",
                [&] {
@@ -543,6 +546,21 @@ struct MambaBlock {
         for (auto& l : layers) {
             l->h = reinterpret_cast<float2*>(c.take<char>(l->state_bytes(batch)));
             l->batch_bound = batch;
+            l->traces = nullptr;  // bound again after the state
+        }
+    }
+    size_t trace_bytes(int batch) const
+    {
+        Carver c(nullptr);
+        for (auto& l : layers) c.take<char>(3 * l->state_bytes(batch));
+        return c.bytes();
+    }
+    void bind_traces(void* base, int batch)
+    {
+        Carver c(base);
+        for (auto& l : layers) {
+            require(batch == l->batch_bound, "traces must be bound for the bound state's batch");
+            l->traces = base ? reinterpret_cast<float2*>(c.take<char>(3 * l->state_bytes(batch))) : nullptr;
         }
     }
     size_t workspace(int64_t rows, void* base, float** y, float** o, uint32_t** a, int8_t** as, uint32_t** b,
@@ -591,6 +609,7 @@ struct Critic {
     aic_critic_desc d;
     float *w1 = nullptr, *w2 = nullptr, *wl = nullptr;
     float2* h = nullptr;
+    float2* traces = nullptr;  // trace_w1 [batch][in][units] | trace_lambda [batch][units][in]; null: inference
     int batch_bound = -1;
     bool bound = false;
     Profiler* prof = nullptr;
@@ -632,10 +651,14 @@ struct Critic {
         cuda_ok(cudaStreamSynchronize(s), "load sync");
     }
     size_t state_bytes(int batch) const { return static_cast<size_t>(batch) * d.units * sizeof(float2); }
+    size_t trace_bytes(int batch) const { return 2 * static_cast<size_t>(batch) * d.in_channels * d.units * sizeof(float2); }
+    float2* trace_l() const { return traces ? traces + static_cast<int64_t>(batch_bound) * d.in_channels * d.units : nullptr; }
     void reset(cudaStream_t s)
     {
         if (batch_bound < 0) fail(AIC_ERR_STATE, "critic state not bound");
         cuda_ok(cudaMemsetAsync(h, 0, state_bytes(batch_bound), s), "reset critic");
+        // critic.h:133-139 zeroes the traces with the state
+        if (traces) cuda_ok(cudaMemsetAsync(traces, 0, trace_bytes(batch_bound), s), "reset critic traces");
     }
     size_t workspace(int64_t rows, void* base, __half** pooled, float2** hseq) const
     {
@@ -661,7 +684,10 @@ struct Critic {
                "critic gap", [&] { return launch_gap_f16(in, in_s, rows, d.dim_in * d.dim_in, d.in_channels, pooled, s); });
         traced(prof, tag + ".cell", s, 8.0 * rows * d.units * d.in_channels,
                2.0 * rows * d.in_channels + 16.0 * d.units * d.in_channels + 16.0 * rows * d.units + 4.0 * rows, "critic",
-               [&] { return launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s); });
+               [&] {
+                   return launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, traces, trace_l(), score, batch,
+                                        seq, s);
+               });
         return 3;
     }
     void forward_pooled(const __half* pooled, float* score, int batch, int seq, void* wsp, cudaStream_t s)
@@ -674,7 +700,8 @@ struct Critic {
         __half* unused;
         float2* hseq;
         workspace(static_cast<int64_t>(batch) * seq, wsp, &unused, &hseq);
-        cuda_ok(launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, score, batch, seq, s), "critic");
+        cuda_ok(launch_critic(pooled, w1, wl, w2, d.in_channels, d.units, h, hseq, traces, trace_l(), score, batch, seq, s),
+                "critic");
     }
 };
 
@@ -1322,6 +1349,24 @@ AIC_API aic_status aic_mamba_layer_bind_state(aic_mamba_layer l, void* dev_state
         require(batch >= 0 && (batch == 0 || (dev_state && aligned256(dev_state))), "state must be 256-byte aligned");
         m->h = static_cast<float2*>(dev_state);
         m->batch_bound = batch;
+        m->traces = nullptr;  // bound again after the state
+    });
+}
+AIC_API aic_status aic_mamba_layer_trace_bytes(aic_mamba_layer l, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = 3 * m->state_bytes(batch);
+    });
+}
+AIC_API aic_status aic_mamba_layer_bind_traces(aic_mamba_layer l, void* dev_traces, int batch)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        require(batch == m->batch_bound, "traces must be bound for the bound state's batch");
+        require(!dev_traces || aligned256(dev_traces), "traces must be 256-byte aligned");
+        m->traces = static_cast<float2*>(dev_traces);
     });
 }
 AIC_API aic_status aic_mamba_layer_reset_state(aic_mamba_layer l, void* stream)
@@ -1422,6 +1467,22 @@ AIC_API aic_status aic_mamba_block_bind_state(aic_mamba_block b, void* dev_state
         m->bind_state(dev_state, batch);
     });
 }
+AIC_API aic_status aic_mamba_block_trace_bytes(aic_mamba_block b, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = m->trace_bytes(batch);
+    });
+}
+AIC_API aic_status aic_mamba_block_bind_traces(aic_mamba_block b, void* dev_traces, int batch)
+{
+    return guarded([&] {
+        auto* m = handle<MambaBlock>(b, "mamba block");
+        require(!dev_traces || aligned256(dev_traces), "traces must be 256-byte aligned");
+        m->bind_traces(dev_traces, batch);
+    });
+}
 AIC_API aic_status aic_mamba_block_reset_state(aic_mamba_block b, void* stream)
 {
     return guarded([&] {
@@ -1508,6 +1569,24 @@ AIC_API aic_status aic_critic_bind_state(aic_critic c, void* dev_state, int batc
         require(batch >= 0 && (batch == 0 || (dev_state && aligned256(dev_state))), "state must be 256-byte aligned");
         k->h = static_cast<float2*>(dev_state);
         k->batch_bound = batch;
+        k->traces = nullptr;  // bound again after the state
+    });
+}
+AIC_API aic_status aic_critic_trace_bytes(aic_critic c, int batch, size_t* bytes)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(bytes && batch >= 0, "bad argument");
+        *bytes = k->trace_bytes(batch);
+    });
+}
+AIC_API aic_status aic_critic_bind_traces(aic_critic c, void* dev_traces, int batch)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        require(batch == k->batch_bound, "traces must be bound for the bound state's batch");
+        require(!dev_traces || aligned256(dev_traces), "traces must be 256-byte aligned");
+        k->traces = static_cast<float2*>(dev_traces);
     });
 }
 AIC_API aic_status aic_critic_reset_state(aic_critic c, void* stream)

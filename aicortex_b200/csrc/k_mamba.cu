@@ -49,11 +49,15 @@ __global__ void __launch_bounds__(kThreads) ssm_prepare_kernel(const uint32_t* _
     if (c == 0) consts2[ch] = make_float2(blob_value(blob, blob_s, ch), blob_value(blob, blob_s, L.offD + ch));
 }
 
-template <int P>
+// TRACE: the training-mode forward also advances the eligibility traces
+// trace_A, trace_B, trace_Delta (kernels.h:1158-1170), held in registers like
+// the state; tr is [3][B][E][P] complex, the layout of h.
+template <int P, bool TRACE>
 __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* __restrict__ x, const int8_t* __restrict__ x_s,
                                                               const uint32_t* __restrict__ blob, const int8_t* __restrict__ blob_s,
                                                               const float4* __restrict__ consts4, const float2* __restrict__ consts2,
-                                                              int D, float2* __restrict__ h, float* __restrict__ y, int T)
+                                                              int D, float2* __restrict__ h, float2* __restrict__ tr,
+                                                              float* __restrict__ y, int T)
 {
     const int E = 2 * D;
     const int ch = blockIdx.x * kScanThreads + threadIdx.x;
@@ -70,6 +74,17 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* 
     float2* hs = h + (static_cast<int64_t>(b) * E + ch) * P;
 #pragma unroll
     for (int c = 0; c < P; ++c) st[c] = hs[c];
+    float2 ta[TRACE ? P : 1], tb[TRACE ? P : 1], td[TRACE ? P : 1];
+    float2* trs = TRACE ? tr + (static_cast<int64_t>(b) * E + ch) * P : nullptr;
+    const int64_t tr_stride = static_cast<int64_t>(gridDim.y) * E * P;  // one trace of the whole batch
+    if (TRACE) {
+#pragma unroll
+        for (int c = 0; c < P; ++c) {
+            ta[c] = trs[c];
+            tb[c] = trs[tr_stride + c];
+            td[c] = trs[2 * tr_stride + c];
+        }
+    }
     const int Gx = D >> 5, xg = in_ch >> 5, xword = (in_ch & 31) >> 3, xnib = in_ch & 7;
     const uint4* xv = reinterpret_cast<const uint4*>(x) + static_cast<int64_t>(b) * T * Gx + xg;
     const int8_t* xsv = x_s + static_cast<int64_t>(b) * T * Gx + xg;
@@ -99,6 +114,23 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* 
             const float dtbx = dt * bx;
             const float hr = st[c].x, hi = st[c].y;
             st[c] = make_float2(fmaf(abr, hr, fmaf(-abi, hi, dtbx * ire)), fmaf(abr, hi, fmaf(abi, hr, dtbx * iim)));
+            if (TRACE) {  // kernels.h:1158-1170, from the state before the step
+                const float i2_re = fmaf(ire, ire, -iim * iim);
+                const float i2_im = 2.0f * ire * iim;
+                const float za_re = fmaf(dt_half, bx, hr);
+                const float dt_i2_za_re = dt * fmaf(i2_re, za_re, -i2_im * hi);
+                const float dt_i2_za_im = dt * fmaf(i2_re, hi, i2_im * za_re);
+                const float zdt_re = fmaf(are, hr, fmaf(-aim, hi, bx));
+                const float zdt_im = fmaf(are, hi, aim * hr);
+                const float d_dt_re = fmaf(i2_re, zdt_re, -i2_im * zdt_im);
+                const float d_dt_im = fmaf(i2_re, zdt_im, i2_im * zdt_re);
+                ta[c] = make_float2(fmaf(abr, ta[c].x, fmaf(-abi, ta[c].y, dt_i2_za_re)),
+                                    fmaf(abr, ta[c].y, fmaf(abi, ta[c].x, dt_i2_za_im)));
+                tb[c] = make_float2(fmaf(abr, tb[c].x, fmaf(-abi, tb[c].y, dt * ire)),
+                                    fmaf(abr, tb[c].y, fmaf(abi, tb[c].x, dt * iim)));
+                td[c] = make_float2(fmaf(abr, td[c].x, fmaf(-abi, td[c].y, d_dt_re)),
+                                    fmaf(abr, td[c].y, fmaf(abi, td[c].x, d_dt_im)));
+            }
             ya[c] = fmaf(st[c].x, k[c].z, -st[c].y * k[c].w);
         }
         float ys = 0.0f;
@@ -108,6 +140,14 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* 
     }
 #pragma unroll
     for (int c = 0; c < P; ++c) hs[c] = st[c];
+    if (TRACE) {
+#pragma unroll
+        for (int c = 0; c < P; ++c) {
+            trs[c] = ta[c];
+            trs[tr_stride + c] = tb[c];
+            trs[2 * tr_stride + c] = td[c];
+        }
+    }
 }
 
 // Out-projection on CUDA cores. A CTA owns R rows and one 256-channel chunk
@@ -214,7 +254,7 @@ cudaError_t launch_ssm_prepare(const uint32_t* blob, const int8_t* blob_s, int D
 }
 
 cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
-                            const float* consts, int D, int d_state, float2* h, float* y, int B, int T,
+                            const float* consts, int D, int d_state, float2* h, float2* traces, float* y, int B, int T,
                             cudaStream_t stream)
 {
     if (B == 0 || T == 0) return cudaSuccess;
@@ -222,7 +262,9 @@ cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t
     const float4* c4 = reinterpret_cast<const float4*>(consts);
     const float2* c2 = reinterpret_cast<const float2*>(consts + E * P * 4);
     dim3 grid(static_cast<unsigned>(E / kScanThreads), static_cast<unsigned>(B));
-#define AIC_SCAN(PP) ssm_scan_kernel<PP><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, y, T)
+#define AIC_SCAN(PP)                                                                                            \
+    (traces ? ssm_scan_kernel<PP, true><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, traces, y, T) \
+            : ssm_scan_kernel<PP, false><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, nullptr, y, T))
     switch (P) {
         case 1: AIC_SCAN(1); break;
         case 2: AIC_SCAN(2); break;

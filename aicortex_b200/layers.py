@@ -238,6 +238,25 @@ class MambaLayer(_Handle):
         n = self.batch * E * Pn * 2
         return self.state.view(self.state.ptr, n, torch.float32).view(self.batch, E, Pn, 2)
 
+    def bind_traces(self, stream=None) -> None:
+        """Training-mode forward: every forward also advances trace_A, trace_B and
+        trace_Delta (kernels.h:1158-1170); reset zeroes them with the state."""
+        nb = _size_out()
+        call("aic_mamba_layer_trace_bytes", self.h, self.batch, C.byref(nb))
+        self.traces = _Arena(nb.value, self.device)
+        call("aic_mamba_layer_bind_traces", self.h, C.c_void_p(self.traces.ptr), self.batch)
+        self.reset(stream)
+
+    def unbind_traces(self) -> None:
+        call("aic_mamba_layer_bind_traces", self.h, None, self.batch)
+        self.traces = None
+
+    def trace_tensor(self) -> torch.Tensor:
+        """[3 (A, B, Delta), batch, 2*d_model, d_state // 32, 2] fp32."""
+        E, Pn = 2 * self.desc.d_model, self.desc.d_state // 32
+        n = 3 * self.batch * E * Pn * 2
+        return self.traces.view(self.traces.ptr, n, torch.float32).view(3, self.batch, E, Pn, 2)
+
     def reset(self, stream=None) -> None:
         call("aic_mamba_layer_reset_state", self.h, _stream(stream))
 
@@ -294,6 +313,14 @@ class MambaBlock(_Handle):
         call("aic_mamba_block_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
         self.reset(stream)
 
+    def bind_traces(self, stream=None) -> None:
+        """Training-mode forward for all three layers (their traces carved in order)."""
+        nb = _size_out()
+        call("aic_mamba_block_trace_bytes", self.h, self.batch, C.byref(nb))
+        self.traces = _Arena(nb.value, self.device)
+        call("aic_mamba_block_bind_traces", self.h, C.c_void_p(self.traces.ptr), self.batch)
+        self.reset(stream)
+
     def reset(self, stream=None) -> None:
         call("aic_mamba_block_reset_state", self.h, _stream(stream))
 
@@ -345,6 +372,22 @@ class Critic(_Handle):
         self.batch = int(batch)
         call("aic_critic_bind_state", self.h, C.c_void_p(self.state.ptr), int(batch))
         self.reset(stream)
+
+    def bind_traces(self, stream=None) -> None:
+        """Training-mode forward: every step also advances the eligibility traces of
+        W1 and Wlambda (kernels.h:1731-1751); reset zeroes them with the state."""
+        nb = _size_out()
+        call("aic_critic_trace_bytes", self.h, self.batch, C.byref(nb))
+        self.traces = _Arena(nb.value, self.device)
+        call("aic_critic_bind_traces", self.h, C.c_void_p(self.traces.ptr), self.batch)
+        self.reset(stream)
+
+    def trace_tensors(self):
+        """(trace_w1 [batch, in, units, 2], trace_lambda [batch, units, in, 2]) fp32 views."""
+        cin, units = self.desc.in_channels, self.desc.units
+        n = self.batch * cin * units * 2
+        t = self.traces.view(self.traces.ptr, 2 * n, torch.float32)
+        return t[:n].view(self.batch, cin, units, 2), t[n:].view(self.batch, units, cin, 2)
 
     def reset(self, stream=None) -> None:
         call("aic_critic_reset_state", self.h, _stream(stream))

@@ -238,7 +238,16 @@ AIC_API aic_status aic_mamba_layer_load_file_sync(aic_mamba_layer l, const char*
  * entries of the reference's h_states, mamba_layer.h:90-92). */
 AIC_API aic_status aic_mamba_layer_state_bytes(aic_mamba_layer l, int batch, size_t* bytes);
 AIC_API aic_status aic_mamba_layer_bind_state(aic_mamba_layer l, void* dev_state, int batch);
-/* MambaLayer::reset (mamba_layer.h:171-177). */
+/* Training-mode forward (replaces mambaSSMFwdStateKernel's trace arguments,
+ * kernels.h:1080, 1158-1170): with traces bound, every forward also advances
+ * trace_A, trace_B and trace_Delta, stored back to back, each in the layout of
+ * the state ([batch][2*d_model][d_state/32] complex fp32; 3x state_bytes).
+ * Bind after aic_mamba_layer_bind_state with the same batch (binding a state
+ * unbinds them); NULL unbinds (the inference forward, which skips them). */
+AIC_API aic_status aic_mamba_layer_trace_bytes(aic_mamba_layer l, int batch, size_t* bytes);
+AIC_API aic_status aic_mamba_layer_bind_traces(aic_mamba_layer l, void* dev_traces, int batch);
+/* MambaLayer::reset (mamba_layer.h:171-177): zeroes the state and, if bound,
+ * the traces. */
 AIC_API aic_status aic_mamba_layer_reset_state(aic_mamba_layer l, void* stream);
 /* y_ssm [rows][2*d_model] fp32 (mamba_layer.h:93-95). */
 AIC_API aic_status aic_mamba_layer_workspace_bytes(aic_mamba_layer l, int64_t rows, size_t* bytes);
@@ -284,6 +293,9 @@ AIC_API aic_status aic_mamba_block_param_bytes(aic_mamba_block b, size_t* bytes)
 AIC_API aic_status aic_mamba_block_bind(aic_mamba_block b, void* dev_params);
 AIC_API aic_status aic_mamba_block_state_bytes(aic_mamba_block b, int batch, size_t* bytes);
 AIC_API aic_status aic_mamba_block_bind_state(aic_mamba_block b, void* dev_state, int batch);
+/* The three layers' traces (aic_mamba_layer_bind_traces), carved in layer order. */
+AIC_API aic_status aic_mamba_block_trace_bytes(aic_mamba_block b, int batch, size_t* bytes);
+AIC_API aic_status aic_mamba_block_bind_traces(aic_mamba_block b, void* dev_traces, int batch);
 AIC_API aic_status aic_mamba_block_reset_state(aic_mamba_block b, void* stream);
 AIC_API aic_status aic_mamba_block_workspace_bytes(aic_mamba_block b, int64_t rows, size_t* bytes);
 /* MambaBlock::loadFromFile (mamba_block.h:23-27): <dir>/mamba_{strategist,tactic,executor}.bin */
@@ -314,6 +326,13 @@ AIC_API aic_status aic_critic_load_weights(aic_critic c, const float* w1, const 
 AIC_API aic_status aic_critic_load_file_sync(aic_critic c, const char* path, void* stream);
 AIC_API aic_status aic_critic_state_bytes(aic_critic c, int batch, size_t* bytes);
 AIC_API aic_status aic_critic_bind_state(aic_critic c, void* dev_state, int batch);
+/* Training-mode forward (criticFwd1Kernel's trace arguments, kernels.h:1685,
+ * 1731-1751): with traces bound, every step also advances trace_w1
+ * [batch][in][units] then trace_lambda [batch][units][in] complex fp32 (the
+ * layouts of W1 and Wlambda, one set per sequence). Bind after
+ * aic_critic_bind_state with the same batch; NULL unbinds. Reset zeroes them. */
+AIC_API aic_status aic_critic_trace_bytes(aic_critic c, int batch, size_t* bytes);
+AIC_API aic_status aic_critic_bind_traces(aic_critic c, void* dev_traces, int batch);
 AIC_API aic_status aic_critic_reset_state(aic_critic c, void* stream);
 AIC_API aic_status aic_critic_workspace_bytes(aic_critic c, int64_t rows, size_t* bytes);
 /* Critic::forward (critic.h:106-116) for `seq` steps of `batch` sequences:

@@ -43,8 +43,10 @@ def _load() -> C.CDLL:
         "orc_gap_f16": ([P, P, I64, I32, I32, P], None),
         "orc_mamba_blob_elems": ([I32, I32, I32], I64),
         "orc_ssm_scan": ([P, P, P, P, I32, I32, I32, P, P, I32, I32], None),
+        "orc_ssm_scan_traced": ([P, P, P, P, I32, I32, I32, P, P, P, I32, I32], None),
         "orc_outproj": ([P, P, P, P, I32, I32, I32, I32, I64, P], None),
         "orc_critic": ([P, P, P, P, I32, I32, P, P, I32, I32], None),
+        "orc_critic_traced": ([P, P, P, P, I32, I32, P, P, P, P, I32, I32], None),
         "orc_set_actions": ([P, I64, I32, P], None),
         "orc_num_threads": ([], I32),
         "orc_audio_pcm_to_half": ([P, I32, P], None),
@@ -130,14 +132,20 @@ def gap_f16(x_w, x_s, frames, hw, channels):
     return out.view(np.float16)
 
 
-def ssm_scan(x_w, x_s, blob_w, blob_s, d_model, d_state, out, h, B, T):
-    """Returns y [B*T][2*d_model]; h [B][E][d_state/32][2] is updated in place."""
+def ssm_scan(x_w, x_s, blob_w, blob_s, d_model, d_state, out, h, B, T, traces=None):
+    """Returns y [B*T][2*d_model]; h [B][E][d_state/32][2] is updated in place,
+    and so are the training-mode traces [3][B][E][d_state/32][2] when given."""
     E = 2 * d_model
     y = np.zeros((B * T, E), dtype=np.float32)
     assert h.dtype == np.float32 and h.flags["C_CONTIGUOUS"]
-    lib.orc_ssm_scan(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
-                     _p(np.ascontiguousarray(blob_w, np.uint32)), _p(np.ascontiguousarray(blob_s, np.int8)),
-                     d_model, d_state, out, _p(h), _p(y), B, T)
+    args = [_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
+            _p(np.ascontiguousarray(blob_w, np.uint32)), _p(np.ascontiguousarray(blob_s, np.int8)), d_model, d_state, out,
+            _p(h)]
+    if traces is None:
+        lib.orc_ssm_scan(*args, _p(y), B, T)
+    else:
+        assert traces.dtype == np.float32 and traces.flags["C_CONTIGUOUS"] and traces.size == 3 * h.size
+        lib.orc_ssm_scan_traced(*args, _p(traces), _p(y), B, T)
     return y
 
 
@@ -150,12 +158,20 @@ def outproj(y, blob_w, blob_s, bias, d_model, d_state, out, act):
     return o
 
 
-def critic(x_f16, w1, wl, w2, in_c, units, h, B, T):
+def critic(x_f16, w1, wl, w2, in_c, units, h, B, T, traces=None):
+    """Returns the scores [B*T]; h [B][units][2] is updated in place, and so are
+    the traces (trace_w1 [B][in][units][2], trace_lambda [B][units][in][2]) when
+    given as a pair of arrays."""
     score = np.zeros(B * T, dtype=np.float32)
     x = np.ascontiguousarray(x_f16, np.float16)
-    lib.orc_critic(_p(x.view(np.uint16)), _p(np.ascontiguousarray(w1, np.float32)),
-                   _p(np.ascontiguousarray(wl, np.float32)), _p(np.ascontiguousarray(w2, np.float32)), in_c, units,
-                   _p(h), _p(score), B, T)
+    args = [_p(x.view(np.uint16)), _p(np.ascontiguousarray(w1, np.float32)), _p(np.ascontiguousarray(wl, np.float32)),
+            _p(np.ascontiguousarray(w2, np.float32)), in_c, units, _p(h)]
+    if traces is None:
+        lib.orc_critic(*args, _p(score), B, T)
+    else:
+        tw, tl = traces
+        assert tw.dtype == np.float32 and tw.flags["C_CONTIGUOUS"] and tl.dtype == np.float32 and tl.flags["C_CONTIGUOUS"]
+        lib.orc_critic_traced(*args, _p(tw), _p(tl), _p(score), B, T)
     return score
 
 

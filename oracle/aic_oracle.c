@@ -524,6 +524,13 @@ void orc_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
                   const int8_t* blob_s, int D, int d_state, int out, float* h,
                   float* y, int B, int T)
 {
+    orc_ssm_scan_traced(x, x_s, blob, blob_s, D, d_state, out, h, NULL, y, B, T);
+}
+
+void orc_ssm_scan_traced(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
+                         const int8_t* blob_s, int D, int d_state, int out, float* h,
+                         float* tr, float* y, int B, int T)
+{
     (void)out;
     const int E = 2 * D, N = d_state, P = d_state >> 5;
     const int64_t offB = E, offCre = 33LL * E, offCim = offCre + (int64_t)E * N;
@@ -554,6 +561,10 @@ void orc_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
             const float wd = orc_blob_dq(blob, blob_s, ch);
             const float dq = orc_blob_dq(blob, blob_s, offD + ch);
             float* hs = h + ((int64_t)b * E + ch) * P * 2;
+            /* trace_A, trace_B, trace_Delta: [3][B][E][P] complex, the layout of h */
+            float* ta = tr ? tr + ((int64_t)b * E + ch) * P * 2 : NULL;
+            float* tb = tr ? ta + (int64_t)B * E * P * 2 : NULL;
+            float* td = tr ? tb + (int64_t)B * E * P * 2 : NULL;
             for (int t = 0; t < T; ++t) {
                 const int64_t row = (int64_t)b * T + t;
                 const uint32_t* xw = x + row * (D >> 3) + (in_ch >> 5) * 4;
@@ -565,7 +576,7 @@ void orc_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
                 const float u = x_local * wd;
                 const float dt = u + logf(1.0f + expf(-fabsf(u))); /* kernels.h:1139 */
                 const float dt_half = dt * 0.5f;
-                for (int c = 0; c < P; ++c) { /* kernels.h:1146-1173 without the traces */
+                for (int c = 0; c < P; ++c) { /* kernels.h:1146-1173 (the traces when tr is given) */
                     const float dim = -dt_half * aim[c];
                     const float dre = fmaf(-dt_half, are[c], 1.0f);
                     const float inv_s = orc_rcp(fmaf(dre, dre, fmaf(dim, dim, ORC_EPS)));
@@ -580,6 +591,25 @@ void orc_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
                     const float nhi = fmaf(abr, hi, fmaf(abi, hr, dtbx * iim));
                     hs[2 * c] = nhr;
                     hs[2 * c + 1] = nhi;
+                    if (tr) { /* kernels.h:1158-1170, from the state before the step */
+                        const float i2_re = fmaf(ire, ire, -iim * iim);
+                        const float i2_im = 2.0f * ire * iim;
+                        const float za_re = fmaf(dt_half, bx, hr);
+                        const float dt_i2_za_re = dt * fmaf(i2_re, za_re, -i2_im * hi);
+                        const float dt_i2_za_im = dt * fmaf(i2_re, hi, i2_im * za_re);
+                        const float zdt_re = fmaf(are[c], hr, fmaf(-aim[c], hi, bx));
+                        const float zdt_im = fmaf(are[c], hi, aim[c] * hr);
+                        const float d_dt_re = fmaf(i2_re, zdt_re, -i2_im * zdt_im);
+                        const float d_dt_im = fmaf(i2_re, zdt_im, i2_im * zdt_re);
+                        float* t3[3] = {ta + 2 * c, tb + 2 * c, td + 2 * c};
+                        const float ur[3] = {dt_i2_za_re, dt * ire, d_dt_re};
+                        const float ui[3] = {dt_i2_za_im, dt * iim, d_dt_im};
+                        for (int k = 0; k < 3; ++k) {
+                            const float r = t3[k][0], i = t3[k][1];
+                            t3[k][0] = fmaf(abr, r, fmaf(-abi, i, ur[k]));
+                            t3[k][1] = fmaf(abr, i, fmaf(abi, r, ui[k]));
+                        }
+                    }
                     yacc[c] = fmaf(nhr, cre[c], -nhi * cim[c]);
                 }
                 float ys = 0.0f;
@@ -648,6 +678,13 @@ void orc_critic(const uint16_t* x, const float* w1, const float* wl,
                 const float* w2, int in, int units, float* h, float* score,
                 int B, int T)
 {
+    orc_critic_traced(x, w1, wl, w2, in, units, h, NULL, NULL, score, B, T);
+}
+
+void orc_critic_traced(const uint16_t* x, const float* w1, const float* wl,
+                       const float* w2, int in, int units, float* h, float* trace_w1,
+                       float* trace_l, float* score, int B, int T)
+{
 #pragma omp parallel
     {
         float* xf = (float*)malloc(sizeof(float) * in);
@@ -681,6 +718,22 @@ void orc_critic(const uint16_t* x, const float* w1, const float* wl,
                     const float hr = hb[2 * j], hi = hb[2 * j + 1];
                     hb[2 * j] = fmaf(hr, lam, dh * actr);
                     hb[2 * j + 1] = fmaf(hi, lam, dh * acti);
+                    if (trace_w1) { /* kernels.h:1731-1751: eligibility traces of w1 and w_lambda */
+                        float* tw = trace_w1 + (int64_t)b * in * units * 2;
+                        float* tl = trace_l + (int64_t)b * in * units * 2;
+                        const float inv = orc_rcp(lam_mod);
+                        const float gr = dh * sr * fmaf(accr, 1.0f - sr, 1.0f);
+                        const float gi = dh * si * fmaf(acci, 1.0f - si, 1.0f);
+                        const float dlam = (hr - actr + hi - acti) * lam * dh * inv;
+                        for (int c = 0; c < in; ++c) {
+                            const int64_t i1 = ((int64_t)c * units + j) << 1;
+                            const int64_t il = ((int64_t)j * in + c) << 1;
+                            tw[i1] = fmaf(tw[i1], lam, gr * xf[c]);
+                            tw[i1 + 1] = fmaf(tw[i1 + 1], lam, gi * xf[c]);
+                            tl[il] = fmaf(tl[il], lam, dlam * xf[c] * lamr);
+                            tl[il + 1] = fmaf(tl[il + 1], lam, dlam * xf[c] * lami);
+                        }
+                    }
                 }
                 /* criticFwd2Kernel (kernels.h:1754-1778), blockDim == units */
                 float warp_sums[32];

@@ -86,6 +86,12 @@ int64_t orc_mamba_blob_elems(int D, int d_state, int out);
 void orc_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
                   const int8_t* blob_s, int D, int d_state, int out, float* h,
                   float* y, int B, int T);
+/* The same with the training-mode eligibility traces (kernels.h:1158-1170):
+ * tr = trace_A | trace_B | trace_Delta, each [B][E][d_state/32] complex like h,
+ * updated in place (tr may be NULL). */
+void orc_ssm_scan_traced(const uint32_t* x, const int8_t* x_s, const uint32_t* blob,
+                         const int8_t* blob_s, int D, int d_state, int out, float* h,
+                         float* tr, float* y, int B, int T);
 
 /* A10: mambaSSMFwdOutProjKernel<act> (kernels.h:1188-1259) over rows. */
 void orc_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s,
@@ -98,6 +104,12 @@ void orc_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s,
 void orc_critic(const uint16_t* x, const float* w1, const float* wl,
                 const float* w2, int in, int units, float* h, float* score,
                 int B, int T);
+/* The same with the traces (kernels.h:1731-1751): trace_w1 [B][in][units][2]
+ * (the layout of w1) and trace_l [B][units][in][2] (the layout of wl), updated
+ * in place (both NULL for none). */
+void orc_critic_traced(const uint16_t* x, const float* w1, const float* wl,
+                       const float* w2, int in, int units, float* h, float* trace_w1,
+                       float* trace_l, float* score, int B, int T);
 
 /* A12: setActionsKernel (kernels.h:1473-1485) per row of A probabilities.
  * actions: [rows][(A+63)/64] words, cleared first. */

@@ -30,7 +30,9 @@ sys.path.insert(0, str(HERE))
 import golden_specs as S  # noqa: E402
 
 REF_DIR = ROOT / "oracle" / "_ref"
-OUT = Path(sys.argv[1]) if len(sys.argv) > 1 else HERE
+_NAMES = {"ssm", "critic"}  # fixture groups that can be regenerated alone
+_dirs = [a for a in sys.argv[1:] if a not in _NAMES]
+OUT = Path(_dirs[0]) if _dirs else HERE
 DEV = torch.device("cuda")
 _libs: dict = {}
 
@@ -174,16 +176,22 @@ def gen_ssm(d_state: int):
     bw, bs = pack_weights(lib, blob)
     pbw, pbs = d.put(bw), d.put(bs)
     h, ph = d.zeros(E * d_state * 2, torch.float32)
-    trs = [d.zeros(E * d_state * 2, torch.float32)[1] for _ in range(3)]
+    trs_t = [d.zeros(E * d_state * 2, torch.float32) for _ in range(3)]  # trace_A, trace_B, trace_Delta
+    trs = [pt for _, pt in trs_t]
     y, py = d.zeros(E, torch.float32)
     xw, xs = act_f(lib, x)
     ys = []
     for t in range(S.SSM_T):
         run(lib, "aicref_ssm_step", d.put(xw[t]), d.put(xs[t]), pbw, pbs, ph, *trs, py)
         ys.append(y.cpu().numpy().copy())
-    hv = h.cpu().numpy().reshape(E, d_state, 2)
     lane = np.arange(E) % 32
-    h_active = np.stack([hv[np.arange(E), lane + 32 * c] for c in range(d_state // 32)], axis=1)
+
+    def active(buf):  # [E][N] complex -> the P states each channel updates, [E][P][2]
+        v = buf.cpu().numpy().reshape(E, d_state, 2)
+        return np.stack([v[np.arange(E), lane + 32 * c] for c in range(d_state // 32)], axis=1)
+
+    h_active = active(h)
+    tr_active = np.stack([active(tt) for tt, _ in trs_t])
     extra = {}
     for out_c, act in S.OUTPROJ_CASES:
         blob_o, bias_o, yin = S.outproj_case(d_state, out_c, act)
@@ -193,7 +201,7 @@ def gen_ssm(d_state: int):
         extra[f"op{out_c}_{act}_sha"] = S.sha(blob_o)
         extra[f"op{out_c}_{act}_out"] = o.cpu().numpy()
     save(f"ssm_N{d_state}", blob_sha=S.sha(blob), w_sha=S.sha(bw), s_sha=S.sha(bs), x_w=xw, x_s=xs, y=np.stack(ys),
-         h=h_active, **extra)
+         h=h_active, traces=tr_active, **extra)
 
 
 def gen_mamba_block():
@@ -266,8 +274,8 @@ def gen_critic(lib):
     w1, w2, wl, x = S.critic_case()
     T, cin, units = x.shape[0], 32, 128
     h, ph = d.zeros(2 * units, torch.float32)
-    _, ptw = d.zeros(cin * units * 2, torch.float32)
-    _, ptl = d.zeros(cin * units * 2, torch.float32)
+    tw, ptw = d.zeros(cin * units * 2, torch.float32)
+    tl, ptl = d.zeros(cin * units * 2, torch.float32)
     score, psc = d.zeros(1, torch.float32)
     pw1, pw2, pwl = d.put(w1), d.put(w2), d.put(wl)
     scores = []
@@ -275,7 +283,7 @@ def gen_critic(lib):
         run(lib, "aicref_critic", d.put(x[t]), pw1, pwl, pw2, ph, ptw, ptl, psc, C.c_int(units), C.c_int(cin))
         scores.append(float(score.cpu().numpy()[0]))
     save("critic", w_sha=np.array([S.sha(w1), S.sha(w2), S.sha(wl), S.sha(x)]), score=np.array(scores, np.float32),
-         h=h.cpu().numpy())
+         h=h.cpu().numpy(), trace_w1=tw.cpu().numpy(), trace_lambda=tl.cpu().numpy())
 
 
 def gen_actions(lib):
@@ -328,6 +336,14 @@ def gen_screen(lib):
 
 
 def main():
+    only = set(sys.argv[1:]) & _NAMES  # e.g. "ssm critic": regenerate those fixtures only
+    if only:
+        if "ssm" in only:
+            for n in (32, 128, 512):
+                gen_ssm(n)
+        if "critic" in only:
+            gen_critic(ref(256, 128))
+        return
     lib = ref(256, 128)
     gen_screen(lib)
     gen_audio(lib)

@@ -132,6 +132,13 @@ def test_oracle_ssm(golden, n):
     y = O.ssm_scan(g["x_w"], g["x_s"], layer.w, layer.s, S.SSM_D, n, S.SSM_D, layer.h, 1, S.SSM_T)
     close(y, g["y"], 2e-5, f"scan y N={n}")
     close(layer.h[0], g["h"], 2e-5, f"scan state N={n}")
+    # training-mode traces (kernels.h:1158-1170), from a zero state as in the fixture
+    h = np.zeros_like(layer.h)
+    tr = np.zeros((3,) + layer.h.shape, np.float32)
+    y2 = O.ssm_scan(g["x_w"], g["x_s"], layer.w, layer.s, S.SSM_D, n, S.SSM_D, h, 1, S.SSM_T, traces=tr)
+    np.testing.assert_array_equal(y2, y)  # the traces do not feed back into y or h
+    for k, name in enumerate(("trace_A", "trace_B", "trace_Delta")):
+        close(tr[k, 0], g["traces"][k], 1e-4, f"{name} N={n}")
     for out_c, act in S.OUTPROJ_CASES:
         blob_o, bias_o, yin = S.outproj_case(n, out_c, act)
         assert S.sha(blob_o) == str(g[f"op{out_c}_{act}_sha"])
@@ -176,6 +183,13 @@ def test_oracle_critic(golden):
     score = O.critic(x, w1, wl, w2, 32, 128, h, 1, x.shape[0])
     close(score, g["score"], 1e-5, "critic score")
     close(h.reshape(-1), g["h"], 1e-5, "critic state")
+    # training-mode traces (kernels.h:1731-1751)
+    h2 = np.zeros((1, 128, 2), np.float32)
+    tw, tl = np.zeros((1, 32, 128, 2), np.float32), np.zeros((1, 128, 32, 2), np.float32)
+    score2 = O.critic(x, w1, wl, w2, 32, 128, h2, 1, x.shape[0], traces=(tw, tl))
+    np.testing.assert_array_equal(score2, score)
+    close(tw.reshape(-1), g["trace_w1"], 1e-4, "critic trace_w1")
+    close(tl.reshape(-1), g["trace_lambda"], 1e-4, "critic trace_lambda")
 
 
 def test_oracle_actions(golden):

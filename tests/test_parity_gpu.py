@@ -160,6 +160,71 @@ def test_golden_ssm(golden, n):
         np.testing.assert_array_equal(h(o)[0], g[f"op{out_c}_{act}_out"], err_msg=f"outproj {out_c}/{act}")
 
 
+@pytest.mark.parametrize("n", [32, 128, 512])
+def test_golden_ssm_traces(golden, n):
+    """Training-mode forward (F3): with traces bound, the scan also advances
+    trace_A, trace_B and trace_Delta exactly as the reference kernel does
+    (kernels.h:1158-1170); y and the state are unchanged."""
+    g = golden(f"ssm_N{n}")
+    D, E, T = S.SSM_D, 2 * S.SSM_D, S.SSM_T
+    blob, _ = S.ssm_case(n)
+    layer = A.MambaLayer(D, n, D, 1)
+    layer.load_weights(t(blob), t(np.zeros(D, np.float32)))
+    layer.bind_state(1)
+    layer.bind_traces()
+    out = torch.empty(T, D, dtype=torch.float32, device=DEV)
+    layer.forward(t(g["x_w"]), t(g["x_s"]), out, 1, T)
+    ws = layer.workspace(T)
+    np.testing.assert_array_equal(h(ws.view(ws.ptr, T * E, torch.float32)).reshape(T, E), g["y"], err_msg="scan output")
+    np.testing.assert_array_equal(h(layer.state_tensor())[0], g["h"], err_msg="state")
+    tr = h(layer.trace_tensor())[:, 0]
+    for k, name in enumerate(("trace_A", "trace_B", "trace_Delta")):
+        np.testing.assert_array_equal(tr[k], g["traces"][k], err_msg=name)
+    layer.reset()
+    assert not h(layer.trace_tensor()).any(), "reset zeroes the traces"
+
+
+def test_traces_batched_vs_oracle():
+    """Traces of B independent sequences over T steps (the batched scan and
+    critic) against the oracle's restatement."""
+    import oracle as O
+    D, N, B, T = 64, 64, 3, 5
+    rng = np.random.default_rng(21)
+    blob = W.mamba_blob(rng, D, N, D, a_im=None)
+    layer = A.MambaLayer(D, N, D, 1)
+    layer.load_weights(t(blob), t(np.zeros(D, np.float32)))
+    layer.bind_state(B)
+    layer.bind_traces()
+    x = rng.standard_normal((B * T, D)).astype(np.float32)
+    xw, xs = O.pack_f32(x)
+    xw, xs = xw.reshape(B * T, -1), xs.reshape(B * T, -1)
+    out = torch.empty(B * T, D, dtype=torch.float32, device=DEV)
+    layer.forward(t(xw.view(np.int32)), t(xs), out, B, T)
+    pw, ps, _ = layer.packed()
+    hs = np.zeros((B, 2 * D, N // 32, 2), np.float32)
+    trs = np.zeros((3,) + hs.shape, np.float32)
+    O.ssm_scan(xw, xs, u32(pw), h(ps), D, N, D, hs, B, T, traces=trs)
+    assert_close(h(layer.trace_tensor()), trs, rtol=1e-4, what="ssm traces")
+    cin, units = 64, 64
+    w1 = (rng.standard_normal((cin, units, 2)) * 0.1).astype(np.float32)
+    wl = (rng.standard_normal((units, cin, 2)) * 0.1).astype(np.float32)
+    w2 = (rng.standard_normal((units, 2)) * 0.1).astype(np.float32)
+    xp = rng.standard_normal((B * T, cin)).astype(np.float16)
+    c = A.Critic(cin, units, 1)
+    c.load_weights(t(w1), t(w2), t(wl))
+    c.bind_state(B)
+    c.bind_traces()
+    score = torch.empty(B * T, dtype=torch.float32, device=DEV)
+    c.forward_pooled(t(xp), score, B, T)
+    hc = np.zeros((B, units, 2), np.float32)
+    tw, tl = np.zeros((B, cin, units, 2), np.float32), np.zeros((B, units, cin, 2), np.float32)
+    ref = O.critic(xp, w1, wl, w2, cin, units, hc, B, T, traces=(tw, tl))
+    assert_close(h(score), ref, rtol=1e-4, what="critic score")
+    gw, gl = c.trace_tensors()
+    assert_close(h(gw), tw, rtol=1e-4, what="critic trace_w1")
+    assert_close(h(gl), tl, rtol=1e-4, what="critic trace_lambda")
+
+
 def test_golden_mamba_block(golden):
     g = golden("mamba_block_N128")
     blobs, biases, _ = S.mamba_block_case()
@@ -198,6 +263,13 @@ def test_golden_critic(golden):
     score = torch.empty(x.shape[0], dtype=torch.float32, device=DEV)
     c.forward_pooled(t(x), score, 1, x.shape[0])
     np.testing.assert_array_equal(h(score), g["score"])
+    # training-mode forward (F3): the traces of W1 and Wlambda, bit for bit
+    c.bind_traces()
+    c.forward_pooled(t(x), score, 1, x.shape[0])
+    np.testing.assert_array_equal(h(score), g["score"])
+    gw, gl = c.trace_tensors()
+    np.testing.assert_array_equal(h(gw).reshape(-1), g["trace_w1"], err_msg="trace_w1")
+    np.testing.assert_array_equal(h(gl).reshape(-1), g["trace_lambda"], err_msg="trace_lambda")
 
 
 def test_golden_actions(golden):
