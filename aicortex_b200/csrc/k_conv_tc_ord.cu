@@ -54,6 +54,7 @@ constexpr int kBK = 64;                   // two 32-element groups per stage
 constexpr int kTileA = kBM * kBK * 2;     // 16 KB of bf16
 constexpr int kNCta = 64;                 // output channels per CTA
 constexpr int kImgRow = kBK * 2 + 2 * 4;  // image bytes per channel per stage: 128 B codes + 2 units
+constexpr int kResidentStages = 8;        // up to this many stages per tile stay resident in shared memory
 
 struct OrdParams {
     const uint32_t* in;
@@ -134,10 +135,17 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
     const int n_cta = min(kNCta, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
     const bool live = n_cta > 0;
-    const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
-    uint8_t* a_tiles = base;                       // [2][kTileA]
-    uint8_t* b_tiles = base + 2 * kTileA;          // [2][slot_b]: codes [n][128 B], then units [2][n]
-    float* din_s = reinterpret_cast<float*>(b_tiles + 2 * slot_b);  // [2 buffers][2 groups][kBM] unit(s_in)
+    // Weights: with at most kResidentStages stages per tile every stage's image
+    // stays in shared memory (fetched once per CTA); otherwise two slots rotate
+    // and each stage is fetched in turn. Codes and units sit in separate arrays
+    // so that every code slot stays 1024-byte aligned for the SW128 layout.
+    const int S = p.stages;
+    const bool resident = S <= kResidentStages;
+    const int nb = resident ? S : 2;
+    uint8_t* a_tiles = base;                                   // [2][kTileA]
+    uint8_t* b_codes = base + 2 * kTileA;                      // [nb][n_max][128 B]
+    float* b_units = reinterpret_cast<float*>(b_codes + nb * p.n_max * 128);  // [nb][2][n_max]
+    float* din_s = b_units + nb * 2 * p.n_max;                 // [2 buffers][2 groups][kBM] unit(s_in)
     float* bias_s = din_s + 4 * kBM;               // [kNCta]
     float* part = bias_s + kNCta;                  // [2 tiles][8][kBM] group sums of squares of the norm chunk
     uint64_t* bars = reinterpret_cast<uint64_t*>(part + 16 * kBM);  // 0,1: B full; 2,3: MMAs done; 4: drain
@@ -165,7 +173,6 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     const int64_t n_tiles = (p.rows + kBM - 1) / kBM;
     const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
     const int my_tiles = tile0 < n_tiles ? static_cast<int>(min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0)) : 0;
-    const int S = p.stages;
     const int total = my_tiles * S;
 
     const int prow = tid & (kBM - 1), pg = tid >> 7;  // producer: (row, group of the stage)
@@ -193,7 +200,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         const int buf = gc & 1;
         if (!mbar_wait(smem_addr(&bars[2 + buf]), static_cast<uint32_t>(gc >> 1) & 1u, p.err, 12)) return false;
         tc_fence_after();
-        const float* units = reinterpret_cast<const float*>(b_tiles + buf * slot_b + n_cta * 128) + 32 * hw;
+        const float* units = b_units + (resident ? sc : buf) * 2 * p.n_max + 32 * hw;
         const float* dins = din_s + buf * 2 * kBM + erow;
         const uint32_t tb = tl + static_cast<uint32_t>(buf * 2 * n_cta);
 #pragma unroll
@@ -286,6 +293,20 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             ++pf_tap;
         }
     };
+    // stage k of the tile's weight image (codes, then the units of its two
+    // groups) into slot j, completing on barrier bar (thread 0 only)
+    auto fetch_stage = [&](int k, int j, int bar) {
+        const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
+        if (bar >= 0) mbar_expect_tx(smem_addr(&bars[bar]), static_cast<uint32_t>(stage_bytes));
+        bulk_g2s(smem_addr(b_codes + j * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
+                 smem_addr(&bars[bar < 0 ? 0 : bar]));
+        bulk_g2s(smem_addr(b_units + j * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
+                 smem_addr(&bars[bar < 0 ? 0 : bar]));
+    };
+    if (resident && live && tid == 0 && total > 0) {  // every stage once, on barrier 0
+        mbar_expect_tx(smem_addr(&bars[0]), static_cast<uint32_t>(S * stage_bytes));
+        for (int k = 0; k < S; ++k) fetch_stage(k, k, -1);
+    }
     if (total > 0) {
         start_tile(0);
         prefetch(0);
@@ -296,16 +317,9 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         const bool run = live && !*abort_flag;
         const bool produce = run && gs < total;
         uint8_t* a_tile = a_tiles + buf * kTileA;
-        uint8_t* b_tile = b_tiles + buf * slot_b;
-        // with at most two stages per tile, buffer b keeps stage b % S: the weights
-        // are fetched for the first two global stages only
-        const bool fetch_b = S > 2 || gs < 2;
+        const int bslot = resident ? sp : buf;
         if (produce) {
-            if (tid == 0 && fetch_b) {
-                mbar_expect_tx(smem_addr(&bars[buf]), static_cast<uint32_t>(stage_bytes));
-                bulk_g2s(smem_addr(b_tile), wimg + static_cast<int64_t>(sp) * stage_bytes,
-                         static_cast<uint32_t>(stage_bytes), smem_addr(&bars[buf]));
-            }
+            if (tid == 0 && !resident) fetch_stage(sp, buf, buf);
             float du = 0.0f;
             if (pf_ok) {
                 du = unit_of(pf_s);
@@ -328,10 +342,13 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         tc_fence_before();
         __syncthreads();
         if (produce && tid == 0) {
-            if (!fetch_b || mbar_wait(smem_addr(&bars[buf]), static_cast<uint32_t>(gs >> 1) & 1u, p.err, 11)) {
+            const bool ready = resident ? (gs > 0 || mbar_wait(smem_addr(&bars[0]), 0u, p.err, 11))
+                                        : mbar_wait(smem_addr(&bars[buf]), static_cast<uint32_t>(gs >> 1) & 1u, p.err, 11);
+            if (ready) {
                 tc_fence_after();
                 // K16 steps advance the SW128 descriptors by 32 bytes (2 in the address field)
-                const uint64_t da = smem_desc(smem_addr(a_tile)), db = smem_desc(smem_addr(b_tile));
+                const uint64_t da = smem_desc(smem_addr(a_tile)),
+                               db = smem_desc(smem_addr(b_codes + bslot * p.n_max * 128));
                 // two K16 MMAs per group; a padding group (odd group count) has no
                 // accumulator slot and is skipped
                 const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
@@ -815,8 +832,8 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // the streaming kernel from three on
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
         return launch_cae_pw(p, stream);
-    const int slot_b = (p.n_max * kImgRow + 1023) & ~1023;
-    size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + 2 * static_cast<size_t>(slot_b) +
+    const int nb = p.stages <= kResidentStages ? p.stages : 2;  // weight slots (the kernel's `nb`)
+    size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + static_cast<size_t>(nb) * p.n_max * kImgRow +
                   (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;
     // Never let more CTAs share an SM than its 512 TMEM columns can serve.
     const int max_ctas = static_cast<int>(512u / ord_tmem_cols(p.n_max, p.stages, p.gk_total));
