@@ -664,6 +664,388 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     }
 }
 
+// ---- warp-specialised streaming kernel ----------------------------------------
+//
+// The streaming kernel's pipeline with its roles on separate warps and its
+// hand-offs on mbarriers instead of CTA-wide barriers. One CTA per SM, 640
+// threads, tiles of 256 rows x 64 channels:
+// * warps 16-19 (one warpgroup, 64 registers after setmaxnreg): producers.
+//   Thread pt stages rows pt and pt + 128 of the tile (both groups of a stage,
+//   loaded one stage ahead into registers) and records unit(s_in). Thread 0
+//   also fetches the stage's weight image and, once the four warps have staged
+//   (named barrier 1), issues the stage's MMAs: two M = 128 halves x two groups
+//   x two K16 steps, into one of two TMEM buffers, committed to full_acc[buf].
+// * warps 0-15 (104 registers): consumers. Warp w owns the rows of TMEM lane
+//   quarter w & 3 in row half w >> 3 and the 32-channel half (w >> 2) & 1; it
+//   runs the reference's fmaf chain stage by stage from TMEM and, after a
+//   tile's last stage, the epilogue.
+// The weight images of all stages (at most kResidentStages) stay in shared
+// memory, fetched once per CTA. Stage slots (A tile halves, unit(s_in)) rotate
+// over kWsSlots; a slot is free again once all 16 consumer warps have run the
+// chain of the stage it held (empty[slot]), and a TMEM buffer once the chain of
+// the stage two before has run (the same barrier). The RMSNorm's per-32-channel sums go
+// to the cluster peers through distributed shared memory, after which each
+// consumer warp arrives on every peer's part_full[tile & 1] (release/acquire
+// at cluster scope): no cluster-wide barrier per tile, so the producers run on.
+// TMEM: column (half h, buffer b, group j, channel c) = 256 h + 128 b + 64 j + c.
+constexpr int kWsConsumerWarps = 16;
+constexpr int kWsThreads = (kWsConsumerWarps + 4) * 32;  // 640
+constexpr int kWsRows = 2 * kBM;                          // 256 rows per tile
+constexpr int kWsSlots = 3;
+constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
+
+template <int KS, int CS, bool ACT, bool G1>
+__global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
+{
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
+    const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
+    const int n_cta = min(kNCta, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
+    const bool live = n_cta > 0;
+    const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
+    uint8_t* a_slots = base;                                                   // [slot][half][kTileA]
+    uint8_t* b_codes = a_slots + kWsSlots * 2 * kTileA;                        // [stage][n_max][128 B]
+    float* b_units = reinterpret_cast<float*>(b_codes + S * p.n_max * 128);   // [stage][2][n_max]
+    float* din_s = b_units + S * 2 * p.n_max;                                 // [slot][2 groups][kWsRows]
+    float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [kNCta]
+    float* part = bias_s + kNCta;                                             // [2 tiles][8][kWsRows]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(part + 2 * 8 * kWsRows);
+    uint64_t* full_b = bars;                   // [0] every stage's weights landed
+    uint64_t* empty = bars + kWsSlots;         // [slot] every consumer warp ran the stage's chain
+    uint64_t* full_acc = bars + 2 * kWsSlots;  // [buf] the stage's MMAs completed
+    uint64_t* part_full = full_acc + 2;        // [tile & 1] the chunk's sums of squares arrived
+    uint64_t* drain = part_full + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    for (int i = tid; i < 2 * 8 * kWsRows; i += kWsThreads) part[i] = 0.0f;
+    if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
+    if (tid == 0) {
+        for (int i = 0; i < kWsSlots; ++i) {
+            mbar_init(smem_addr(&full_b[i]), 1);
+            mbar_init(smem_addr(&empty[i]), kWsConsumerWarps);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_addr(&full_acc[i]), 1);
+            mbar_init(smem_addr(&part_full[i]), CS * kWsConsumerWarps);
+        }
+        mbar_init(smem_addr(drain), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (live && warp == 0) tmem_alloc(smem_addr(tmem_slot), 512);
+    tc_fence_before();
+    __syncthreads();
+    if (CS > 1) cluster_sync_all();  // every peer's barriers and `part` are initialised before any remote access
+    tc_fence_after();
+    const uint32_t tmem = live ? *tmem_slot : 0u;
+
+    const int64_t n_tiles = (p.rows + kWsRows - 1) / kWsRows;
+    const int64_t tile0 = static_cast<int64_t>(blockIdx.x) * p.tiles_per_cta;
+    const int my_tiles = tile0 < n_tiles ? static_cast<int>(min(static_cast<int64_t>(p.tiles_per_cta), n_tiles - tile0)) : 0;
+    const int total = my_tiles * S;
+    const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
+
+    if (warp >= kWsConsumerWarps) {
+        // ------------------------------------------------------------ producers
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+        const int pt = tid - kWsConsumerWarps * 32;  // rows pt and pt + 128 of each tile
+        const int stage_bytes = n_cta * kImgRow;
+        const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
+        const uint32_t idesc = instr_desc(n_cta > 0 ? n_cta : 32);
+        // this thread's two rows: group base of the row's pixel (pointwise) or of
+        // the top-left pixel of its 2x2 window, per tile
+        const uint4* rb[2] = {nullptr, nullptr};
+        const int8_t* sb[2] = {nullptr, nullptr};
+        bool rok[2] = {false, false};
+        auto start_tile = [&](int t_local) {
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                const int64_t row = (tile0 + t_local) * kWsRows + hh * kBM + pt;
+                rok[hh] = row < p.rows;
+                const int64_t pix0 = KS == 2 ? (rok[hh] ? tap_pixel_pow2(row, 0, KS, lg_din, lg_dout) : 0) : row;
+                rb[hh] = reinterpret_cast<const uint4*>(p.in) + pix0 * G;
+                sb[hh] = p.in_s + pix0 * G;
+            }
+        };
+        // im2col position of group gk = 2 sp (j = 0) of the stage being loaded
+        int tap0 = 0, g0 = 0;
+        uint4 pw[2][2];
+        int8_t ps[2][2];
+        auto load_stage = [&](int sp) {  // into pw/ps, then advance (tap0, g0) by two groups
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                int tap = tap0, g = g0 + j;
+                if (g >= G) {
+                    g -= G;
+                    ++tap;
+                }
+                const bool gok = 2 * sp + j < GK;
+                const int off = (KS == 2 ? (((tap >> 1) << lg_din) + (tap & 1)) * G : 0) + g;
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    if (gok && rok[hh]) {
+                        pw[hh][j] = __ldg(rb[hh] + off);
+                        ps[hh][j] = __ldg(sb[hh] + off);
+                    } else {
+                        pw[hh][j] = make_uint4(0u, 0u, 0u, 0u);
+                        ps[hh][j] = -128;  // marks a padding (row, group): staged as zeros
+                    }
+                }
+            }
+            g0 += 2;
+            while (g0 >= G) {
+                g0 -= G;
+                ++tap0;
+            }
+        };
+        if (live && total > 0) {
+            if (pt == 0) {  // every stage's weights, once, on full_b[0]
+                mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
+                for (int k = 0; k < S; ++k) {
+                    const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
+                    bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
+                             smem_addr(&full_b[0]));
+                    bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
+                             smem_addr(&full_b[0]));
+                }
+            }
+            start_tile(0);
+            load_stage(0);
+        }
+        int sp = 0, tp = 0;
+        for (int gs = 0; live && gs < total; ++gs) {
+            const int slot = gs % kWsSlots;
+            bool run = !*abort_flag;
+            // the slot is free once the consumers ran the chain of stage gs - kWsSlots
+            if (run && gs >= kWsSlots &&
+                !mbar_wait(smem_addr(&empty[slot]), static_cast<uint32_t>(gs / kWsSlots - 1) & 1u, p.err, 31)) {
+                *abort_flag = 1;
+                run = false;
+            }
+            if (run) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    uint8_t* a_tile = a_slots + (slot * 2 + hh) * kTileA;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        float du = 0.0f;
+                        if (ps[hh][j] != -128) {
+                            du = unit_of(ps[hh][j]);
+                            stage_group_f(a_tile, pt, j, pw[hh][j], 1.0f);
+                        } else {
+                            stage_zero(a_tile, pt, j);
+                        }
+                        din_s[(slot * 2 + j) * kWsRows + hh * kBM + pt] = du;
+                    }
+                }
+                fence_async_smem();
+            }
+            // the next stage's activations, one stage ahead
+            if (gs + 1 < total) {
+                if (sp + 1 == S) {
+                    start_tile(tp + 1);
+                    tap0 = 0;
+                    g0 = 0;
+                    load_stage(0);
+                } else {
+                    load_stage(sp + 1);
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four producer warps staged stage gs
+            if (pt == 0 && run && !*abort_flag) {
+                const int buf = gs & 1;
+                // weights landed; TMEM buffer free once the consumers ran the chain of gs - 2
+                bool ok = gs > 0 || mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 32);
+                if (ok && gs >= 2)
+                    ok = mbar_wait(smem_addr(&empty[(gs - 2) % kWsSlots]), static_cast<uint32_t>((gs - 2) / kWsSlots) & 1u,
+                                   p.err, 33);
+                if (ok) {
+                    tc_fence_after();
+                    const uint64_t db = smem_desc(smem_addr(b_codes + sp * p.n_max * 128));
+                    const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint64_t da = smem_desc(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
+#pragma unroll
+                        for (int j = 0; j < kBK / 16; ++j)
+                            if (j < n_mma)
+                                mma_bf16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 2 * j,
+                                         db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
+                    }
+                    mma_commit(smem_addr(&full_acc[buf]));
+                } else {
+                    *abort_flag = 1;
+                }
+            }
+            if (++sp == S) {
+                sp = 0;
+                ++tp;
+            }
+        }
+        if (live && pt == 0) {  // every MMA issued has completed before TMEM is released
+            if (total > 0) mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 37);  // and the weight copy landed
+            mma_commit(smem_addr(drain));
+            mbar_wait(smem_addr(drain), 0u, p.err, 34);
+        }
+    } else {
+        // ------------------------------------------------------------ consumers
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
+        const int h = warp >> 3, q = warp & 3, hw = (warp >> 2) & 1;
+        const int erow = q * 32 + lane;    // TMEM lane = row within the half
+        const int trow = h * kBM + erow;   // row within the 256-row tile
+        const bool has_cols = hw < (n_cta >> 5);
+        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(256 * h + 32 * hw);
+        const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
+        const int gidx = ((n0 & (kNormChunk - 1)) >> 5) + hw;  // this warp's group within the norm chunk
+        constexpr bool kFold = KS == 2 && !G1;
+        float2 acc[16], sacc[kFold ? 16 : 1];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = dup2(0.0f);
+#pragma unroll
+        for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
+        for (int t = 0; t < my_tiles; ++t) {
+            bool ok = !*abort_flag;
+            for (int sc = 0; sc < S; ++sc) {
+                const int gs = t * S + sc, slot = gs % kWsSlots, buf = gs & 1;
+                if (live && ok) {
+                    if (!mbar_wait(smem_addr(&full_acc[buf]), static_cast<uint32_t>(gs >> 1) & 1u, p.err, 35)) {
+                        ok = false;
+                        *abort_flag = 1;
+                    }
+                }
+                if (live && ok) {
+                    tc_fence_after();
+                    const float* units = b_units + sc * 2 * p.n_max + 32 * hw;
+                    const float* dins = din_s + slot * 2 * kWsRows + trow;
+                    const uint32_t tb = tl + static_cast<uint32_t>(128 * buf);
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int gk = 2 * sc + j;
+                        if (gk >= GK) break;
+                        if (kFold && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
+#pragma unroll
+                            for (int i = 0; i < 16; ++i) {
+                                sacc[kFold ? i : 0] = add2(sacc[kFold ? i : 0], acc[i]);
+                                acc[i] = dup2(0.0f);
+                            }
+                        }
+                        if (has_cols) {
+                            const float2 du = dup2(dins[j * kWsRows]);
+                            const float4* u4 = reinterpret_cast<const float4*>(units + j * n_cta);
+#pragma unroll
+                            for (int h16 = 0; h16 < 2; ++h16) {
+                                float pv[16];
+                                tmem_ld16(tb + static_cast<uint32_t>(64 * j + 16 * h16), pv);
+#pragma unroll
+                                for (int i4 = 0; i4 < 4; ++i4) {
+                                    const float4 u = u4[4 * h16 + i4];
+                                    const int b = 8 * h16 + 2 * i4;
+                                    const float2 p0 = mul2(make_float2(u.x, u.y), make_float2(pv[4 * i4], pv[4 * i4 + 1]));
+                                    const float2 p1 = mul2(make_float2(u.z, u.w), make_float2(pv[4 * i4 + 2], pv[4 * i4 + 3]));
+                                    if (G1) {  // scalar: the product is rounded before the add
+                                        acc[b].x = __fadd_rn(acc[b].x, __fmul_rn(du.x, p0.x));
+                                        acc[b].y = __fadd_rn(acc[b].y, __fmul_rn(du.y, p0.y));
+                                        acc[b + 1].x = __fadd_rn(acc[b + 1].x, __fmul_rn(du.x, p1.x));
+                                        acc[b + 1].y = __fadd_rn(acc[b + 1].y, __fmul_rn(du.y, p1.y));
+                                    } else {
+                                        acc[b] = fma2(du, p0, acc[b]);
+                                        acc[b + 1] = fma2(du, p1, acc[b + 1]);
+                                    }
+                                }
+                            }
+                        }
+                    }
+                    tc_fence_before();
+                }
+                // slot and TMEM buffer may be reused once every consumer warp is here
+                __syncwarp();
+                if (live && lane == 0) mbar_arrive(smem_addr(&empty[slot]));
+            }
+
+            // Epilogue of the tile: fold the taps, square-sum the 32-channel group,
+            // share the sums across the norm chunk, normalise, activate, pack.
+            float* part_t = part + (t & 1) * 8 * kWsRows;
+            const bool emit = live && ok && has_cols;
+            if (kFold) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = add2(sacc[kFold ? i : 0], acc[i]);
+            }
+            if (emit) {
+                const float gs2 = tree_sq32x2(acc);
+                float* dst = &part_t[gidx * kWsRows + trow];
+                if (CS > 1) {
+#pragma unroll
+                    for (int r = 0; r < CS; ++r) st_peer_f32(smem_addr(dst), static_cast<uint32_t>(r), gs2);
+                } else {
+                    *dst = gs2;
+                }
+            }
+            bool got = true;
+            if (CS > 1) {
+                asm volatile("fence.acq_rel.cluster;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int r = 0; r < CS; ++r) mbar_arrive_peer(smem_addr(&part_full[t & 1]), static_cast<uint32_t>(r));
+                }
+                if (!*abort_flag && !mbar_wait_cluster(smem_addr(&part_full[t & 1]), static_cast<uint32_t>(t >> 1) & 1u, p.err, 36)) {
+                    got = false;
+                    *abort_flag = 1;
+                }
+            } else {
+                asm volatile("bar.sync 2, 512;" ::: "memory");  // the 16 consumer warps' sums are in `part`
+            }
+            if (emit && got) {
+                // the reference's cross-warp butterfly over the chunk's 8 group sums (kernels.h:271-276)
+                float w8[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) w8[i] = part_t[i * kWsRows + trow];
+#pragma unroll
+                for (int o = 4; o > 0; o >>= 1)
+#pragma unroll
+                    for (int i = 0; i < o; ++i) w8[i] = __fadd_rn(w8[i], w8[i + o]);
+                const float sc_norm = __frsqrt_rn(fmaf(w8[0], inv_div, kEps));
+                const int64_t row = (tile0 + t) * kWsRows + trow;
+                const float2 sc2 = dup2(sc_norm);
+                const float4* b4 = reinterpret_cast<const float4*>(bias_s + 32 * hw);
+#pragma unroll
+                for (int i4 = 0; i4 < 8; ++i4) {
+                    const float4 b = b4[i4];
+                    acc[2 * i4] = fma2(acc[2 * i4], sc2, make_float2(b.x, b.y));
+                    acc[2 * i4 + 1] = fma2(acc[2 * i4 + 1], sc2, make_float2(b.z, b.w));
+                    if (ACT) {
+                        acc[2 * i4] = silu2(acc[2 * i4]);
+                        acc[2 * i4 + 1] = silu2(acc[2 * i4 + 1]);
+                    }
+                }
+                uint4 words;
+                int8_t e;
+                quantize_group2(acc, &words, &e);
+                if (row < p.rows) {
+                    const int64_t gi = row * (p.out_c >> 5) + (n0 >> 5) + hw;
+                    reinterpret_cast<uint4*>(p.out)[gi] = words;
+                    p.out_s[gi] = e;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = dup2(0.0f);
+#pragma unroll
+            for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
+        }
+    }
+    // every role is done; no CTA of the cluster leaves while a peer may still
+    // write into its shared memory, and TMEM is released after all MMAs completed
+    tc_fence_before();
+    __syncthreads();
+    if (CS > 1) cluster_sync_all();
+    if (live && warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
 // Per (64-channel chunk, stage) image: the codes of both groups as bf16 in the
 // SW128 K-major layout ([n][64] elements), then unit(s_w) of group 0 and
 // group 1 ([2][n] fp32). One thread per (output channel, group slot).
@@ -739,6 +1121,63 @@ cudaError_t launch_ord_cs(const OrdParams& p, size_t smem, cudaStream_t stream)
     if (cs == 1) return launch_ord<KS, 1>(q, smem, chunks, stream);
     if (cs == 2) return launch_ord<KS, 2>(q, smem, chunks, stream);
     return launch_ord<KS, 4>(q, smem, chunks, stream);
+}
+
+template <int KS, int CS>
+cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
+{
+    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false> : conv_gemm_tc_ws_kernel<KS, CS, false, false>;
+    if constexpr (KS == 2) {
+        if (p.in_c == 32)  // one group per tap
+            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true> : conv_gemm_tc_ws_kernel<KS, CS, false, true>;
+    }
+    // The role split (setmaxnreg: 512 consumer threads x 104 + 128 producer
+    // threads x 64 registers) draws on the block's launch allocation of
+    // 640 x 96; with any other count the increase could never be granted.
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != 96) return cudaErrorNotSupported;
+    if (p.stages > kResidentStages) return cudaErrorNotSupported;  // the weights must stay resident
+    const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * 2 * kTileA + static_cast<size_t>(p.stages) * p.n_max * kImgRow +
+                        (static_cast<size_t>(kWsSlots) * 2 * kWsRows + kNCta + 16 * kWsRows) * sizeof(float) +
+                        (2 * kWsSlots + 5) * 8 + 16;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return e;
+    // One CTA per SM (its 512 TMEM columns and ~160 KB of shared memory); runs of
+    // tiles sized for about four CTAs per SM over the launch.
+    const int64_t n_tiles = (p.rows + kWsRows - 1) / kWsRows;
+    int64_t t = n_tiles * chunks * CS / (148 * 4);
+    OrdParams q = p;
+    q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 16 ? 16 : t);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>((n_tiles + q.tiles_per_cta - 1) / q.tiles_per_cta), chunks * CS, 1);
+    cfg.blockDim = dim3(kWsThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = CS;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = CS > 1 ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, kern, q);
+    if (e != cudaSuccess) return e;
+    return cudaGetLastError();
+}
+
+template <int KS>
+cudaError_t launch_ws_cs(const OrdParams& p, cudaStream_t stream)
+{
+    const int w = p.out_c < kNormChunk ? p.out_c : kNormChunk;
+    const int cs = w <= kNCta ? 1 : w <= 2 * kNCta ? 2 : 4;
+    const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
+    if (cs == 1) return launch_ws<KS, 1>(p, chunks, stream);
+    if (cs == 2) return launch_ws<KS, 2>(p, chunks, stream);
+    return launch_ws<KS, 4>(p, chunks, stream);
 }
 
 }  // namespace
@@ -832,6 +1271,17 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // the streaming kernel from three on
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
         return launch_cae_pw(p, stream);
+    // measured: the warp-specialised kernel wins up to four stages per tile and
+    // norm clusters of up to two CTAs (8% on such layers of the cortex); with
+    // longer K its four staging warps fall behind, and with clusters of four the
+    // per-tile exchange of the sums of squares idles its single CTA per SM,
+    // where the two-role kernel's second CTA keeps the SM busy
+    const int w_chunk = p.out_c < kNormChunk ? p.out_c : kNormChunk;
+    if (p.stages <= kWsMaxStages && w_chunk <= 2 * kNCta) {
+        const cudaError_t e = ksize == 1 ? launch_ws_cs<1>(p, stream) : launch_ws_cs<2>(p, stream);
+        if (e != cudaErrorNotSupported) return e;
+        (void)cudaGetLastError();  // the warp-specialised build is unusable: the two-role kernel below
+    }
     const int nb = p.stages <= kResidentStages ? p.stages : 2;  // weight slots (the kernel's `nb`)
     size_t smem = 1024 + 2 * static_cast<size_t>(kTileA) + static_cast<size_t>(nb) * p.n_max * kImgRow +
                   (4 * kBM + kNCta + 16 * kBM) * sizeof(float) + 5 * 8 + 16;

@@ -66,6 +66,43 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* er
     return false;
 }
 
+// Arrive once on a barrier of this CTA (release at CTA scope).
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Arrive once on the barrier at the same offset in cluster CTA `peer`, with
+// release at cluster scope (orders this thread's prior distributed-shared
+// stores before the peer's acquire).
+__device__ __forceinline__ void mbar_arrive_peer(uint32_t local_bar, uint32_t peer)
+{
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_bar), "r"(peer));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+// mbar_wait with acquire at cluster scope: after it, stores that cluster peers
+// made before their releasing arrive are visible.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code)
+{
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < kWaitLimit; ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(20000u)
+            : "memory");
+        if (ok) return true;
+        if (global_ns() - t0 > kWaitNs) break;
+    }
+    atomicCAS(err, 0, code);
+    return false;
+}
+
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
 {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
