@@ -161,6 +161,101 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
     if (groups == 1) *reinterpret_cast<uint32_t*>(out_s + pix) = packed_s;
 }
 
+// Residual add when a position has exactly S = C/32 groups (S a power of two):
+// lane gl of a segment of S lanes owns group gl of two positions 32/S apart,
+// and all four of its loads are issued before any arithmetic (twice the bytes
+// in flight of one position per lane). Per element, as residualAddFwdKernel
+// (kernels.h:1020-1026): r = fmaf(q_m, unit(s_m) * mult, q_r * unit(s_r)), two
+// channels per packed instruction (the products feed an fma's addend, which is
+// never fused). One exponent per position: the absmax (from 0, kernels.h:1008)
+// over its S groups, reduced across the segment's lanes; requant as
+// quantize_group (the reference's sequence for a group holding a NaN or inf).
+template <int S>
+__global__ void __launch_bounds__(kThreads) residual_pos2_kernel(const uint32_t* __restrict__ main_in, const int8_t* __restrict__ main_s,
+                                                               const uint32_t* __restrict__ res, const int8_t* __restrict__ res_s,
+                                                               uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
+                                                               int64_t positions, float main_mult, bool skipped)
+{
+    constexpr int kPos = 32 / S;  // positions per warp row
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) >> 5;
+    const int gl = lane % S;
+    const int64_t p0 = warp * 2 * kPos + lane / S;
+    uint4 a[2], b[2];
+    int8_t sa[2], sb[2];
+    bool live[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const int64_t pos = p0 + k * kPos;
+        live[k] = pos < positions;
+        const int64_t gi = (live[k] ? pos : 0) * S + gl;
+        a[k] = skipped ? make_uint4(0u, 0u, 0u, 0u) : __ldg(reinterpret_cast<const uint4*>(main_in) + gi);
+        b[k] = __ldg(reinterpret_cast<const uint4*>(res) + gi);
+        sa[k] = skipped ? static_cast<int8_t>(0) : __ldg(main_s + gi);
+        sb[k] = __ldg(res_s + gi);
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float2 s_res = dup2(unit_of(sb[k]));
+        const float2 s_in = dup2(skipped ? 0.0f : unit_of(sa[k]) * main_mult);
+        const uint32_t aw[4] = {a[k].x, a[k].y, a[k].z, a[k].w}, bw[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
+        float2 r[16];
+        float amax = 0.0f, amaxn = 0.0f;  // the reference's absmax, and one that keeps a NaN
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            // byte j of lo / hi: code 2j / 2j + 1 of the word as n ^ 8, placed in
+            // the mantissa of 2^23 (0x4B0000bb = 2^23 + q + 8)
+            const uint32_t alo = (aw[q] & 0x0F0F0F0Fu) ^ 0x08080808u, ahi = ((aw[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+            const uint32_t blo = (bw[q] & 0x0F0F0F0Fu) ^ 0x08080808u, bhi = ((bw[q] >> 4) & 0x0F0F0F0Fu) ^ 0x08080808u;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 qa = add2(make_float2(__uint_as_float(__byte_perm(alo, 0x4B000000u, 0x7440u | j)),
+                                                   __uint_as_float(__byte_perm(ahi, 0x4B000000u, 0x7440u | j))),
+                                       dup2(-8388616.0f));
+                const float2 qb = add2(make_float2(__uint_as_float(__byte_perm(blo, 0x4B000000u, 0x7440u | j)),
+                                                   __uint_as_float(__byte_perm(bhi, 0x4B000000u, 0x7440u | j))),
+                                       dup2(-8388616.0f));
+                const float2 v = fma2(qa, s_in, mul2(qb, s_res));
+                r[4 * q + j] = v;
+                amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
+                amaxn = amax_nan(amax_nan(amaxn, v.x), v.y);
+            }
+        }
+#pragma unroll
+        for (int o = S >> 1; o > 0; o >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+            amaxn = max_nan(amaxn, __shfl_xor_sync(0xFFFFFFFFu, amaxn, o));
+        }
+        if (!live[k]) continue;
+        const float scale = amax < kEps ? 1.0f : amax;
+        const float inv = kQMax * rcp_rn_pos(scale);
+        uint32_t w[4];
+        if (is_finite_amax(amaxn)) {  // rn without the clamp (aic_common.cuh)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                uint32_t z[8];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    z[2 * i] = magic_bits(__fmul_rn(r[4 * q + i].x, inv));
+                    z[2 * i + 1] = magic_bits(__fmul_rn(r[4 * q + i].y, inv));
+                }
+                w[q] = pack8_magic(z);
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                w[q] = 0u;
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    w[q] |= (code_rn(r[4 * q + i].x, inv) << (8 * i)) | (code_rn(r[4 * q + i].y, inv) << (8 * i + 4));
+            }
+        }
+        const int64_t gi = (p0 + k * kPos) * S + gl;
+        reinterpret_cast<uint4*>(out)[gi] = make_uint4(w[0], w[1], w[2], w[3]);
+        out_s[gi] = exponent_of(scale);
+    }
+}
+
 // Residual add with one exponent per position. A position is handled by a
 // segment of S lanes (S = next power of two >= C/32, at most 32); each lane
 // walks groups gl, gl+S, ... The values are recomputed in the second pass
@@ -373,6 +468,21 @@ cudaError_t launch_residual(const uint32_t* main_in, const int8_t* main_s, const
     const int G = C >> 5;
     int S = 1;
     while (S < G && S < 32) S <<= 1;
+    if (S == G) {  // one group per lane, two positions per lane
+        const int64_t warps2 = (positions + 2 * (32 / S) - 1) / (2 * (32 / S));
+        const unsigned grid2 = grid_for(warps2 * 32);
+#define AIC_RES2(SS) residual_pos2_kernel<SS><<<grid2, kThreads, 0, stream>>>(main_in, main_s, res, res_s, out, out_s, positions, main_mult, skipped)
+        switch (S) {
+            case 1: AIC_RES2(1); break;
+            case 2: AIC_RES2(2); break;
+            case 4: AIC_RES2(4); break;
+            case 8: AIC_RES2(8); break;
+            case 16: AIC_RES2(16); break;
+            default: AIC_RES2(32); break;
+        }
+#undef AIC_RES2
+        return cudaGetLastError();
+    }
     const int64_t warps = (positions + (32 / S) - 1) / (32 / S);
     const unsigned grid = grid_for(warps * 32);
 #define AIC_RES(SS) residual_kernel<SS><<<grid, kThreads, 0, stream>>>(main_in, main_s, res, res_s, out, out_s, positions, C, main_mult, skipped)
