@@ -189,8 +189,16 @@ __device__ __forceinline__ uint32_t pack8_magic(const uint32_t (&z)[8])
 // the result is NaN only when every value is NaN.
 __device__ __forceinline__ float butterfly_start() { return __int_as_float(0x7FFFFFFF); }
 
-// The reference's epilogue sequence for 32 values held by one thread.
-static __device__ __noinline__ void quantize_group_ref(const float* v, uint4* words, int8_t* exp_out)
+// The packed group a quantiser returns: 4 code words and the exponent.
+struct QuantGroup {
+    uint4 words;
+    int exp;
+};
+
+// The reference's epilogue sequence for 32 values held by one thread. Not
+// inlined (it is the rare path) and returning by value, so that only its
+// caller's copy of the values, made on that path, lives in local memory.
+static __device__ __noinline__ QuantGroup quantize_group_ref(const float* v)
 {
     float amax = butterfly_start();
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
@@ -198,8 +206,7 @@ static __device__ __noinline__ void quantize_group_ref(const float* v, uint4* wo
     const float inv = kQMax * rcp_rn_pos(scale);
     uint32_t w[4] = {0u, 0u, 0u, 0u};
     for (int i = 0; i < 32; ++i) w[i >> 3] |= code_rn(v[i], inv) << ((i & 7) << 2);
-    *words = make_uint4(w[0], w[1], w[2], w[3]);
-    *exp_out = exponent_of(scale);
+    return QuantGroup{make_uint4(w[0], w[1], w[2], w[3]), exponent_of(scale)};
 }
 
 // Quantise 32 values held by one thread into 4 words + exponent.
@@ -212,7 +219,9 @@ __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* word
         float f[32];  // a copy, so that only the rare path takes an array's address
 #pragma unroll
         for (int i = 0; i < 32; ++i) f[i] = v[i];
-        quantize_group_ref(f, words, exp_out);
+        const QuantGroup r = quantize_group_ref(f);
+        *words = r.words;
+        *exp_out = static_cast<int8_t>(r.exp);
         return;
     }
     const float scale = amax < kEps ? 1.0f : amax;
@@ -242,7 +251,9 @@ __device__ __forceinline__ void quantize_group2(const float2 (&v)[16], uint4* wo
             f[2 * i] = v[i].x;
             f[2 * i + 1] = v[i].y;
         }
-        quantize_group_ref(f, words, exp_out);
+        const QuantGroup r = quantize_group_ref(f);
+        *words = r.words;
+        *exp_out = static_cast<int8_t>(r.exp);
         return;
     }
     const float scale = amax < kEps ? 1.0f : amax;

@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 4) conv_gemm_tc_kernel(TcParams p)
                 const uint32_t a_addr = smem_addr(a_tile), b_addr = smem_addr(b_tile);
 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j)
-                    mma_bf16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
+                    mma_f16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc,
                              (s > 0 || j > 0) ? 1u : 0u);
                 mma_commit(smem_addr(&bars[nst + buf]));
             } else {

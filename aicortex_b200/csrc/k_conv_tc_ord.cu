@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     const int GK = p.gk_total;
     const int stage_bytes = n_cta * kImgRow;
     const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
-    const uint32_t idesc = instr_desc(n_cta);
+    const uint32_t idesc = instr_desc_h(n_cta);
     const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
 
     // chain role: row erow (== prow), 32-channel group hw of the tile
@@ -323,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
             float du = 0.0f;
             if (pf_ok) {
                 du = unit_of(pf_s);
-                stage_group_f(a_tile, prow, pg, pf_words, 1.0f);
+                stage_group_h(a_tile, prow, pg, pf_words);
             } else {
                 stage_zero(a_tile, prow, pg);
             }
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j)
                     if (j < n_mma)
-                        mma_bf16(tmem + static_cast<uint32_t>((buf * 2 + (j >> 1)) * n_cta), da + 2 * j, db + 2 * j, idesc,
+                        mma_f16(tmem + static_cast<uint32_t>((buf * 2 + (j >> 1)) * n_cta), da + 2 * j, db + 2 * j, idesc,
                                  static_cast<uint32_t>(j & 1));
                 mma_commit(smem_addr(&bars[2 + buf]));
             } else {
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     }
 
     const int prow = tid & (kBM - 1), pg = tid >> 7;
-    const uint32_t idesc = instr_desc(n_cta > 0 ? n_cta : 32);
+    const uint32_t idesc = instr_desc_h(n_cta > 0 ? n_cta : 32);
     const int q = warp & 3, hw = warp >> 2;
     const int erow = q * 32 + lane;
     const int ngroups = n_cta >> 5;
@@ -544,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
                 const int64_t gi = prow_g * GK + pg;  // pointwise: the row's own pixel, group pg
                 const uint4 words = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
                 du = unit_of(__ldg(p.in_s + gi));
-                stage_group_f(a_tile, prow, pg, words, 1.0f);
+                stage_group_h(a_tile, prow, pg, words);
             } else {
                 stage_zero(a_tile, prow, pg);
             }
@@ -561,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 #pragma unroll
                 for (int j = 0; j < kBK / 16; ++j)
                     if (j < n_mma)
-                        mma_bf16(tmem + static_cast<uint32_t>((j >> 1) * n_cta), smem_desc(a_addr + 32 * j),
+                        mma_f16(tmem + static_cast<uint32_t>((j >> 1) * n_cta), smem_desc(a_addr + 32 * j),
                                  smem_desc(b_addr + 32 * j), idesc, static_cast<uint32_t>(j & 1));
             } else {
                 *abort_flag = 1;
@@ -669,12 +669,15 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 // The streaming kernel's pipeline with its roles on separate warps and its
 // hand-offs on mbarriers instead of CTA-wide barriers. One CTA per SM, 640
 // threads, tiles of 256 rows x 64 channels:
-// * warps 16-19 (one warpgroup, 64 registers after setmaxnreg): producers.
-//   Thread pt stages rows pt and pt + 128 of the tile (both groups of a stage,
-//   loaded one stage ahead into registers) and records unit(s_in). Thread 0
-//   also fetches the stage's weight image and, once the four warps have staged
-//   (named barrier 1), issues the stage's MMAs: two M = 128 halves x two groups
-//   x two K16 steps, into one of two TMEM buffers, committed to full_acc[buf].
+// * warps 16-18 (64 registers after setmaxnreg): staging. Thread pt stages
+//   rows pt, pt + 96 and pt + 192 (< 256) of the tile (both groups of a
+//   stage, loaded one stage ahead into registers) and records unit(s_in); each
+//   warp then arrives on staged[slot].
+// * warp 19 (the same warpgroup): one thread fetches the weight images
+//   and issues each staged stage's MMAs (two M = 128 halves x two groups x two
+//   K16 steps) into one of two TMEM buffers, committed to full_acc[buf]. On
+//   its own warp the MMA issue, which waits for the tensor pipe, overlaps the
+//   staging of the next stage.
 // * warps 0-15 (104 registers): consumers. Warp w owns the rows of TMEM lane
 //   quarter w & 3 in row half w >> 3 and the 32-channel half (w >> 2) & 1; it
 //   runs the reference's fmaf chain stage by stage from TMEM and, after a
@@ -689,8 +692,11 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 // at cluster scope): no cluster-wide barrier per tile, so the producers run on.
 // TMEM: column (half h, buffer b, group j, channel c) = 256 h + 128 b + 64 j + c.
 constexpr int kWsConsumerWarps = 16;
-constexpr int kWsThreads = (kWsConsumerWarps + 4) * 32;  // 640
-constexpr int kWsRows = 2 * kBM;                          // 256 rows per tile
+constexpr int kWsStageWarps = 3;
+constexpr int kWsThreads = (kWsConsumerWarps + kWsStageWarps + 1) * 32;  // 640
+constexpr int kWsRows = 2 * kBM;                                           // 256 rows per tile
+constexpr int kWsStageRows = kWsStageWarps * 32;                           // 96 staging threads
+constexpr int kWsRowsPerThread = (kWsRows + kWsStageRows - 1) / kWsStageRows;  // 3
 constexpr int kWsSlots = 3;
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
 
@@ -710,9 +716,10 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [kNCta]
     float* part = bias_s + kNCta;                                             // [2 tiles][8][kWsRows]
     uint64_t* bars = reinterpret_cast<uint64_t*>(part + 2 * 8 * kWsRows);
-    uint64_t* full_b = bars;                   // [0] every stage's weights landed
-    uint64_t* empty = bars + kWsSlots;         // [slot] every consumer warp ran the stage's chain
-    uint64_t* full_acc = bars + 2 * kWsSlots;  // [buf] the stage's MMAs completed
+    uint64_t* full_b = bars;                       // every stage's weights landed
+    uint64_t* staged = bars + 1;                   // [slot] the staging warps filled the slot
+    uint64_t* empty = staged + kWsSlots;           // [slot] every consumer warp ran the stage's chain
+    uint64_t* full_acc = empty + kWsSlots;         // [buf] the stage's MMAs completed
     uint64_t* part_full = full_acc + 2;        // [tile & 1] the chunk's sums of squares arrived
     uint64_t* drain = part_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -722,8 +729,9 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     for (int i = tid; i < 2 * 8 * kWsRows; i += kWsThreads) part[i] = 0.0f;
     if (live && tid < n_cta) bias_s[tid] = p.bias[n0 + tid];
     if (tid == 0) {
+        mbar_init(smem_addr(&full_b[0]), 1);
         for (int i = 0; i < kWsSlots; ++i) {
-            mbar_init(smem_addr(&full_b[i]), 1);
+            mbar_init(smem_addr(&staged[i]), kWsStageWarps);
             mbar_init(smem_addr(&empty[i]), kWsConsumerWarps);
         }
         for (int i = 0; i < 2; ++i) {
@@ -747,32 +755,77 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     const int total = my_tiles * S;
     const int lg_dout = 31 - __clz(p.dout), lg_din = 31 - __clz(p.din);
 
-    if (warp >= kWsConsumerWarps) {
-        // ------------------------------------------------------------ producers
+    if (warp == kWsConsumerWarps + kWsStageWarps) {
+        // ------------------------------------------------------------ MMA issuer
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");  // with the staging warps: one warpgroup
+        // One thread fetches every
+        // stage's weights once, then issues each staged stage's MMAs into the
+        // TMEM buffer the consumers freed.
+        if (live && lane == 0 && total > 0) {
+            const int stage_bytes = n_cta * kImgRow;
+            const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
+            const uint32_t idesc = instr_desc_h(n_cta);
+            mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
+            for (int k = 0; k < S; ++k) {
+                const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
+                bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128), smem_addr(&full_b[0]));
+                bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
+                         smem_addr(&full_b[0]));
+            }
+            int sp = 0;
+            for (int gs = 0; gs < total; ++gs) {
+                const int slot = gs % kWsSlots, buf = gs & 1;
+                // staged; weights landed; TMEM buffer free once the consumers ran the chain of gs - 2
+                bool ok = !*abort_flag &&
+                          mbar_wait(smem_addr(&staged[slot]), static_cast<uint32_t>(gs / kWsSlots) & 1u, p.err, 39) &&
+                          (gs > 0 || mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 32)) &&
+                          (gs < 2 || mbar_wait(smem_addr(&empty[(gs - 2) % kWsSlots]),
+                                               static_cast<uint32_t>((gs - 2) / kWsSlots) & 1u, p.err, 33));
+                if (ok) {
+                    tc_fence_after();
+                    const uint64_t db = smem_desc(smem_addr(b_codes + sp * p.n_max * 128));
+                    const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        const uint64_t da = smem_desc(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
+#pragma unroll
+                        for (int j = 0; j < kBK / 16; ++j)
+                            if (j < n_mma)
+                                mma_f16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 2 * j,
+                                        db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
+                    }
+                    mma_commit(smem_addr(&full_acc[buf]));
+                } else {
+                    *abort_flag = 1;
+                }
+                if (++sp == S) sp = 0;
+            }
+            // every MMA issued has completed (and the weight copy landed) before TMEM is released
+            mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 37);
+            mma_commit(smem_addr(drain));
+            mbar_wait(smem_addr(drain), 0u, p.err, 34);
+        }
+    } else if (warp >= kWsConsumerWarps) {
+        // ------------------------------------------------------------ staging
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
-        const int pt = tid - kWsConsumerWarps * 32;  // rows pt and pt + 128 of each tile
-        const int stage_bytes = n_cta * kImgRow;
-        const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
-        const uint32_t idesc = instr_desc(n_cta > 0 ? n_cta : 32);
-        // this thread's two rows: group base of the row's pixel (pointwise) or of
-        // the top-left pixel of its 2x2 window, per tile
-        const uint4* rb[2] = {nullptr, nullptr};
-        const int8_t* sb[2] = {nullptr, nullptr};
-        bool rok[2] = {false, false};
+        const int pt = tid - kWsConsumerWarps * 32;  // rows pt + kWsStageRows * i of each tile
+        // this thread's rows: pixel of the row (pointwise) or of the top-left
+        // pixel of its 2x2 window, per tile (-1: past the end)
+        int pix[kWsRowsPerThread];
         auto start_tile = [&](int t_local) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int64_t row = (tile0 + t_local) * kWsRows + hh * kBM + pt;
-                rok[hh] = row < p.rows;
-                const int64_t pix0 = KS == 2 ? (rok[hh] ? tap_pixel_pow2(row, 0, KS, lg_din, lg_dout) : 0) : row;
-                rb[hh] = reinterpret_cast<const uint4*>(p.in) + pix0 * G;
-                sb[hh] = p.in_s + pix0 * G;
+            for (int i = 0; i < kWsRowsPerThread; ++i) {
+                const int rl = pt + kWsStageRows * i;
+                const int64_t row = (tile0 + t_local) * kWsRows + rl;
+                pix[i] = rl < kWsRows && row < p.rows
+                             ? static_cast<int>(KS == 2 ? tap_pixel_pow2(row, 0, KS, lg_din, lg_dout) : row)
+                             : -1;
             }
         };
         // im2col position of group gk = 2 sp (j = 0) of the stage being loaded
         int tap0 = 0, g0 = 0;
-        uint4 pw[2][2];
-        int8_t ps[2][2];
+        uint4 pw[kWsRowsPerThread][2];
+        int8_t ps[kWsRowsPerThread][2];
         auto load_stage = [&](int sp) {  // into pw/ps, then advance (tap0, g0) by two groups
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -784,13 +837,14 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                 const bool gok = 2 * sp + j < GK;
                 const int off = (KS == 2 ? (((tap >> 1) << lg_din) + (tap & 1)) * G : 0) + g;
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    if (gok && rok[hh]) {
-                        pw[hh][j] = __ldg(rb[hh] + off);
-                        ps[hh][j] = __ldg(sb[hh] + off);
+                for (int i = 0; i < kWsRowsPerThread; ++i) {
+                    if (gok && pix[i] >= 0) {
+                        const int64_t gi = static_cast<int64_t>(pix[i]) * G + off;
+                        pw[i][j] = __ldg(reinterpret_cast<const uint4*>(p.in) + gi);
+                        ps[i][j] = __ldg(p.in_s + gi);
                     } else {
-                        pw[hh][j] = make_uint4(0u, 0u, 0u, 0u);
-                        ps[hh][j] = -128;  // marks a padding (row, group): staged as zeros
+                        pw[i][j] = make_uint4(0u, 0u, 0u, 0u);
+                        ps[i][j] = -128;  // marks a padding (row, group): staged as zeros
                     }
                 }
             }
@@ -801,16 +855,6 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
             }
         };
         if (live && total > 0) {
-            if (pt == 0) {  // every stage's weights, once, on full_b[0]
-                mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
-                for (int k = 0; k < S; ++k) {
-                    const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
-                    bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
-                             smem_addr(&full_b[0]));
-                    bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
-                             smem_addr(&full_b[0]));
-                }
-            }
             start_tile(0);
             load_stage(0);
         }
@@ -826,22 +870,26 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
             }
             if (run) {
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    uint8_t* a_tile = a_slots + (slot * 2 + hh) * kTileA;
+                for (int i = 0; i < kWsRowsPerThread; ++i) {
+                    const int rl = pt + kWsStageRows * i;
+                    if (rl >= kWsRows) break;
+                    uint8_t* a_tile = a_slots + (slot * 2 + (rl >> 7)) * kTileA;
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         float du = 0.0f;
-                        if (ps[hh][j] != -128) {
-                            du = unit_of(ps[hh][j]);
-                            stage_group_f(a_tile, pt, j, pw[hh][j], 1.0f);
+                        if (ps[i][j] != -128) {
+                            du = unit_of(ps[i][j]);
+                            stage_group_h(a_tile, rl & (kBM - 1), j, pw[i][j]);
                         } else {
-                            stage_zero(a_tile, pt, j);
+                            stage_zero(a_tile, rl & (kBM - 1), j);
                         }
-                        din_s[(slot * 2 + j) * kWsRows + hh * kBM + pt] = du;
+                        din_s[(slot * 2 + j) * kWsRows + rl] = du;
                     }
                 }
-                fence_async_smem();
+                fence_async_smem();  // the tile is read by the MMAs (async proxy)
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(&staged[slot]));  // also after an abort: the MMA thread never waits in vain
             // the next stage's activations, one stage ahead
             if (gs + 1 < total) {
                 if (sp + 1 == S) {
@@ -853,41 +901,10 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                     load_stage(sp + 1);
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four producer warps staged stage gs
-            if (pt == 0 && run && !*abort_flag) {
-                const int buf = gs & 1;
-                // weights landed; TMEM buffer free once the consumers ran the chain of gs - 2
-                bool ok = gs > 0 || mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 32);
-                if (ok && gs >= 2)
-                    ok = mbar_wait(smem_addr(&empty[(gs - 2) % kWsSlots]), static_cast<uint32_t>((gs - 2) / kWsSlots) & 1u,
-                                   p.err, 33);
-                if (ok) {
-                    tc_fence_after();
-                    const uint64_t db = smem_desc(smem_addr(b_codes + sp * p.n_max * 128));
-                    const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
-#pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const uint64_t da = smem_desc(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
-#pragma unroll
-                        for (int j = 0; j < kBK / 16; ++j)
-                            if (j < n_mma)
-                                mma_bf16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 2 * j,
-                                         db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
-                    }
-                    mma_commit(smem_addr(&full_acc[buf]));
-                } else {
-                    *abort_flag = 1;
-                }
-            }
             if (++sp == S) {
                 sp = 0;
                 ++tp;
             }
-        }
-        if (live && pt == 0) {  // every MMA issued has completed before TMEM is released
-            if (total > 0) mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 37);  // and the weight copy landed
-            mma_commit(smem_addr(drain));
-            mbar_wait(smem_addr(drain), 0u, p.err, 34);
         }
     } else {
         // ------------------------------------------------------------ consumers
@@ -1046,9 +1063,10 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     }
 }
 
-// Per (64-channel chunk, stage) image: the codes of both groups as bf16 in the
-// SW128 K-major layout ([n][64] elements), then unit(s_w) of group 0 and
-// group 1 ([2][n] fp32). One thread per (output channel, group slot).
+// Per (64-channel chunk, stage) image: the codes of both groups as fp16 in the
+// SW128 K-major layout ([n][64] elements, pairs ordered and scaled as
+// stage_group_w16 writes them), then unit(s_w) of group 0 and group 1
+// ([2][n] fp32). One thread per (output channel, group slot).
 __global__ void build_wimg_ord_kernel(const uint32_t* __restrict__ w, const int8_t* __restrict__ w_s, int out_c,
                                       int gk_total, int stages, uint8_t* __restrict__ img)
 {
@@ -1064,7 +1082,7 @@ __global__ void build_wimg_ord_kernel(const uint32_t* __restrict__ w, const int8
     float* units = reinterpret_cast<float*>(tile + n_chunk * 128);
     if (gk < gk_total) {
         const int64_t gi = static_cast<int64_t>(n) * gk_total + gk;
-        stage_group_f(tile, nl, gl, reinterpret_cast<const uint4*>(w)[gi], 1.0f);
+        stage_group_w16(tile, nl, gl, reinterpret_cast<const uint4*>(w)[gi]);
         units[gl * n_chunk + nl] = unit_of(w_s[gi]);
     } else {
         stage_zero(tile, nl, gl);
@@ -1131,17 +1149,19 @@ cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
         if (p.in_c == 32)  // one group per tap
             kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true> : conv_gemm_tc_ws_kernel<KS, CS, false, true>;
     }
-    // The role split (setmaxnreg: 512 consumer threads x 104 + 128 producer
-    // threads x 64 registers) draws on the block's launch allocation of
-    // 640 x 96; with any other count the increase could never be granted.
+    // The role split (setmaxnreg: 512 consumer threads x 104 + the staging and
+    // MMA warpgroup's 128 threads x 64 registers) draws on the block's launch
+    // allocation of 640 x 96; with any other count the increase could never
+    // be granted.
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
     if (fa.numRegs != 96) return cudaErrorNotSupported;
     if (p.stages > kResidentStages) return cudaErrorNotSupported;  // the weights must stay resident
+    if (p.rows * KS * KS > 0x7FFFFFFFll) return cudaErrorNotSupported;  // input pixel indices are 32-bit
     const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * 2 * kTileA + static_cast<size_t>(p.stages) * p.n_max * kImgRow +
                         (static_cast<size_t>(kWsSlots) * 2 * kWsRows + kNCta + 16 * kWsRows) * sizeof(float) +
-                        (2 * kWsSlots + 5) * 8 + 16;
+                        (2 * kWsSlots + 6) * 8 + 16;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);

@@ -1,5 +1,5 @@
-// tcgen05 / mbarrier / bulk-copy PTX wrappers and the int4 -> bf16 operand
-// staging shared by the tensor-core conv kernels (k_conv_tc.cu,
+// tcgen05 / mbarrier / bulk-copy PTX wrappers and the int4 -> bf16 / fp16
+// operand staging shared by the tensor-core conv kernels (k_conv_tc.cu,
 // k_conv_tc_ord.cu).
 #pragma once
 #include <cstdint>
@@ -143,7 +143,13 @@ __host__ __device__ constexpr uint32_t instr_desc(int n)
     return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+// The same for fp16 x fp16 -> f32 (the reference-order kernels' operands).
+__host__ __device__ constexpr uint32_t instr_desc_h(int n)
+{
+    return (1u << 4) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
 {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -282,6 +288,66 @@ __device__ __forceinline__ void stage_zero(uint8_t* tile, int row, int group_in_
     for (int cl = 0; cl < 4; ++cl) {
         const int chunk = (group_in_stage << 2) + cl;
         *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+// ---- int4 -> fp16 staging of the reference-order kernels ------------------------
+//
+// A word's 8 codes n_0..n_7 become the fp16 pairs (n_0, n_4), (n_1, n_5),
+// (n_2, n_6), (n_3, n_7). An even-indexed code is placed at mantissa bit 0 of
+// a half with exponent 2^10 (the half 0x6400 | (n ^ 8) is 1032 + q), an
+// odd-indexed one at mantissa bit 4 (0x6400 | (n ^ 8) << 4 is 1152 + 16 q): one
+// LOP3 per pair and one shift per word; one HADD2 per pair then removes the
+// offset exactly, leaving q and 16 q. The weight image holds w at the even
+// slots and w / 16 at the odd ones, so every product is q * w exactly, and A
+// and B share the K permutation.
+__device__ __forceinline__ uint4 unpack_word_h(uint32_t w)
+{
+    const uint32_t t = w >> 8;
+    uint32_t o[4] = {(w & 0x000F000Fu) ^ 0x64086408u, (w & 0x00F000F0u) ^ 0x64806480u, (t & 0x000F000Fu) ^ 0x64086408u,
+                     (t & 0x00F000F0u) ^ 0x64806480u};
+    const __half2 ce = __halves2half2(__ushort_as_half(0xE408u), __ushort_as_half(0xE408u));  // -1032
+    const __half2 co = __halves2half2(__ushort_as_half(0xE480u), __ushort_as_half(0xE480u));  // -1152
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        __half2 v = *reinterpret_cast<__half2*>(&o[j]);
+        v = __hadd2(v, (j & 1) ? co : ce);
+        o[j] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ uint8_t* sw128_row(uint8_t* tile, int row) { return tile + (row >> 3) * 1024 + (row & 7) * 128; }
+
+// One 32-element group of a K-major SW128 row as fp16 (q, 16 q).
+__device__ __forceinline__ void stage_group_h(uint8_t* tile, int row, int group_in_stage, uint4 words)
+{
+    uint8_t* rowp = sw128_row(tile, row);
+    const uint32_t w[4] = {words.x, words.y, words.z, words.w};
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+        const int chunk = (group_in_stage << 2) + cl;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = unpack_word_h(w[cl]);
+    }
+}
+
+// A weight group for the fp16 operands: w at the even slots, w / 16 at the odd.
+__device__ __forceinline__ void stage_group_w16(uint8_t* tile, int row, int group_in_stage, uint4 words)
+{
+    uint8_t* rowp = sw128_row(tile, row);
+    const uint32_t w[4] = {words.x, words.y, words.z, words.w};
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // pair j: codes (j, j + 4), as unpack_word_h orders them
+            const float s = (j & 1) ? 0.0625f : 1.0f;
+            const __half2 h = __floats2half2_rn(static_cast<float>(code_of(w[cl], j)) * s,
+                                                static_cast<float>(code_of(w[cl], j + 4)) * s);
+            o[j] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+        const int chunk = (group_in_stage << 2) + cl;
+        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
     }
 }
 

@@ -97,6 +97,22 @@ def test_golden_stem(golden):
     assert_f_equal(w, h(s), g["w"], g["s"], "stem")
 
 
+@pytest.mark.parametrize("planes,dim,channels", [(1, 8, 32), (3, 16, 32), (5, 8, 32), (8, 4, 32), (9, 8, 32),
+                                                 (3, 6, 32), (3, 5, 32), (32, 4, 32), (40, 4, 64), (3, 8, 64)])
+def test_stem_vs_oracle(planes, dim, channels):
+    """Every stem variant (8, 4 and 1 pixels per thread; one or several groups;
+    partial and full groups) against the oracle, with all-zero, tiny and
+    large-magnitude pixels mixed in."""
+    rng = np.random.default_rng(1200 + planes * 7 + dim)
+    x = (rng.standard_normal((3, planes, dim, dim)) * rng.choice([1e-6, 1.0, 300.0], size=(3, 1, dim, dim)))
+    x[:, :, 0, :2] = 0.0
+    x = x.astype(np.float16)
+    w, s = A.stem_pack(t(x), channels)
+    import oracle as O
+    wo, so = O.stem_pack(x, channels)
+    assert_f_equal(w, h(s), wo, so, "stem")
+
+
 @pytest.mark.parametrize("case", sorted(S.CONV_CASES))
 def test_golden_conv(golden, case):
     g = golden(f"conv_{case}")
