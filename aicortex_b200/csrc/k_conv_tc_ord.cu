@@ -787,11 +787,11 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                     const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
-                        const uint64_t da = smem_desc(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
+                        const uint64_t da = smem_desc_il(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
 #pragma unroll
                         for (int j = 0; j < kBK / 16; ++j)
                             if (j < n_mma)
-                                mma_f16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 2 * j,
+                                mma_f16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 16 * j,
                                         db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
                     }
                     mma_commit(smem_addr(&full_acc[buf]));
@@ -809,6 +809,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
         // ------------------------------------------------------------ staging
         asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
         const int pt = tid - kWsConsumerWarps * 32;  // rows pt + kWsStageRows * i of each tile
+        const uint32_t a_base = smem_addr(a_slots);
         // this thread's rows: pixel of the row (pointwise) or of the top-left
         // pixel of its 2x2 window, per tile (-1: past the end)
         int pix[kWsRowsPerThread];
@@ -869,20 +870,19 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                 run = false;
             }
             if (run) {
+                const uint32_t slot_base = a_base + static_cast<uint32_t>(slot * 2 * kTileA);
 #pragma unroll
                 for (int i = 0; i < kWsRowsPerThread; ++i) {
                     const int rl = pt + kWsStageRows * i;
                     if (rl >= kWsRows) break;
-                    uint8_t* a_tile = a_slots + (slot * 2 + (rl >> 7)) * kTileA;
+                    // the row's place in the interleaved layout of its 128-row half
+                    const uint32_t row_base = slot_base + static_cast<uint32_t>((rl >> 7) * kTileA + ((rl & (kBM - 1)) >> 3) * 1024 +
+                                                                             (rl & 7) * 16);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
-                        float du = 0.0f;
-                        if (ps[i][j] != -128) {
-                            du = unit_of(ps[i][j]);
-                            stage_group_h(a_tile, rl & (kBM - 1), j, pw[i][j]);
-                        } else {
-                            stage_zero(a_tile, rl & (kBM - 1), j);
-                        }
+                        // a padding (row, group) was loaded as zero words: zero codes, unit 0
+                        const float du = ps[i][j] != -128 ? unit_of(ps[i][j]) : 0.0f;
+                        stage_group_h_il(row_base, j, pw[i][j]);
                         din_s[(slot * 2 + j) * kWsRows + rl] = du;
                     }
                 }

@@ -137,6 +137,21 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
     return d;
 }
 
+// K-major operand without swizzle: 8-row x 16-byte core matrices of 128
+// contiguous bytes, the next along K at +128 B (leading byte offset), the next
+// 8 rows at +1024 B (stride byte offset), so element chunk c (8 fp16) of row r
+// sits at (r / 8) * 1024 + c * 128 + (r % 8) * 16 of a 128-row x 64-element
+// tile. A K16 step advances the start address by two core matrices (256 B).
+__device__ __forceinline__ uint64_t smem_desc_il(uint32_t addr)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);   // start address
+    d |= static_cast<uint64_t>(128u >> 4) << 16;          // leading byte offset: next core matrix along K
+    d |= static_cast<uint64_t>(1024u >> 4) << 32;         // stride byte offset: next 8 rows
+    d |= static_cast<uint64_t>(1u) << 46;                 // descriptor version (sm_100)
+    return d;                                             // layout 0: no swizzle
+}
+
 // kind::f16 instruction descriptor: bf16 x bf16 -> f32, both K-major, M = 128.
 __host__ __device__ constexpr uint32_t instr_desc(int n)
 {
@@ -328,6 +343,20 @@ __device__ __forceinline__ void stage_group_h(uint8_t* tile, int row, int group_
     for (int cl = 0; cl < 4; ++cl) {
         const int chunk = (group_in_stage << 2) + cl;
         *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = unpack_word_h(w[cl]);
+    }
+}
+
+// One group into the interleaved (no-swizzle) layout of smem_desc_il: the row's
+// chunk c at row_base + c * 128, row_base = (r / 8) * 1024 + (r % 8) * 16.
+__device__ __forceinline__ void stage_group_h_il(uint32_t row_base, int group_in_stage, uint4 words)
+{
+    const uint32_t w[4] = {words.x, words.y, words.z, words.w};
+#pragma unroll
+    for (int cl = 0; cl < 4; ++cl) {
+        const uint4 v = unpack_word_h(w[cl]);
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(row_base + ((group_in_stage * 4 + cl) << 7)),
+                     "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                     : "memory");
     }
 }
 
