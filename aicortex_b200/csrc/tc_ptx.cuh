@@ -334,18 +334,6 @@ __device__ __forceinline__ uint4 unpack_word_h(uint32_t w)
 
 __device__ __forceinline__ uint8_t* sw128_row(uint8_t* tile, int row) { return tile + (row >> 3) * 1024 + (row & 7) * 128; }
 
-// One 32-element group of a K-major SW128 row as fp16 (q, 16 q).
-__device__ __forceinline__ void stage_group_h(uint8_t* tile, int row, int group_in_stage, uint4 words)
-{
-    uint8_t* rowp = sw128_row(tile, row);
-    const uint32_t w[4] = {words.x, words.y, words.z, words.w};
-#pragma unroll
-    for (int cl = 0; cl < 4; ++cl) {
-        const int chunk = (group_in_stage << 2) + cl;
-        *reinterpret_cast<uint4*>(rowp + ((chunk ^ (row & 7)) << 4)) = unpack_word_h(w[cl]);
-    }
-}
-
 // One group into the interleaved (no-swizzle) layout of smem_desc_il: the row's
 // chunk c at row_base + c * 128, row_base = (r / 8) * 1024 + (r % 8) * 16.
 __device__ __forceinline__ void stage_group_h_il(uint32_t row_base, int group_in_stage, uint4 words)
