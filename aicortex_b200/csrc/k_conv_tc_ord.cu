@@ -679,42 +679,58 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 // ---- warp-specialised streaming kernel ----------------------------------------
 //
 // The streaming kernel's pipeline with its roles on separate warps and its
-// hand-offs on mbarriers instead of CTA-wide barriers. One CTA per SM, 640
-// threads, tiles of 256 rows x 64 channels:
-// * warps 16-18 (64 registers after setmaxnreg): staging. Thread pt stages
-//   rows pt, pt + 96 and pt + 192 (< 256) of the tile (both groups of a
-//   stage, loaded one stage ahead into registers) and records unit(s_in); each
-//   warp then arrives on staged[slot].
-// * warp 19 (the same warpgroup): one thread fetches the weight images
-//   and issues each staged stage's MMAs (two M = 128 halves x two groups x two
-//   K16 steps) into one of two TMEM buffers, committed to full_acc[buf]. On
-//   its own warp the MMA issue, which waits for the tensor pipe, overlaps the
-//   staging of the next stage.
-// * warps 0-15 (104 registers): consumers. Warp w owns the rows of TMEM lane
-//   quarter w & 3 in row half w >> 3 and the 32-channel half (w >> 2) & 1; it
-//   runs the reference's fmaf chain stage by stage from TMEM and, after a
-//   tile's last stage, the epilogue.
+// hand-offs on mbarriers instead of CTA-wide barriers. Tiles of ROWS = 128 or
+// 256 rows x 64 channels (WsCfg), with C = ROWS / 16 consumer warps:
+// * warps C..C+2 (after setmaxnreg, kStageRegs registers): staging. Thread pt
+//   stages rows pt, pt + 96 (and pt + 192) < ROWS of the tile (both groups of
+//   a stage, loaded one stage ahead into registers) and records unit(s_in);
+//   each warp then arrives on staged[slot].
+// * warp C+3 (the same warpgroup): one thread fetches the weight images and
+//   issues each staged stage's MMAs (ROWS / 128 M = 128 halves x two groups x
+//   two K16 steps) into one of two TMEM buffers, committed to full_acc[buf].
+//   On its own warp the MMA issue, which waits for the tensor pipe, overlaps
+//   the staging of the next stage.
+// * warps 0..C-1 (kConsumerRegs registers): consumers. Warp w owns the rows of
+//   TMEM lane quarter w & 3 in row half w >> 3 and the 32-channel half
+//   (w >> 2) & 1; it runs the reference's fmaf chain stage by stage from TMEM
+//   and, after a tile's last stage, the epilogue.
 // The weight images of all stages (at most kResidentStages) stay in shared
 // memory, fetched once per CTA. Stage slots (A tile halves, unit(s_in)) rotate
-// over kWsSlots; a slot is free again once all 16 consumer warps have run the
+// over kWsSlots; a slot is free again once all consumer warps have run the
 // chain of the stage it held (empty[slot]), and a TMEM buffer once the chain of
 // the stage two before has run (the same barrier). The RMSNorm's per-32-channel sums go
 // to the cluster peers through distributed shared memory, after which each
 // consumer warp arrives on every peer's part_full[tile & 1] (release/acquire
 // at cluster scope): no cluster-wide barrier per tile, so the producers run on.
 // TMEM: column (half h, buffer b, group j, channel c) = 256 h + 128 b + 64 j + c.
-constexpr int kWsConsumerWarps = 16;
 constexpr int kWsStageWarps = 3;
-constexpr int kWsThreads = (kWsConsumerWarps + kWsStageWarps + 1) * 32;  // 640
-constexpr int kWsRows = 2 * kBM;                                           // 256 rows per tile
-constexpr int kWsStageRows = kWsStageWarps * 32;                           // 96 staging threads
-constexpr int kWsRowsPerThread = (kWsRows + kWsStageRows - 1) / kWsStageRows;  // 3
+constexpr int kWsStageRows = kWsStageWarps * 32;  // 96 staging threads
+// Tile shapes: 128 rows (8 consumer warps, 384 threads, two CTAs per SM, each
+// with 256 TMEM columns) or 256 rows (16 consumer warps, 640 threads, one CTA
+// per SM with all 512 columns). The block launches with kLaunchRegs x kThreads
+// registers, exactly the consumers' kConsumerRegs plus the staging/MMA
+// warpgroup's kStageRegs (a setmaxnreg.inc that cannot be granted never returns).
+template <int ROWS>
+struct WsCfg {
+    static constexpr int kHalves = ROWS / kBM;
+    static constexpr int kConsumerWarps = 8 * kHalves;
+    static constexpr int kThreads = (kConsumerWarps + kWsStageWarps + 1) * 32;
+    static constexpr int kTmemCols = 256 * kHalves;
+    static constexpr int kRowsPerThread = (ROWS + kWsStageRows - 1) / kWsStageRows;
+    static constexpr int kLaunchRegs = ROWS == kBM ? 80 : 96;
+    static constexpr int kConsumerRegs = ROWS == kBM ? 96 : 104;
+    static constexpr int kStageRegs = ROWS == kBM ? 48 : 64;
+    static_assert(kConsumerWarps * 32 * kConsumerRegs + 128 * kStageRegs == kThreads * kLaunchRegs, "register split");
+};
 constexpr int kWsSlots = 3;
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
 
-template <int KS, int CS, bool ACT, bool G1>
-__global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
+template <int KS, int CS, bool ACT, bool G1, int ROWS>
+__global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(OrdParams p)
 {
+    using Cfg = WsCfg<ROWS>;
+    constexpr int kWsConsumerWarps = Cfg::kConsumerWarps, kWsThreads = Cfg::kThreads, kWsRows = ROWS,
+                  kWsRowsPerThread = Cfg::kRowsPerThread, kWsHalves = Cfg::kHalves;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
@@ -722,7 +738,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     const bool live = n_cta > 0;
     const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
     uint8_t* a_slots = base;                                                   // [slot][half][kTileA]
-    uint8_t* b_codes = a_slots + kWsSlots * 2 * kTileA;                        // [stage][n_max][128 B]
+    uint8_t* b_codes = a_slots + kWsSlots * kWsHalves * kTileA;                        // [stage][n_max][128 B]
     float* b_units = reinterpret_cast<float*>(b_codes + S * p.n_max * 128);   // [stage][2][n_max]
     float* din_s = b_units + S * 2 * p.n_max;                                 // [slot][2 groups][kWsRows]
     float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [kNCta]
@@ -754,7 +770,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (live && warp == 0) tmem_alloc(smem_addr(tmem_slot), 512);
+    if (live && warp == 0) tmem_alloc(smem_addr(tmem_slot), Cfg::kTmemCols);
     tc_fence_before();
     __syncthreads();
     if (CS > 1) cluster_sync_all();  // every peer's barriers and `part` are initialised before any remote access
@@ -769,7 +785,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
 
     if (warp == kWsConsumerWarps + kWsStageWarps) {
         // ------------------------------------------------------------ MMA issuer
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");  // with the staging warps: one warpgroup
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::kStageRegs));  // with the staging warps: one warpgroup
         // One thread fetches every
         // stage's weights once, then issues each staged stage's MMAs into the
         // TMEM buffer the consumers freed.
@@ -798,8 +814,8 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                     const uint64_t db = smem_desc(smem_addr(b_codes + sp * p.n_max * 128));
                     const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        const uint64_t da = smem_desc_il(smem_addr(a_slots + (slot * 2 + hh) * kTileA));
+                    for (int hh = 0; hh < kWsHalves; ++hh) {
+                        const uint64_t da = smem_desc_il(smem_addr(a_slots + (slot * kWsHalves + hh) * kTileA));
 #pragma unroll
                         for (int j = 0; j < kBK / 16; ++j)
                             if (j < n_mma)
@@ -819,7 +835,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
         }
     } else if (warp >= kWsConsumerWarps) {
         // ------------------------------------------------------------ staging
-        asm volatile("setmaxnreg.dec.sync.aligned.u32 64;");
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Cfg::kStageRegs));
         const int pt = tid - kWsConsumerWarps * 32;  // rows pt + kWsStageRows * i of each tile
         const uint32_t a_base = smem_addr(a_slots);
         // this thread's rows: pixel of the row (pointwise) or of the top-left
@@ -882,7 +898,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                 run = false;
             }
             if (run) {
-                const uint32_t slot_base = a_base + static_cast<uint32_t>(slot * 2 * kTileA);
+                const uint32_t slot_base = a_base + static_cast<uint32_t>(slot * kWsHalves * kTileA);
 #pragma unroll
                 for (int i = 0; i < kWsRowsPerThread; ++i) {
                     const int rl = pt + kWsStageRows * i;
@@ -920,7 +936,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
         }
     } else {
         // ------------------------------------------------------------ consumers
-        asm volatile("setmaxnreg.inc.sync.aligned.u32 104;");
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::kConsumerRegs));
         const int h = warp >> 3, q = warp & 3, hw = (warp >> 2) & 1;
         const int erow = q * 32 + lane;    // TMEM lane = row within the half
         const int trow = h * kBM + erow;   // row within the 256-row tile
@@ -1024,7 +1040,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
                     *abort_flag = 1;
                 }
             } else {
-                asm volatile("bar.sync 2, 512;" ::: "memory");  // the 16 consumer warps' sums are in `part`
+                asm volatile("bar.sync 2, %0;" ::"n"(kWsConsumerWarps * 32) : "memory");  // every consumer warp's sums are in `part`
             }
             if (emit && got) {
                 // the reference's cross-warp butterfly over the chunk's 8 group sums (kernels.h:271-276)
@@ -1071,7 +1087,7 @@ __global__ void __maxnreg__(96) conv_gemm_tc_ws_kernel(OrdParams p)
     if (CS > 1) cluster_sync_all();
     if (live && warp == 0) {
         tc_fence_after();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc(tmem, Cfg::kTmemCols);
     }
 }
 
@@ -1153,40 +1169,41 @@ cudaError_t launch_ord_cs(const OrdParams& p, size_t smem, cudaStream_t stream)
     return launch_ord<KS, 4>(q, smem, chunks, stream);
 }
 
-template <int KS, int CS>
+template <int KS, int CS, int ROWS>
 cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
 {
-    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false> : conv_gemm_tc_ws_kernel<KS, CS, false, false>;
+    using Cfg = WsCfg<ROWS>;
+    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false, ROWS> : conv_gemm_tc_ws_kernel<KS, CS, false, false, ROWS>;
     if constexpr (KS == 2) {
         if (p.in_c == 32)  // one group per tap
-            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true> : conv_gemm_tc_ws_kernel<KS, CS, false, true>;
+            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true, ROWS> : conv_gemm_tc_ws_kernel<KS, CS, false, true, ROWS>;
     }
-    // The role split (setmaxnreg: 512 consumer threads x 104 + the staging and
-    // MMA warpgroup's 128 threads x 64 registers) draws on the block's launch
-    // allocation of 640 x 96; with any other count the increase could never
-    // be granted.
+    // The role split (setmaxnreg) draws on the block's launch allocation of
+    // kLaunchRegs x kThreads; with any other compiled count the increase could
+    // never be granted.
     cudaFuncAttributes fa;
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
-    if (fa.numRegs != 96) return cudaErrorNotSupported;
+    if (fa.numRegs != Cfg::kLaunchRegs) return cudaErrorNotSupported;
     if (p.stages > kResidentStages) return cudaErrorNotSupported;  // the weights must stay resident
     if (p.rows * KS * KS > 0x7FFFFFFFll) return cudaErrorNotSupported;  // input pixel indices are 32-bit
-    const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * 2 * kTileA + static_cast<size_t>(p.stages) * p.n_max * kImgRow +
-                        (static_cast<size_t>(kWsSlots) * 2 * kWsRows + kNCta + 16 * kWsRows) * sizeof(float) +
+    const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * Cfg::kHalves * kTileA +
+                        static_cast<size_t>(p.stages) * p.n_max * kImgRow +
+                        (static_cast<size_t>(kWsSlots) * 2 * ROWS + kNCta + 16 * ROWS) * sizeof(float) +
                         (2 * kWsSlots + 6) * 8 + 16;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
-    // One CTA per SM (its 512 TMEM columns and ~160 KB of shared memory); runs of
-    // tiles sized for about four CTAs per SM over the launch.
-    const int64_t n_tiles = (p.rows + kWsRows - 1) / kWsRows;
+    // One or two CTAs per SM (TMEM columns, shared memory); runs of tiles sized
+    // for about four CTA runs per SM over the launch.
+    const int64_t n_tiles = (p.rows + ROWS - 1) / ROWS;
     int64_t t = n_tiles * chunks * CS / (148 * 4);
     OrdParams q = p;
     q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 16 ? 16 : t);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((n_tiles + q.tiles_per_cta - 1) / q.tiles_per_cta), chunks * CS, 1);
-    cfg.blockDim = dim3(kWsThreads, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -1207,9 +1224,15 @@ cudaError_t launch_ws_cs(const OrdParams& p, cudaStream_t stream)
     const int w = p.out_c < kNormChunk ? p.out_c : kNormChunk;
     const int cs = w <= kNCta ? 1 : w <= 2 * kNCta ? 2 : 4;
     const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
-    if (cs == 1) return launch_ws<KS, 1>(p, chunks, stream);
-    if (cs == 2) return launch_ws<KS, 2>(p, chunks, stream);
-    return launch_ws<KS, 4>(p, chunks, stream);
+    // 128-row tiles, two CTAs per SM, except where a 2x2 conv folds taps of
+    // several groups: the fold's second accumulator set does not fit the
+    // 96 consumer registers of that shape (measured 10 % slower), so 256 rows
+    if (cs > 2) return cudaErrorNotSupported;  // clusters of 4 take the two-role kernel
+    if constexpr (KS == 2) {
+        if (p.in_c > 32)
+            return cs == 1 ? launch_ws<KS, 1, 2 * kBM>(p, chunks, stream) : launch_ws<KS, 2, 2 * kBM>(p, chunks, stream);
+    }
+    return cs == 1 ? launch_ws<KS, 1, kBM>(p, chunks, stream) : launch_ws<KS, 2, kBM>(p, chunks, stream);
 }
 
 }  // namespace
