@@ -721,6 +721,11 @@ struct WsCfg {
     static constexpr int kConsumerRegs = ROWS == kBM ? 96 : 104;
     static constexpr int kStageRegs = ROWS == kBM ? 48 : 64;
     static_assert(kConsumerWarps * 32 * kConsumerRegs + 128 * kStageRegs == kThreads * kLaunchRegs, "register split");
+    // the register file admits at most this many CTAs per SM; their TMEM
+    // allocations must fit the SM's 512 columns, or an alloc would wait for a
+    // CTA that may itself wait on a cluster peer
+    static constexpr int kMaxCtasPerSm = 65536 / (kThreads * kLaunchRegs);
+    static_assert(kMaxCtasPerSm * kTmemCols <= 512, "TMEM columns per SM");
 };
 constexpr int kWsSlots = 3;
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
