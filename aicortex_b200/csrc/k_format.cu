@@ -161,6 +161,47 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
     if (groups == 1) *reinterpret_cast<uint32_t*>(out_s + pix) = packed_s;
 }
 
+// stem_pack4_kernel for one 32-channel group and NP <= 8 present planes known
+// at compile time: each plane's four pixels are loaded once, before any
+// arithmetic, and kept in registers for both the absmax and the codes.
+template <int NP>
+__global__ void __launch_bounds__(kThreads) stem_pack4_np_kernel(const __half* __restrict__ planes, int64_t quads, int hw,
+                                                               uint32_t* __restrict__ out, int8_t* __restrict__ out_s)
+{
+    const int64_t qd = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+    if (qd >= quads) return;
+    const int64_t pix = qd * 4;
+    const int64_t frame = pix / hw;
+    const int64_t sp = pix - frame * hw;
+    const __half* src = planes + frame * NP * hw + sp;
+    float x[NP][4];
+#pragma unroll
+    for (int c = 0; c < NP; ++c) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(src + static_cast<int64_t>(c) * hw));
+        const __half2 h01 = *reinterpret_cast<const __half2*>(&v.x), h23 = *reinterpret_cast<const __half2*>(&v.y);
+        x[c][0] = __low2float(h01);
+        x[c][1] = __high2float(h01);
+        x[c][2] = __low2float(h23);
+        x[c][3] = __high2float(h23);
+    }
+    uint4* ov = reinterpret_cast<uint4*>(out) + pix;
+    uint32_t packed_s = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float amax = 0.0f;  // fewer than 32 planes: the padding channels are zeros (as stem_pack_kernel)
+#pragma unroll
+        for (int c = 0; c < NP; ++c) amax = fmaxf(amax, fabsf(x[c][k]));
+        const float scale = amax < kEps ? 1.0f : amax;
+        const float inv = kQMax * rcp_rn_pos(scale);
+        uint32_t w = 0;
+#pragma unroll
+        for (int c = 0; c < NP; ++c) w |= code_rn(x[c][k], inv) << (4 * c);
+        ov[k] = make_uint4(w, 0u, 0u, 0u);
+        packed_s |= static_cast<uint32_t>(static_cast<uint8_t>(exponent_of(scale))) << (8 * k);
+    }
+    *reinterpret_cast<uint32_t*>(out_s + pix) = packed_s;
+}
+
 // Residual add when a position has exactly S = C/32 groups (S a power of two):
 // lane gl of a segment of S lanes owns group gl of two positions 32/S apart,
 // and all four of its loads are issued before any arithmetic (twice the bytes
@@ -451,6 +492,24 @@ cudaError_t launch_stem_pack(const __half* planes, int64_t frames, int planes_pr
     const int64_t pixels = frames * dim * dim;
     if (pixels == 0) return cudaSuccess;
     const int hw = dim * dim;
+    if (hw % 4 == 0 && reinterpret_cast<uintptr_t>(planes) % 8 == 0 && reinterpret_cast<uintptr_t>(out_s) % 4 == 0 &&
+        channels == 32 && planes_present >= 1 && planes_present <= 8) {
+        const int64_t quads = pixels / 4;
+        const unsigned grid = grid_for(quads);
+#define AIC_STEM_NP(NP) stem_pack4_np_kernel<NP><<<grid, kThreads, 0, stream>>>(planes, quads, hw, out, out_s)
+        switch (planes_present) {
+            case 1: AIC_STEM_NP(1); break;
+            case 2: AIC_STEM_NP(2); break;
+            case 3: AIC_STEM_NP(3); break;
+            case 4: AIC_STEM_NP(4); break;
+            case 5: AIC_STEM_NP(5); break;
+            case 6: AIC_STEM_NP(6); break;
+            case 7: AIC_STEM_NP(7); break;
+            default: AIC_STEM_NP(8); break;
+        }
+#undef AIC_STEM_NP
+        return cudaGetLastError();
+    }
     if (hw % 4 == 0 && reinterpret_cast<uintptr_t>(planes) % 8 == 0 && reinterpret_cast<uintptr_t>(out_s) % 4 == 0) {
         const int64_t quads = pixels / 4;
         stem_pack4_kernel<<<grid_for(quads), kThreads, 0, stream>>>(planes, quads, hw, planes_present, channels, out, out_s);

@@ -100,7 +100,7 @@ def test_golden_stem(golden):
 @pytest.mark.parametrize("planes,dim,channels", [(1, 8, 32), (3, 16, 32), (5, 8, 32), (8, 4, 32), (9, 8, 32),
                                                  (3, 6, 32), (3, 5, 32), (32, 4, 32), (40, 4, 64), (3, 8, 64)])
 def test_stem_vs_oracle(planes, dim, channels):
-    """Every stem variant (8, 4 and 1 pixels per thread; one or several groups;
+    """Every stem variant (4 and 1 pixels per thread; one or several groups;
     partial and full groups) against the oracle, with all-zero, tiny and
     large-magnitude pixels mixed in."""
     rng = np.random.default_rng(1200 + planes * 7 + dim)
@@ -432,6 +432,10 @@ def test_cortex_small_vs_oracle():
     (160, 96, 2, 2, 16, 8, 1),
     (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps
     (32, 64, 2, 2, 32, 16, 1),      # one group per tap
+    (128, 64, 1, 1, 12, 12, 0),     # warp-specialised, 128-row tiles: 288 rows, a partial tile
+    (256, 128, 1, 1, 10, 10, 1),    # warp-specialised, CTA pairs, 200 rows, SiLU
+    (64, 128, 2, 2, 16, 8, 0),      # warp-specialised, 256-row tiles (tap fold): one partial tile
+    (32, 128, 2, 2, 16, 8, 1),      # warp-specialised, one group per tap, CTA pairs
 ])
 def test_tensor_core_conv_vs_reference_order(geo):
     """tcgen05 convs vs the CUDA-core kernel with the reference's structure:
