@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kThreads) residual_pos2_kernel(const uint32_t*
         const float2 s_in = dup2(skipped ? 0.0f : unit_of(sa[k]) * main_mult);
         const uint32_t aw[4] = {a[k].x, a[k].y, a[k].z, a[k].w}, bw[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
         float2 r[16];
-        float amax = 0.0f, amaxn = 0.0f;  // the reference's absmax, and one that keeps a NaN
+        float amaxn = 0.0f;  // absmax that keeps a NaN; equal to the reference's when finite
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             // byte j of lo / hi: code 2j / 2j + 1 of the word as n ^ 8, placed in
@@ -258,14 +258,20 @@ __global__ void __launch_bounds__(kThreads) residual_pos2_kernel(const uint32_t*
                                        dup2(-8388616.0f));
                 const float2 v = fma2(qa, s_in, mul2(qb, s_res));
                 r[4 * q + j] = v;
-                amax = fmaxf(amax, fmaxf(fabsf(v.x), fabsf(v.y)));
                 amaxn = amax_nan(amax_nan(amaxn, v.x), v.y);
             }
         }
 #pragma unroll
-        for (int o = S >> 1; o > 0; o >>= 1) {
-            amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
-            amaxn = max_nan(amaxn, __shfl_xor_sync(0xFFFFFFFFu, amaxn, o));
+        for (int o = S >> 1; o > 0; o >>= 1) amaxn = max_nan(amaxn, __shfl_xor_sync(0xFFFFFFFFu, amaxn, o));
+        // the reference's absmax (fmaxf from 0, a NaN skipped) differs only where
+        // a NaN or an infinity is present: recomputed then, warp-wide
+        float amax = amaxn;
+        if (__any_sync(0xFFFFFFFFu, !is_finite_amax(amaxn))) {
+            amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fmaxf(fabsf(r[i].x), fabsf(r[i].y)));
+#pragma unroll
+            for (int o = S >> 1; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
         }
         if (!live[k]) continue;
         const float scale = amax < kEps ? 1.0f : amax;

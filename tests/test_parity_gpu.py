@@ -142,6 +142,35 @@ def test_golden_residual(golden, name):
     assert_f_equal(w, h(s), g["out_w"], g["out_s"], name)
 
 
+@pytest.mark.parametrize("ch,pos,mult,skipped,extreme", [
+    (32, 1000, 1.0, False, False),   # one group per position
+    (64, 777, 1.0, False, True),     # two groups; saturated exponents: infinities
+    (128, 300, 4.0, False, True),    # main * 4 overflows the unit: infinities and NaN (0 * inf)
+    (256, 99, 1.0, True, False),     # a skipped block: the residual alone
+    (96, 123, 1.0, False, True),     # three groups: the generic kernel
+    (64, 513, 4.0, False, True),
+])
+def test_residual_vs_oracle(ch, pos, mult, skipped, extreme):
+    """Residual add against the oracle on random codes, including positions
+    whose sums are infinite or NaN, where the reference's absmax (fmaxf from 0,
+    NaN skipped) decides the exponent and the codes saturate."""
+    import oracle as O
+    rng = np.random.default_rng(ch * 1000 + pos)
+    G = ch // 32
+    mw = rng.integers(0, 2**32, size=(pos, ch // 8), dtype=np.uint64).astype(np.uint32)
+    rw = rng.integers(0, 2**32, size=(pos, ch // 8), dtype=np.uint64).astype(np.uint32)
+    ms = rng.integers(-12, 7, size=(pos, G)).astype(np.int8)
+    rs = rng.integers(-12, 7, size=(pos, G)).astype(np.int8)
+    if extreme:
+        hot = rng.random(pos) < 0.2
+        ms[hot] = 120
+        rs[hot] = 120
+        mw[hot & (rng.random(pos) < 0.5)] = 0  # zero codes: 0 * inf where the main unit overflows
+    w, s = A.residual_add(t(mw), t(ms), t(rw), t(rs), pos, ch, main_mult=mult, skipped=skipped)
+    wo, so = O.residual(mw, ms, rw, rs, pos, ch, mult, skipped)
+    assert_f_equal(w, h(s), wo, so, f"residual C={ch}")
+
+
 def test_golden_gap(golden):
     g = golden("gap")
     out, qw, qs = A.gap(t(g["x_w"]), t(g["x_s"]), 1, 64, 256)
