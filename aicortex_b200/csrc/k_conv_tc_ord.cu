@@ -1332,10 +1332,9 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
         return launch_cae_pw(p, stream);
     // measured: the warp-specialised kernel wins up to four stages per tile and
-    // norm clusters of up to two CTAs (8% on such layers of the cortex); with
-    // longer K its four staging warps fall behind, and with clusters of four the
-    // per-tile exchange of the sums of squares idles its single CTA per SM,
-    // where the two-role kernel's second CTA keeps the SM busy
+    // norm clusters of up to two CTAs (two 128-row CTAs per SM: 15-19 % on the
+    // block-0 layers of the cortex); on clusters of four it is equal or slower,
+    // and longer K needs more resident weights than two CTAs' shared memory holds
     const int w_chunk = p.out_c < kNormChunk ? p.out_c : kNormChunk;
     if (p.stages <= kWsMaxStages && w_chunk <= 2 * kNCta) {
         const cudaError_t e = ksize == 1 ? launch_ws_cs<1>(p, stream) : launch_ws_cs<2>(p, stream);
