@@ -8,8 +8,8 @@ bit-exactly. Activations in the packed int4 format are compared as codes plus
 exponents; a code may flip by one only where the fp32 value sits on a rounding
 boundary, which the fast-math intrinsics (GPU) and libm (oracle) resolve
 differently, so flips are bounded by a rate. fp32 outputs are compared with
-max-abs error <= 1e-3 relative to the tensor's max magnitude (the tolerance
-of the task), and tighter where the computation is order-identical.
+max-abs error <= 1e-3 relative to the tensor's max magnitude (the float
+tolerance of this path), and tighter where the computation is order-identical.
 """
 import ctypes as C
 import sys
