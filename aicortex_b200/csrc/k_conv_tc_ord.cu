@@ -9,9 +9,10 @@
 //     acc[k & 3] = fmaf(unit(s_in[k][g]), unit(s_w[k][g]) * dot[k][g], acc[k & 3])
 // where dot is the exact integer dot product of the two groups' codes, and
 // folds the partial sums as ((acc0 + acc1) + acc2) + acc3. The integer dots
-// are what a tensor core computes exactly: with the codes themselves (-8..7,
-// exact in bf16) as operands, a K=32 kind::f16 MMA sums 32 integer products of
-// magnitude <= 64 in fp32, which is exact. So each stage of two groups issues
+// are what a tensor core computes exactly: with the codes themselves as fp16
+// operands (q and 16 q against w and w / 16, see unpack_word_h), a K=32
+// kind::f16 MMA sums 32 integer products of magnitude <= 64 in fp32, which is
+// exact. So each stage of two groups issues
 // two MMAs per group into a group-private TMEM accumulator, and the CUDA cores
 // run the reference's fmaf chain over the groups, in group order, from those
 // exact dots. Only the chain runs in fp32, exactly as the reference does.
@@ -26,9 +27,10 @@
 //
 // Pipeline (256 threads, a run of consecutive row tiles per CTA): the CTA
 // walks one sequence of stages across its tiles. For stage s every thread stages one
-// (row, group) of the A tile from the packed activations (im2col on the fly
-// for k=2) and records unit(s_in); thread 0 fetches the stage's B image
-// (codes as bf16 in the SW128 layout, followed by unit(s_w) of both groups)
+// (row, group) of the A tile (interleaved K-major layout) from the packed
+// activations (im2col on the fly for k=2) and records unit(s_in); thread 0
+// fetches the stage's B image (fp16 codes in the SW128 layout, followed by
+// unit(s_w) of both groups)
 // with one cp.async.bulk and issues the MMAs for stage s; meanwhile all
 // threads run the chain for stage s-1 from TMEM (tcgen05.ld), and after a
 // tile's last stage its epilogue, which so overlaps the next tile's first
@@ -51,7 +53,7 @@ using namespace tc;
 
 constexpr int kThreads = 256;
 constexpr int kBK = 64;                   // two 32-element groups per stage
-constexpr int kTileA = kBM * kBK * 2;     // 16 KB of bf16
+constexpr int kTileA = kBM * kBK * 2;     // 16 KB of fp16
 constexpr int kNCta = 64;                 // output channels per CTA
 constexpr int kImgRow = kBK * 2 + 2 * 4;  // image bytes per channel per stage: 128 B codes + 2 units
 constexpr int kResidentStages = 8;        // up to this many stages per tile stay resident in shared memory
