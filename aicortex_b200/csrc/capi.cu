@@ -155,19 +155,25 @@ struct Profiler {
         sites.back().name = name;
         return sites.back();
     }
+    // Accumulates and recycles the oldest `count` pending event pairs of a site
+    // (waiting for them if the device has not reached them yet).
+    void settle(Site& s, size_t count)
+    {
+        count = std::min(count, s.pending.size());
+        for (size_t i = 0; i < count; ++i) {
+            auto& p = s.pending[i];
+            cuda_ok(cudaEventSynchronize(p.second), "profile sync");
+            float ms = 0.0f;
+            cuda_ok(cudaEventElapsedTime(&ms, p.first, p.second), "profile elapsed");
+            s.ms += ms;
+            pool.push_back(p.first);
+            pool.push_back(p.second);
+        }
+        s.pending.erase(s.pending.begin(), s.pending.begin() + static_cast<std::ptrdiff_t>(count));
+    }
     void collect()
     {
-        for (auto& s : sites) {
-            for (auto& p : s.pending) {
-                cuda_ok(cudaEventSynchronize(p.second), "profile sync");
-                float ms = 0.0f;
-                cuda_ok(cudaEventElapsedTime(&ms, p.first, p.second), "profile elapsed");
-                s.ms += ms;
-                pool.push_back(p.first);
-                pool.push_back(p.second);
-            }
-            s.pending.clear();
-        }
+        for (auto& s : sites) settle(s, s.pending.size());
     }
     void reset()
     {
@@ -191,6 +197,11 @@ void traced(Profiler* p, const std::string& name, cudaStream_t s, double flops, 
     cuda_ok(launch(), what);
     cuda_ok(cudaEventRecord(b, s), "profile record");
     site.pending.emplace_back(a, b);
+    // bounded event count on long runs: once a site holds kMaxPending pairs,
+    // the older half is settled (the host is then still half that many
+    // launches of the site ahead of the device)
+    constexpr size_t kMaxPending = 256;
+    if (site.pending.size() >= kMaxPending) p->settle(site, kMaxPending / 2);
     site.launches += 1;
     site.flops += flops;
     site.bytes += bytes;
@@ -1410,8 +1421,9 @@ AIC_API aic_status aic_mamba_layer_forward_noalloc(aic_mamba_layer l, const uint
             fail(AIC_ERR_INVALID, "aic_mamba_layer_forward_noalloc: batch * seq * 2 * d_model = " + std::to_string(need) +
                                       " floats exceeds the fixed scratch of " + std::to_string(kNoAllocScratchFloats) +
                                       " floats (4 MiB); use aic_mamba_layer_forward with a workspace");
-        if (need == 0) return;
-        m->forward(in, in_s, out, batch, seq, noalloc_scratch(), as_stream(stream));
+        // empty extents still go through forward()'s checks of the bound
+        // parameters, state and batch, so both entry points agree on them
+        m->forward(in, in_s, out, batch, seq, need ? noalloc_scratch() : nullptr, as_stream(stream));
     });
 }
 AIC_API aic_status aic_mamba_layer_destroy(aic_mamba_layer l)

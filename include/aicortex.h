@@ -264,7 +264,10 @@ AIC_API aic_status aic_mamba_layer_forward(aic_mamba_layer l, const uint32_t* in
  * held from load until process exit; batch * seq * 2 * d_model must not
  * exceed 1,048,576 floats (AIC_ERR_INVALID otherwise). The first call on a
  * device looks up that array's device address (cudaGetSymbolAddress); make
- * that first call before capturing a stream. All calls share the one array:
+ * that first call before capturing a stream. The address is then kept per
+ * device ordinal until the process exits, which assumes that the device's
+ * primary context is not reset (cudaDeviceReset) while the library is
+ * loaded. All calls share the one array:
  * calls that can overlap on the GPU (different streams, no ordering) race.
  * The scratch is fully overwritten before it is read, so nothing needs
  * clearing between calls. Parameters and state are bound as usual; the

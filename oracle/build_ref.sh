@@ -13,8 +13,9 @@
 # Windows SDK header that kernels.h includes (kernels.h:14); it declares only
 # the BYTE and DWORD types named by ca.cu's capture entry point.
 set -euo pipefail
-REF=${AICORTEX_REFERENCE:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+# the reference checkout: AICORTEX_REFERENCE, default "reference" beside this repository
+REF=${AICORTEX_REFERENCE:-$HERE/../../reference}
 OUT="$HERE/_ref"
 if [ ! -f "$REF/kernels.h" ]; then
   echo "reference sources not found at $REF; skipping oracle/_ref build" >&2
