@@ -5,9 +5,9 @@ include/aicortex.h); this package binds it with ctypes and mirrors the
 reference's layer classes. Importing the package fails if the library is not
 built: there is no fallback path.
 """
-from ._lib import AIC_CONV_FAST, AIC_CONV_ORDERED, AIC_CONV_SIMT, AicError, lib  # noqa: F401  (fails loudly when the .so is missing)
+from ._lib import AIC_CONV_FAST, AIC_CONV_ORDERED, AIC_CONV_SIMT, AIC_MAMBA_EXACT, AIC_MAMBA_TENSOR, AicError, lib  # noqa: F401  (fails loudly when the .so is missing)
 from .layers import (ConvBlock, ConvLayer, Cortex, Critic, MambaBlock, MambaLayer, audio_frontend, empty_f,  # noqa: F401
                      gap, gap_f16, pack_f32, residual_add, screen_frontend, set_actions, stem_pack)
 
-__all__ = ["AIC_CONV_FAST", "AIC_CONV_ORDERED", "AIC_CONV_SIMT", "AicError", "ConvBlock", "ConvLayer", "Cortex", "Critic", "MambaBlock", "MambaLayer", "audio_frontend", "empty_f", "gap",
+__all__ = ["AIC_CONV_FAST", "AIC_CONV_ORDERED", "AIC_CONV_SIMT", "AIC_MAMBA_EXACT", "AIC_MAMBA_TENSOR", "AicError", "ConvBlock", "ConvLayer", "Cortex", "Critic", "MambaBlock", "MambaLayer", "audio_frontend", "empty_f", "gap",
            "gap_f16", "pack_f32", "residual_add", "screen_frontend", "set_actions", "stem_pack"]

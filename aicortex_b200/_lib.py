@@ -20,6 +20,8 @@ AIC_MAX_BLOCKS = 16
 AIC_CONV_ORDERED = 0
 AIC_CONV_FAST = 1
 AIC_CONV_SIMT = 2
+AIC_MAMBA_TENSOR = 0
+AIC_MAMBA_EXACT = 1
 
 
 class AicError(RuntimeError):
@@ -112,6 +114,9 @@ _SIGS = {
     "aic_mamba_layer_workspace_bytes": [P, I64, SZ],
     "aic_mamba_layer_forward": [P, P, P, P, I32, I32, P, P],
     "aic_mamba_layer_outproj": [P, P, P, I64, P],
+    "aic_mamba_layer_set_mode": [P, I32],
+    "aic_mamba_layer_scan": [P, P, P, P, I32, I32, I32, P],
+    "aic_mamba_layer_outproj_split": [P, P, P, I64, P],
     "aic_mamba_layer_forward_noalloc": [P, P, P, P, I32, I32, P],
     "aic_mamba_layer_destroy": [P],
     "aic_mamba_block_create": [C.POINTER(MambaBlockDesc), PP],
@@ -126,6 +131,7 @@ _SIGS = {
     "aic_mamba_block_workspace_bytes": [P, I64, SZ],
     "aic_mamba_block_load_dir_sync": [P, C.c_char_p, P],
     "aic_mamba_block_forward": [P, P, P, P, I32, I32, I32, I32, I32, P, P],
+    "aic_mamba_block_set_mode": [P, I32],
     "aic_mamba_block_destroy": [P],
     "aic_critic_create": [C.POINTER(CriticDesc), PP],
     "aic_critic_param_bytes": [P, SZ],
@@ -157,6 +163,7 @@ _SIGS = {
     "aic_cortex_forward_host": [P, P, I32, I32, P, P, P, P],
     "aic_cortex_set_exact": [P, I32],
     "aic_cortex_set_conv_mode": [P, I32],
+    "aic_cortex_set_mamba_mode": [P, I32],
     "aic_cortex_last_launches": [P, PI64],
     "aic_cortex_profile_enable": [P, I32],
     "aic_cortex_profile_count": [P, C.POINTER(C.c_int)],

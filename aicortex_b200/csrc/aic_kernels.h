@@ -87,13 +87,26 @@ cudaError_t launch_ssm_prepare(const uint32_t* blob, const int8_t* blob_s, int D
 size_t ssm_consts_floats(int D, int d_state);
 // traces: nullptr, or trace_A | trace_B | trace_Delta [3][B][E][d_state/32]
 // complex, advanced with the state (training-mode forward, kernels.h:1158-1170).
+// split: y as two bf16 planes hi | lo [B*T][E] (the tensor-core out-projection's
+// operands) instead of fp32 [B*T][E]; both take B*T*E*4 bytes.
 cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
-                            const float* consts, int D, int d_state, float2* h, float2* traces, float* y, int B, int T,
-                            cudaStream_t stream);
+                            const float* consts, int D, int d_state, float2* h, float2* traces, void* y, bool split,
+                            int B, int T, cudaStream_t stream);
 
 // A10: out-projection GEMM y[rows][E] x W_out -> RMSNorm(256-chunk) + bias + act -> fp32 [rows][out].
 cudaError_t launch_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s, const float* bias, int D,
                            int d_state, int out, int act, int64_t rows, float* o, cudaStream_t stream);
+
+// A10 on the tensor cores (k_outproj_tc.cu): the weight image holds W_out as
+// bf16 q * F(s) [out][E] (exact), y comes as the scan's split bf16 planes; two
+// MMAs per K step, fp32 accumulation, the same fused epilogue. Supported for
+// E % 64 == 0 and out a multiple of 32 that is <= 256 or a multiple of 256.
+bool outproj_tc_supported(int E, int out_c);
+size_t outproj_tc_wimg_bytes(int E, int out_c);
+cudaError_t launch_build_outproj_wimg(const uint32_t* blob, const int8_t* blob_s, int64_t off_w, int E, int out_c,
+                                      void* img, cudaStream_t stream);
+cudaError_t launch_outproj_tc(const void* y_planes, const void* wimg, const float* bias, int E, int out_c, int act,
+                              int64_t rows, float* out, int* err, cudaStream_t stream);
 
 // A13: critic recurrence over T for B sequences; x fp16 [B*T][in]. trace_w1
 // [B][in][units] and trace_l [B][units][in] complex: nullptr, or the

@@ -440,9 +440,11 @@ struct MambaLayer {
     int8_t* ws = nullptr;
     float* bias = nullptr;
     float* consts = nullptr;
+    void* wimg = nullptr;      // W_out as exact bf16 q * F(s) [out][E] for the tensor-core out-projection
     float2* h = nullptr;
     float2* traces = nullptr;  // trace_A | trace_B | trace_Delta [3][batch][E][P]; null: inference forward
     int batch_bound = -1;
+    int mode = AIC_MAMBA_TENSOR;
     bool bound = false;
     Profiler* prof = nullptr;
     std::string tag = "mamba";
@@ -468,8 +470,15 @@ struct MambaLayer {
         ws = c.take<int8_t>(groups);
         bias = c.take<float>(d.out_channels);
         consts = c.take<float>(ssm_consts_floats(d.d_model, d.d_state));
+        wimg = tc_ok() ? c.take<char>(outproj_tc_wimg_bytes(E, d.out_channels)) : nullptr;
         return c.bytes();
     }
+    bool tc_ok() const { return outproj_tc_supported(E, d.out_channels); }
+    // the out-projection runs on the tensor cores (split-bf16 operands) unless
+    // the reference-order CUDA-core kernel is selected or the shape has no
+    // tensor-core tiling
+    bool use_tc() const { return mode == AIC_MAMBA_TENSOR && tc_ok(); }
+    int64_t off_w() const { return static_cast<int64_t>(E) * (34 + 4LL * d.d_state); }
     size_t state_bytes(int batch) const { return static_cast<size_t>(batch) * E * P * sizeof(float2); }
     void check_bound() const
     {
@@ -482,6 +491,7 @@ struct MambaLayer {
         cuda_ok(launch_pack_f32(master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s), "pack blob");
         cuda_ok(cudaMemcpyAsync(bias, b, sizeof(float) * d.out_channels, cudaMemcpyDefault, s), "copy bias");
         cuda_ok(launch_ssm_prepare(w, ws, d.d_model, d.d_state, consts, s), "ssm prepare");
+        if (wimg) cuda_ok(launch_build_outproj_wimg(w, ws, off_w(), E, d.out_channels, wimg, s), "out-proj image");
     }
     void load_file(const char* path, cudaStream_t s)
     {
@@ -506,19 +516,41 @@ struct MambaLayer {
         require(seq >= 0, "negative sequence length");
         if (seq == 0 || batch == 0) return 0;
         require(in && in_s && out && wsp && aligned256(wsp), "null or misaligned tensor");
-        float* y = static_cast<float*>(wsp);
+        const bool tc = use_tc();
+        scan(in, in_s, wsp, tc, batch, seq, s);
+        const int64_t rows = static_cast<int64_t>(batch) * seq;
+        if (tc)
+            outproj_split(wsp, out, rows, s);
+        else
+            traced(prof, tag + ".outproj", s, 2.0 * rows * E * d.out_channels,
+                   4.0 * rows * E + f_bytes(static_cast<double>(E) * d.out_channels) + 4.0 * rows * d.out_channels,
+                   "outproj", [&] {
+                       return launch_outproj(static_cast<const float*>(wsp), w, ws, bias, d.d_model, d.d_state,
+                                             d.out_channels, d.activation, rows, out, s);
+                   });
+        return 2;
+    }
+    // The SSM scan alone: y as fp32 [rows][E], or (split) as the bf16 planes hi | lo.
+    void scan(const uint32_t* in, const int8_t* in_s, void* y, bool split, int batch, int seq, cudaStream_t s)
+    {
         const double rows = static_cast<double>(batch) * seq;
         // per (row, channel): 31 flops per state plus ~15 (kernels.h:1126-1176)
         traced(prof, tag + ".scan", s, rows * E * (31.0 * P + 15.0),
                f_bytes(rows * d.d_model) + 4.0 * rows * E + 2.0 * batch * E * P * 8.0 + E * P * 16.0, "ssm scan",
-               [&] { return launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, traces, y, batch, seq, s); });
-        traced(prof, tag + ".outproj", s, 2.0 * rows * E * d.out_channels,
-               4.0 * rows * E + f_bytes(static_cast<double>(E) * d.out_channels) + 4.0 * rows * d.out_channels, "outproj",
                [&] {
-                   return launch_outproj(y, w, ws, bias, d.d_model, d.d_state, d.out_channels, d.activation,
-                                         static_cast<int64_t>(batch) * seq, out, s);
+                   return launch_ssm_scan(in, in_s, w, ws, consts, d.d_model, d.d_state, h, traces, y, split, batch, seq,
+                                          s);
                });
-        return 2;
+    }
+    // The tensor-core out-projection of split-bf16 y planes.
+    void outproj_split(const void* y_planes, float* out, int64_t rows, cudaStream_t s)
+    {
+        // algorithmic work 2 * rows * E * out (the tensor pipe runs it twice: hi and lo)
+        traced(prof, tag + ".outproj", s, 2.0 * rows * E * d.out_channels,
+               4.0 * rows * E + 2.0 * E * d.out_channels + 4.0 * rows * d.out_channels, "tensor-core outproj", [&] {
+                   return launch_outproj_tc(y_planes, wimg, bias, E, d.out_channels, d.activation, rows, out,
+                                            device_error_word(), s);
+               });
     }
 };
 
@@ -1410,6 +1442,40 @@ AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, fl
                 "outproj");
     });
 }
+AIC_API aic_status aic_mamba_layer_set_mode(aic_mamba_layer l, int mode)
+{
+    return guarded([&] {
+        require(mode == AIC_MAMBA_TENSOR || mode == AIC_MAMBA_EXACT, "unknown mamba mode");
+        handle<MambaLayer>(l, "mamba layer")->mode = mode;
+    });
+}
+AIC_API aic_status aic_mamba_layer_scan(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s, void* y, int batch,
+                                        int seq, int y_split, void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        m->check_bound();
+        if (m->batch_bound < 0) fail(AIC_ERR_STATE, "mamba state not bound");
+        require(batch == m->batch_bound, "batch differs from the bound state's batch");
+        require(seq >= 0, "negative sequence length");
+        if (batch == 0 || seq == 0) return;
+        require(in && in_s && y && aligned256(y), "null or misaligned tensor");
+        m->scan(in, in_s, y, y_split != 0, batch, seq, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_layer_outproj_split(aic_mamba_layer l, const void* y_planes, float* out, int64_t rows,
+                                                 void* stream)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        m->check_bound();
+        if (!m->tc_ok())
+            fail(AIC_ERR_UNSUPPORTED, "out channels have no tensor-core tiling (multiple of 32, <= 256 or a multiple of 256)");
+        require(rows >= 0 && (rows == 0 || (y_planes && out)), "bad out-projection arguments");
+        require(rows == 0 || aligned256(y_planes), "y planes must be 256-byte aligned");
+        m->outproj_split(y_planes, out, rows, as_stream(stream));
+    });
+}
 AIC_API aic_status aic_mamba_layer_forward_noalloc(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s,
                                                    float* out, int batch, int seq, void* stream)
 {
@@ -1525,6 +1591,13 @@ AIC_API aic_status aic_mamba_block_forward(aic_mamba_block b, const uint32_t* in
     return guarded([&] {
         handle<MambaBlock>(b, "mamba block")
             ->forward(in, in_s, out, batch, seq, on_training != 0, add_seed, is_survived != 0, workspace, as_stream(stream));
+    });
+}
+AIC_API aic_status aic_mamba_block_set_mode(aic_mamba_block b, int mode)
+{
+    return guarded([&] {
+        require(mode == AIC_MAMBA_TENSOR || mode == AIC_MAMBA_EXACT, "unknown mamba mode");
+        for (auto& l : handle<MambaBlock>(b, "mamba block")->layers) l->mode = mode;
     });
 }
 AIC_API aic_status aic_mamba_block_destroy(aic_mamba_block b)
@@ -1756,9 +1829,19 @@ AIC_API aic_status aic_cortex_set_conv_mode(aic_cortex c, int mode)
             for (auto& l : b->layers) l->mode = mode;
     });
 }
+AIC_API aic_status aic_cortex_set_mamba_mode(aic_cortex c, int mode)
+{
+    return guarded([&] {
+        require(mode == AIC_MAMBA_TENSOR || mode == AIC_MAMBA_EXACT, "unknown mamba mode");
+        auto* x = handle<Cortex>(c, "cortex");
+        for (auto& u : x->units) u->mode = mode;
+        x->actor->mode = mode;
+    });
+}
 AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact)
 {
-    return aic_cortex_set_conv_mode(c, exact ? AIC_CONV_SIMT : AIC_CONV_ORDERED);
+    const aic_status st = aic_cortex_set_conv_mode(c, exact ? AIC_CONV_SIMT : AIC_CONV_ORDERED);
+    return st != AIC_OK ? st : aic_cortex_set_mamba_mode(c, exact ? AIC_MAMBA_EXACT : AIC_MAMBA_TENSOR);
 }
 AIC_API aic_status aic_cortex_profile_enable(aic_cortex c, int enable)
 {

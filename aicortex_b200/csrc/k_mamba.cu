@@ -4,10 +4,12 @@
 // Semantics follow AICortex kernels.h:1080-1259: channel ch of d_inner = 2*D
 // reads input channel ch & (D-1), uses MIMO row (ch & 31) of block ch >> 5,
 // and owns the P = d_state/32 states n = (ch & 31) + 32c of its row. The
-// reference advances one step per launch; here one thread keeps its channel's
-// states in registers and walks all T steps of a sequence, which is the same
-// recurrence because a layer's input at step t does not depend on that layer's
-// own state.
+// reference advances one step per launch; here a channel's states stay in
+// registers (of one thread, or of several lanes when the batch is small) for
+// all T steps of a sequence, which is the same recurrence because a layer's
+// input at step t does not depend on that layer's own state.
+#include <cuda_bf16.h>
+
 #include "aic_common.cuh"
 #include "aic_kernels.h"
 
@@ -49,49 +51,104 @@ __global__ void __launch_bounds__(kThreads) ssm_prepare_kernel(const uint32_t* _
     if (c == 0) consts2[ch] = make_float2(blob_value(blob, blob_s, ch), blob_value(blob, blob_s, L.offD + ch));
 }
 
+// Runs step(t, words, unit) for t = 0..T-1 over one channel's input group
+// (words at xv[t * Gx], exponent at xsv[t * Gx]) with the loads of step
+// t + PF issued when step t starts: a register ring of PF steps hides the
+// global-memory latency behind the serial recurrence.
+template <int PF, class Step>
+__device__ __forceinline__ void scan_steps(const uint4* __restrict__ xv, const int8_t* __restrict__ xsv, int Gx, int T,
+                                           Step& step)
+{
+    uint4 rw[PF];
+    int8_t rs[PF];
+#pragma unroll
+    for (int j = 0; j < PF; ++j) {
+        if (j < T) {
+            rw[j] = xv[static_cast<int64_t>(j) * Gx];
+            rs[j] = xsv[static_cast<int64_t>(j) * Gx];
+        }
+    }
+    for (int t0 = 0; t0 < T; t0 += PF) {
+#pragma unroll
+        for (int j = 0; j < PF; ++j) {
+            const int t = t0 + j;
+            if (t < T) {
+                const uint4 xw = rw[j];
+                const float xu = unit_of(rs[j]);
+                if (t + PF < T) {
+                    rw[j] = xv[static_cast<int64_t>(t + PF) * Gx];
+                    rs[j] = xsv[static_cast<int64_t>(t + PF) * Gx];
+                }
+                step(t, xw, xu);
+            }
+        }
+    }
+}
+
+// Input steps in flight per thread: threads with few states per step need a
+// deeper ring to cover the load latency.
+template <int S>
+__host__ __device__ constexpr int scan_prefetch() { return S >= 16 ? 2 : (S >= 8 ? 4 : 8); }
+
+// The batched, time-looped scan. Channel ch's P = S * L states are spread over
+// L consecutive lanes, S states each (L = 1: one thread per channel; L > 1
+// where batch x channels alone cannot fill the GPU). Every lane of a channel
+// recomputes the step's channel terms (x, Bx, dt) and advances its S states;
+// y = sum_c Re(h_c C_c) is folded in the reference's order c = 0, 1, ... by
+// passing the partial sum from lane to lane with shuffles, so every L gives
+// the same bits. The reciprocal is rcp_rn_pos, bit-identical to __frcp_rn for
+// the operand |1 - dt A / 2|^2 + eps >= eps.
 // TRACE: the training-mode forward also advances the eligibility traces
 // trace_A, trace_B, trace_Delta (kernels.h:1158-1170), held in registers like
 // the state; tr is [3][B][E][P] complex, the layout of h.
-template <int P, bool TRACE>
+// SPLIT: y is written as two bf16 planes [B*T][E], hi = bf16(y) then
+// lo = bf16(y - hi), the operands of the tensor-core out-projection;
+// otherwise as fp32 [B*T][E].
+template <int S, int L, bool TRACE, bool SPLIT>
 __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* __restrict__ x, const int8_t* __restrict__ x_s,
                                                               const uint32_t* __restrict__ blob, const int8_t* __restrict__ blob_s,
                                                               const float4* __restrict__ consts4, const float2* __restrict__ consts2,
                                                               int D, float2* __restrict__ h, float2* __restrict__ tr,
-                                                              float* __restrict__ y, int T)
+                                                              void* __restrict__ y_out, int T)
 {
+    static_assert(L >= 1 && L <= 32 && (L & (L - 1)) == 0, "lanes per channel");
+    constexpr int P = S * L;
     const int E = 2 * D;
-    const int ch = blockIdx.x * kScanThreads + threadIdx.x;
+    const int gt = blockIdx.x * kScanThreads + threadIdx.x;
+    const int ch = gt / L, j = gt & (L - 1);  // channel and this lane's index within it
     const int b = blockIdx.y;
     const int lane = ch & 31, in_ch = ch & (D - 1);
-    float4 k[P];
+    const int gbase = (threadIdx.x & 31) & ~(L - 1);
+    float4 k[S];
 #pragma unroll
-    for (int c = 0; c < P; ++c) k[c] = consts4[static_cast<int64_t>(ch) * P + c];
+    for (int i = 0; i < S; ++i) k[i] = consts4[static_cast<int64_t>(ch) * P + j * S + i];
     const float2 wdd = consts2[ch];
     const int64_t brow = E + static_cast<int64_t>(ch >> 5) * 1024 + lane * 32;
     const uint4 bw = reinterpret_cast<const uint4*>(blob)[brow >> 5];
     const float bu = unit_of(blob_s[brow >> 5]);
-    float2 st[P];
-    float2* hs = h + (static_cast<int64_t>(b) * E + ch) * P;
+    float2 st[S];
+    float2* hs = h + (static_cast<int64_t>(b) * E + ch) * P + j * S;
 #pragma unroll
-    for (int c = 0; c < P; ++c) st[c] = hs[c];
-    float2 ta[TRACE ? P : 1], tb[TRACE ? P : 1], td[TRACE ? P : 1];
-    float2* trs = TRACE ? tr + (static_cast<int64_t>(b) * E + ch) * P : nullptr;
+    for (int i = 0; i < S; ++i) st[i] = hs[i];
+    float2 ta[TRACE ? S : 1], tb[TRACE ? S : 1], td[TRACE ? S : 1];
+    float2* trs = TRACE ? tr + (static_cast<int64_t>(b) * E + ch) * P + j * S : nullptr;
     const int64_t tr_stride = static_cast<int64_t>(gridDim.y) * E * P;  // one trace of the whole batch
     if (TRACE) {
 #pragma unroll
-        for (int c = 0; c < P; ++c) {
-            ta[c] = trs[c];
-            tb[c] = trs[tr_stride + c];
-            td[c] = trs[2 * tr_stride + c];
+        for (int i = 0; i < S; ++i) {
+            ta[i] = trs[i];
+            tb[i] = trs[tr_stride + i];
+            td[i] = trs[2 * tr_stride + i];
         }
     }
     const int Gx = D >> 5, xg = in_ch >> 5, xword = (in_ch & 31) >> 3, xnib = in_ch & 7;
     const uint4* xv = reinterpret_cast<const uint4*>(x) + static_cast<int64_t>(b) * T * Gx + xg;
     const int8_t* xsv = x_s + static_cast<int64_t>(b) * T * Gx + xg;
-    float* yv = y + static_cast<int64_t>(b) * T * E + ch;
-    for (int t = 0; t < T; ++t) {
-        const uint4 xw = xv[static_cast<int64_t>(t) * Gx];
-        const float xu = unit_of(xsv[static_cast<int64_t>(t) * Gx]);
+    const int64_t yoff = static_cast<int64_t>(b) * T * E + ch;
+    float* yv = static_cast<float*>(y_out) + yoff;
+    __nv_bfloat16* yh = static_cast<__nv_bfloat16*>(y_out) + yoff;
+    const int64_t lo_plane = static_cast<int64_t>(gridDim.y) * T * E;
+    auto step = [&](int t, uint4 xw, float xu) {
         const int dot = dot8(xw.x, bw.x) + dot8(xw.y, bw.y) + dot8(xw.z, bw.z) + dot8(xw.w, bw.w);
         const uint32_t xsel = xword == 0 ? xw.x : (xword == 1 ? xw.y : (xword == 2 ? xw.z : xw.w));
         const float x_local = static_cast<float>(code_of(xsel, xnib)) * xu;
@@ -99,21 +156,21 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* 
         const float u = x_local * wdd.x;
         const float dt = u + __logf(1.0f + __expf(-fabsf(u)));
         const float dt_half = dt * 0.5f;
-        float ya[P];
+        float ya[S];
 #pragma unroll
-        for (int c = 0; c < P; ++c) {
-            const float are = k[c].x, aim = k[c].y;
+        for (int i = 0; i < S; ++i) {
+            const float are = k[i].x, aim = k[i].y;
             const float dim = -dt_half * aim;
             const float dre = fmaf(-dt_half, are, 1.0f);
-            const float inv_s = __frcp_rn(fmaf(dre, dre, fmaf(dim, dim, kEps)));
+            const float inv_s = rcp_rn_pos(fmaf(dre, dre, fmaf(dim, dim, kEps)));
             const float ire = dre * inv_s;
             const float iim = -dim * inv_s;
             const float nre = fmaf(dt_half, are, 1.0f);
             const float abr = fmaf(nre, ire, dim * iim);
             const float abi = fmaf(nre, iim, -dim * ire);
             const float dtbx = dt * bx;
-            const float hr = st[c].x, hi = st[c].y;
-            st[c] = make_float2(fmaf(abr, hr, fmaf(-abi, hi, dtbx * ire)), fmaf(abr, hi, fmaf(abi, hr, dtbx * iim)));
+            const float hr = st[i].x, hi = st[i].y;
+            st[i] = make_float2(fmaf(abr, hr, fmaf(-abi, hi, dtbx * ire)), fmaf(abr, hi, fmaf(abi, hr, dtbx * iim)));
             if (TRACE) {  // kernels.h:1158-1170, from the state before the step
                 const float i2_re = fmaf(ire, ire, -iim * iim);
                 const float i2_im = 2.0f * ire * iim;
@@ -124,28 +181,45 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_kernel(const uint32_t* 
                 const float zdt_im = fmaf(are, hi, aim * hr);
                 const float d_dt_re = fmaf(i2_re, zdt_re, -i2_im * zdt_im);
                 const float d_dt_im = fmaf(i2_re, zdt_im, i2_im * zdt_re);
-                ta[c] = make_float2(fmaf(abr, ta[c].x, fmaf(-abi, ta[c].y, dt_i2_za_re)),
-                                    fmaf(abr, ta[c].y, fmaf(abi, ta[c].x, dt_i2_za_im)));
-                tb[c] = make_float2(fmaf(abr, tb[c].x, fmaf(-abi, tb[c].y, dt * ire)),
-                                    fmaf(abr, tb[c].y, fmaf(abi, tb[c].x, dt * iim)));
-                td[c] = make_float2(fmaf(abr, td[c].x, fmaf(-abi, td[c].y, d_dt_re)),
-                                    fmaf(abr, td[c].y, fmaf(abi, td[c].x, d_dt_im)));
+                ta[i] = make_float2(fmaf(abr, ta[i].x, fmaf(-abi, ta[i].y, dt_i2_za_re)),
+                                    fmaf(abr, ta[i].y, fmaf(abi, ta[i].x, dt_i2_za_im)));
+                tb[i] = make_float2(fmaf(abr, tb[i].x, fmaf(-abi, tb[i].y, dt * ire)),
+                                    fmaf(abr, tb[i].y, fmaf(abi, tb[i].x, dt * iim)));
+                td[i] = make_float2(fmaf(abr, td[i].x, fmaf(-abi, td[i].y, d_dt_re)),
+                                    fmaf(abr, td[i].y, fmaf(abi, td[i].x, d_dt_im)));
             }
-            ya[c] = fmaf(st[c].x, k[c].z, -st[c].y * k[c].w);
+            ya[i] = fmaf(st[i].x, k[i].z, -st[i].y * k[i].w);
         }
+        // y: 0 + ya_0 + ya_1 + ... in state order across the channel's lanes
         float ys = 0.0f;
 #pragma unroll
-        for (int c = 0; c < P; ++c) ys += ya[c];
-        yv[static_cast<int64_t>(t) * E] = fmaf(wdd.y, x_local, ys);
-    }
+        for (int q = 0; q < L; ++q) {
+            if (j == q) {
 #pragma unroll
-    for (int c = 0; c < P; ++c) hs[c] = st[c];
+                for (int i = 0; i < S; ++i) ys += ya[i];
+            }
+            if (L > 1) ys = __shfl_sync(0xFFFFFFFFu, ys, gbase + q);
+        }
+        if (j == 0) {
+            const float yt = fmaf(wdd.y, x_local, ys);
+            if (SPLIT) {
+                const __nv_bfloat16 hb = __float2bfloat16_rn(yt);
+                yh[static_cast<int64_t>(t) * E] = hb;
+                yh[lo_plane + static_cast<int64_t>(t) * E] = __float2bfloat16_rn(yt - __bfloat162float(hb));
+            } else {
+                yv[static_cast<int64_t>(t) * E] = yt;
+            }
+        }
+    };
+    scan_steps<scan_prefetch<S>()>(xv, xsv, Gx, T, step);
+#pragma unroll
+    for (int i = 0; i < S; ++i) hs[i] = st[i];
     if (TRACE) {
 #pragma unroll
-        for (int c = 0; c < P; ++c) {
-            trs[c] = ta[c];
-            trs[tr_stride + c] = tb[c];
-            trs[2 * tr_stride + c] = td[c];
+        for (int i = 0; i < S; ++i) {
+            trs[i] = ta[i];
+            trs[tr_stride + i] = tb[i];
+            trs[2 * tr_stride + i] = td[i];
         }
     }
 }
@@ -234,6 +308,55 @@ __global__ void __launch_bounds__(kThreads) outproj_kernel(const float* __restri
     }
 }
 
+// Lanes per channel: the smallest L (a power of two, at most P) that gives the
+// scan 16 warps per SM, since each lane's S = P / L states are a serial
+// recurrence over T; L = 1 when batch x channels already fills the GPU.
+int scan_lanes(int64_t channels, int P)
+{
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t want = static_cast<int64_t>(sms) * 512;
+    int L = 1;
+    while (L < P && channels * L < want) L <<= 1;
+    return L;
+}
+
+template <int S, int L>
+cudaError_t launch_scan_sl(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
+                           const float4* c4, const float2* c2, int D, float2* h, float2* traces, void* y, bool split,
+                           int B, int T, cudaStream_t stream)
+{
+    const dim3 grid(static_cast<unsigned>(2LL * D * L / kScanThreads), static_cast<unsigned>(B));
+    if (traces)
+        ssm_scan_kernel<S, L, true, false><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, traces, y, T);
+    else if (split)
+        ssm_scan_kernel<S, L, false, true><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, nullptr, y, T);
+    else
+        ssm_scan_kernel<S, L, false, false><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, nullptr, y, T);
+    return cudaGetLastError();
+}
+
+// P states per channel over L lanes: S = P / L.
+template <int P>
+cudaError_t launch_scan_p(int L, const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
+                          const float4* c4, const float2* c2, int D, float2* h, float2* traces, void* y, bool split, int B,
+                          int T, cudaStream_t stream)
+{
+#define AIC_SCAN_L(LL)                                                                                          \
+    if (L == LL) {                                                                                              \
+        if constexpr (P % LL == 0)                                                                              \
+            return launch_scan_sl<P / LL, LL>(x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream); \
+    }
+    AIC_SCAN_L(1)
+    AIC_SCAN_L(2)
+    AIC_SCAN_L(4)
+    AIC_SCAN_L(8)
+    AIC_SCAN_L(16)
+#undef AIC_SCAN_L
+    return cudaErrorInvalidValue;
+}
+
 }  // namespace
 
 size_t ssm_consts_floats(int D, int d_state)
@@ -254,27 +377,23 @@ cudaError_t launch_ssm_prepare(const uint32_t* blob, const int8_t* blob_s, int D
 }
 
 cudaError_t launch_ssm_scan(const uint32_t* x, const int8_t* x_s, const uint32_t* blob, const int8_t* blob_s,
-                            const float* consts, int D, int d_state, float2* h, float2* traces, float* y, int B, int T,
-                            cudaStream_t stream)
+                            const float* consts, int D, int d_state, float2* h, float2* traces, void* y, bool split,
+                            int B, int T, cudaStream_t stream)
 {
     if (B == 0 || T == 0) return cudaSuccess;
-    const int64_t E = 2LL * D, P = d_state >> 5;
+    const int64_t E = 2LL * D;
+    const int P = d_state >> 5;
     const float4* c4 = reinterpret_cast<const float4*>(consts);
     const float2* c2 = reinterpret_cast<const float2*>(consts + E * P * 4);
-    dim3 grid(static_cast<unsigned>(E / kScanThreads), static_cast<unsigned>(B));
-#define AIC_SCAN(PP)                                                                                            \
-    (traces ? ssm_scan_kernel<PP, true><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, traces, y, T) \
-            : ssm_scan_kernel<PP, false><<<grid, kScanThreads, 0, stream>>>(x, x_s, blob, blob_s, c4, c2, D, h, nullptr, y, T))
+    const int L = scan_lanes(static_cast<int64_t>(B) * E, P);
     switch (P) {
-        case 1: AIC_SCAN(1); break;
-        case 2: AIC_SCAN(2); break;
-        case 4: AIC_SCAN(4); break;
-        case 8: AIC_SCAN(8); break;
-        case 16: AIC_SCAN(16); break;
+        case 1: return launch_scan_p<1>(L, x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream);
+        case 2: return launch_scan_p<2>(L, x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream);
+        case 4: return launch_scan_p<4>(L, x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream);
+        case 8: return launch_scan_p<8>(L, x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream);
+        case 16: return launch_scan_p<16>(L, x, x_s, blob, blob_s, c4, c2, D, h, traces, y, split, B, T, stream);
         default: return cudaErrorInvalidValue;
     }
-#undef AIC_SCAN
-    return cudaGetLastError();
 }
 
 cudaError_t launch_outproj(const float* y, const uint32_t* blob, const int8_t* blob_s, const float* bias, int D,

@@ -2,7 +2,9 @@
 
     python -m aicortex_b200.kbench conv --cin 32 --cout 128 --k 1 --dim 64 --frames 2048 --act
     python -m aicortex_b200.kbench dw --cin 32 --k 3 --stride 2 --dim 128 --frames 2048
-    python -m aicortex_b200.kbench scan --d-model 256 --d-state 512 --batch 256 --seq 128
+    python -m aicortex_b200.kbench layer --d-model 256 --d-state 512 --batch 256 --seq 128
+    python -m aicortex_b200.kbench scan --d-model 1024 --d-state 512 --batch 32 --seq 8192
+    python -m aicortex_b200.kbench outproj --d-model 1024 --d-state 512 --batch 32 --seq 8192 [--mode exact]
 
 Times `--iters` launches with CUDA events after `--warmup` launches and prints
 one JSON line with the mean time per launch and the algorithmic throughput
@@ -40,7 +42,7 @@ def _f_bytes(n: float) -> float:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["conv", "dw", "scan"])
+    ap.add_argument("kind", choices=["conv", "dw", "layer", "scan", "outproj"])
     ap.add_argument("--cin", type=int, default=32)
     ap.add_argument("--cout", type=int, default=128)
     ap.add_argument("--k", type=int, default=1)
@@ -49,7 +51,8 @@ def main(argv=None) -> None:
     ap.add_argument("--frames", type=int, default=2048)
     ap.add_argument("--act", action="store_true")
     ap.add_argument("--exact", action="store_true", help="reference-order CUDA-core kernel")
-    ap.add_argument("--mode", choices=["ordered", "fast", "simt"], default="ordered", help="conv mode")
+    ap.add_argument("--mode", choices=["ordered", "fast", "simt", "tensor", "exact"], default=None,
+                    help="conv mode (ordered, fast, simt) or Mamba out-projection mode (tensor, exact)")
     ap.add_argument("--d-model", type=int, default=256)
     ap.add_argument("--d-state", type=int, default=512)
     ap.add_argument("--batch", type=int, default=256)
@@ -75,7 +78,7 @@ def main(argv=None) -> None:
         xw, xs = L.pack_f32(x)
         del x
         ow, os_ = L.empty_f(a.frames * dout * dout, cout, dev)
-        layer.set_mode({"ordered": 0, "fast": 1, "simt": 2}[a.mode])
+        layer.set_mode({"ordered": 0, "fast": 1, "simt": 2}[a.mode or "ordered"])
         fwd = layer.forward_exact if a.exact else layer.forward
         ms = _time(lambda: fwd(xw, xs, ow, os_, a.frames), a.iters, a.warmup)
         rows = a.frames * dout * dout
@@ -84,16 +87,34 @@ def main(argv=None) -> None:
     else:
         E = 2 * a.d_model
         layer = L.MambaLayer(a.d_model, a.d_state, a.d_model, 1)
-        blob = W.mamba_blob(rng, a.d_model, a.d_state, a.d_model, wd_scale=W.WD_SCALE)
+        layer.set_mode(1 if a.mode == "exact" else 0)
+        blob = W.mamba_blob(rng, a.d_model, a.d_state, a.d_model)
         layer.load_weights(t(blob), t(W.bias(rng, a.d_model)))
         layer.bind_state(a.batch)
         rows = a.batch * a.seq
         xw, xs = L.pack_f32(torch.randn(rows * a.d_model, device=dev))
         out = torch.empty(rows, a.d_model, dtype=torch.float32, device=dev)
-        ms = _time(lambda: layer.forward(xw, xs, out, a.batch, a.seq), a.iters, a.warmup)
         P = a.d_state // 32
-        flops = rows * E * (31.0 * P + 15.0) + 2.0 * rows * E * a.d_model
-        nbytes = _f_bytes(rows * a.d_model) + 8.0 * rows * E + 4.0 * rows * a.d_model
+        scan_flops = rows * E * (31.0 * P + 15.0)
+        gemm_flops = 2.0 * rows * E * a.d_model
+        if a.kind == "layer":
+            ms = _time(lambda: layer.forward(xw, xs, out, a.batch, a.seq), a.iters, a.warmup)
+            flops = scan_flops + gemm_flops
+            nbytes = _f_bytes(rows * a.d_model) + 8.0 * rows * E + 4.0 * rows * a.d_model
+        else:
+            y = torch.empty(rows * E, dtype=torch.float32, device=dev)
+            split = a.mode != "exact"
+            layer.scan(xw, xs, y, a.batch, a.seq, split=split)
+            if a.kind == "scan":
+                ms = _time(lambda: layer.scan(xw, xs, y, a.batch, a.seq, split=split), a.iters, a.warmup)
+                flops = scan_flops
+                nbytes = _f_bytes(rows * a.d_model) + 4.0 * rows * E
+            else:
+                fn = (lambda: layer.outproj(y, out, rows)) if a.mode == "exact" else \
+                    (lambda: layer.outproj_split(y, out, rows))
+                ms = _time(fn, a.iters, a.warmup)
+                flops = gemm_flops
+                nbytes = 4.0 * rows * E + (4.0 if a.mode == "exact" else 2.0) * E * a.d_model + 4.0 * rows * a.d_model
     print(json.dumps({"kind": a.kind, "ms_per_launch": ms, "tflops": flops / ms / 1e9, "gbs": nbytes / ms / 1e6,
                       "flops": flops, "bytes": nbytes, "args": vars(a)}))
 

@@ -270,6 +270,19 @@ class MambaLayer(_Handle):
     def outproj(self, y: torch.Tensor, out: torch.Tensor, rows: int, stream=None) -> None:
         call("aic_mamba_layer_outproj", self.h, _vp(y), _vp(out), int(rows), _stream(stream))
 
+    def set_mode(self, mode: int) -> None:
+        """AIC_MAMBA_TENSOR (default) or AIC_MAMBA_EXACT out-projection."""
+        call("aic_mamba_layer_set_mode", self.h, int(mode))
+
+    def scan(self, x, x_s, y, batch: int, seq: int, split: bool = False, stream=None) -> None:
+        """The SSM scan alone into y (256-byte aligned, batch*seq*2*d_model*4 bytes)."""
+        call("aic_mamba_layer_scan", self.h, _vp(x), _vp(x_s), _vp(y), int(batch), int(seq), int(split),
+             _stream(stream))
+
+    def outproj_split(self, y_planes, out: torch.Tensor, rows: int, stream=None) -> None:
+        """The tensor-core out-projection of split-bf16 y planes (as scan(split=True) writes them)."""
+        call("aic_mamba_layer_outproj_split", self.h, _vp(y_planes), _vp(out), int(rows), _stream(stream))
+
     def forward(self, x, x_s, out, batch: int, seq: int, stream=None) -> None:
         ws = self.workspace(batch * seq)
         call("aic_mamba_layer_forward", self.h, _vp(x), _vp(x_s), _vp(out), int(batch), int(seq), C.c_void_p(ws.ptr),
@@ -323,6 +336,10 @@ class MambaBlock(_Handle):
 
     def reset(self, stream=None) -> None:
         call("aic_mamba_block_reset_state", self.h, _stream(stream))
+
+    def set_mode(self, mode: int) -> None:
+        """AIC_MAMBA_TENSOR (default) or AIC_MAMBA_EXACT for the three layers."""
+        call("aic_mamba_block_set_mode", self.h, int(mode))
 
     def load_dir(self, path: str, stream=None) -> None:
         call("aic_mamba_block_load_dir_sync", self.h, str(path).encode(), _stream(stream))
@@ -465,9 +482,13 @@ class Cortex(_Handle):
 
     def set_exact(self, exact: bool) -> None:
         """True: every quantized conv on CUDA cores with the reference kernels' structure
-        (AIC_CONV_SIMT); False: the default AIC_CONV_ORDERED. Both are bit-identical to
-        the reference."""
+        (AIC_CONV_SIMT) and the reference-order Mamba out-projection (AIC_MAMBA_EXACT);
+        False: the defaults AIC_CONV_ORDERED (bit-identical too) and AIC_MAMBA_TENSOR."""
         call("aic_cortex_set_exact", self.h, int(exact))
+
+    def set_mamba_mode(self, mode: int) -> None:
+        """AIC_MAMBA_TENSOR (default) or AIC_MAMBA_EXACT for every Mamba layer."""
+        call("aic_cortex_set_mamba_mode", self.h, int(mode))
 
     def set_conv_mode(self, mode: int) -> None:
         """AIC_CONV_ORDERED (default), AIC_CONV_FAST or AIC_CONV_SIMT for every conv layer."""

@@ -275,8 +275,33 @@ AIC_API aic_status aic_mamba_layer_forward(aic_mamba_layer l, const uint32_t* in
 AIC_API aic_status aic_mamba_layer_forward_noalloc(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s,
                                                    float* out, int batch, int seq, void* stream);
 /* The out-projection alone (mambaSSMFwdOutProjKernel, kernels.h:1188-1259):
- * y_ssm fp32 [rows][2*d_model] -> out fp32 [rows][out]. */
+ * y_ssm fp32 [rows][2*d_model] -> out fp32 [rows][out], on CUDA cores in the
+ * reference's accumulation order (bit-identical to the reference kernel). */
 AIC_API aic_status aic_mamba_layer_outproj(aic_mamba_layer l, const float* y, float* out, int64_t rows, void* stream);
+/* Out-projection arithmetic of a Mamba layer:
+ *   AIC_MAMBA_TENSOR (default) tcgen05 GEMM: W_out held exactly as bf16
+ *       q * F(s) (the 1/7 of the int4 unit is applied in the epilogue), y as
+ *       two bf16 planes hi + lo (16 significant bits), fp32 accumulation;
+ *       within about 1e-5 of the output scale of the reference's fp32 chain
+ *       (stated tolerance 1e-3). Out channels: a multiple of 32 that is at most
+ *       256 or a multiple of 256 (others run as AIC_MAMBA_EXACT).
+ *   AIC_MAMBA_EXACT  CUDA cores in the reference's accumulation order:
+ *       bit-identical to mambaSSMFwdOutProjKernel.
+ * The SSM scan is the reference's arithmetic in both modes. */
+#define AIC_MAMBA_TENSOR 0
+#define AIC_MAMBA_EXACT 1
+AIC_API aic_status aic_mamba_layer_set_mode(aic_mamba_layer l, int mode);
+/* The SSM scan alone (mambaSSMFwdStateKernel, kernels.h:1080-1187, over `seq`
+ * steps of `batch` sequences; advances the bound state): y 256-byte aligned,
+ * batch*seq*2*d_model*4 bytes, written as fp32 [rows][2*d_model] when
+ * y_split == 0, else as the bf16 planes hi [rows][2*d_model] then lo. */
+AIC_API aic_status aic_mamba_layer_scan(aic_mamba_layer l, const uint32_t* in, const int8_t* in_s, void* y, int batch,
+                                        int seq, int y_split, void* stream);
+/* The tensor-core out-projection alone over split-bf16 y planes (as
+ * aic_mamba_layer_scan writes them with y_split != 0); AIC_ERR_UNSUPPORTED
+ * for out channels without a tensor-core tiling. */
+AIC_API aic_status aic_mamba_layer_outproj_split(aic_mamba_layer l, const void* y_planes, float* out, int64_t rows,
+                                                 void* stream);
 AIC_API aic_status aic_mamba_layer_destroy(aic_mamba_layer l);
 
 /* ------------------------------------------------------------------------
@@ -309,6 +334,8 @@ AIC_API aic_status aic_mamba_block_load_dir_sync(aic_mamba_block b, const char* 
 AIC_API aic_status aic_mamba_block_forward(aic_mamba_block b, const uint32_t* in, const int8_t* in_s, float* out,
                                            int batch, int seq, int on_training, int add_seed, int is_survived,
                                            void* workspace, void* stream);
+/* AIC_MAMBA_* of the block's three layers. */
+AIC_API aic_status aic_mamba_block_set_mode(aic_mamba_block b, int mode);
 AIC_API aic_status aic_mamba_block_destroy(aic_mamba_block b);
 
 /* ------------------------------------------------------------------------
@@ -393,7 +420,11 @@ AIC_API aic_status aic_cortex_forward_host(aic_cortex c, const uint16_t* planes_
                                            float* actor_host, float* critic_host, void* workspace, void* stream);
 /* Conv mode (AIC_CONV_*) of every conv layer of the cortex. */
 AIC_API aic_status aic_cortex_set_conv_mode(aic_cortex c, int mode);
-/* exact != 0: AIC_CONV_SIMT; 0: AIC_CONV_ORDERED (the default). */
+/* AIC_MAMBA_* of every Mamba layer of the cortex (units and actor). */
+AIC_API aic_status aic_cortex_set_mamba_mode(aic_cortex c, int mode);
+/* exact != 0: AIC_CONV_SIMT and AIC_MAMBA_EXACT (every kernel in the
+ * reference's arithmetic order); 0: AIC_CONV_ORDERED and AIC_MAMBA_TENSOR
+ * (the defaults). */
 AIC_API aic_status aic_cortex_set_exact(aic_cortex c, int exact);
 /* Number of kernel launches the last forward issued. */
 AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches);
