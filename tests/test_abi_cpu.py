@@ -139,3 +139,21 @@ def test_cortex_desc_chaining():
 @pytest.mark.parametrize("n", [31, -32])
 def test_pack_rejects_bad_sizes(n):
     assert lib.aic_pack_f32(None, n, None, None, 0, 0, None) == AIC_ERR_INVALID
+
+
+def test_dropin_header_and_driver_compile(tmp_path):
+    """include/aicortex_layers.hpp (the reference's layer classes over the C
+    ABI) and the test driver that uses it compile and link against the
+    library; running it needs a GPU (tests/test_dropin_gpu.py)."""
+    import shutil
+    import subprocess
+    from conftest import ROOT
+    if shutil.which("g++") is None:
+        pytest.skip("no g++")
+    exe = tmp_path / "dropin_main"
+    cmd = ["g++", "-std=c++17", "-O0", "-Wall", "-Werror", "-Wno-unused-parameter", "-DAIC_LAYERS_D_MODEL=256",
+           "-DAIC_LAYERS_D_STATE=128", "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include",
+           str(ROOT / "tests" / "dropin" / "dropin_main.cpp"), "-L", str(ROOT / "aicortex_b200"), "-laicortex_b200",
+           "-L", "/usr/local/cuda/lib64", "-lcudart", "-o", str(exe)]
+    subprocess.run(cmd, check=True)
+    assert exe.exists()
