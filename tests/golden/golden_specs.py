@@ -84,7 +84,13 @@ def mamba_block_case():
     return blobs, biases, x
 
 
+# training-mode forward (mamba_block.h:58-72 with on_training): stochastic
+# requant seeded by add_seed, survival scaling 1/p, and one skipped step
+MB_TRAIN_SEED, MB_TRAIN_SURV = 4321, 0.8
+MB_TRAIN_SKIPPED = (2,)  # time steps run with is_survived = false
+
 CB_GEO = (64, 256, 128, 2, 32, 16, 3)  # in, mid, out, stride, din, dout, dw k
+CB_TRAIN_SURV = 0.75  # ConvBlock survival probability in the training-mode fixture
 CB_RF = 0.75
 
 

@@ -30,7 +30,7 @@ sys.path.insert(0, str(HERE))
 import golden_specs as S  # noqa: E402
 
 REF_DIR = ROOT / "oracle" / "_ref"
-_NAMES = {"ssm", "critic"}  # fixture groups that can be regenerated alone
+_NAMES = {"ssm", "critic", "train"}  # fixture groups that can be regenerated alone
 _dirs = [a for a in sys.argv[1:] if a not in _NAMES]
 OUT = Path(_dirs[0]) if _dirs else HERE
 DEV = torch.device("cuda")
@@ -242,6 +242,85 @@ def gen_mamba_block():
     save("mamba_block_N128", blob_sha=np.array([S.sha(b) for b in blobs]), x_w=xw, x_s=xs, out=np.stack(res))
 
 
+def gen_mamba_block_train():
+    """MambaBlock::forward in training mode (mamba_block.h:58-72, on_training =
+    true): both requants stochastic with add_seed (quantizeKernel<float,false>,
+    :63,69) and the residual scaled by 1/p when the step survives, or the main
+    branch dropped when it does not (:65). Same weights and inputs as the
+    inference fixture; the skipped steps are MB_TRAIN_SKIPPED."""
+    lib = ref(S.MB_D, S.MB_N)
+    d = Dev()
+    blobs, biases, x = S.mamba_block_case()
+    D, N, E = S.MB_D, S.MB_N, 2 * S.MB_D
+    packed = [tuple(d.put(a) for a in pack_weights(lib, b)) for b in blobs]
+    pbias = [d.put(b) for b in biases]
+    outs_c = (D, D, S.MB_OUT)
+    acts = (1, 1, 2)
+    st = [[d.zeros(E * N * 2, torch.float32)[1] for _ in range(4)] for _ in range(3)]
+    _, py = d.zeros(E, torch.float32)
+    o = [d.zeros(c, torch.float32) for c in outs_c]
+    _, paw = d.zeros(D // 8, torch.int32)
+    _, pas = d.zeros(D // 32, torch.int8)
+    _, pbw = d.zeros(D // 8, torch.int32)
+    _, pbs = d.zeros(D // 32, torch.int8)
+    xw, xs = act_f(lib, x)
+    res = []
+    surv_inv = np.float32(1.0) / np.float32(S.MB_TRAIN_SURV)
+
+    def layer(i, inw, ins):
+        run(lib, "aicref_ssm_step", inw, ins, packed[i][0], packed[i][1], *st[i], py)
+        run(lib, "aicref_outproj", py, packed[i][0], packed[i][1], pbias[i], o[i][1], C.c_int(outs_c[i]),
+            C.c_int(acts[i]))
+
+    seed = C.c_int(S.MB_TRAIN_SEED)
+    for t in range(S.MB_T):
+        survived = t not in S.MB_TRAIN_SKIPPED
+        xin_w, xin_s = d.put(xw[t]), d.put(xs[t])
+        layer(0, xin_w, xin_s)
+        run(lib, "aicref_quantize_f32", o[0][1], paw, pas, C.c_int(D), C.c_int(1), seed)
+        run(lib, "aicref_residual", paw, pas, xin_w, xin_s, pbw, pbs, C.c_int(D), C.c_int(1),
+            C.c_float(surv_inv if survived else 1.0), C.c_int(0 if survived else 1), C.c_float(1.0))
+        layer(1, pbw, pbs)
+        run(lib, "aicref_quantize_f32", o[1][1], paw, pas, C.c_int(D), C.c_int(1), seed)
+        layer(2, paw, pas)
+        res.append(o[2][0].cpu().numpy().copy())
+    save("mamba_block_train_N128", blob_sha=np.array([S.sha(b) for b in blobs]), x_w=xw, x_s=xs,
+         out=np.stack(res))
+
+
+def gen_conv_block_train(lib):
+    """ConvBlock::forward in training mode (conv_block.h:74-82, train_mode =
+    true): the residual scales the main branch by 1/p when the block survives
+    and drops it when it does not (:81). One frame, both cases."""
+    d = Dev()
+    masters, biases, x = S.conv_block_case()
+    cin, mid, cout, st, din, dout, k = S.CB_GEO
+    packed = []
+    for m, b in zip(masters, biases):
+        w, s = pack_weights(lib, m)
+        packed.append((d.put(w), d.put(s), d.put(b)))
+    xw, xs = act_f(lib, x)
+    pxw, pxs = d.put(xw), d.put(xs)
+    _, paw = d.zeros(dout * dout * mid // 8, torch.int32)
+    _, pas = d.zeros(dout * dout * mid // 32, torch.int8)
+    _, pbw = d.zeros(dout * dout * mid // 8, torch.int32)
+    _, pbs = d.zeros(dout * dout * mid // 32, torch.int8)
+    out = {}
+    surv_inv = np.float32(1.0) / np.float32(S.CB_TRAIN_SURV)
+    for name, survived in (("survived", True), ("skipped", False)):
+        ow, pow_ = d.zeros(dout * dout * cout // 8, torch.int32)
+        os_, pos = d.zeros(dout * dout * cout // 32, torch.int8)
+        run(lib, "aicref_conv_dw", pxw, pxs, *packed[0], paw, pas, *map(C.c_int, (cin, k, st, din, dout)))
+        run(lib, "aicref_conv_pw", paw, pas, *packed[1], pbw, pbs, *map(C.c_int, (dout * dout, cin, mid, 1)))
+        run(lib, "aicref_conv_pw", pbw, pbs, *packed[2], paw, pas, *map(C.c_int, (dout * dout, mid, cout, 0)))
+        run(lib, "aicref_conv_dense", pxw, pxs, *packed[3], pbw, pbs, *map(C.c_int, (cin, cout, 2, 2, din, dout, 0)))
+        run(lib, "aicref_residual", paw, pas, pbw, pbs, pow_, pos, C.c_int(cout), C.c_int(dout),
+            C.c_float(surv_inv if survived else 1.0), C.c_int(0 if survived else 1), C.c_float(S.CB_RF))
+        out[f"{name}_w"] = u32(ow)
+        out[f"{name}_s"] = os_.cpu().numpy()
+    save("conv_block_train", master_sha=np.array([S.sha(m) for m in masters]), x_w=xw, x_s=xs, **out)
+
+
 def gen_conv_block(lib):
     """ConvBlock::forward (conv_block.h:74-82, inference) on one frame."""
     d = Dev()
@@ -343,6 +422,9 @@ def main():
                 gen_ssm(n)
         if "critic" in only:
             gen_critic(ref(256, 128))
+        if "train" in only:
+            gen_mamba_block_train()
+            gen_conv_block_train(ref(256, 128))
         return
     lib = ref(256, 128)
     gen_screen(lib)
@@ -356,6 +438,8 @@ def main():
         gen_ssm(n)
     gen_mamba_block()
     gen_conv_block(lib)
+    gen_mamba_block_train()
+    gen_conv_block_train(lib)
     gen_critic(lib)
     gen_actions(lib)
 

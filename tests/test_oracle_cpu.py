@@ -175,6 +175,41 @@ def test_oracle_conv_block(golden):
     check_f(ow, os_, g["out_w"], g["out_s"], flip_rate=5e-3, what="conv block")
 
 
+def test_oracle_mamba_block_train(golden):
+    """Training-mode block (stochastic requants seeded by add_seed, survival
+    scaling, one skipped step) against the reference kernels' fixture."""
+    g = golden("mamba_block_train_N128")
+    blobs, biases, _ = S.mamba_block_case()
+    assert [S.sha(b) for b in blobs] == [str(v) for v in g["blob_sha"]]
+    D, N = S.MB_D, S.MB_N
+    layers = [O.MambaLayerRef(D, N, D, 1, blobs[0], biases[0], 1), O.MambaLayerRef(D, N, D, 1, blobs[1], biases[1], 1),
+              O.MambaLayerRef(D, N, S.MB_OUT, 2, blobs[2], biases[2], 1)]
+    surv_inv = np.float32(1.0) / np.float32(S.MB_TRAIN_SURV)
+    outs = []
+    for t in range(S.MB_T):
+        survived = t not in S.MB_TRAIN_SKIPPED
+        xw, xs = g["x_w"][t:t + 1], g["x_s"][t:t + 1]
+        o0 = layers[0].forward(xw, xs, 1, 1)
+        aw, as_ = O.pack_f32(o0, True, S.MB_TRAIN_SEED)
+        bw, bs = O.residual(aw, as_, xw, xs, 1, D, float(surv_inv) if survived else 1.0, not survived)
+        o1 = layers[1].forward(bw, bs, 1, 1)
+        aw, as_ = O.pack_f32(o1, True, S.MB_TRAIN_SEED)
+        outs.append(layers[2].forward(aw.reshape(1, -1), as_.reshape(1, -1), 1, 1)[0])
+    close(np.stack(outs), g["out"], 1e-4, "mamba block, training mode")
+
+
+def test_oracle_conv_block_train(golden):
+    g = golden("conv_block_train")
+    masters, biases, _ = S.conv_block_case()
+    assert [S.sha(m) for m in masters] == [str(v) for v in g["master_sha"]]
+    layers = [O.pack_conv_layer(m, b) for m, b in zip(masters, biases)]
+    surv_inv = np.float32(1.0) / np.float32(S.CB_TRAIN_SURV)
+    for name, survived in (("survived", True), ("skipped", False)):
+        mult = float(np.float32(S.CB_RF) * surv_inv) if survived else S.CB_RF
+        ow, os_ = O.conv_block(g["x_w"], g["x_s"], layers, 1, S.CB_GEO, main_mult=mult, skipped=not survived)
+        check_f(ow, os_, g[f"{name}_w"], g[f"{name}_s"], flip_rate=5e-3, what=f"conv block, training mode, {name}")
+
+
 def test_oracle_critic(golden):
     g = golden("critic")
     w1, w2, wl, x = S.critic_case()

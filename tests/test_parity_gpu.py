@@ -401,6 +401,43 @@ def test_golden_conv_block(golden):
     assert_f_close(ow, h(os_), g["out_w"], g["out_s"], flip_rate=5e-3, what="conv block (fast)")
 
 
+def test_golden_mamba_block_train(golden):
+    """Training-mode MambaBlock forward (mamba_block.h:58-72, on_training):
+    stochastic requants seeded by add_seed, the residual scaled by 1/p on
+    surviving steps and the main branch dropped on a skipped step; one step
+    per call, state carried, bit-exact with the reference kernels."""
+    g = golden("mamba_block_train_N128")
+    blobs, biases, _ = S.mamba_block_case()
+    blk = A.MambaBlock(S.MB_D, S.MB_N, S.MB_OUT, activation=2, survival_probability=S.MB_TRAIN_SURV)
+    for i in range(3):
+        blk.layers[i].load_weights(t(blobs[i]), t(biases[i]))
+    blk.bind_state(1)
+    blk.set_mode(A.AIC_MAMBA_EXACT)
+    xw, xs = t(g["x_w"]), t(g["x_s"])
+    out = torch.empty(S.MB_T, S.MB_OUT, dtype=torch.float32, device=DEV)
+    for step in range(S.MB_T):
+        blk.forward(xw[step:step + 1], xs[step:step + 1], out[step:step + 1], 1, 1, on_training=True,
+                    add_seed=S.MB_TRAIN_SEED, is_survived=step not in S.MB_TRAIN_SKIPPED)
+    np.testing.assert_array_equal(h(out), g["out"])
+    # the inference fixture differs: the stochastic requant and survival scaling did act
+    assert not np.array_equal(h(out), golden("mamba_block_N128")["out"])
+
+
+def test_golden_conv_block_train(golden):
+    """Training-mode ConvBlock forward (conv_block.h:74-82, train_mode): main
+    branch x 1/p when the block survives, dropped when it is skipped."""
+    g = golden("conv_block_train")
+    masters, biases, _ = S.conv_block_case()
+    cin, mid, cout, st, din, dout, k = S.CB_GEO
+    blk = A.ConvBlock(cin, mid, cout, st, din, dout, k, S.CB_TRAIN_SURV, S.CB_RF)
+    for i in range(4):
+        blk.layers[i].load_weights(t(masters[i]), t(biases[i]))
+    for name, survived in (("survived", True), ("skipped", False)):
+        ow, os_ = A.empty_f(dout * dout, cout)
+        blk.forward(t(g["x_w"]), t(g["x_s"]), ow, os_, 1, train_mode=True, is_survived=survived)
+        assert_f_equal(ow, h(os_), g[f"{name}_w"], g[f"{name}_s"], f"conv block, training mode, {name}")
+
+
 def test_golden_critic(golden):
     g = golden("critic")
     w1, w2, wl, x = S.critic_case()
