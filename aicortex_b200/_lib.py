@@ -100,6 +100,22 @@ _SIGS = {
     "aic_conv_block_load_dir_sync": [P, C.c_char_p, P],
     "aic_conv_block_forward": [P, P, P, P, P, I64, I32, I32, P, P],
     "aic_conv_block_destroy": [P],
+    "aic_grad_clip_partials": [I64, PI64],
+    "aic_grad_clip_factor": [P, I64, P, P, P],
+    "aic_sgd_update": [P, P, I64, P, F32, F32, P],
+    "aic_residual_backward": [P, P, I64, F32, F32, P],
+    "aic_conv_layer_train_bytes": [P, SZ],
+    "aic_conv_layer_train_bind": [P, P, P, F32, F32, P],
+    "aic_conv_layer_backward": [P, P, P, P, P, P],
+    "aic_conv_layer_train_views": [P, PP, PP, PP, PP],
+    "aic_mamba_layer_train_bytes": [P, SZ],
+    "aic_mamba_layer_train_bind": [P, P, P, F32, F32, P],
+    "aic_mamba_layer_backward": [P, P, P, P, P, P],
+    "aic_mamba_layer_train_views": [P, PP, PP, PP, PP],
+    "aic_critic_train_bytes": [P, SZ],
+    "aic_critic_train_bind": [P, P, F32, F32],
+    "aic_critic_backward": [P, P, F32, P],
+    "aic_critic_train_views": [P, PP, PP, PP],
     "aic_mamba_layer_create": [C.POINTER(MambaLayerDesc), PP],
     "aic_mamba_layer_sizes": [P, PI64, PI64, SZ],
     "aic_mamba_layer_bind": [P, P],

@@ -132,4 +132,41 @@ cudaError_t launch_screen_frontend(const uint8_t* bgra, __half* frame, int dim, 
 cudaError_t launch_set_actions(const float* probs, int64_t rows, int A, unsigned long long* actions,
                                cudaStream_t stream);
 
+// F4: training path (k_train.cu), one layer step per call as the reference's
+// layer classes run it. Clip factor of a gradient (conv_layer.h:207-213):
+// factor[0] = 1/norm above 1, factor[1] = the square sum; partial holds
+// sumsq_blocks(n, sms) floats.
+int sumsq_blocks(int64_t n, int sms);
+cudaError_t launch_clip_factor(const float* x, int64_t n, int sms, float* partial, float* factor, cudaStream_t s);
+// updateParamsKernel (kernels.h:196-216) with the factor read from the device.
+cudaError_t launch_sgd_update(float* data, const float* grad, int64_t n, const float* factor, float lr, float penalty,
+                              cudaStream_t s);
+// Gradients of one conv layer on one frame (ConvLayer::backward,
+// conv_layer.h:150-206): grad_out [dout^2][out] fp32, input the layer's packed
+// forward input; gw / gb written, grad_in [din^2][in] added to (pointwise,
+// dense) or written (depthwise), or skipped when null. scratch: 4 *
+// dout^2 * out floats (unused by the depthwise conv).
+cudaError_t launch_conv_backward_grads(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
+                                       const float* bias, const float* master, const float* dy, int in_c, int out_c,
+                                       int ks, int stride, int din, int dout, bool act, float* scratch, float* gw,
+                                       float* gb, float* grad_in, cudaStream_t s);
+// residualAddBwdKernel (kernels.h:1056-1079) over n floats.
+cudaError_t launch_residual_backward(float* grad_next, float* grad_res, int64_t n, float survival_inv,
+                                     float residual_factor, cudaStream_t s);
+// Gradients of one Mamba layer step (MambaLayer::backward, mamba_layer.h:146-
+// 167) of one sequence: h and the traces [E][P] complex after the step;
+// master the fp32 blob; gw zeroed here and written, gb written, grad_in [D]
+// written. partial: (2D / 256) * out floats, gnorm: out, gx_ch: 2D.
+cudaError_t launch_mamba_backward_grads(const uint32_t* in, const int8_t* in_s, const float2* h, const float2* ta,
+                                        const float2* tb, const float2* td, const float* master, const float* bias,
+                                        const float* dy, int D, int N, int out_c, int act, float* partial,
+                                        float* gnorm, float* gx_ch, float* gw, float* gb, float* grad_in,
+                                        cudaStream_t s);
+// Critic gradients (Critic::backward, critic.h:117-124): gw1 / gl [in][units]
+// / [units][in] complex, gw2 [units] complex; units a power of two; pred
+// points at the step's score on the device.
+cudaError_t launch_critic_backward_grads(const float* w2, const float2* tw1, const float2* tl, const float2* hidden,
+                                         const float* pred, float real, int units, int in_c, float* gw1, float* gl, float* gw2,
+                                         cudaStream_t s);
+
 }  // namespace aic

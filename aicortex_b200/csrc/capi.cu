@@ -78,6 +78,56 @@ struct Carver {
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
+int device_sms()
+{
+    int dev = 0, sms = 0;
+    cuda_ok(cudaGetDevice(&dev), "device");
+    cuda_ok(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "SM count");
+    return sms;
+}
+
+// Training state of a layer (the reference's master weights, gradients and
+// SGD hyper-parameters, conv_layer.h / mamba_layer.h / critic.h), in one
+// caller-provided device buffer. The fp32 master copies of the packed
+// weights live here; fp32 parameters (biases, the critic) are updated in place.
+struct TrainState {
+    float* master = nullptr;          // fp32 masters of the packed weights (null when all weights are fp32)
+    float* gw = nullptr;              // weight gradients
+    float* gb = nullptr;              // bias / second-tensor gradients
+    float* gx = nullptr;              // third gradient tensor (critic lambda)
+    float* scratch = nullptr;         // kernel scratch
+    float* partial = nullptr;         // clip-factor block sums
+    float* factor = nullptr;          // [3][2] clip factors and square sums
+    float lr = 0.0f, penalty = 0.0f;  // learning_rate, f_penalty
+    int sms = 0;
+    bool bound = false;
+    static size_t bytes(int64_t master_n, int64_t gw_n, int64_t gb_n, int64_t gx_n, int64_t scratch_n, int sms)
+    {
+        Carver c(nullptr);
+        TrainState t;
+        t.carve(c, master_n, gw_n, gb_n, gx_n, scratch_n, sms);
+        return c.bytes();
+    }
+    void carve(Carver& c, int64_t master_n, int64_t gw_n, int64_t gb_n, int64_t gx_n, int64_t scratch_n, int n_sms)
+    {
+        const int64_t biggest = std::max(std::max(gw_n, gb_n), gx_n);
+        master = master_n ? c.take<float>(master_n) : nullptr;
+        gw = c.take<float>(gw_n);
+        gb = c.take<float>(gb_n);
+        gx = gx_n ? c.take<float>(gx_n) : nullptr;
+        scratch = scratch_n ? c.take<float>(scratch_n) : nullptr;
+        partial = c.take<float>(sumsq_blocks(biggest, n_sms));
+        factor = c.take<float>(6);
+        sms = n_sms;
+    }
+    // clip_op + updateParamsKernel (conv_layer.h:207-216) of one tensor
+    void step(float* data, const float* grad, int64_t n, int slot, float pen, cudaStream_t s)
+    {
+        cuda_ok(launch_clip_factor(grad, n, sms, partial, factor + 2 * slot, s), "clip factor");
+        cuda_ok(launch_sgd_update(data, grad, n, factor + 2 * slot, lr, pen, s), "sgd update");
+    }
+};
+
 // Host staging of fp32 checkpoint data in mapped pinned memory, which the
 // packer reads directly, as the reference keeps its master weights
 // (uv.h:122, conv_layer.h:80-82). The file is read and checked before any
@@ -256,6 +306,55 @@ struct ConvLayer {
     uint8_t* wimg_ord = nullptr;  // tensor-core images, AIC_CONV_ORDERED (k = 1, 2)
     float* wf = nullptr;          // dequantised weights (depthwise only)
     int mode = AIC_CONV_ORDERED;
+    TrainState train;
+
+    int64_t train_scratch() const { return is_dw ? 0 : 4LL * d.dim_out * d.dim_out * d.out_channels; }
+    size_t train_bytes() const
+    {
+        return TrainState::bytes(weight_elems, weight_elems, d.out_channels, 0, train_scratch(), device_sms());
+    }
+    // Binds the training state and takes `m` (weight_elems fp32, device or
+    // host) as the master weights; the packed weights are re-derived from it.
+    void train_bind(void* buf, const float* m, float lr, float penalty, cudaStream_t s)
+    {
+        check_bound();
+        require(buf && aligned256(buf) && m, "training buffer must be 256-byte aligned; master weights required");
+        Carver c(buf);
+        train.carve(c, weight_elems, weight_elems, d.out_channels, 0, train_scratch(), device_sms());
+        train.lr = lr;
+        train.penalty = penalty;
+        cuda_ok(cudaMemcpyAsync(train.master, m, sizeof(float) * weight_elems, cudaMemcpyDefault, s), "copy master");
+        repack(s);
+        train.bound = true;
+    }
+    // quantizeKernel of the masters (conv_layer.h:98, 218) and the images
+    void repack(cudaStream_t s)
+    {
+        cuda_ok(launch_pack_f32(train.master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s),
+                "pack weights");
+        prepare(s);
+    }
+    // ConvLayer::backward (conv_layer.h:150-219) on one frame: gradients,
+    // clipped SGD on the masters and biases, re-quantised weights. grad_in:
+    // added to (pointwise, dense; the reference's atomics) or written
+    // (depthwise), or null.
+    void backward(const float* dy, const uint32_t* in, const int8_t* in_s, float* grad_in, cudaStream_t s)
+    {
+        check_bound();
+        if (!train.bound) fail(AIC_ERR_STATE, "conv layer training state not bound");
+        require(dy && in && in_s, "null tensor");
+        const int positions = d.dim_out * d.dim_out;
+        if (d.kernel_size == 1 && positions % 32 != 0)
+            fail(AIC_ERR_UNSUPPORTED, "pointwise backward needs a multiple of 32 positions (kernels.h:375-379)");
+        if (is_dw && positions % 4 != 0) fail(AIC_ERR_UNSUPPORTED, "depthwise backward needs a multiple of 4 positions");
+        cuda_ok(launch_conv_backward_grads(in, in_s, w, ws, bias, train.master, dy, d.in_channels, d.out_channels,
+                                           d.kernel_size, d.stride, d.dim_in, d.dim_out, !is_dw && !d.disable_activation,
+                                           train.scratch, train.gw, train.gb, grad_in, s),
+                "conv backward");
+        train.step(train.master, train.gw, weight_elems, 0, train.penalty, s);
+        train.step(bias, train.gb, d.out_channels, 1, 0.0f, s);
+        repack(s);
+    }
 
     size_t carve(void* base)
     {
@@ -446,6 +545,7 @@ struct MambaLayer {
     int batch_bound = -1;
     int mode = AIC_MAMBA_TENSOR;
     bool bound = false;
+    TrainState train;
     Profiler* prof = nullptr;
     std::string tag = "mamba";
 
@@ -499,6 +599,53 @@ struct MambaLayer {
         MappedHost m(read_floats(path, {static_cast<size_t>(weight_elems), static_cast<size_t>(d.out_channels)}));
         load(m.dev, m.dev + weight_elems, s);
         cuda_ok(cudaStreamSynchronize(s), "load sync");
+    }
+    // training scratch: out-projection chunk sums, normalised gradient, per-channel input terms
+    int64_t train_scratch() const { return static_cast<int64_t>(E / 256) * d.out_channels + d.out_channels + E; }
+    size_t train_bytes() const
+    {
+        return TrainState::bytes(weight_elems, weight_elems, d.out_channels, 0, train_scratch(), device_sms());
+    }
+    void train_bind(void* buf, const float* m, float lr, float penalty, cudaStream_t s)
+    {
+        check_bound();
+        require(buf && aligned256(buf) && m, "training buffer must be 256-byte aligned; master weights required");
+        require(E % 256 == 0, "the backward kernels run 256-channel blocks: d_model must be a multiple of 128");
+        Carver c(buf);
+        train.carve(c, weight_elems, weight_elems, d.out_channels, 0, train_scratch(), device_sms());
+        train.lr = lr;
+        train.penalty = penalty;
+        cuda_ok(cudaMemcpyAsync(train.master, m, sizeof(float) * weight_elems, cudaMemcpyDefault, s), "copy master");
+        repack(s);
+        train.bound = true;
+    }
+    void repack(cudaStream_t s)
+    {
+        cuda_ok(launch_pack_f32(train.master, weight_elems, w, ws, true, static_cast<int32_t>(weight_elems), 0, s),
+                "pack blob");
+        cuda_ok(launch_ssm_prepare(w, ws, d.d_model, d.d_state, consts, s), "ssm prepare");
+        if (wimg) cuda_ok(launch_build_outproj_wimg(w, ws, off_w(), E, d.out_channels, wimg, s), "out-proj image");
+    }
+    // MambaLayer::backward (mamba_layer.h:146-167) of the step just run: the
+    // state and traces of sequence 0 after it, the step's packed input;
+    // grad_in [d_model] written.
+    void backward(const float* dy, const uint32_t* in, const int8_t* in_s, float* grad_in, cudaStream_t s)
+    {
+        check_bound();
+        if (!train.bound) fail(AIC_ERR_STATE, "mamba layer training state not bound");
+        if (batch_bound != 1 || !traces) fail(AIC_ERR_STATE, "backward needs the state bound for batch 1 and traces bound");
+        require(dy && in && in_s && grad_in, "null tensor");
+        const int64_t plane = static_cast<int64_t>(E) * P;
+        float* partial = train.scratch;
+        float* gnorm = partial + static_cast<int64_t>(E / 256) * d.out_channels;
+        float* gx_ch = gnorm + d.out_channels;
+        cuda_ok(launch_mamba_backward_grads(in, in_s, h, traces, traces + plane, traces + 2 * plane, train.master, bias, dy,
+                                            d.d_model, d.d_state, d.out_channels, d.activation, partial, gnorm, gx_ch,
+                                            train.gw, train.gb, grad_in, s),
+                "mamba backward");
+        train.step(train.master, train.gw, weight_elems, 0, train.penalty, s);
+        train.step(bias, train.gb, d.out_channels, 1, 0.0f, s);
+        repack(s);
     }
     void reset(cudaStream_t s)
     {
@@ -665,6 +812,34 @@ struct Critic {
         require(d.dim_in >= 1, "bad critic input dimension");
     }
     int64_t w1_elems() const { return 2LL * d.in_channels * d.units; }
+    TrainState train;
+    size_t train_bytes() const { return TrainState::bytes(0, w1_elems(), 2 * d.units, w1_elems(), 0, device_sms()); }
+    void train_bind(void* buf, float lr, float penalty)
+    {
+        check_bound();
+        require(buf && aligned256(buf), "training buffer must be 256-byte aligned");
+        if (d.units & (d.units - 1)) fail(AIC_ERR_UNSUPPORTED, "critic backward needs a power-of-two unit count (kernels.h:1786)");
+        Carver c(buf);
+        train.carve(c, 0, w1_elems(), 2 * d.units, w1_elems(), 0, device_sms());
+        train.lr = lr;
+        train.penalty = penalty;
+        train.bound = true;
+    }
+    // Critic::backward (critic.h:117-131) of the step just run (batch 1): the
+    // score it produced (device pointer) against real_score.
+    void backward(const float* pred, float real, cudaStream_t s)
+    {
+        check_bound();
+        if (!train.bound) fail(AIC_ERR_STATE, "critic training state not bound");
+        if (batch_bound != 1 || !traces) fail(AIC_ERR_STATE, "backward needs the state bound for batch 1 and traces bound");
+        require(pred != nullptr, "null score");
+        cuda_ok(launch_critic_backward_grads(w2, traces, trace_l(), h, pred, real, d.units, d.in_channels, train.gw,
+                                             train.gx, train.gb, s),
+                "critic backward");
+        train.step(w1, train.gw, w1_elems(), 0, train.penalty, s);
+        train.step(w2, train.gb, 2 * d.units, 1, train.penalty, s);
+        train.step(wl, train.gx, w1_elems(), 2, train.penalty, s);
+    }
     size_t carve(void* base)
     {
         Carver c(base);
@@ -1890,6 +2065,122 @@ AIC_API aic_status aic_cortex_last_launches(aic_cortex c, int64_t* launches)
 AIC_API aic_status aic_cortex_destroy(aic_cortex c)
 {
     return guarded([&] { delete reinterpret_cast<Cortex*>(c); });
+}
+
+// ---------------------------------------------------------------- training (F4)
+AIC_API aic_status aic_grad_clip_factor(const float* grad, int64_t n, float* partial, float* factor, void* stream)
+{
+    return guarded([&] {
+        require(grad && partial && factor && n > 0, "bad clip arguments");
+        cuda_ok(launch_clip_factor(grad, n, device_sms(), partial, factor, as_stream(stream)), "clip factor");
+    });
+}
+AIC_API aic_status aic_grad_clip_partials(int64_t n, int64_t* floats)
+{
+    return guarded([&] {
+        require(floats && n > 0, "bad arguments");
+        *floats = sumsq_blocks(n, device_sms());
+    });
+}
+AIC_API aic_status aic_sgd_update(float* data, const float* grad, int64_t n, const float* factor, float lr,
+                                  float penalty, void* stream)
+{
+    return guarded([&] {
+        require(data && grad && factor && n >= 0, "bad update arguments");
+        cuda_ok(launch_sgd_update(data, grad, n, factor, lr, penalty, as_stream(stream)), "sgd update");
+    });
+}
+AIC_API aic_status aic_residual_backward(float* grad_next, float* grad_res, int64_t n, float survival_prob_inv,
+                                         float residual_factor, void* stream)
+{
+    return guarded([&] {
+        require(n >= 0 && (n == 0 || (grad_next && grad_res)), "bad residual arguments");
+        cuda_ok(launch_residual_backward(grad_next, grad_res, n, survival_prob_inv, residual_factor, as_stream(stream)),
+                "residual backward");
+    });
+}
+AIC_API aic_status aic_conv_layer_train_bytes(aic_conv_layer l, size_t* bytes)
+{
+    return guarded([&] {
+        require(bytes != nullptr, "null output");
+        *bytes = handle<ConvLayer>(l, "conv layer")->train_bytes();
+    });
+}
+AIC_API aic_status aic_conv_layer_train_bind(aic_conv_layer l, void* buffer, const float* master, float learning_rate,
+                                             float penalty, void* stream)
+{
+    return guarded([&] { handle<ConvLayer>(l, "conv layer")->train_bind(buffer, master, learning_rate, penalty, as_stream(stream)); });
+}
+AIC_API aic_status aic_conv_layer_backward(aic_conv_layer l, const float* grad_out, const uint32_t* in,
+                                           const int8_t* in_s, float* grad_in, void* stream)
+{
+    return guarded([&] { handle<ConvLayer>(l, "conv layer")->backward(grad_out, in, in_s, grad_in, as_stream(stream)); });
+}
+AIC_API aic_status aic_conv_layer_train_views(aic_conv_layer l, float** master, float** grad_w, float** grad_b,
+                                              float** bias)
+{
+    return guarded([&] {
+        auto* c = handle<ConvLayer>(l, "conv layer");
+        if (!c->train.bound) fail(AIC_ERR_STATE, "conv layer training state not bound");
+        if (master) *master = c->train.master;
+        if (grad_w) *grad_w = c->train.gw;
+        if (grad_b) *grad_b = c->train.gb;
+        if (bias) *bias = c->bias;
+    });
+}
+AIC_API aic_status aic_mamba_layer_train_bytes(aic_mamba_layer l, size_t* bytes)
+{
+    return guarded([&] {
+        require(bytes != nullptr, "null output");
+        *bytes = handle<MambaLayer>(l, "mamba layer")->train_bytes();
+    });
+}
+AIC_API aic_status aic_mamba_layer_train_bind(aic_mamba_layer l, void* buffer, const float* master,
+                                              float learning_rate, float penalty, void* stream)
+{
+    return guarded([&] { handle<MambaLayer>(l, "mamba layer")->train_bind(buffer, master, learning_rate, penalty, as_stream(stream)); });
+}
+AIC_API aic_status aic_mamba_layer_backward(aic_mamba_layer l, const float* grad_out, const uint32_t* in,
+                                            const int8_t* in_s, float* grad_in, void* stream)
+{
+    return guarded([&] { handle<MambaLayer>(l, "mamba layer")->backward(grad_out, in, in_s, grad_in, as_stream(stream)); });
+}
+AIC_API aic_status aic_mamba_layer_train_views(aic_mamba_layer l, float** master, float** grad_w, float** grad_b,
+                                               float** bias)
+{
+    return guarded([&] {
+        auto* m = handle<MambaLayer>(l, "mamba layer");
+        if (!m->train.bound) fail(AIC_ERR_STATE, "mamba layer training state not bound");
+        if (master) *master = m->train.master;
+        if (grad_w) *grad_w = m->train.gw;
+        if (grad_b) *grad_b = m->train.gb;
+        if (bias) *bias = m->bias;
+    });
+}
+AIC_API aic_status aic_critic_train_bytes(aic_critic c, size_t* bytes)
+{
+    return guarded([&] {
+        require(bytes != nullptr, "null output");
+        *bytes = handle<Critic>(c, "critic")->train_bytes();
+    });
+}
+AIC_API aic_status aic_critic_train_bind(aic_critic c, void* buffer, float learning_rate, float penalty)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->train_bind(buffer, learning_rate, penalty); });
+}
+AIC_API aic_status aic_critic_backward(aic_critic c, const float* pred_score, float real_score, void* stream)
+{
+    return guarded([&] { handle<Critic>(c, "critic")->backward(pred_score, real_score, as_stream(stream)); });
+}
+AIC_API aic_status aic_critic_train_views(aic_critic c, float** grad_w1, float** grad_w2, float** grad_lambda)
+{
+    return guarded([&] {
+        auto* k = handle<Critic>(c, "critic");
+        if (!k->train.bound) fail(AIC_ERR_STATE, "critic training state not bound");
+        if (grad_w1) *grad_w1 = k->train.gw;
+        if (grad_w2) *grad_w2 = k->train.gb;
+        if (grad_lambda) *grad_lambda = k->train.gx;
+    });
 }
 
 }  // extern "C"

@@ -53,6 +53,19 @@ def _size_out() -> C.c_size_t:
     return C.c_size_t(0)
 
 
+def _train_views(fn: str, h, arena: "_Arena", counts) -> list:
+    """fp32 device views of the pointers a *_train_views entry point returns."""
+    ptrs = [C.c_void_p() for _ in counts]
+    call(fn, h, *[C.byref(p) for p in ptrs])
+    out = []
+    for p, n in zip(ptrs, counts):
+        if arena is not None and arena.raw.data_ptr() <= p.value < arena.raw.data_ptr() + arena.raw.numel():
+            out.append(arena.view(p.value, n, torch.float32))
+        else:
+            out.append(p.value)
+    return out
+
+
 def empty_f(rows: int, channels: int, device="cuda") -> tuple[torch.Tensor, torch.Tensor]:
     """Uninitialised packed int4 activation tensor pair for rows x channels."""
     return (torch.empty(rows, channels // 8, dtype=torch.int32, device=device),
@@ -131,6 +144,27 @@ class ConvLayer(_Handle):
         """Reference accumulation order on CUDA cores (bit-exact with the reference)."""
         call("aic_conv_layer_forward_exact", self.h, _vp(x), _vp(x_s), _vp(out), _vp(out_s), int(frames),
              _stream(stream))
+
+    def train_bind(self, master: torch.Tensor, learning_rate: float, penalty: float, stream=None) -> None:
+        """Training state (ConvLayer::backward): fp32 masters, gradients, SGD settings."""
+        assert master.dtype == torch.float32 and master.numel() == self.weight_elems and master.is_contiguous()
+        nb = _size_out()
+        call("aic_conv_layer_train_bytes", self.h, C.byref(nb))
+        self.train_state = _Arena(nb.value, self.device)
+        call("aic_conv_layer_train_bind", self.h, C.c_void_p(self.train_state.ptr), _vp(master), float(learning_rate),
+             float(penalty), _stream(stream))
+
+    def backward(self, grad_out: torch.Tensor, x, x_s, grad_in: Optional[torch.Tensor] = None, stream=None) -> None:
+        """One frame: gradients, clipped SGD on masters and biases, re-quantised weights.
+        grad_in (fp32 [dim_in^2 * in]) is added to (dense / pointwise) or written (depthwise)."""
+        call("aic_conv_layer_backward", self.h, _vp(grad_out), _vp(x), _vp(x_s),
+             _vp(grad_in) if grad_in is not None else None, _stream(stream))
+
+    def train_views(self):
+        """(master, grad_w, grad_b) fp32 device views and the bias pointer."""
+        m, gw, gb, b = _train_views("aic_conv_layer_train_views", self.h, self.train_state,
+                                    (self.weight_elems, self.weight_elems, self.bias_elems, self.bias_elems))
+        return m, gw, gb
 
 
 class ConvBlock(_Handle):
@@ -256,6 +290,32 @@ class MambaLayer(_Handle):
         E, Pn = 2 * self.desc.d_model, self.desc.d_state // 32
         n = 3 * self.batch * E * Pn * 2
         return self.traces.view(self.traces.ptr, n, torch.float32).view(3, self.batch, E, Pn, 2)
+
+    def train_bind(self, master: torch.Tensor, learning_rate: float, penalty: float, stream=None) -> None:
+        """Training state (MambaLayer::backward): fp32 master blob, gradients, SGD settings."""
+        assert master.dtype == torch.float32 and master.is_contiguous()
+        nb = _size_out()
+        call("aic_mamba_layer_train_bytes", self.h, C.byref(nb))
+        self.train_state = _Arena(nb.value, self.device)
+        self.blob_elems = master.numel()
+        call("aic_mamba_layer_train_bind", self.h, C.c_void_p(self.train_state.ptr), _vp(master),
+             float(learning_rate), float(penalty), _stream(stream))
+
+    def backward(self, grad_out: torch.Tensor, x, x_s, grad_in: torch.Tensor, stream=None) -> None:
+        """The step just run (batch 1, traces bound): gradients, clipped SGD, re-quantised blob."""
+        call("aic_mamba_layer_backward", self.h, _vp(grad_out), _vp(x), _vp(x_s), _vp(grad_in), _stream(stream))
+
+    def train_views(self):
+        """(master blob, grad blob, grad bias) fp32 device views."""
+        m, gw, gb, _ = _train_views("aic_mamba_layer_train_views", self.h, self.train_state,
+                                    (self.blob_elems, self.blob_elems, self.desc.out_channels, 0))
+        return m, gw, gb
+
+    def train_bias(self) -> torch.Tensor:
+        """The fp32 bias the backward updates, as a device view."""
+        b = C.c_void_p()
+        call("aic_mamba_layer_train_views", self.h, None, None, None, C.byref(b))
+        return self.params.view(b.value, self.desc.out_channels, torch.float32)
 
     def reset(self, stream=None) -> None:
         call("aic_mamba_layer_reset_state", self.h, _stream(stream))
@@ -427,6 +487,36 @@ class Critic(_Handle):
         call("aic_critic_forward", self.h, _vp(x), _vp(x_s), _vp(score), int(batch), int(seq),
              C.c_void_p(self._ws.ptr), _stream(stream))
 
+    def train_bind(self, learning_rate: float, penalty: float) -> None:
+        """Training state (Critic::backward): gradients and SGD settings; W1, W2 and
+        Wlambda are updated in place."""
+        nb = _size_out()
+        call("aic_critic_train_bytes", self.h, C.byref(nb))
+        self.train_state = _Arena(nb.value, self.device)
+        call("aic_critic_train_bind", self.h, C.c_void_p(self.train_state.ptr), float(learning_rate), float(penalty))
+
+    def backward(self, pred_score: torch.Tensor, real_score: float, stream=None) -> None:
+        """The step just run (batch 1, traces bound): pred_score the device score it wrote."""
+        call("aic_critic_backward", self.h, _vp(pred_score), float(real_score), _stream(stream))
+
+    def train_views(self):
+        """(grad_w1, grad_w2, grad_lambda) fp32 device views."""
+        n1 = 2 * self.desc.in_channels * self.desc.units
+        return tuple(_train_views("aic_critic_train_views", self.h, self.train_state, (n1, 2 * self.desc.units, n1)))
+
+    def weights(self):
+        """(w1, w2, wlambda) fp32 device views of the bound parameters (laid out
+        in order, each at a 256-byte boundary)."""
+        n1, n2 = 2 * self.desc.in_channels * self.desc.units, 2 * self.desc.units
+
+        def up(b):
+            return (b + 255) // 256 * 256
+        o2 = up(4 * n1)
+        o3 = up(o2 + 4 * n2)
+        base = self.params.ptr
+        return (self.params.view(base, n1, torch.float32), self.params.view(base + o2, n2, torch.float32),
+                self.params.view(base + o3, n1, torch.float32))
+
 
 class Cortex(_Handle):
     """Full forward: stem -> conv blocks -> GAP -> Mamba units -> actor (+ critic)."""
@@ -513,6 +603,31 @@ class Cortex(_Handle):
         n = C.c_int64()
         call("aic_cortex_last_launches", self.h, C.byref(n))
         return n.value
+
+
+def grad_clip_factor(grad: torch.Tensor, stream=None) -> torch.Tensor:
+    """[clip factor, square sum] of a gradient (clip_op of the layer classes), on the device."""
+    n = grad.numel()
+    nf = C.c_int64()
+    call("aic_grad_clip_partials", int(n), C.byref(nf))
+    partial = torch.empty(nf.value, dtype=torch.float32, device=grad.device)
+    factor = torch.empty(2, dtype=torch.float32, device=grad.device)
+    call("aic_grad_clip_factor", _vp(grad), int(n), _vp(partial), _vp(factor), _stream(stream))
+    return factor
+
+
+def sgd_update(data: torch.Tensor, grad: torch.Tensor, factor: torch.Tensor, learning_rate: float, penalty: float,
+               stream=None) -> None:
+    """updateParamsKernel: data = grad * (-lr * factor[0]) + data * (1 - lr * penalty), in place."""
+    call("aic_sgd_update", _vp(data), _vp(grad), int(data.numel()), _vp(factor), float(learning_rate), float(penalty),
+         _stream(stream))
+
+
+def residual_backward(grad_next: torch.Tensor, grad_res: torch.Tensor, survival_prob_inv: float,
+                      residual_factor: float, stream=None) -> None:
+    """residualAddBwdKernel: grad_res = grad_next; grad_next *= survival_prob_inv * residual_factor."""
+    call("aic_residual_backward", _vp(grad_next), _vp(grad_res), int(grad_next.numel()), float(survival_prob_inv),
+         float(residual_factor), _stream(stream))
 
 
 def pack_f32(x: torch.Tensor, stochastic=False, add_idx=0, stream=None):

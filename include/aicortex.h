@@ -440,6 +440,74 @@ AIC_API aic_status aic_cortex_profile_get(aic_cortex c, int site, char name[32],
 AIC_API aic_status aic_cortex_profile_reset(aic_cortex c);
 AIC_API aic_status aic_cortex_destroy(aic_cortex c);
 
+/* ---------------------------------------------------------------- training
+ * The reference's online training step, one layer at a time, as its layer
+ * classes' backward() run it: gradients of one frame (conv) or one env step
+ * (Mamba, critic), clip_op + updateParamsKernel on every parameter tensor
+ * (norm = sqrt(sum g^2 + epsilon), factor 1/norm above 1; data = g * (-lr *
+ * factor) + data * (1 - lr * penalty), biases with penalty 0), then the
+ * weights re-quantised from their fp32 masters (quantizeKernel, stochastic,
+ * add_idx = n). Replaces ConvLayer::backward (conv_layer.h:150-219),
+ * MambaLayer::backward (mamba_layer.h:146-167), Critic::backward
+ * (critic.h:117-131), residualAddBwdKernel (kernels.h:1056-1079) and
+ * updateParamsKernel (kernels.h:196-216). The gradients are the reference
+ * kernels' own formulas (kernels.h:283-988, 1260-1419, 1779-1805), including
+ * where they differ from the textbook gradient; the header of k_train.cu
+ * lists those and the inputs on which the reference reads unwritten memory. */
+
+/* Square-sum clip factor of a gradient: factor[0] = 1/norm above 1 else 1,
+ * factor[1] = sum g^2 (device floats). `partial` holds
+ * aic_grad_clip_partials(n) floats. The reference adds its block sums with
+ * atomics in arrival order; these are added in block order. */
+AIC_API aic_status aic_grad_clip_partials(int64_t n, int64_t* floats);
+AIC_API aic_status aic_grad_clip_factor(const float* grad, int64_t n, float* partial, float* factor, void* stream);
+/* updateParamsKernel with grad_norm_factor read from factor[0] (device). Like
+ * the reference, updates the first floor(n / 4) * 4 elements. */
+AIC_API aic_status aic_sgd_update(float* data, const float* grad, int64_t n, const float* factor, float lr,
+                                  float penalty, void* stream);
+/* grad_res = grad_next; grad_next *= survival_prob_inv * residual_factor. */
+AIC_API aic_status aic_residual_backward(float* grad_next, float* grad_res, int64_t n, float survival_prob_inv,
+                                         float residual_factor, void* stream);
+
+/* Training state of a conv layer: bytes of the 256-byte-aligned device buffer,
+ * and binding it with the fp32 master weights (weight layout of
+ * aic_conv_layer_load, device or host memory), from which the packed weights
+ * are re-derived. */
+AIC_API aic_status aic_conv_layer_train_bytes(aic_conv_layer l, size_t* bytes);
+AIC_API aic_status aic_conv_layer_train_bind(aic_conv_layer l, void* buffer, const float* master, float learning_rate,
+                                             float penalty, void* stream);
+/* One frame: grad_out fp32 [dim_out^2][out]; in / in_s the layer's forward
+ * input (F); grad_in fp32 [dim_in^2][in] is added to (pointwise and dense
+ * convs, the reference's atomic adds) or written (depthwise), or NULL.
+ * Pointwise convs need dim_out^2 % 32 == 0, depthwise dim_out^2 % 4 == 0. */
+AIC_API aic_status aic_conv_layer_backward(aic_conv_layer l, const float* grad_out, const uint32_t* in,
+                                           const int8_t* in_s, float* grad_in, void* stream);
+/* Device pointers into the training state (any may be NULL): masters,
+ * gradients of the last backward, and the fp32 biases. */
+AIC_API aic_status aic_conv_layer_train_views(aic_conv_layer l, float** master, float** grad_w, float** grad_b,
+                                              float** bias);
+
+/* Training state of a Mamba layer (master = the fp32 blob of
+ * aic_mamba_layer_load); d_model a multiple of 128. */
+AIC_API aic_status aic_mamba_layer_train_bytes(aic_mamba_layer l, size_t* bytes);
+AIC_API aic_status aic_mamba_layer_train_bind(aic_mamba_layer l, void* buffer, const float* master,
+                                              float learning_rate, float penalty, void* stream);
+/* The step just run: state bound for batch 1 with traces bound; in / in_s the
+ * step's input; grad_out fp32 [out]; grad_in fp32 [d_model] written. */
+AIC_API aic_status aic_mamba_layer_backward(aic_mamba_layer l, const float* grad_out, const uint32_t* in,
+                                            const int8_t* in_s, float* grad_in, void* stream);
+AIC_API aic_status aic_mamba_layer_train_views(aic_mamba_layer l, float** master, float** grad_w, float** grad_b,
+                                               float** bias);
+
+/* Training state of the critic (its weights are fp32 and updated in place);
+ * units a power of two. */
+AIC_API aic_status aic_critic_train_bytes(aic_critic c, size_t* bytes);
+AIC_API aic_status aic_critic_train_bind(aic_critic c, void* buffer, float learning_rate, float penalty);
+/* The step just run (batch 1, traces bound): pred_score the score it wrote
+ * (device pointer), real_score the target. */
+AIC_API aic_status aic_critic_backward(aic_critic c, const float* pred_score, float real_score, void* stream);
+AIC_API aic_status aic_critic_train_views(aic_critic c, float** grad_w1, float** grad_w2, float** grad_lambda);
+
 #ifdef __cplusplus
 }
 #endif

@@ -194,4 +194,115 @@ AICREF_API int aicref_augment(__half2* v, int pairs, float brightness, float con
     return aicref_status();
 }
 
+// ---- training path (F4)
+
+// updateParamsKernel, launched as conv_layer.h:214-216.
+AICREF_API int aicref_update_params(float* data, const float* grad, int n, float grad_norm_factor, float lr, float penalty)
+{
+    updateParamsKernel<><<<(n + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(data, grad, n, grad_norm_factor,
+                                                                                                 lr, penalty);
+    return aicref_status();
+}
+
+// universal_vector::transform_reduce(SquareOp) (uv.h:230-248) over a device
+// array: the same kernel and grid, result copied to *out.
+AICREF_API int aicref_sum_sq(const float* x, int n, float* out)
+{
+    static float* d_res = nullptr;
+    if (!d_res && cudaMalloc(&d_res, sizeof(float)) != cudaSuccess) return -1;
+    int dev = 0, sms = 0, tpm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&tpm, cudaDevAttrMaxThreadsPerMultiProcessor, dev);
+    size_t per_sm = tpm / gpu_block_threads;
+    if (per_sm < 1) per_sm = 1;
+    const size_t opt = sms * per_sm, need = (static_cast<size_t>(n) + gpu_block_threads - 1) / gpu_block_threads;
+    const size_t blocks = std::max<size_t>(1, std::min(opt, need));
+    cudaMemset(d_res, 0, sizeof(float));
+    transformReduceKernel<float, float, SquareOp<float>><<<blocks, gpu_block_threads>>>(x, d_res, SquareOp<float>{}, n);
+    if (cudaMemcpy(out, d_res, sizeof(float), cudaMemcpyDeviceToHost) != cudaSuccess) return -2;
+    return aicref_status();
+}
+
+// The gradient kernels of ConvLayer::backward (conv_layer.h:152-206), same
+// launch geometry; grad_in is accumulated into (dense / pointwise) or written
+// (depthwise) as the reference does.
+AICREF_API int aicref_conv_bwd(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s, const float* bias,
+                               const float* master, const float* grad_out, float* grad_in, float* gw, float* gb, int InC,
+                               int OutC, int ks, int stride, int Din, int Dout, int act)
+{
+    const int T = gpu_block_threads;
+    if (ks > 1 && (ks & 1)) {
+        dim3 grid_b((InC + T - 1) / T), grid_w(grid_b.x), grid_i(Din * Din, grid_b.x);
+        convDepthwiseBwdGradBiasKernel<><<<grid_b, T>>>(grad_out, gb, InC, Dout * Dout);
+#define AICREF_DWB(K) convDepthwiseBwdGradWeightKernel<K><<<grid_w, T>>>(in, in_s, grad_out, gw, InC, Din, Dout, stride); \
+                      convDepthwiseBwdGradInputKernel<K><<<grid_i, T>>>(grad_out, master, grad_in, InC, Din, Dout, stride)
+        if (ks == 3) { AICREF_DWB(3); } else if (ks == 5) { AICREF_DWB(5); } else if (ks == 7) { AICREF_DWB(7); } else return -1;
+#undef AICREF_DWB
+    } else if ((ks & 1) == 0) {
+        dim3 grid_b((OutC + T - 1) / T), grid_w((OutC + T - 1) / T, InC), grid_i(Dout * Dout, (OutC + T - 1) / T);
+#define AICREF_DB(NOACT, K) \
+    convDenseBwdGradBiasKernel<NOACT, K><<<grid_b, T>>>(in, in_s, w, w_s, bias, grad_out, gb, InC, OutC, Din, Dout, stride); \
+    convDenseBwdGradWeightKernel<NOACT, K><<<grid_w, T>>>(in, in_s, w, w_s, bias, grad_out, gw, InC, OutC, Din, Dout, stride); \
+    convDenseBwdGradInputKernel<NOACT, K><<<grid_i, T>>>(in, in_s, w, w_s, bias, grad_out, master, grad_in, InC, OutC, Din, Dout, stride)
+        if (ks == 2) { if (act) { AICREF_DB(false, 2); } else { AICREF_DB(true, 2); } }
+        else if (ks == 4) { if (act) { AICREF_DB(false, 4); } else { AICREF_DB(true, 4); } }
+        else return -1;
+#undef AICREF_DB
+    } else {
+        dim3 grid_b((OutC + T - 1) / T);
+        dim3 block_w(dim_block_pw_bwd_gw_size, dim_block_pw_bwd_gw_size);
+        dim3 grid_w(OutC / dim_block_pw_bwd_gw_size, InC / dim_block_pw_bwd_gw_size);
+        dim3 grid_in(Dout * Dout, grid_b.x);
+        const int nhw = Dout * Dout;
+        if (act) {
+            convPointwiseBwdGradBiasKernel<false><<<grid_b, T>>>(in, in_s, w, w_s, bias, grad_out, gb, InC, OutC, nhw);
+            convPointwiseBwdGradWeightKernel<false><<<grid_w, block_w>>>(in, in_s, w, w_s, bias, grad_out, gw, InC, OutC, nhw);
+            convPointwiseBwdGradInputKernel<false><<<grid_in, T>>>(in, in_s, w, w_s, bias, grad_out, master, grad_in, InC, OutC);
+        } else {
+            convPointwiseBwdGradBiasKernel<true><<<grid_b, T>>>(in, in_s, w, w_s, bias, grad_out, gb, InC, OutC, nhw);
+            convPointwiseBwdGradWeightKernel<true><<<grid_w, block_w>>>(in, in_s, w, w_s, bias, grad_out, gw, InC, OutC, nhw);
+            convPointwiseBwdGradInputKernel<true><<<grid_in, T>>>(in, in_s, w, w_s, bias, grad_out, master, grad_in, InC, OutC);
+        }
+    }
+    return aicref_status();
+}
+
+// conv_block.h:89 residualAddBwdKernel over dim x dim positions.
+AICREF_API int aicref_residual_bwd(float* grad_next, float* grad_res, int C, int dim, float survival_prob_inv, float residual_factor)
+{
+    residualAddBwdKernel<><<<dim3(dim, dim), gpu_block_threads>>>(grad_next, grad_res, C, dim, survival_prob_inv, residual_factor);
+    return aicref_status();
+}
+
+// The gradient kernels of MambaLayer::backward (mamba_layer.h:148-157); the
+// caller zeroes raw_out, gw, gb and grad_in first (:148-151).
+AICREF_API int aicref_mamba_bwd(const uint32_t* in, const int8_t* in_s, const float2* h, const float2* ta, const float2* tb,
+                                const float2* td, const float* master, const float* bias, const float* grad_out, float* raw_out,
+                                float* gw, float* gb, float* grad_in, int OutC, int act)
+{
+    dim3 proj_grid(OutC >> 5, mamba_d_inner / gpu_block_threads, 1);
+    mambaSSMBwdOutProjKernel<><<<proj_grid, gpu_block_threads>>>(in, in_s, h, master, raw_out, OutC);
+    const int act_grid = (OutC + gpu_block_threads - 1) / gpu_block_threads;
+    if (act == 0) mambaSSMBwdNormActKernel<0><<<act_grid, gpu_block_threads>>>(raw_out, bias, grad_out, gb, OutC);
+    else if (act == 1) mambaSSMBwdNormActKernel<1><<<act_grid, gpu_block_threads>>>(raw_out, bias, grad_out, gb, OutC);
+    else mambaSSMBwdNormActKernel<2><<<act_grid, gpu_block_threads>>>(raw_out, bias, grad_out, gb, OutC);
+    mambaSSMApplyTracesKernel<><<<mamba_d_inner / gpu_block_threads, gpu_block_threads>>>(in, in_s, raw_out, h, ta, tb, td, master,
+                                                                                         gw, grad_in, OutC);
+    return aicref_status();
+}
+
+// The gradient kernels of Critic::backward (critic.h:120-121); w1 / wl are
+// [in][units] / [units][in] complex, `out_channels` 2 * units.
+AICREF_API int aicref_critic_bwd(const float* w2, const float* trace_w1, const float* trace_l, const float* hidden, float* gw1,
+                                 float* gl, float* gw2, float pred, float real, int units, int in)
+{
+    const int real_size = 2 * units * in;
+    criticApplyTracesKernel<><<<((real_size >> 1) + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(
+        w2, trace_w1, trace_l, gw1, gl, pred, real, units, in);
+    criticOutputGradKernel<><<<(units + gpu_block_threads - 1) / gpu_block_threads, gpu_block_threads>>>(hidden, gw2, pred, real,
+                                                                                                         units);
+    return aicref_status();
+}
+
 AICREF_API int aicref_sync() { return (int)cudaDeviceSynchronize(); }

@@ -161,3 +161,46 @@ def screen_case():
     """A seeded BGRA8 frame of SCREEN_DIM^2 pixels."""
     rng = np.random.default_rng(1300)
     return rng.integers(0, 256, (SCREEN_DIM, SCREEN_DIM, 4), dtype=np.uint8)
+
+
+# ---- training path (one layer step of ConvLayer / MambaLayer / Critic ::backward)
+TRAIN_LR, TRAIN_PENALTY = 0.01, 1e-4
+# (name, in, out, k, stride, dim_in, dim_out, act). Shapes on which the
+# reference's backward kernels stay inside their buffers: pointwise with 256 or
+# 512 output channels (fewer read unwritten shared memory and past the master
+# weights), depthwise with 256 channels (fewer write past the gradients).
+CONV_BWD_CASES = (
+    ("pw_silu", 128, 256, 1, 1, 8, 8, 1),
+    ("pw_512", 256, 512, 1, 1, 8, 8, 0),
+    ("dense_k2", 64, 128, 2, 2, 16, 8, 0),
+    ("dense_k2_silu", 64, 256, 2, 2, 8, 4, 1),
+    ("dw_k3", 256, 256, 3, 2, 16, 8, 0),
+)
+
+
+def conv_bwd_case(name):
+    spec = next(c for c in CONV_BWD_CASES if c[0] == name)
+    _, cin, cout, k, st, din, dout, act = spec
+    rng = np.random.default_rng(900 + cin + 3 * cout + 7 * k)
+    dw = k > 1 and k % 2 == 1
+    master = W.conv_weights(rng, cin, cout, k, dw)
+    bias = W.bias(rng, cout)
+    x = rng.standard_normal((din * din, cin)).astype(np.float32)
+    grad_out = (rng.standard_normal((dout * dout, cout)) * 0.1).astype(np.float32)
+    return master, bias, x, grad_out
+
+
+MB_BWD_CASES = ((256, 1), (128, 2))  # (out channels, activation) of the Mamba layer step
+MB_BWD_T = 3
+
+
+def mamba_bwd_case(out_c, act):
+    rng = np.random.default_rng(1000 + out_c + act)
+    blob = W.mamba_blob(rng, SSM_D, 128, out_c, a_im=None)
+    bias = W.bias(rng, out_c)
+    x = rng.standard_normal((MB_BWD_T, SSM_D)).astype(np.float32)
+    grad_out = (rng.standard_normal(out_c) * 0.1).astype(np.float32)
+    return blob, bias, x, grad_out
+
+
+CRITIC_BWD_REAL = 0.5

@@ -30,7 +30,7 @@ sys.path.insert(0, str(HERE))
 import golden_specs as S  # noqa: E402
 
 REF_DIR = ROOT / "oracle" / "_ref"
-_NAMES = {"ssm", "critic", "train"}  # fixture groups that can be regenerated alone
+_NAMES = {"ssm", "critic", "train", "backward"}  # fixture groups that can be regenerated alone
 _dirs = [a for a in sys.argv[1:] if a not in _NAMES]
 OUT = Path(_dirs[0]) if _dirs else HERE
 DEV = torch.device("cuda")
@@ -52,9 +52,12 @@ class Dev:
         self.keep = []
 
     def put(self, a: np.ndarray) -> C.c_void_p:
+        return self.put_t(a)[1]
+
+    def put_t(self, a: np.ndarray) -> tuple[torch.Tensor, C.c_void_p]:
         t = torch.from_numpy(np.ascontiguousarray(a)).to(DEV)
         self.keep.append(t)
-        return C.c_void_p(t.data_ptr())
+        return t, C.c_void_p(t.data_ptr())
 
     def zeros(self, n: int, dtype) -> tuple[torch.Tensor, C.c_void_p]:
         t = torch.zeros(n, dtype=dtype, device=DEV)
@@ -321,6 +324,116 @@ def gen_conv_block_train(lib):
     save("conv_block_train", master_sha=np.array([S.sha(m) for m in masters]), x_w=xw, x_s=xs, **out)
 
 
+def _clip(sum_sq: float) -> float:
+    """clip_op (conv_layer.h:209-213) in fp32, as the host computes it."""
+    norm = np.sqrt(np.float32(sum_sq) + np.float32(1.0 / 8192.0), dtype=np.float32)
+    return float(np.float32(1.0) / norm) if norm > np.float32(1.0) else 1.0
+
+
+def _sum_sq(lib, ptr, n):
+    out = C.c_float(0.0)
+    run(lib, "aicref_sum_sq", ptr, C.c_int(n), C.byref(out))
+    return out.value
+
+
+def _update(lib, data_ptr, grad_ptr, n, factor, penalty):
+    run(lib, "aicref_update_params", data_ptr, grad_ptr, C.c_int(n), C.c_float(factor), C.c_float(S.TRAIN_LR),
+        C.c_float(penalty))
+
+
+def gen_backward_conv(lib):
+    """ConvLayer::backward (conv_layer.h:150-219) on one frame per case: the
+    reference's gradient kernels, its square-sum reduction, clip and update
+    kernels, and the re-quantisation of the masters."""
+    out = {}
+    for (name, cin, cout, k, st, din, dout, act) in S.CONV_BWD_CASES:
+        d = Dev()
+        master, bias, x, gout = S.conv_bwd_case(name)
+        w, s = pack_weights(lib, master)
+        xw, xs = act_f(lib, x)
+        (tm, pm), (tb, pb) = d.put_t(master), d.put_t(bias)
+        gw, pgw = d.zeros(master.size, torch.float32)
+        gb, pgb = d.zeros(cout, torch.float32)
+        gi, pgi = d.zeros(din * din * cin, torch.float32)
+        pw, ps = d.put(w), d.put(s)
+        run(lib, "aicref_conv_bwd", d.put(xw), d.put(xs), pw, ps, pb, pm, d.put(gout), pgi, pgw, pgb,
+            *map(C.c_int, (cin, cout, k, st, din, dout, act)))
+        sw, sb = _sum_sq(lib, pgw, master.size), _sum_sq(lib, pgb, cout)
+        out[f"{name}_gw"], out[f"{name}_gb"], out[f"{name}_gi"] = (gw.cpu().numpy(), gb.cpu().numpy(),
+                                                                   gi.cpu().numpy())
+        _update(lib, pm, pgw, master.size, _clip(sw), S.TRAIN_PENALTY)
+        _update(lib, pb, pgb, cout, _clip(sb), 0.0)
+        nw, ns = d.zeros(master.size // 8, torch.int32), d.zeros(master.size // 32, torch.int8)
+        run(lib, "aicref_quantize_f32", pm, nw[1], ns[1], C.c_int(master.size), C.c_int(1), C.c_int(master.size))
+        out[f"{name}_sums"] = np.array([sw, sb], np.float32)
+        out[f"{name}_master"], out[f"{name}_bias"] = tm.cpu().numpy(), tb.cpu().numpy()
+        out[f"{name}_w"], out[f"{name}_s"] = u32(nw[0]), ns[0].cpu().numpy()
+        out[f"{name}_xw"], out[f"{name}_xs"] = xw, xs
+    save("backward_conv", **out)
+
+
+def gen_backward_mamba():
+    """MambaLayer::backward (mamba_layer.h:146-167) after MB_BWD_T training
+    forward steps from zero state (traces advancing), per case."""
+    lib = ref(S.SSM_D, 128)
+    D, N, E = S.SSM_D, 128, 2 * S.SSM_D
+    out = {}
+    for out_c, act in S.MB_BWD_CASES:
+        d = Dev()
+        blob, bias, x, gout = S.mamba_bwd_case(out_c, act)
+        bw, bs = pack_weights(lib, blob)
+        pbw, pbs = d.put(bw), d.put(bs)
+        st = [d.zeros(E * N * 2, torch.float32)[1] for _ in range(4)]
+        _, py = d.zeros(E, torch.float32)
+        xw, xs = act_f(lib, x)
+        ins = [(d.put(xw[t]), d.put(xs[t])) for t in range(S.MB_BWD_T)]
+        for t in range(S.MB_BWD_T):
+            run(lib, "aicref_ssm_step", ins[t][0], ins[t][1], pbw, pbs, *st, py)
+        (tm, pm), (tb, pb) = d.put_t(blob), d.put_t(bias)
+        _, praw = d.zeros(out_c, torch.float32)
+        gw, pgw = d.zeros(blob.size, torch.float32)
+        gb, pgb = d.zeros(out_c, torch.float32)
+        gi, pgi = d.zeros(D, torch.float32)
+        run(lib, "aicref_mamba_bwd", ins[-1][0], ins[-1][1], st[0], st[1], st[2], st[3], pm, pb, d.put(gout), praw, pgw,
+            pgb, pgi, C.c_int(out_c), C.c_int(act))
+        sw, sb = _sum_sq(lib, pgw, blob.size), _sum_sq(lib, pgb, out_c)
+        tag = f"o{out_c}_a{act}"
+        out[f"{tag}_gw"], out[f"{tag}_gb"], out[f"{tag}_gi"] = gw.cpu().numpy(), gb.cpu().numpy(), gi.cpu().numpy()
+        _update(lib, pm, pgw, blob.size, _clip(sw), S.TRAIN_PENALTY)
+        _update(lib, pb, pgb, out_c, _clip(sb), 0.0)
+        out[f"{tag}_sums"] = np.array([sw, sb], np.float32)
+        out[f"{tag}_master"], out[f"{tag}_bias"] = tm.cpu().numpy(), tb.cpu().numpy()
+        out[f"{tag}_xw"], out[f"{tag}_xs"] = xw, xs
+    save("backward_mamba_N128", **out)
+
+
+def gen_backward_critic(lib):
+    """Critic::backward (critic.h:117-131) after the critic fixture's steps."""
+    d = Dev()
+    w1, w2, wl, x = S.critic_case()
+    T, cin, units = x.shape[0], 32, 128
+    h, ph = d.zeros(2 * units, torch.float32)
+    tw, ptw = d.zeros(cin * units * 2, torch.float32)
+    tl, ptl = d.zeros(cin * units * 2, torch.float32)
+    score, psc = d.zeros(1, torch.float32)
+    (t1, pw1), (t2, pw2), (tlw, pwl) = d.put_t(w1), d.put_t(w2), d.put_t(wl)
+    for t in range(T):
+        run(lib, "aicref_critic", d.put(x[t]), pw1, pwl, pw2, ph, ptw, ptl, psc, C.c_int(units), C.c_int(cin))
+    pred = float(score.cpu().numpy()[0])
+    g1, pg1 = d.zeros(w1.size, torch.float32)
+    gl, pgl = d.zeros(wl.size, torch.float32)
+    g2, pg2 = d.zeros(w2.size, torch.float32)
+    run(lib, "aicref_critic_bwd", pw2, ptw, ptl, ph, pg1, pgl, pg2, C.c_float(pred), C.c_float(S.CRITIC_BWD_REAL),
+        C.c_int(units), C.c_int(cin))
+    s1, s2, sl = _sum_sq(lib, pg1, w1.size), _sum_sq(lib, pg2, w2.size), _sum_sq(lib, pgl, wl.size)
+    grads = dict(gw1=g1.cpu().numpy(), gw2=g2.cpu().numpy(), gl=gl.cpu().numpy())
+    _update(lib, pw1, pg1, w1.size, _clip(s1), S.TRAIN_PENALTY)
+    _update(lib, pw2, pg2, w2.size, _clip(s2), S.TRAIN_PENALTY)
+    _update(lib, pwl, pgl, wl.size, _clip(sl), S.TRAIN_PENALTY)
+    save("backward_critic", pred=np.array([pred], np.float32), sums=np.array([s1, s2, sl], np.float32), **grads,
+         w1_after=t1.cpu().numpy(), w2_after=t2.cpu().numpy(), wl_after=tlw.cpu().numpy())
+
+
 def gen_conv_block(lib):
     """ConvBlock::forward (conv_block.h:74-82, inference) on one frame."""
     d = Dev()
@@ -422,6 +535,10 @@ def main():
                 gen_ssm(n)
         if "critic" in only:
             gen_critic(ref(256, 128))
+        if "backward" in only:
+            gen_backward_conv(ref(256, 128))
+            gen_backward_mamba()
+            gen_backward_critic(ref(256, 128))
         if "train" in only:
             gen_mamba_block_train()
             gen_conv_block_train(ref(256, 128))
@@ -441,6 +558,9 @@ def main():
     gen_mamba_block_train()
     gen_conv_block_train(lib)
     gen_critic(lib)
+    gen_backward_conv(lib)
+    gen_backward_mamba()
+    gen_backward_critic(lib)
     gen_actions(lib)
 
 
