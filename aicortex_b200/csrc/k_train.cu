@@ -11,7 +11,7 @@
 //    y + 32 by of position p0 + y with output gradient of position p0 + k and
 //    takes inv_rms from a 32-channel x 8-position square sum;
 //  * Mamba's out-projection recompute reduces its 8-lane partial sums with
-//    absolute-lane shuffles (kernels.h:1295), which mix in lanes 1, 2 and 4.
+//    absolute-lane shuffles (kernels.h:1299), which mix in lanes 1, 2 and 4.
 // Where the reference reads memory it did not write (pointwise input gradient
 // with fewer than 256 output channels, depthwise weight / bias gradients with
 // fewer than 256 channels, positions past the frame), the kernels here skip
