@@ -174,9 +174,12 @@ AIC_API aic_status aic_conv_layer_forward_exact(aic_conv_layer l, const uint32_t
  *       dots; the fp32 accumulation over groups follows the reference order,
  *       so outputs are bit-identical to the reference (the 4x4 dense conv
  *       runs as AIC_CONV_SIMT);
- *   AIC_CONV_FAST  tensor cores accumulate all of K in fp32 in MMA order;
- *       equal to the reference up to fp32 summation order (a requant code
- *       flips only where a value sits on a rounding boundary);
+ *   AIC_CONV_FAST  NOT a parity mode: tensor cores accumulate all of K in
+ *       fp32 in MMA order. A layer matches the reference up to that summation
+ *       order (a requant code flips where a value sits on a rounding boundary,
+ *       about 1e-4 of the codes), but the flips propagate through the stack:
+ *       end to end the features drift (mean error ~0.1 of their scale), so
+ *       only use it where the reference's bits do not matter;
  *   AIC_CONV_SIMT  CUDA cores, reference order (bit-identical). */
 #define AIC_CONV_ORDERED 0
 #define AIC_CONV_FAST 1

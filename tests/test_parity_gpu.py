@@ -581,6 +581,8 @@ def test_cortex_small_vs_oracle():
     assert_close(critic, c_ref, rtol=1e-3, what="critic (reference order)")
     for x, y, name in zip(outs[A.AIC_CONV_ORDERED], outs[A.AIC_CONV_SIMT], ("words", "exponents", "actor", "critic")):
         assert np.array_equal(x, y), f"tensor cores (reference order) vs CUDA cores: {name} differ"
+    # AIC_CONV_FAST is not a parity mode (its per-layer summation-order flips
+    # propagate): only a loose agreement with the reference order is checked
     fw2, fs2 = outs[A.AIC_CONV_FAST][:2]
     a, r = fmt.dequant(fw2, fs2).astype(np.float64).ravel(), fmt.dequant(fw, fs).astype(np.float64).ravel()
     rel = np.abs(a - r).mean() / np.abs(r).mean()
