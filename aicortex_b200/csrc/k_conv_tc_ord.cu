@@ -440,8 +440,12 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
     }
     if (live) {
         // every MMA this CTA issued has completed before TMEM is released
+        // A timeout here (error 13 recorded) means an MMA has not completed within
+        // the wait's limit; one more bounded wait gives it a second window before
+        // TMEM is released. The outputs of such a launch are undefined and the host
+        // learns of it through the error word.
         if (tid == 0) mma_commit(smem_addr(&bars[4]));
-        if (warp == 0) mbar_wait(smem_addr(&bars[4]), 0u, p.err, 13);
+        if (warp == 0 && !mbar_wait(smem_addr(&bars[4]), 0u, p.err, 13)) mbar_wait(smem_addr(&bars[4]), 0u, p.err, 13);
         tc_fence_before();
         __syncthreads();
         if (warp == 0) {
@@ -836,9 +840,10 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
                 if (++sp == S) sp = 0;
             }
             // every MMA issued has completed (and the weight copy landed) before TMEM is released
+            // (a timeout records 37 / 34; the drain gets a second bounded window, as above)
             mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 37);
             mma_commit(smem_addr(drain));
-            mbar_wait(smem_addr(drain), 0u, p.err, 34);
+            if (!mbar_wait(smem_addr(drain), 0u, p.err, 34)) mbar_wait(smem_addr(drain), 0u, p.err, 34);
         }
     } else if (warp >= kWsConsumerWarps) {
         // ------------------------------------------------------------ staging

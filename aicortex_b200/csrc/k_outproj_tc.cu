@@ -169,9 +169,10 @@ __global__ void __launch_bounds__(kOpThreads, 1)
                 }
                 mma_commit(smem_addr(&acc_full[ab]));
             }
-            // every MMA this CTA issued has completed before TMEM is released
+            // every MMA this CTA issued has completed before TMEM is released (a
+            // timeout records 44 and gets one more bounded window)
             mma_commit(smem_addr(drain));
-            mbar_wait(smem_addr(drain), 0u, p.err, 44);
+            if (!mbar_wait(smem_addr(drain), 0u, p.err, 44)) mbar_wait(smem_addr(drain), 0u, p.err, 44);
         }
     } else {
         const int q = warp & 3;  // this warp's quarter of the TMEM lanes

@@ -22,10 +22,19 @@
  * compile-time final_channels and mamba_d_state (base_constants.h); define
  * AIC_LAYERS_D_MODEL / AIC_LAYERS_D_STATE to give them without that header.
  *
+ * Training: ConvLayer, MambaLayer and Critic keep the reference's backward()
+ * (conv_layer.h:150, mamba_layer.h:146, critic.h:117) over the C ABI's layer
+ * backward. Their training state (fp32 master copy on the device, gradients,
+ * scratch) is counted into the main device arena by every constructor, since
+ * only initData learns whether the layer trains, and is bound when
+ * is_in_inference is false (the critic always trains, as in the reference).
+ * After each backward the updated masters are copied back into the host
+ * arena, where the reference's update kernel writes them.
+ *
  * Differences from the reference classes: errors (status codes of the C ABI)
  * are thrown as std::runtime_error with aic_last_error()'s message, as the
- * reference's checkCudaError does; the training-only members (gradients,
- * backward, saveToFile) are not provided; a short checkpoint file is an
+ * reference's checkCudaError does; the block-level backward (ConvBlock,
+ * MambaBlock) and saveToFile are not provided; a short checkpoint file is an
  * error (the reference reads it silently); weights drawn when no checkpoint
  * is loaded come from a seeded std::mt19937 (the reference's generator
  * hashes thread indices and is not reproducible).
@@ -110,30 +119,35 @@ struct DeviceSpan {
 // ---------------------------------------------------------------- ConvLayer
 class ConvLayer {
     aic_conv_layer h_ = nullptr;
-    cudaStream_t stream_forward;
+    cudaStream_t stream_forward, stream_backward;
     int in_channels, out_channels, kernel_size;
     bool is_dw, disable_activation;
     int64_t weight_elems = 0;
-    size_t param_bytes = 0;
+    size_t param_bytes = 0, train_bytes = 0;
+    float learning_rate, f_penalty;
     float* master_weights = nullptr;  // host arena view
+    float* master_dev = nullptr;      // the training state's device copy
+    bool training = false;
     std::vector<float> bias_host;
 
 public:
     ConvLayer(int inChannels, int outChannels, int kernelSize, int str_ide, int in_dimension, int out_dimension,
-              cudaStream_t stream_fwd, int* total_size_grad_weights, int* total_size_grad_biases, cudaStream_t,
-              float, float, size_t* total_mem_main_device, size_t* total_mem_main_host, size_t* total_learnable_data,
-              size_t* total_learnable_data_count, bool is_activation_disabled = false)
-        : stream_forward(stream_fwd), in_channels(inChannels), out_channels(outChannels), kernel_size(kernelSize),
-          is_dw(kernelSize > 1 && (kernelSize & 1) == 1), disable_activation(is_activation_disabled)
+              cudaStream_t stream_fwd, int* total_size_grad_weights, int* total_size_grad_biases, cudaStream_t stream_bwd,
+              float learningRate, float penalty, size_t* total_mem_main_device, size_t* total_mem_main_host,
+              size_t* total_learnable_data, size_t* total_learnable_data_count, bool is_activation_disabled = false)
+        : stream_forward(stream_fwd), stream_backward(stream_bwd), in_channels(inChannels), out_channels(outChannels),
+          kernel_size(kernelSize), is_dw(kernelSize > 1 && (kernelSize & 1) == 1),
+          disable_activation(is_activation_disabled), learning_rate(learningRate), f_penalty(penalty)
     {
         const aic_conv_layer_desc d{inChannels, outChannels, kernelSize, str_ide, in_dimension, out_dimension,
                                     is_activation_disabled ? 1 : 0};
         check(aic_conv_layer_create(&d, &h_));
         int64_t be = 0;
         check(aic_conv_layer_sizes(h_, &weight_elems, &be, &param_bytes));
+        check(aic_conv_layer_train_bytes(h_, &train_bytes));
         if (*total_size_grad_weights < weight_elems) *total_size_grad_weights = static_cast<int>(weight_elems);
         if (*total_size_grad_biases < out_channels) *total_size_grad_biases = out_channels;
-        *total_mem_main_device += carve_bytes(param_bytes);
+        *total_mem_main_device += carve_bytes(param_bytes) + carve_bytes(train_bytes);
         *total_mem_main_host += align16(static_cast<size_t>(weight_elems) * sizeof(float));
         if (total_learnable_data) *total_learnable_data += static_cast<size_t>(weight_elems) + out_channels;
         if (total_learnable_data_count) *total_learnable_data_count += 2;
@@ -147,9 +161,41 @@ public:
     aic_conv_layer handle() const { return h_; }
 
     void initData(bool isLoaded, std::string dir_path, uint8_t*& current_dev_main_ptr, uint8_t*& current_host_main_ptr,
-                  uint8_t*&, uint8_t*&, bool, float***, size_t**, int, int)
+                  uint8_t*&, uint8_t*&, bool is_in_inference, float*** meta_adapted_data, size_t** meta_adapted_offsets,
+                  int, int)
     {
         check(aic_conv_layer_bind(h_, carve(current_dev_main_ptr, param_bytes)));
+        void* train_buf = carve(current_dev_main_ptr, train_bytes);
+        init_weights(isLoaded, dir_path, current_host_main_ptr);
+        if (is_in_inference) return;
+        // conv_layer.h:82-92: the training state, and the parameter list of the meta-learner
+        check(aic_conv_layer_train_bind(h_, train_buf, master_weights, learning_rate, f_penalty, stream_backward));
+        check_cuda(cudaStreamSynchronize(stream_backward));
+        float* bias_dev = nullptr;
+        check(aic_conv_layer_train_views(h_, &master_dev, nullptr, nullptr, &bias_dev));
+        training = true;
+        if (meta_adapted_data && *meta_adapted_data) {
+            *(*meta_adapted_data)++ = master_weights;
+            *(*meta_adapted_data)++ = bias_dev;
+        }
+        if (meta_adapted_offsets && *meta_adapted_offsets) {
+            *(*meta_adapted_offsets)++ = static_cast<size_t>(weight_elems);
+            *(*meta_adapted_offsets)++ = static_cast<size_t>(out_channels);
+        }
+    }
+    // conv_layer.h:150-219: one frame; grad_input is added to (pointwise and
+    // dense convs) or written (depthwise), as the reference's kernels do
+    void backward(const float* grad_output, const uint32_t* input, const int8_t* input_scales, float* grad_input)
+    {
+        if (!training) throw std::runtime_error("[aicortex_b200] ConvLayer::backward needs initData in training mode");
+        check(aic_conv_layer_backward(h_, grad_output, input, input_scales, grad_input, stream_backward));
+        check_cuda(cudaMemcpyAsync(master_weights, master_dev, static_cast<size_t>(weight_elems) * sizeof(float),
+                                   cudaMemcpyDeviceToHost, stream_backward));
+    }
+
+private:
+    void init_weights(bool isLoaded, const std::string& dir_path, uint8_t*& current_host_main_ptr)
+    {
         master_weights = reinterpret_cast<float*>(
             carve_host(current_host_main_ptr, static_cast<size_t>(weight_elems) * sizeof(float)));
         bias_host.assign(out_channels, 0.0f);
@@ -163,6 +209,8 @@ public:
             check_cuda(cudaStreamSynchronize(stream_forward));
         }
     }
+
+public:
     // conv_layer.h:31-44: fp32 master weights then fp32 bias; packed bit-exactly
     void loadFromFile(std::string pathFile)
     {
@@ -284,11 +332,14 @@ public:
 // ---------------------------------------------------------------- MambaLayer
 class MambaLayer {
     aic_mamba_layer h_ = nullptr;
-    cudaStream_t stream_forward;
+    cudaStream_t stream_forward, stream_backward;
     int out_channels;
     int64_t weight_elems = 0;
-    size_t param_bytes = 0, state_bytes = 0, ws_bytes = 0, trace_bytes = 0;
+    size_t param_bytes = 0, state_bytes = 0, ws_bytes = 0, trace_bytes = 0, train_bytes = 0;
+    float learning_rate, f_penalty;
     float* master_weights = nullptr;
+    float* master_dev = nullptr;
+    bool training = false;
     std::vector<float> bias_host;
     DeviceSpan<float> mamba_output;
     void* workspace = nullptr;
@@ -297,9 +348,11 @@ public:
     static constexpr int d_model = AIC_LAYERS_D_MODEL, d_state = AIC_LAYERS_D_STATE;
 
     MambaLayer(int output_channels, cudaStream_t stream_fwd, int* total_size_grad_weights, int* total_size_grad_biases,
-               cudaStream_t, float, float, size_t* total_mem_device, size_t* total_mem_host,
-               size_t* total_learnable_data, size_t* total_learnable_data_count, int type_activation)
-        : stream_forward(stream_fwd), out_channels(output_channels)
+               cudaStream_t stream_bwd, float learningRate, float penalty, size_t* total_mem_device,
+               size_t* total_mem_host, size_t* total_learnable_data, size_t* total_learnable_data_count,
+               int type_activation)
+        : stream_forward(stream_fwd), stream_backward(stream_bwd), out_channels(output_channels),
+          learning_rate(learningRate), f_penalty(penalty)
     {
         const aic_mamba_layer_desc d{d_model, d_state, output_channels, type_activation};
         check(aic_mamba_layer_create(&d, &h_));
@@ -312,11 +365,13 @@ public:
         check(aic_mamba_layer_state_bytes(h_, 1, &state_bytes));
         check(aic_mamba_layer_workspace_bytes(h_, 1, &ws_bytes));
         check(aic_mamba_layer_trace_bytes(h_, 1, &trace_bytes));
+        check(aic_mamba_layer_train_bytes(h_, &train_bytes));
         if (*total_size_grad_weights < weight_elems) *total_size_grad_weights = static_cast<int>(weight_elems);
         if (*total_size_grad_biases < out_channels) *total_size_grad_biases = out_channels;
-        // mamba_layer.h:68: output, parameters, state and y_ssm in the main device arena
+        // mamba_layer.h:68: output, parameters, state and y_ssm in the main device
+        // arena; then the training state
         *total_mem_device += carve_bytes(out_channels * sizeof(float)) + carve_bytes(param_bytes) +
-                             carve_bytes(state_bytes) + carve_bytes(ws_bytes);
+                             carve_bytes(state_bytes) + carve_bytes(ws_bytes) + carve_bytes(train_bytes);
         *total_mem_host += align16(static_cast<size_t>(weight_elems) * sizeof(float));
         if (total_learnable_data) *total_learnable_data += static_cast<size_t>(weight_elems) + out_channels;
         if (total_learnable_data_count) *total_learnable_data_count += 2;
@@ -341,11 +396,33 @@ public:
         check(aic_mamba_layer_bind(h_, carve(current_dev_main_ptr, param_bytes)));
         check(aic_mamba_layer_bind_state(h_, carve(current_dev_main_ptr, state_bytes), 1));
         workspace = carve(current_dev_main_ptr, ws_bytes);
+        void* train_buf = carve(current_dev_main_ptr, train_bytes);
         if (!is_in_inference) check(aic_mamba_layer_bind_traces(h_, carve(current_dev_side_ptr, trace_bytes), 1));
         master_weights = reinterpret_cast<float*>(
             carve_host(current_host_main_ptr, static_cast<size_t>(weight_elems) * sizeof(float)));
         bias_host.assign(out_channels, 0.0f);
         reset(stream_forward);
+        init_weights(isLoaded, dir_path);
+        if (is_in_inference) return;
+        check(aic_mamba_layer_train_bind(h_, train_buf, master_weights, learning_rate, f_penalty, stream_backward));
+        check_cuda(cudaStreamSynchronize(stream_backward));
+        check(aic_mamba_layer_train_views(h_, &master_dev, nullptr, nullptr, nullptr));
+        training = true;
+    }
+    // mamba_layer.h:146-167: the step just run; grad_input (the reference's
+    // universal_vector, or anything with data()) receives d_model floats
+    template <class Vec>
+    void backward(const float* grad_output, const uint32_t* input, const int8_t* input_scales, Vec& grad_input)
+    {
+        if (!training) throw std::runtime_error("[aicortex_b200] MambaLayer::backward needs initData in training mode");
+        check(aic_mamba_layer_backward(h_, grad_output, input, input_scales, grad_input.data(), stream_backward));
+        check_cuda(cudaMemcpyAsync(master_weights, master_dev, static_cast<size_t>(weight_elems) * sizeof(float),
+                                   cudaMemcpyDeviceToHost, stream_backward));
+    }
+
+private:
+    void init_weights(bool isLoaded, const std::string& dir_path)
+    {
         if (isLoaded) {
             loadFromFile(dir_path);
             return;
@@ -369,6 +446,8 @@ public:
         check(aic_mamba_layer_load_weights(h_, master_weights, bias_host.data(), stream_forward));
         check_cuda(cudaStreamSynchronize(stream_forward));
     }
+
+public:
     // mamba_layer.h:40-53
     void loadFromFile(std::string pathFile)
     {
@@ -480,27 +559,34 @@ public:
 // ---------------------------------------------------------------- Critic
 class Critic {
     aic_critic h_ = nullptr;
-    cudaStream_t stream_forward;
+    cudaStream_t stream_forward, stream_backward;
     int in_channels, units;
-    size_t param_bytes = 0, state_bytes = 0, ws_bytes = 0;
+    size_t param_bytes = 0, state_bytes = 0, ws_bytes = 0, trace_bytes = 0, train_bytes = 0;
+    float learning_rate, f_penalty;
     float* score_dev = nullptr;
     void* workspace = nullptr;
     float score_host = 0.0f;
 
 public:
     Critic(int inChannels, int outChannels, int in_dimension, cudaStream_t stream_fwd, int* total_size_grad_weights,
-           int* total_size_grad_biases, cudaStream_t, float, float, size_t* total_mem_main_device)
-        : stream_forward(stream_fwd), in_channels(inChannels), units(outChannels / 2)
+           int* total_size_grad_biases, cudaStream_t stream_bwd, float learningRate, float penalty,
+           size_t* total_mem_main_device)
+        : stream_forward(stream_fwd), stream_backward(stream_bwd), in_channels(inChannels), units(outChannels / 2),
+          learning_rate(learningRate), f_penalty(penalty)
     {
         const aic_critic_desc d{inChannels, units, in_dimension};
         check(aic_critic_create(&d, &h_));
         check(aic_critic_param_bytes(h_, &param_bytes));
         check(aic_critic_state_bytes(h_, 1, &state_bytes));
         check(aic_critic_workspace_bytes(h_, 1, &ws_bytes));
+        check(aic_critic_trace_bytes(h_, 1, &trace_bytes));
+        check(aic_critic_train_bytes(h_, &train_bytes));
         if (*total_size_grad_weights < inChannels * outChannels) *total_size_grad_weights = inChannels * outChannels;
         if (*total_size_grad_biases < outChannels) *total_size_grad_biases = outChannels;
+        // critic.h:68: parameters, traces and gradients in the main device arena (the
+        // reference's critic always keeps its traces and trains)
         *total_mem_main_device += carve_bytes(param_bytes) + carve_bytes(state_bytes) + carve_bytes(ws_bytes) +
-                                  carve_bytes(sizeof(float));
+                                  carve_bytes(sizeof(float)) + carve_bytes(trace_bytes) + carve_bytes(train_bytes);
     }
     Critic(const Critic&) = delete;
     Critic& operator=(const Critic&) = delete;
@@ -518,6 +604,11 @@ public:
         check(aic_critic_bind_state(h_, carve(current_dev_main_ptr, state_bytes), 1));
         workspace = carve(current_dev_main_ptr, ws_bytes);
         score_dev = reinterpret_cast<float*>(carve(current_dev_main_ptr, sizeof(float)));
+        check(aic_critic_bind_traces(h_, carve(current_dev_main_ptr, trace_bytes), 1));
+        if (units & (units - 1))  // the reference's backward indexes units with a mask (kernels.h:1786)
+            current_dev_main_ptr += carve_bytes(train_bytes);
+        else
+            check(aic_critic_train_bind(h_, carve(current_dev_main_ptr, train_bytes), learning_rate, f_penalty));
         reset(stream_forward);
         if (isLoaded) {
             loadFromFile(dir_path);
@@ -541,6 +632,8 @@ public:
         check_cuda(cudaStreamSynchronize(stream_forward));
     }
     void reset(cudaStream_t stream_lnk = 0) { check(aic_critic_reset_state(h_, stream_lnk)); }
+    // critic.h:117-131: against the last forward's score
+    void backward(float real_score) { check(aic_critic_backward(h_, score_dev, real_score, stream_backward)); }
 };
 
 }  // namespace aic_dropin

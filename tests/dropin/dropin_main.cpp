@@ -13,6 +13,15 @@
 //   critic in units dim steps
 // Inputs <dir>/{conv,mamba,critic}_in_{w,s}.bin, checkpoints <dir>/conv_block/,
 // <dir>/mamba_block/, <dir>/critic.bin; outputs <dir>/*_out*.bin.
+//
+// With <dir>/train_spec.txt it also trains one ConvLayer frame and one
+// MambaLayer step through the classes' backward (conv_layer.h:150,
+// mamba_layer.h:146) in training mode (is_in_inference = false):
+//   convtrain in out k stride din dout act lr penalty
+//   mambatrain steps out activation lr penalty
+// Inputs train_conv.bin / train_mamba.bin (checkpoints), train_conv_in_{w,s},
+// train_conv_gout, train_mamba_in_{w,s}, train_mamba_gout; outputs
+// train_{conv,mamba}_gin.bin and the host masters train_{conv,mamba}_master.bin.
 #include <cstdio>
 #include <fstream>
 #include <iostream>
@@ -149,6 +158,64 @@ int main(int argc, char** argv)
                 scores[t] = critic.get_score_output();
             }
             write_file(dir + "/critic_out.bin", scores.data(), scores.size() * 4);
+        }
+        std::ifstream tspec(dir + "/train_spec.txt");
+        if (tspec) {
+            int tci, tco, tk, tst, tdi, tdo, tact, msteps, mo, ma;
+            float clr, cpen, mlr, mpen;
+            tspec >> tag >> tci >> tco >> tk >> tst >> tdi >> tdo >> tact >> clr >> cpen;
+            tspec >> tag >> msteps >> mo >> ma >> mlr >> mpen;
+            if (!tspec) throw std::runtime_error("bad train_spec.txt");
+            int gw = 0, gb = 0;
+            size_t tdev = 0, thost = 0;
+            ConvLayer layer(tci, tco, tk, tst, tdi, tdo, stream, &gw, &gb, stream, clr, cpen, &tdev, &thost, nullptr,
+                            nullptr, tact == 0);
+            MambaLayer ml(mo, stream, &gw, &gb, stream, mlr, mpen, &tdev, &thost, nullptr, nullptr, ma);
+            uint8_t *tdev_base = nullptr, *thost_base = nullptr, *side = nullptr;
+            aic_dropin::check_cuda(cudaMalloc(&tdev_base, tdev + 16));
+            aic_dropin::check_cuda(cudaMallocHost(&thost_base, thost + 16));
+            aic_dropin::check_cuda(cudaMalloc(&side, 64u << 20));  // traces (side arena)
+            uint8_t *d = tdev_base, *h = thost_base, *sd = side, *unused = nullptr;
+            float** no_data = nullptr;
+            size_t* no_offsets = nullptr;
+            layer.initData(true, dir + "/train_conv.bin", d, h, unused, unused, false, &no_data, &no_offsets, gw, gb);
+            ml.initData(true, dir + "/train_mamba.bin", d, h, sd, unused, unused, false, &no_data, &no_offsets, gw, gb);
+            if (d > tdev_base + tdev + 16 || h > thost_base + thost + 16)
+                throw std::runtime_error("initData carved past the counted training arena");
+            // the conv layer: one frame, grad_in accumulated into zeros
+            auto* cin_w = to_device<uint32_t>(read_file(dir + "/train_conv_in_w.bin"));
+            auto* cin_s = to_device<int8_t>(read_file(dir + "/train_conv_in_s.bin"));
+            auto* cgout = to_device<float>(read_file(dir + "/train_conv_gout.bin"));
+            const size_t n_in = static_cast<size_t>(tdi) * tdi * tci;
+            float* cgin = nullptr;
+            aic_dropin::check_cuda(cudaMalloc(&cgin, n_in * sizeof(float)));
+            aic_dropin::check_cuda(cudaMemset(cgin, 0, n_in * sizeof(float)));
+            layer.backward(cgout, cin_w, cin_s, cgin);
+            aic_dropin::check_cuda(cudaStreamSynchronize(stream));
+            std::vector<float> hg(n_in);
+            aic_dropin::check_cuda(cudaMemcpy(hg.data(), cgin, n_in * sizeof(float), cudaMemcpyDeviceToHost));
+            write_file(dir + "/train_conv_gin.bin", hg.data(), hg.size() * 4);
+            const size_t n_cw = static_cast<size_t>(tco) * tk * tk * tci;
+            write_file(dir + "/train_conv_master.bin", thost_base, n_cw * sizeof(float));
+            // the Mamba layer: `msteps` training-mode steps, then the last step's backward
+            auto* min_w = to_device<uint32_t>(read_file(dir + "/train_mamba_in_w.bin"));
+            auto* min_s = to_device<int8_t>(read_file(dir + "/train_mamba_in_s.bin"));
+            auto* mgout = to_device<float>(read_file(dir + "/train_mamba_gout.bin"));
+            const int D = MambaLayer::d_model;
+            for (int t = 0; t < msteps; ++t)
+                ml.forward(min_w + static_cast<size_t>(t) * D / 8, min_s + static_cast<size_t>(t) * D / 32);
+            aic_dropin::DeviceSpan<float> mgin;
+            aic_dropin::check_cuda(cudaMalloc(&mgin.ptr, D * sizeof(float)));
+            mgin.count = D;
+            ml.backward(mgout, min_w + static_cast<size_t>(msteps - 1) * D / 8,
+                        min_s + static_cast<size_t>(msteps - 1) * D / 32, mgin);
+            aic_dropin::check_cuda(cudaStreamSynchronize(stream));
+            std::vector<float> hm(D);
+            aic_dropin::check_cuda(cudaMemcpy(hm.data(), mgin.ptr, D * sizeof(float), cudaMemcpyDeviceToHost));
+            write_file(dir + "/train_mamba_gin.bin", hm.data(), hm.size() * 4);
+            const size_t n_mw = static_cast<size_t>(2 * D) * (34 + 4 * MambaLayer::d_state + mo);
+            write_file(dir + "/train_mamba_master.bin", thost_base + ((n_cw * sizeof(float) + 15) & ~size_t(15)),
+                       n_mw * sizeof(float));
         }
         int code = -1;
         aic_dropin::check(aic_device_error_sync(&code));

@@ -70,6 +70,26 @@ def test_dropin_layer_classes(golden, tmp_path):
     (tmp_path / "spec.txt").write_text(f"conv {cin} {mid} {cout} {st} {din} {dout} {k} {S.CB_RF}\n"
                                        f"mamba {S.MB_T} {S.MB_OUT} 2\n"
                                        f"critic {c_in} {units} {dim} {steps}\n")
+    # training (conv_layer.h:150, mamba_layer.h:146): one pointwise-conv frame and
+    # one Mamba step through the classes' backward, against the reference kernels
+    gbc, gbm = golden("backward_conv"), golden("backward_mamba_N128")
+    case = "pw_silu"
+    _, tci, tco, tk, tst, tdi, tdo, tact = next(c for c in S.CONV_BWD_CASES if c[0] == case)
+    cm, cb, _, cgo = S.conv_bwd_case(case)
+    write_bin(tmp_path / "train_conv.bin", cm, cb)
+    gbc[f"{case}_xw"].astype("<u4").tofile(tmp_path / "train_conv_in_w.bin")
+    gbc[f"{case}_xs"].astype(np.int8).tofile(tmp_path / "train_conv_in_s.bin")
+    cgo.astype("<f4").tofile(tmp_path / "train_conv_gout.bin")
+    mo, ma = S.MB_BWD_CASES[0]
+    mblob, mbias, _, mgo = S.mamba_bwd_case(mo, ma)
+    write_bin(tmp_path / "train_mamba.bin", mblob, mbias)
+    tag = f"o{mo}_a{ma}"
+    gbm[f"{tag}_xw"].astype("<u4").tofile(tmp_path / "train_mamba_in_w.bin")
+    gbm[f"{tag}_xs"].astype(np.int8).tofile(tmp_path / "train_mamba_in_s.bin")
+    mgo.astype("<f4").tofile(tmp_path / "train_mamba_gout.bin")
+    (tmp_path / "train_spec.txt").write_text(
+        f"convtrain {tci} {tco} {tk} {tst} {tdi} {tdo} {tact} {S.TRAIN_LR} {S.TRAIN_PENALTY}\n"
+        f"mambatrain {S.MB_BWD_T} {mo} {ma} {S.TRAIN_LR} {S.TRAIN_PENALTY}\n")
     exe = build_driver(tmp_path, S.MB_D, S.MB_N)
     res = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True, timeout=300)
     assert res.returncode == 0, res.stdout + res.stderr
@@ -83,3 +103,15 @@ def test_dropin_layer_classes(golden, tmp_path):
     ref = O.critic(pooled, w1, wl, w2, c_in, units, np.zeros((1, units, 2), np.float32), 1, steps)
     got = np.fromfile(tmp_path / "critic_out.bin", dtype="<f4")
     assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max(), (got, ref)
+    # training through the drop-in classes: input gradients bit for bit, host
+    # masters updated within the clip factor's rounding (the reference adds its
+    # square-sum blocks in arrival order)
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "train_conv_gin.bin", dtype="<f4"), gbc[f"{case}_gi"],
+                                  err_msg="ConvLayer::backward input gradient")
+    np.testing.assert_array_equal(np.fromfile(tmp_path / "train_mamba_gin.bin", dtype="<f4"), gbm[f"{tag}_gi"],
+                                  err_msg="MambaLayer::backward input gradient")
+    for name, got_path, ref, grad in (("conv", "train_conv_master.bin", gbc[f"{case}_master"], gbc[f"{case}_gw"]),
+                                      ("mamba", "train_mamba_master.bin", gbm[f"{tag}_master"], gbm[f"{tag}_gw"])):
+        got = np.fromfile(tmp_path / got_path, dtype="<f4").astype(np.float64)
+        tol = np.abs(grad.astype(np.float64)) * S.TRAIN_LR * 2e-6 + np.abs(ref.astype(np.float64)) * 2.4e-7
+        assert (np.abs(got - ref) <= tol).all(), f"{name}: host masters after backward"
