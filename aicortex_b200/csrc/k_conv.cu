@@ -380,11 +380,14 @@ cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* 
 {
     if (frames == 0) return cudaSuccess;
     // 3x3 (the stack's kernel) tiled, 16 x 8 output blocks at stride 2 (measured
-    // 16 % faster than 8 x 8 on the stack's first block); larger kernels keep
-    // k*k weight quads per thread only at very high register counts, so they
-    // run direct
+    // 16 % faster than 8 x 8 on the stack's first block), 8 x 8 when the whole
+    // output frame is at most 8 rows (a 16-row block would leave half its
+    // threads idle); larger kernels keep k*k weight quads per thread only at
+    // very high register counts, so they run direct
     if (ksize == 3 && stride == 1)
         return launch_dw_tiled<3, 1>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+    if (ksize == 3 && stride == 2 && Dout <= 8)
+        return launch_dw_tiled<3, 2, 8>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
     if (ksize == 3 && stride == 2)
         return launch_dw_tiled<3, 2, 16>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
     return launch_conv_dw_direct(in, in_s, wf, bias, out, out_s, frames, C, ksize, stride, Din, Dout, stream);
