@@ -54,6 +54,11 @@ def _load() -> C.CDLL:
         "orc_fft_rows": ([P, I32, P], None),
         "orc_fft_cols": ([P, I32, P], None),
         "orc_screen_frontend": ([P, I32, I32, C.c_uint32, C.c_float, C.c_float, P], None),
+        "orc_sgd_update": ([P, P, I64, F, F, F], None),
+        "orc_clip_factor": ([P, I64, I32, P], F),
+        "orc_conv_backward": ([P, P, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, P, P, P], None),
+        "orc_mamba_backward": ([P, P, P, P, P, P, P, P, P, I32, I32, I32, I32, P, P, P], None),
+        "orc_critic_backward": ([P, P, P, P, F, F, I32, I32, P, P, P], None),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(lib, name)
@@ -300,3 +305,60 @@ def cortex_forward(weights: dict, planes_f16: np.ndarray, B: int, T: int, blocks
     """One-shot CortexRef(...).forward(...)."""
     return CortexRef(weights, blocks_geo, d_model, d_state, actor_out, critic_units, stem_channels).forward(
         planes_f16, B, T)
+
+
+# ---------------------------------------------------------------- training path
+
+def _f32(a):
+    return np.ascontiguousarray(a, np.float32)
+
+
+def sgd_update(data, grad, factor, lr, penalty):
+    """updateParamsKernel on a copy of `data` with grad_norm_factor `factor`."""
+    d = _f32(data).copy()
+    lib.orc_sgd_update(_p(d), _p(_f32(grad)), d.size, float(factor), float(lr), float(penalty))
+    return d
+
+
+def clip_factor(grad, blocks):
+    """(clip factor, square sum) over `blocks` 256-thread blocks, added in block order."""
+    s = np.zeros(1, np.float32)
+    f = lib.orc_clip_factor(_p(_f32(grad)), grad.size, int(blocks), _p(s))
+    return float(f), float(s[0])
+
+
+def conv_backward(x_w, x_s, w_w, w_s, bias, master, dy, in_c, out_c, k, stride, d_in, d_out, act):
+    """ConvLayer::backward's gradients on one frame: (gw, gb, grad_in from zeros)."""
+    dw = k > 1 and k % 2 == 1
+    gw = np.zeros(master.size, np.float32)
+    gb = np.zeros(out_c, np.float32)
+    gi = np.zeros(d_in * d_in * in_c, np.float32)
+    lib.orc_conv_backward(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
+                          _p(np.ascontiguousarray(w_w, np.uint32)), _p(np.ascontiguousarray(w_s, np.int8)),
+                          _p(_f32(bias)), _p(_f32(master)), _p(_f32(dy)), in_c, out_c, k, stride, d_in, d_out,
+                          int(act and not dw), _p(gw), _p(gb), _p(gi))
+    return gw, gb, gi
+
+
+def mamba_backward(x_w, x_s, h, traces, blob, bias, dy, d_model, d_state, out_c, act):
+    """MambaLayer::backward's gradients for one sequence after a step: h [E][P][2],
+    traces [3][E][P][2] (this sequence). Returns (gw, gb, grad_in)."""
+    gw = np.zeros(blob.size, np.float32)
+    gb = np.zeros(out_c, np.float32)
+    gi = np.zeros(d_model, np.float32)
+    t = _f32(traces)
+    lib.orc_mamba_backward(_p(np.ascontiguousarray(x_w, np.uint32)), _p(np.ascontiguousarray(x_s, np.int8)),
+                           _p(_f32(h)), _p(np.ascontiguousarray(t[0])), _p(np.ascontiguousarray(t[1])),
+                           _p(np.ascontiguousarray(t[2])), _p(_f32(blob)), _p(_f32(bias)), _p(_f32(dy)), d_model,
+                           d_state, out_c, act, _p(gw), _p(gb), _p(gi))
+    return gw, gb, gi
+
+
+def critic_backward(w2, trace_w1, trace_l, hidden, pred, real, units, in_c):
+    """Critic::backward's gradients (gw1, gl, gw2) for one sequence."""
+    gw1 = np.zeros(2 * units * in_c, np.float32)
+    gl = np.zeros(2 * units * in_c, np.float32)
+    gw2 = np.zeros(2 * units, np.float32)
+    lib.orc_critic_backward(_p(_f32(w2)), _p(_f32(trace_w1)), _p(_f32(trace_l)), _p(_f32(hidden)), float(pred),
+                            float(real), units, in_c, _p(gw1), _p(gl), _p(gw2))
+    return gw1, gl, gw2

@@ -131,6 +131,18 @@ void orc_screen_frontend(const uint8_t* bgra, int pixels, int train, uint32_t fr
 
 int orc_num_threads(void);
 
+/* ---- training path (aic_oracle_train.c) ---- */
+void orc_sgd_update(float* data, const float* grad, int64_t n, float factor, float lr, float penalty);
+float orc_clip_factor(const float* g, int64_t n, int blocks, float* sum_out);
+void orc_conv_backward(const uint32_t* in, const int8_t* in_s, const uint32_t* w, const int8_t* w_s,
+                       const float* bias, const float* master, const float* dy, int InC, int OutC, int ks,
+                       int stride, int Din, int Dout, int act, float* gw, float* gb, float* grad_in);
+void orc_mamba_backward(const uint32_t* in, const int8_t* in_s, const float* h, const float* ta, const float* tb,
+                        const float* td, const float* m, const float* bias, const float* dy, int D, int N, int OutC,
+                        int act, float* gw, float* gb, float* grad_in);
+void orc_critic_backward(const float* w2, const float* tw1, const float* tl, const float* hidden, float pred,
+                         float real, int units, int in, float* gw1, float* gl, float* gw2);
+
 #ifdef __cplusplus
 }
 #endif

@@ -264,3 +264,77 @@ def test_oracle_screen(golden):
     train = O.screen_frontend(bgra, True, S.SCREEN_SEED, *S.SCREEN_AUG)
     np.testing.assert_array_equal(plain.view(np.uint16), g["out"][0].view(np.uint16))
     np.testing.assert_array_equal(train.view(np.uint16), g["out"][1].view(np.uint16))
+
+
+# ---------------------------------------------------------------- training path
+
+def _rel(a, b):
+    a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.mark.parametrize("case", [c[0] for c in S.CONV_BWD_CASES])
+def test_oracle_conv_backward(golden, case):
+    """The oracle's ConvLayer::backward against the reference's own backward
+    kernels (fixture backward_conv): gradients within 1e-5 of their largest
+    value (libm in place of the fast-math rsqrt and exp), and the update with
+    the reference's square sums reproduces its masters."""
+    g = golden("backward_conv")
+    _, cin, cout, k, st, din, dout, act = next(c for c in S.CONV_BWD_CASES if c[0] == case)
+    master, bias, _, gout = S.conv_bwd_case(case)
+    w, s, b = O.pack_conv_layer(master, bias)
+    gw, gb, gi = O.conv_backward(g[f"{case}_xw"], g[f"{case}_xs"], w, s, b, master, gout, cin, cout, k, st, din,
+                                 dout, act)
+    for name, got in (("gw", gw), ("gb", gb), ("gi", gi)):
+        ref = g[f"{case}_{name}"]
+        assert _rel(got, ref) <= 1e-5, (case, name, _rel(got, ref))
+    sw, sb = g[f"{case}_sums"]
+    for data, grad, ssum, pen, name in ((master, g[f"{case}_gw"], sw, S.TRAIN_PENALTY, "master"),
+                                        (bias, g[f"{case}_gb"], sb, 0.0, "bias")):
+        norm = np.sqrt(np.float32(ssum) + np.float32(1 / 8192), dtype=np.float32)
+        f = np.float32(1) / norm if norm > 1 else np.float32(1)
+        np.testing.assert_array_equal(O.sgd_update(data, grad, f, S.TRAIN_LR, pen), g[f"{case}_{name}"])
+
+
+@pytest.mark.parametrize("out_c,act", S.MB_BWD_CASES)
+def test_oracle_mamba_backward(golden, out_c, act):
+    """The oracle's MambaLayer::backward after the fixture's training-mode
+    steps (state and traces from the oracle's own forward) against the
+    reference's backward kernels."""
+    g = golden("backward_mamba_N128")
+    tag = f"o{out_c}_a{act}"
+    blob, bias, _, gout = S.mamba_bwd_case(out_c, act)
+    D, N = S.SSM_D, 128
+    E, P = 2 * D, N // 32
+    bw, bs = O.pack_f32(blob, True, blob.size)
+    h = np.zeros((1, E, P, 2), np.float32)
+    tr = np.zeros((3, 1, E, P, 2), np.float32)
+    xw, xs = g[f"{tag}_xw"], g[f"{tag}_xs"]
+    O.ssm_scan(xw, xs, bw, bs, D, N, out_c, h, 1, S.MB_BWD_T, traces=tr)
+    gw, gb, gi = O.mamba_backward(xw[-1:], xs[-1:], h[0], tr[:, 0], blob, bias, gout, D, N, out_c, act)
+    for name, got in (("gw", gw), ("gb", gb), ("gi", gi)):
+        ref = g[f"{tag}_{name}"]
+        assert _rel(got, ref) <= 1e-4, (tag, name, _rel(got, ref))
+
+
+def test_oracle_critic_backward(golden):
+    g = golden("backward_critic")
+    w1, w2, wl, x = S.critic_case()
+    units, cin = 128, 32
+    h = np.zeros((1, units, 2), np.float32)
+    tw = np.zeros((1, cin, units, 2), np.float32)
+    tl = np.zeros((1, units, cin, 2), np.float32)
+    score = O.critic(x, w1, wl, w2, cin, units, h, 1, x.shape[0], traces=(tw, tl))
+    assert abs(score[-1] - g["pred"][0]) <= 1e-5 * abs(g["pred"][0])
+    gw1, gl, gw2 = O.critic_backward(w2, tw, tl, h, g["pred"][0], S.CRITIC_BWD_REAL, units, cin)
+    for name, got in (("gw1", gw1), ("gl", gl), ("gw2", gw2)):
+        assert _rel(got, g[name]) <= 1e-4, (name, _rel(got, g[name]))
+
+
+def test_oracle_clip_factor_block_order():
+    """The square sum over one block equals the reference's (no atomics to order)."""
+    rng = np.random.default_rng(3)
+    gsmall = rng.standard_normal(200).astype(np.float32)
+    f, s = O.clip_factor(gsmall, 1)
+    assert abs(s - float(np.sum(gsmall.astype(np.float64) ** 2))) <= 1e-5 * s
+    assert f == pytest.approx(1.0 / np.sqrt(s + 1 / 8192), rel=1e-6)
