@@ -85,10 +85,14 @@ __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t*
     constexpr int kPad = K >> 1, kHin = (TH - 1) * S + K, kWin = 7 * S + K;
     extern __shared__ float4 xs[];  // [kHin * kWin][8] float4, quad q of pixel i at i * 8 + (q ^ (i & 7))
     const int G = C >> 5;
-    const int g = blockIdx.y;
+    // the channel groups of one tile are consecutive blocks, so they run
+    // together and share the L2 lines of the tile's pixels (a pixel's groups
+    // lie in the same DRAM lines; one group per grid row re-read them per group)
+    const int g = static_cast<int>(blockIdx.x % G);
+    const int64_t tile = blockIdx.x / G;
     const int tiles_pf = tiles_x * tiles_y;
-    const int64_t frame = blockIdx.x / tiles_pf;
-    const int tin = static_cast<int>(blockIdx.x - frame * tiles_pf);
+    const int64_t frame = tile / tiles_pf;
+    const int tin = static_cast<int>(tile - frame * tiles_pf);
     const int ty = tin / tiles_x, tx = tin - ty * tiles_x;
     const int oy0 = ty * TH, ox0 = tx * 8;
     const int iy0 = oy0 * S - kPad, ix0 = ox0 * S - kPad;
@@ -368,7 +372,9 @@ cudaError_t launch_dw_tiled(const uint32_t* in, const int8_t* in_s, const float*
         if (e != cudaSuccess) return e;
     }
     const int tiles_x = (Dout + 7) / 8, tiles_y = (Dout + TH - 1) / TH;
-    const dim3 grid(static_cast<unsigned>(frames * tiles_x * tiles_y), static_cast<unsigned>(C >> 5));
+    const int64_t blocks = frames * tiles_x * tiles_y * (C >> 5);
+    if (blocks > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    const dim3 grid(static_cast<unsigned>(blocks), 1u);
     conv_dw_tiled_kernel<K, S, TH><<<grid, kThreads, smem, stream>>>(in, in_s, wf, bias, out, out_s, C, Din, Dout,
                                                                      tiles_x, tiles_y);
     return cudaGetLastError();
