@@ -100,6 +100,7 @@ _SIGS = {
     "aic_conv_block_load_dir_sync": [P, C.c_char_p, P],
     "aic_conv_block_forward": [P, P, P, P, P, I64, I32, I32, P, P],
     "aic_conv_block_destroy": [P],
+    "aic_selftest_wait_timeout": [I32, P, P],
     "aic_grad_clip_partials": [I64, PI64],
     "aic_grad_clip_factor": [P, I64, P, P, P],
     "aic_sgd_update": [P, P, I64, P, F32, F32, P],

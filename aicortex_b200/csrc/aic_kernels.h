@@ -66,6 +66,9 @@ cudaError_t launch_selftest_rcp(unsigned long long* mismatches, float* first_bad
 
 // Device-side error word written by kernels whose bounded waits time out.
 int* device_error_word();
+// One CTA waits on an mbarrier nothing arrives on: the bounded wait records
+// `code` in the device error word and *returned becomes 1 (2 if it completed).
+cudaError_t launch_selftest_wait(int code, int* returned, cudaStream_t stream);
 
 // A6: out = requant(q_main * s_main * main_mult + q_res * s_res), one exponent per position.
 cudaError_t launch_residual(const uint32_t* main_in, const int8_t* main_s, const uint32_t* res, const int8_t* res_s,

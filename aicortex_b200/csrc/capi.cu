@@ -1314,6 +1314,13 @@ AIC_API aic_status aic_gap_f16(const uint32_t* in, const int8_t* in_s, int64_t f
     });
 }
 
+AIC_API aic_status aic_selftest_wait_timeout(int code, int* returned, void* stream)
+{
+    return guarded([&] {
+        require(returned != nullptr && code != 0, "bad self-test arguments");
+        cuda_ok(launch_selftest_wait(code, returned, as_stream(stream)), "wait self-test");
+    });
+}
 AIC_API aic_status aic_selftest_rcp(uint64_t* mismatches, float* first_bad, void* stream)
 {
     return guarded([&] {

@@ -112,6 +112,12 @@ AIC_API aic_status aic_audio_workspace_bytes(size_t* bytes);
  * d >= 1 over every significand of ten binades where it differs from the IEEE
  * round-to-nearest reciprocal __frcp_rn; *first_bad (device) gets one such d. */
 AIC_API aic_status aic_selftest_rcp(uint64_t* mismatches, float* first_bad, void* stream);
+/* The failure path of the kernels' bounded waits, without a GPU fault: one CTA
+ * waits on an mbarrier that nothing arrives on; after the wait's limit (about
+ * 1 s) it records `code` in the device error word (read and cleared by
+ * aic_device_error_sync) and writes 1 to *returned (device int; 2 would mean
+ * the wait completed). The context stays usable. */
+AIC_API aic_status aic_selftest_wait_timeout(int code, int* returned, void* stream);
 AIC_API aic_status aic_audio_frontend(const int16_t* pcm, uint16_t* frame, int dim, int first_channel,
                                       void* workspace, void* stream);
 

@@ -766,3 +766,23 @@ def test_reciprocal_matches_ieee():
     A._lib.call("aic_selftest_rcp", C.c_void_p(bad.data_ptr()), C.c_void_p(first.data_ptr()),
                 C.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert int(h(bad)[0]) == 0, f"{int(h(bad)[0])} mismatches, e.g. d = {float(h(first)[0])!r}"
+
+
+def test_bounded_wait_times_out_without_fault():
+    """The failure path of the pipelined kernels' mbarrier waits: a wait that
+    nothing completes gives up after its limit, records its code in the device
+    error word and lets the kernel return; the context stays usable."""
+    import time
+    ret = torch.zeros(1, dtype=torch.int32, device=DEV)
+    t0 = time.time()
+    A._lib.call("aic_selftest_wait_timeout", 77, C.c_void_p(ret.data_ptr()), None)
+    code = C.c_int(-1)
+    A._lib.call("aic_device_error_sync", C.byref(code))
+    assert code.value == 77 and int(h(ret)[0]) == 1, (code.value, h(ret))
+    assert time.time() - t0 < 30.0
+    assert_no_device_error()  # the word was cleared by the read
+    import oracle as O
+    xs = np.random.default_rng(1).standard_normal(4096).astype(np.float32)
+    w, s = A.pack_f32(t(xs))
+    rw, rs = O.pack_f32(xs)
+    assert_f_equal(w, h(s), rw, rs, "pack after the timed-out wait")
