@@ -61,7 +61,7 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="product", choices=["product", "reference"])
     p.add_argument("--workload", default="b4096_t256", choices=sorted(WORKLOADS))
-    p.add_argument("--chunk", type=int, default=2048, help="frames per conv-stack pass")
+    p.add_argument("--chunk", type=int, default=8192, help="frames per conv-stack pass")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-parity", action="store_true")
@@ -102,6 +102,9 @@ def load_peaks():
         return {"hbm_gbs": d["hbm_gbs"], "tflops": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
                 "source": "measured"}
     return {"hbm_gbs": 6650.0, "tflops": 1400.0, "source": "fallback"}
+
+
+TRAFFIC_FRAMES = 2048  # frames per launch of the committed traffic measurements
 
 
 def traffic_from_profiles(site: str):
@@ -407,6 +410,10 @@ def main():
     else:
         achieved, peak, unit, bound = top["bytes"] / per_launch_s / 1e9, peaks["hbm_gbs"], "GB/s", "hbm"
     traffic, traffic_note = traffic_from_profiles(top["site"])
+    if traffic is not None:  # measured per 2048-frame launch; a conv site's traffic grows with its frames
+        traffic *= args.chunk / TRAFFIC_FRAMES
+        traffic_note = f"ncu DRAM read+write of a {TRAFFIC_FRAMES}-frame launch x {args.chunk / TRAFFIC_FRAMES:g} " \
+                       f"(read, write, algorithmic bytes at {TRAFFIC_FRAMES} frames: {traffic_note})"
     roofline = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak,
                 "traffic": traffic, "traffic_source": traffic_note, "site": top["site"],
                 "share_of_step": top["ms"] / (ms * args.steps), "peak_source": peaks["source"],
