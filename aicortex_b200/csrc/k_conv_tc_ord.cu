@@ -686,20 +686,24 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 //
 // The streaming kernel's pipeline with its roles on separate warps and its
 // hand-offs on mbarriers instead of CTA-wide barriers. Tiles of ROWS = 128 or
-// 256 rows x 64 channels (WsCfg), with C = ROWS / 16 consumer warps:
+// 256 rows x NC = 64 channels, or 128 rows x NC = 128 channels (WsCfg), with
+// C = ROWS * NC / 1024 consumer warps:
 // * warps C..C+2 (after setmaxnreg, kStageRegs registers): staging. Thread pt
 //   stages rows pt, pt + 96 (and pt + 192) < ROWS of the tile (both groups of
 //   a stage, loaded one stage ahead into registers) and records unit(s_in);
 //   each warp then arrives on staged[slot].
 // * warp C+3 (the same warpgroup): one thread fetches the weight images and
 //   issues each staged stage's MMAs (ROWS / 128 M = 128 halves x two groups x
-//   two K16 steps) into one of two TMEM buffers, committed to full_acc[buf].
+//   two K16 steps, N = NC) into one of two TMEM buffers, committed to
+//   full_acc[buf].
 //   On its own warp the MMA issue, which waits for the tensor pipe, overlaps
 //   the staging of the next stage.
 // * warps 0..C-1 (kConsumerRegs registers): consumers. Warp w owns the rows of
-//   TMEM lane quarter w & 3 in row half w >> 3 and the 32-channel half
-//   (w >> 2) & 1; it runs the reference's fmaf chain stage by stage from TMEM
-//   and, after a tile's last stage, the epilogue.
+//   TMEM lane quarter w & 3 in row half w / (NC / 8) and the 32-channel group
+//   (w >> 2) % (NC / 32) of the CTA's channels; it runs the reference's fmaf
+//   chain stage by stage from TMEM and, after a tile's last stage, the
+//   epilogue. Every consumer thread so owns one row x 32 channels, whatever
+//   the shape.
 // The weight images of all stages (at most kResidentStages) stay in shared
 // memory, fetched once per CTA. Stage slots (A tile halves, unit(s_in)) rotate
 // over kWsSlots; a slot is free again once all consumer warps have run the
@@ -708,24 +712,34 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 // to the cluster peers through distributed shared memory, after which each
 // consumer warp arrives on every peer's part_full[tile & 1] (release/acquire
 // at cluster scope): no cluster-wide barrier per tile, so the producers run on.
-// TMEM: column (half h, buffer b, group j, channel c) = 256 h + 128 b + 64 j + c.
+// TMEM: column (half h, buffer b, group j, channel c) = 4 NC h + 2 NC b + NC j + c.
+// With NC = 128 the A tile that the staging warps fill per stage serves twice
+// the output channels, and a 256-channel norm chunk needs a cluster of two
+// CTAs instead of four; the weights of both 64-channel image chunks are
+// fetched side by side, so one N = 128 MMA covers them (the SW128 atoms of
+// the second chunk continue those of the first).
 constexpr int kWsStageWarps = 3;
 constexpr int kWsStageRows = kWsStageWarps * 32;  // 96 staging threads
-// Tile shapes: 128 rows (8 consumer warps, 384 threads, two CTAs per SM, each
-// with 256 TMEM columns) or 256 rows (16 consumer warps, 640 threads, one CTA
-// per SM with all 512 columns). The block launches with kLaunchRegs x kThreads
+// Tile shapes: 128 rows x 64 channels (8 consumer warps, 384 threads, two
+// CTAs per SM, each with 256 TMEM columns); 256 rows x 64 channels or 128 rows
+// x 128 channels (16 consumer warps, 640 threads, one CTA per SM with all 512
+// columns). The block launches with kLaunchRegs x kThreads
 // registers, exactly the consumers' kConsumerRegs plus the staging/MMA
 // warpgroup's kStageRegs (a setmaxnreg.inc that cannot be granted never returns).
-template <int ROWS>
+template <int ROWS, int NC = kNCta>
 struct WsCfg {
+    static_assert((ROWS == kBM || ROWS == 2 * kBM) && (NC == kNCta || NC == 2 * kNCta) && ROWS * NC <= 2 * kBM * kNCta,
+                  "tile shape");
+    static constexpr bool kSmall = ROWS == kBM && NC == kNCta;
     static constexpr int kHalves = ROWS / kBM;
-    static constexpr int kConsumerWarps = 8 * kHalves;
+    static constexpr int kGroups = NC / 32;  // 32-channel groups per CTA
+    static constexpr int kConsumerWarps = 4 * kGroups * kHalves;
     static constexpr int kThreads = (kConsumerWarps + kWsStageWarps + 1) * 32;
-    static constexpr int kTmemCols = 256 * kHalves;
+    static constexpr int kTmemCols = 4 * NC * kHalves;
     static constexpr int kRowsPerThread = (ROWS + kWsStageRows - 1) / kWsStageRows;
-    static constexpr int kLaunchRegs = ROWS == kBM ? 80 : 96;
-    static constexpr int kConsumerRegs = ROWS == kBM ? 96 : 104;
-    static constexpr int kStageRegs = ROWS == kBM ? 48 : 64;
+    static constexpr int kLaunchRegs = kSmall ? 80 : 96;
+    static constexpr int kConsumerRegs = kSmall ? 96 : 104;
+    static constexpr int kStageRegs = kSmall ? 48 : 64;
     static_assert(kConsumerWarps * 32 * kConsumerRegs + 128 * kStageRegs == kThreads * kLaunchRegs, "register split");
     // the register file admits at most this many CTAs per SM; their TMEM
     // allocations must fit the SM's 512 columns, or an alloc would wait for a
@@ -736,24 +750,24 @@ struct WsCfg {
 constexpr int kWsSlots = 3;
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
 
-template <int KS, int CS, bool ACT, bool G1, int ROWS>
-__global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(OrdParams p)
+template <int KS, int CS, bool ACT, bool G1, int ROWS, int NC>
+__global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kernel(OrdParams p)
 {
-    using Cfg = WsCfg<ROWS>;
+    using Cfg = WsCfg<ROWS, NC>;
     constexpr int kWsConsumerWarps = Cfg::kConsumerWarps, kWsThreads = Cfg::kThreads, kWsRows = ROWS,
                   kWsRowsPerThread = Cfg::kRowsPerThread, kWsHalves = Cfg::kHalves;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = smem_raw + ((1024u - (smem_addr(smem_raw) & 1023u)) & 1023u);  // stays a shared-space pointer
-    const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * kNCta;
-    const int n_cta = min(kNCta, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
+    const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * NC;
+    const int n_cta = min(NC, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk (NC = 64 only)
     const bool live = n_cta > 0;
     const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
     uint8_t* a_slots = base;                                                   // [slot][half][kTileA]
     uint8_t* b_codes = a_slots + kWsSlots * kWsHalves * kTileA;                        // [stage][n_max][128 B]
     float* b_units = reinterpret_cast<float*>(b_codes + S * p.n_max * 128);   // [stage][2][n_max]
     float* din_s = b_units + S * 2 * p.n_max;                                 // [slot][2 groups][kWsRows]
-    float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [kNCta]
-    float* part = bias_s + kNCta;                                             // [2 tiles][8][kWsRows]
+    float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [NC]
+    float* part = bias_s + NC;                                                // [2 tiles][8][kWsRows]
     uint64_t* bars = reinterpret_cast<uint64_t*>(part + 2 * 8 * kWsRows);
     uint64_t* full_b = bars;                       // every stage's weights landed
     uint64_t* staged = bars + 1;                   // [slot] the staging warps filled the slot
@@ -805,11 +819,30 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
             const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
             const uint32_t idesc = instr_desc_h(n_cta);
             mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
-            for (int k = 0; k < S; ++k) {
-                const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
-                bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128), smem_addr(&full_b[0]));
-                bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
-                         smem_addr(&full_b[0]));
+            if constexpr (NC == kNCta) {
+                for (int k = 0; k < S; ++k) {
+                    const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
+                    bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
+                             smem_addr(&full_b[0]));
+                    bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
+                             smem_addr(&full_b[0]));
+                }
+            } else {
+                // the 64-channel image chunks side by side (every chunk of a layer
+                // on this shape is full): codes [stage][NC][128 B], units
+                // [stage][group][NC]
+                for (int hn = 0; hn < NC / kNCta; ++hn) {
+                    const uint8_t* wimg_h = p.wimg + static_cast<int64_t>(n0 + hn * kNCta) * S * kImgRow;
+                    for (int k = 0; k < S; ++k) {
+                        const uint8_t* img = wimg_h + static_cast<int64_t>(k) * kNCta * kImgRow;
+                        bulk_g2s(smem_addr(b_codes + (k * p.n_max + hn * kNCta) * 128), img, kNCta * 128u,
+                                 smem_addr(&full_b[0]));
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+                            bulk_g2s(smem_addr(b_units + (k * 2 + j) * p.n_max + hn * kNCta), img + kNCta * 128 + j * kNCta * 4,
+                                     kNCta * 4u, smem_addr(&full_b[0]));
+                    }
+                }
             }
             int sp = 0;
             for (int gs = 0; gs < total; ++gs) {
@@ -830,8 +863,8 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
 #pragma unroll
                         for (int j = 0; j < kBK / 16; ++j)
                             if (j < n_mma)
-                                mma_f16(tmem + static_cast<uint32_t>(256 * hh + 128 * buf + 64 * (j >> 1)), da + 16 * j,
-                                        db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
+                                mma_f16(tmem + static_cast<uint32_t>(4 * NC * hh + 2 * NC * buf + NC * (j >> 1)),
+                                        da + 16 * j, db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
                     }
                     mma_commit(smem_addr(&full_acc[buf]));
                 } else {
@@ -949,11 +982,11 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
     } else {
         // ------------------------------------------------------------ consumers
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Cfg::kConsumerRegs));
-        const int h = warp >> 3, q = warp & 3, hw = (warp >> 2) & 1;
+        const int h = warp / (4 * Cfg::kGroups), q = warp & 3, hw = (warp >> 2) % Cfg::kGroups;
         const int erow = q * 32 + lane;    // TMEM lane = row within the half
         const int trow = h * kBM + erow;   // row within the 256-row tile
         const bool has_cols = hw < (n_cta >> 5);
-        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(256 * h + 32 * hw);
+        const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(4 * NC * h + 32 * hw);
         const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
         const int gidx = ((n0 & (kNormChunk - 1)) >> 5) + hw;  // this warp's group within the norm chunk
         constexpr bool kFold = KS == 2 && !G1;
@@ -976,7 +1009,7 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
                     tc_fence_after();
                     const float* units = b_units + sc * 2 * p.n_max + 32 * hw;
                     const float* dins = din_s + slot * 2 * kWsRows + trow;
-                    const uint32_t tb = tl + static_cast<uint32_t>(128 * buf);
+                    const uint32_t tb = tl + static_cast<uint32_t>(2 * NC * buf);
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const int gk = 2 * sc + j;
@@ -994,7 +1027,7 @@ __global__ void __maxnreg__(WsCfg<ROWS>::kLaunchRegs) conv_gemm_tc_ws_kernel(Ord
 #pragma unroll
                             for (int h16 = 0; h16 < 2; ++h16) {
                                 float pv[16];
-                                tmem_ld16(tb + static_cast<uint32_t>(64 * j + 16 * h16), pv);
+                                tmem_ld16(tb + static_cast<uint32_t>(NC * j + 16 * h16), pv);
 #pragma unroll
                                 for (int i4 = 0; i4 < 4; ++i4) {
                                     const float4 u = u4[4 * h16 + i4];
@@ -1181,15 +1214,19 @@ cudaError_t launch_ord_cs(const OrdParams& p, size_t smem, cudaStream_t stream)
     return launch_ord<KS, 4>(q, smem, chunks, stream);
 }
 
-template <int KS, int CS, int ROWS>
+template <int KS, int CS, int ROWS, int NC = kNCta>
 cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
 {
-    using Cfg = WsCfg<ROWS>;
-    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false, ROWS> : conv_gemm_tc_ws_kernel<KS, CS, false, false, ROWS>;
-    if constexpr (KS == 2) {
+    using Cfg = WsCfg<ROWS, NC>;
+    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false, ROWS, NC>
+                      : conv_gemm_tc_ws_kernel<KS, CS, false, false, ROWS, NC>;
+    if constexpr (KS == 2 && NC == kNCta) {
         if (p.in_c == 32)  // one group per tap
-            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true, ROWS> : conv_gemm_tc_ws_kernel<KS, CS, false, true, ROWS>;
+            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true, ROWS, NC>
+                         : conv_gemm_tc_ws_kernel<KS, CS, false, true, ROWS, NC>;
     }
+    if (NC != kNCta && (p.out_c % NC != 0 || p.n_max != NC || (KS == 2 && p.in_c == 32)))
+        return cudaErrorNotSupported;  // 128-channel CTAs: full chunks only, no one-group-per-tap form
     // The role split (setmaxnreg) draws on the block's launch allocation of
     // kLaunchRegs x kThreads; with any other compiled count the increase could
     // never be granted.
@@ -1201,18 +1238,28 @@ cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
     if (p.rows * KS * KS > 0x7FFFFFFFll) return cudaErrorNotSupported;  // input pixel indices are 32-bit
     const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * Cfg::kHalves * kTileA +
                         static_cast<size_t>(p.stages) * p.n_max * kImgRow +
-                        (static_cast<size_t>(kWsSlots) * 2 * ROWS + kNCta + 16 * ROWS) * sizeof(float) +
+                        (static_cast<size_t>(kWsSlots) * 2 * ROWS + NC + 16 * ROWS) * sizeof(float) +
                         (2 * kWsSlots + 6) * 8 + 16;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return e;
-    // One or two CTAs per SM (TMEM columns, shared memory); runs of tiles sized
-    // for about four CTA runs per SM over the launch.
     const int64_t n_tiles = (p.rows + ROWS - 1) / ROWS;
-    int64_t t = n_tiles * chunks * CS / (148 * 4);
     OrdParams q = p;
-    q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 16 ? 16 : t);
+    if constexpr (Cfg::kSmall) {
+        // Two CTAs per SM (TMEM columns, shared memory); runs of tiles sized
+        // for about four CTA runs per SM over the launch.
+        const int64_t t = n_tiles * chunks * CS / (148 * 4);
+        q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t > 16 ? 16 : t);
+    } else {
+        // One CTA per SM: runs of at most 16 tiles, sized so the CTAs fill a
+        // whole number of waves over the 148 SMs (a partial last wave of
+        // single-CTA SMs idles the rest of the GPU)
+        const int64_t per_sm = (n_tiles * chunks * CS + 147) / 148;
+        const int64_t waves = (per_sm + 15) / 16;
+        const int64_t t = (per_sm + waves - 1) / waves;
+        q.tiles_per_cta = static_cast<int>(t < 1 ? 1 : t);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>((n_tiles + q.tiles_per_cta - 1) / q.tiles_per_cta), chunks * CS, 1);
     cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
@@ -1245,6 +1292,16 @@ cudaError_t launch_ws_cs(const OrdParams& p, cudaStream_t stream)
             return cs == 1 ? launch_ws<KS, 1, 2 * kBM>(p, chunks, stream) : launch_ws<KS, 2, 2 * kBM>(p, chunks, stream);
     }
     return cs == 1 ? launch_ws<KS, 1, kBM>(p, chunks, stream) : launch_ws<KS, 2, kBM>(p, chunks, stream);
+}
+
+// 128-row x 128-channel CTAs: one per 128 channels, a cluster of two per
+// 256-channel norm chunk.
+template <int KS>
+cudaError_t launch_ws_wide(const OrdParams& p, cudaStream_t stream)
+{
+    const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
+    return p.out_c >= kNormChunk ? launch_ws<KS, 2, kBM, 2 * kNCta>(p, chunks, stream)
+                                 : launch_ws<KS, 1, kBM, 2 * kNCta>(p, chunks, stream);
 }
 
 }  // namespace
@@ -1334,6 +1391,7 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     p.n_max = out_c < kNCta ? out_c : kNCta;
     p.tiles_per_cta = 1;
     p.err = err;
+    const bool one_group_taps = ksize == 2 && in_c == 32;
     // measured: the chain at the end wins with one or two groups per output,
     // the streaming kernel from three on
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
@@ -1342,6 +1400,16 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // norm clusters of up to two CTAs (two 128-row CTAs per SM: 15-19 % on the
     // block-0 layers of the cortex); on clusters of four it is equal or slower,
     // and longer K needs more resident weights than two CTAs' shared memory holds
+    // 128-channel CTAs where the channels come in whole 128-channel CTAs and
+    // every stage's weights stay resident: the staged A tile serves twice the
+    // channels, and a 256-channel norm chunk is a cluster of two
+    if (p.out_c % (2 * kNCta) == 0 && p.stages <= kResidentStages && !one_group_taps) {
+        OrdParams w = p;
+        w.n_max = 2 * kNCta;
+        const cudaError_t e = ksize == 1 ? launch_ws_wide<1>(w, stream) : launch_ws_wide<2>(w, stream);
+        if (e != cudaErrorNotSupported) return e;
+        (void)cudaGetLastError();  // that build is unusable: the kernels below
+    }
     const int w_chunk = p.out_c < kNormChunk ? p.out_c : kNormChunk;
     if (p.stages <= kWsMaxStages && w_chunk <= 2 * kNCta) {
         const cudaError_t e = ksize == 1 ? launch_ws_cs<1>(p, stream) : launch_ws_cs<2>(p, stream);

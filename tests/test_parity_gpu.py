@@ -593,18 +593,25 @@ def test_cortex_small_vs_oracle():
 
 @pytest.mark.parametrize("geo", [
     (64, 128, 1, 1, 24, 24, 1),     # 576 rows: 4 full tiles + a partial one
-    (256, 512, 1, 1, 16, 16, 1),    # two 256-channel norm chunks (two CTA pairs)
+    (256, 512, 1, 1, 16, 16, 1),    # 128-channel CTAs: two 256-channel norm chunks (two CTA pairs)
     (512, 288, 1, 1, 12, 12, 0),    # chunks of 256 and 32 (a pair with an empty CTA)
     (32, 64, 1, 1, 16, 16, 0),      # K = 32: one half-filled stage
     (96, 96, 1, 1, 16, 16, 1),      # 96-channel tile
-    (128, 256, 2, 2, 32, 16, 0),    # shortcut conv 2x2 / stride 2, one CTA pair
+    (128, 256, 2, 2, 32, 16, 0),    # shortcut conv 2x2 / stride 2, 128-channel CTA pair, tap fold
     (32, 64, 4, 4, 64, 16, 0),      # patcher conv 4x4 / stride 4
     (160, 96, 2, 2, 16, 8, 1),
-    (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps
+    (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps (16 stages: two-role kernel, clusters of 4)
     (32, 64, 2, 2, 32, 16, 1),      # one group per tap
     (128, 64, 1, 1, 12, 12, 0),     # warp-specialised, 128-row tiles: 288 rows, a partial tile
-    (256, 128, 1, 1, 10, 10, 1),    # warp-specialised, CTA pairs, 200 rows, SiLU
-    (64, 128, 2, 2, 16, 8, 0),      # warp-specialised, 256-row tiles (tap fold): one partial tile
+    (256, 128, 1, 1, 10, 10, 1),    # 128-channel CTA, 200 rows, SiLU
+    (64, 128, 2, 2, 16, 8, 0),      # 128-channel CTA, tap fold: one partial tile
+    (64, 96, 2, 2, 16, 8, 0),       # warp-specialised, 256-row tiles (tap fold), CTA pairs
+    (512, 256, 1, 1, 12, 12, 0),    # 128-channel CTA pair, 8 resident stages, 288 rows
+    (128, 512, 1, 1, 12, 12, 1),    # 128-channel CTAs, two CTA pairs, SiLU
+    (128, 128, 1, 1, 12, 12, 0),    # 128-channel CTA, two stages
+    (96, 128, 1, 1, 12, 12, 1),     # 128-channel CTA, three groups (a padding group)
+    (384, 128, 1, 1, 10, 10, 1),    # 128-channel CTA, six stages
+    (96, 256, 2, 2, 16, 8, 1),      # 128-channel CTA pair, three groups per tap (taps end mid-stage)
     (32, 128, 2, 2, 16, 8, 1),      # warp-specialised, one group per tap, CTA pairs
 ])
 def test_tensor_core_conv_vs_reference_order(geo):
@@ -635,9 +642,11 @@ def test_tensor_core_conv_vs_reference_order(geo):
 @pytest.mark.parametrize("geo", [
     (32, 128, 1, 1, 8, 8, 1),    # chain at the end, one group
     (64, 128, 1, 1, 8, 8, 0),    # chain at the end, two groups
-    (512, 256, 1, 1, 4, 4, 0),   # streaming, 16 groups, clusters of 4
+    (512, 256, 1, 1, 4, 4, 0),   # 128-channel CTA pair, 16 groups
+    (512, 288, 1, 1, 4, 4, 0),   # streaming two-role kernel, clusters of 4
     (32, 64, 2, 2, 16, 8, 1),    # 2x2, one group per tap
-    (128, 256, 2, 2, 8, 4, 0),   # 2x2, four groups per tap
+    (128, 256, 2, 2, 8, 4, 0),   # 2x2, four groups per tap (128-channel CTA pair)
+    (64, 96, 2, 2, 8, 4, 0),     # 2x2, two groups per tap (256-row warp-specialised tiles)
     (32, 32, 3, 2, 16, 8, 0),    # depthwise 3x3 / 2 (tiled and direct kernels)
 ])
 def test_conv_overflow_vs_oracle(geo):
