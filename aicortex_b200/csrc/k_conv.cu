@@ -98,16 +98,33 @@ __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t*
     const int iy0 = oy0 * S - kPad, ix0 = ox0 * S - kPad;
     const int64_t fbase = frame * Din * Din;
 
-    for (int i = threadIdx.x; i < kHin * kWin; i += kThreads) {
+    // every load of the thread's input pixels is issued before any is used,
+    // so the block waits for one memory round trip instead of one per pixel
+    constexpr int kPixIn = kHin * kWin, kPerThread = (kPixIn + kThreads - 1) / kThreads;
+    uint4 xw[kPerThread];
+    int xe[kPerThread];  // -128 (no exponent is below -120): outside the image
+#pragma unroll
+    for (int it = 0; it < kPerThread; ++it) {
+        const int i = static_cast<int>(threadIdx.x) + it * kThreads;
         const int ry = i / kWin, rx = i - ry * kWin;
         const int iy = iy0 + ry, ix = ix0 + rx;
+        xw[it] = make_uint4(0u, 0u, 0u, 0u);
+        xe[it] = -128;
+        if (i < kPixIn && iy >= 0 && iy < Din && ix >= 0 && ix < Din) {
+            const int64_t pix = fbase + static_cast<int64_t>(iy) * Din + ix;
+            xw[it] = __ldg(reinterpret_cast<const uint4*>(in) + pix * G + g);
+            xe[it] = __ldg(in_s + pix * G + g);
+        }
+    }
+#pragma unroll
+    for (int it = 0; it < kPerThread; ++it) {
+        const int i = static_cast<int>(threadIdx.x) + it * kThreads;
+        if (i >= kPixIn) break;
         float4* dst = xs + i * 8;
         const int sw = i & 7;
-        if (iy >= 0 && iy < Din && ix >= 0 && ix < Din) {
-            const int64_t pix = fbase + static_cast<int64_t>(iy) * Din + ix;
-            const uint4 w = __ldg(reinterpret_cast<const uint4*>(in) + pix * G + g);
-            const float2 u = dup2(unit_of(__ldg(in_s + pix * G + g)));
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+        if (xe[it] != -128) {
+            const float2 u = dup2(unit_of(static_cast<int8_t>(xe[it])));
+            const uint32_t ww[4] = {xw[it].x, xw[it].y, xw[it].z, xw[it].w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 // byte j of lo / hi: code 2j / 2j + 1 of the word as n ^ 8; each
