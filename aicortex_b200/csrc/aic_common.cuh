@@ -166,6 +166,33 @@ __device__ __forceinline__ float max_nan(float a, float b)
     asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
     return r;
 }
+// max.NaN over |v_i| of N values as a pairwise tree (depth log2 N instead of
+// N): max.NaN is exact, commutative and associative (NaN if any operand is
+// NaN, else the largest magnitude), so the order does not change the result.
+template <int N>
+__device__ __forceinline__ float amax_tree(const float (&v)[N])
+{
+    static_assert(N >= 2 && (N & (N - 1)) == 0, "power of two");
+    float m[N / 2];
+#pragma unroll
+    for (int i = 0; i < N / 2; ++i) m[i] = max_nan(fabsf(v[i]), fabsf(v[i + N / 2]));
+#pragma unroll
+    for (int o = N / 4; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < o; ++i) m[i] = max_nan(m[i], m[i + o]);
+    return m[0];
+}
+__device__ __forceinline__ float amax_tree2(const float2 (&v)[16])
+{
+    float m[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) m[i] = max_nan(fabsf(v[i].x), fabsf(v[i].y));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+        for (int i = 0; i < o; ++i) m[i] = max_nan(m[i], m[i + o]);
+    return m[0];
+}
 // false for a NaN or an infinity
 __device__ __forceinline__ bool is_finite_amax(float a) { return a <= 3.40282347e38f; }
 
@@ -212,9 +239,7 @@ static __device__ __noinline__ QuantGroup quantize_group_ref(const float* v)
 // Quantise 32 values held by one thread into 4 words + exponent.
 __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* words, int8_t* exp_out)
 {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) amax = amax_nan(amax, v[i]);
+    const float amax = amax_tree(v);
     if (!is_finite_amax(amax)) {
         float f[32];  // a copy, so that only the rare path takes an array's address
 #pragma unroll
@@ -241,9 +266,7 @@ __device__ __forceinline__ void quantize_group(const float (&v)[32], uint4* word
 // quantize_group over 32 values held as 16 pairs (value 2i + j in v[i].j).
 __device__ __forceinline__ void quantize_group2(const float2 (&v)[16], uint4* words, int8_t* exp_out)
 {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = amax_nan(amax_nan(amax, v[i].x), v[i].y);
+    const float amax = amax_tree2(v);
     if (!is_finite_amax(amax)) {
         float f[32];
 #pragma unroll
@@ -279,9 +302,7 @@ __device__ __forceinline__ void quantize_group2(const float2 (&v)[16], uint4* wo
 // is a warp vote, so the slow path's shuffles run on the whole warp).
 __device__ __forceinline__ uint32_t quantize_word_x4(const float (&v)[8], int8_t* exp_out)
 {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = amax_nan(amax, v[i]);
+    float amax = amax_tree(v);
     amax = max_nan(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
     amax = max_nan(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
     uint32_t w = 0;
