@@ -706,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
 //   the shape.
 // The weight images of all stages (at most kResidentStages) stay in shared
 // memory, fetched once per CTA. Stage slots (A tile halves, unit(s_in)) rotate
-// over kWsSlots; a slot is free again once all consumer warps have run the
+// over ws_slots(); a slot is free again once all consumer warps have run the
 // chain of the stage it held (empty[slot]), and a TMEM buffer once the chain of
 // the stage two before has run (the same barrier). The RMSNorm's per-32-channel sums go
 // to the cluster peers through distributed shared memory, after which each
@@ -747,13 +747,17 @@ struct WsCfg {
     static constexpr int kMaxCtasPerSm = 65536 / (kThreads * kLaunchRegs);
     static_assert(kMaxCtasPerSm * kTmemCols <= 512, "TMEM columns per SM");
 };
-constexpr int kWsSlots = 3;
+// A-tile slots: 3, or 4 for pointwise convs on 128-channel CTAs (measured 7 %
+// faster on the 512 -> 256 layer with 8 stages per tile; equal or slower on
+// the 2x2 convs, whose shared memory the fold's shapes need elsewhere)
+__host__ __device__ constexpr int ws_slots(int ks, int nc) { return ks == 1 && nc == 128 ? 4 : 3; }
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
 
 template <int KS, int CS, bool ACT, bool G1, int ROWS, int NC>
 __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kernel(OrdParams p)
 {
     using Cfg = WsCfg<ROWS, NC>;
+    constexpr int kWsSlots = ws_slots(KS, NC);
     constexpr int kWsConsumerWarps = Cfg::kConsumerWarps, kWsThreads = Cfg::kThreads, kWsRows = ROWS,
                   kWsRowsPerThread = Cfg::kRowsPerThread, kWsHalves = Cfg::kHalves;
     extern __shared__ uint8_t smem_raw[];
@@ -1236,6 +1240,7 @@ cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
     if (fa.numRegs != Cfg::kLaunchRegs) return cudaErrorNotSupported;
     if (p.stages > kResidentStages) return cudaErrorNotSupported;  // the weights must stay resident
     if (p.rows * KS * KS > 0x7FFFFFFFll) return cudaErrorNotSupported;  // input pixel indices are 32-bit
+    constexpr int kWsSlots = ws_slots(KS, NC);
     const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * Cfg::kHalves * kTileA +
                         static_cast<size_t>(p.stages) * p.n_max * kImgRow +
                         (static_cast<size_t>(kWsSlots) * 2 * ROWS + NC + 16 * ROWS) * sizeof(float) +
