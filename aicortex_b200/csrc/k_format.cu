@@ -241,7 +241,6 @@ __global__ void __launch_bounds__(kThreads) residual_pos2_kernel(const uint32_t*
         const float2 s_in = dup2(skipped ? 0.0f : unit_of(sa[k]) * main_mult);
         const uint32_t aw[4] = {a[k].x, a[k].y, a[k].z, a[k].w}, bw[4] = {b[k].x, b[k].y, b[k].z, b[k].w};
         float2 r[16];
-        float amaxn = 0.0f;  // absmax that keeps a NaN; equal to the reference's when finite
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             // byte j of lo / hi: code 2j / 2j + 1 of the word as n ^ 8, placed in
@@ -256,11 +255,11 @@ __global__ void __launch_bounds__(kThreads) residual_pos2_kernel(const uint32_t*
                 const float2 qb = add2(make_float2(__uint_as_float(__byte_perm(blo, 0x4B000000u, 0x7440u | j)),
                                                    __uint_as_float(__byte_perm(bhi, 0x4B000000u, 0x7440u | j))),
                                        dup2(-8388616.0f));
-                const float2 v = fma2(qa, s_in, mul2(qb, s_res));
-                r[4 * q + j] = v;
-                amaxn = amax_nan(amax_nan(amaxn, v.x), v.y);
+                r[4 * q + j] = fma2(qa, s_in, mul2(qb, s_res));
             }
         }
+        // absmax that keeps a NaN (equal to the reference's when finite), as a tree
+        float amaxn = amax_tree2(r);
 #pragma unroll
         for (int o = S >> 1; o > 0; o >>= 1) amaxn = max_nan(amaxn, __shfl_xor_sync(0xFFFFFFFFu, amaxn, o));
         // the reference's absmax (fmaxf from 0, a NaN skipped) differs only where
