@@ -197,8 +197,12 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
 #pragma unroll
     for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
 
-    // fmaf chain over the groups of global stage gc (stage sc of its tile)
+    // fmaf chain over the groups of global stage gc (stage sc of its tile);
+    // next_fold: the group index at which the current tap's chain ends (the
+    // stages of a tile arrive in order, so no division per group)
+    int next_fold = G;
     auto chain = [&](int gc, int sc) -> bool {
+        if (sc == 0) next_fold = G;
         const int buf = gc & 1;
         if (!mbar_wait(smem_addr(&bars[2 + buf]), static_cast<uint32_t>(gc >> 1) & 1u, p.err, 12)) return false;
         tc_fence_after();
@@ -209,7 +213,8 @@ __global__ void __launch_bounds__(kThreads, 2) conv_gemm_tc_ord_kernel(OrdParams
         for (int j = 0; j < 2; ++j) {
             const int gk = 2 * sc + j;
             if (gk >= GK) break;
-            if (kFold && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
+            if (kFold && gk == next_fold) {  // a tap's chain ends: fold it, start the next from 0
+                next_fold += G;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
                     sacc[kFold ? i : 0] = add2(sacc[kFold ? i : 0], acc[i]);
@@ -1001,6 +1006,7 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
         for (int i = 0; i < (kFold ? 16 : 1); ++i) sacc[i] = dup2(0.0f);
         for (int t = 0; t < my_tiles; ++t) {
             bool ok = !*abort_flag;
+            int next_fold = G;  // the group index at which the current tap's chain ends
             for (int sc = 0; sc < S; ++sc) {
                 const int gs = t * S + sc, slot = gs % kWsSlots, buf = gs & 1;
                 if (live && ok) {
@@ -1018,7 +1024,8 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
                     for (int j = 0; j < 2; ++j) {
                         const int gk = 2 * sc + j;
                         if (gk >= GK) break;
-                        if (kFold && gk > 0 && gk % G == 0) {  // a tap's chain ends: fold it, start the next from 0
+                        if (kFold && gk == next_fold) {  // a tap's chain ends: fold it, start the next from 0
+                            next_fold += G;
 #pragma unroll
                             for (int i = 0; i < 16; ++i) {
                                 sacc[kFold ? i : 0] = add2(sacc[kFold ? i : 0], acc[i]);
