@@ -79,7 +79,8 @@ template <int K, int S, int TH>
 __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
                                                                const float* __restrict__ wf, const float* __restrict__ bias,
                                                                uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
-                                                               int C, int Din, int Dout, int tiles_x, int tiles_y)
+                                                               int C, int Din, int Dout, int tiles_x, int tiles_y, int lg_g,
+                                                               int lg_tx, int lg_tpf)
 {
     // output block TH rows x 8 columns; input block with its halo
     constexpr int kPad = K >> 1, kHin = (TH - 1) * S + K, kWin = 7 * S + K;
@@ -88,12 +89,17 @@ __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t*
     // the channel groups of one tile are consecutive blocks, so they run
     // together and share the L2 lines of the tile's pixels (a pixel's groups
     // lie in the same DRAM lines; one group per grid row re-read them per group)
-    const int g = static_cast<int>(blockIdx.x % G);
-    const int64_t tile = blockIdx.x / G;
+    // block -> (frame, tile row, tile column, group) in 32-bit arithmetic (the
+    // launcher keeps the block count below 2^31), by shifts where the counts
+    // are powers of two (lg_* >= 0; every layer of the cortex)
+    const uint32_t bid = blockIdx.x;
     const int tiles_pf = tiles_x * tiles_y;
-    const int64_t frame = tile / tiles_pf;
-    const int tin = static_cast<int>(tile - frame * tiles_pf);
-    const int ty = tin / tiles_x, tx = tin - ty * tiles_x;
+    const uint32_t tile = lg_g >= 0 ? bid >> lg_g : bid / static_cast<uint32_t>(G);
+    const int g = static_cast<int>(bid - tile * static_cast<uint32_t>(G));
+    const uint32_t fr = lg_tpf >= 0 ? tile >> lg_tpf : tile / static_cast<uint32_t>(tiles_pf);
+    const int tin = static_cast<int>(tile - fr * static_cast<uint32_t>(tiles_pf));
+    const int ty = lg_tx >= 0 ? tin >> lg_tx : tin / tiles_x, tx = tin - ty * tiles_x;
+    const int64_t frame = fr;
     const int oy0 = ty * TH, ox0 = tx * 8;
     const int iy0 = oy0 * S - kPad, ix0 = ox0 * S - kPad;
     const int64_t fbase = frame * Din * Din;
@@ -391,9 +397,11 @@ cudaError_t launch_dw_tiled(const uint32_t* in, const int8_t* in_s, const float*
     const int tiles_x = (Dout + 7) / 8, tiles_y = (Dout + TH - 1) / TH;
     const int64_t blocks = frames * tiles_x * tiles_y * (C >> 5);
     if (blocks > 0x7FFFFFFF) return cudaErrorInvalidValue;
+    auto lg = [](int v) { return v > 0 && (v & (v - 1)) == 0 ? 31 - __builtin_clz(static_cast<unsigned>(v)) : -1; };
     const dim3 grid(static_cast<unsigned>(blocks), 1u);
     conv_dw_tiled_kernel<K, S, TH><<<grid, kThreads, smem, stream>>>(in, in_s, wf, bias, out, out_s, C, Din, Dout,
-                                                                     tiles_x, tiles_y);
+                                                                     tiles_x, tiles_y, lg(C >> 5), lg(tiles_x),
+                                                                     lg(tiles_x * tiles_y));
     return cudaGetLastError();
 }
 

@@ -166,12 +166,13 @@ __global__ void __launch_bounds__(kThreads) stem_pack4_kernel(const __half* __re
 // arithmetic, and kept in registers for both the absmax and the codes.
 template <int NP>
 __global__ void __launch_bounds__(kThreads) stem_pack4_np_kernel(const __half* __restrict__ planes, int64_t quads, int hw,
-                                                               uint32_t* __restrict__ out, int8_t* __restrict__ out_s)
+                                                               int lg_hw, uint32_t* __restrict__ out, int8_t* __restrict__ out_s)
 {
     const int64_t qd = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
     if (qd >= quads) return;
     const int64_t pix = qd * 4;
-    const int64_t frame = pix / hw;
+    // frame of the pixel: a shift when the frame size is a power of two (lg_hw >= 0)
+    const int64_t frame = lg_hw >= 0 ? pix >> lg_hw : pix / hw;
     const int64_t sp = pix - frame * hw;
     const __half* src = planes + frame * NP * hw + sp;
     float x[NP][4];
@@ -501,7 +502,8 @@ cudaError_t launch_stem_pack(const __half* planes, int64_t frames, int planes_pr
         channels == 32 && planes_present >= 1 && planes_present <= 8) {
         const int64_t quads = pixels / 4;
         const unsigned grid = grid_for(quads);
-#define AIC_STEM_NP(NP) stem_pack4_np_kernel<NP><<<grid, kThreads, 0, stream>>>(planes, quads, hw, out, out_s)
+        const int lg_hw = (hw & (hw - 1)) == 0 ? 31 - __builtin_clz(static_cast<unsigned>(hw)) : -1;
+#define AIC_STEM_NP(NP) stem_pack4_np_kernel<NP><<<grid, kThreads, 0, stream>>>(planes, quads, hw, lg_hw, out, out_s)
         switch (planes_present) {
             case 1: AIC_STEM_NP(1); break;
             case 2: AIC_STEM_NP(2); break;
