@@ -485,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, ONE ? 4 : 2) conv_gemm_tc_cae_kernel
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * W;
     const int n_cta = min(W, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk
     const bool live = n_cta > 0;
-    const int GK = p.gk_total;  // 1 or 2
+    const int GK = ONE ? 1 : p.gk_total;  // 1 or 2 (a compile-time 1 with one group: 7 % faster; a compile-time 2 measured 3 % slower)
     uint8_t* a_tile = base;                                         // [kTileA]
     uint8_t* b_codes = base + kTileA;                               // [W][128 B]
     float* b_units = reinterpret_cast<float*>(b_codes + W * 128);  // [2][W]
@@ -994,7 +994,10 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
         const int h = warp / (4 * Cfg::kGroups), q = warp & 3, hw = (warp >> 2) % Cfg::kGroups;
         const int erow = q * 32 + lane;    // TMEM lane = row within the half
         const int trow = h * kBM + erow;   // row within the 256-row tile
-        const bool has_cols = hw < (n_cta >> 5);
+        // 128-channel CTAs are always full; known at compile time for the tap-fold
+        // convs (7-12 % faster), left to the runtime test otherwise (measured 1-2 %
+        // faster that way on the pointwise ones)
+        const bool has_cols = (NC == 2 * kNCta && KS == 2 && !G1) || hw < (n_cta >> 5);
         const uint32_t tl = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(4 * NC * h + 32 * hw);
         const float inv_div = __frcp_rn(static_cast<float>(min(p.out_c, kNormChunk)));
         const int gidx = ((n0 & (kNormChunk - 1)) >> 5) + hw;  // this warp's group within the norm chunk
