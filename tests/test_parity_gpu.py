@@ -640,6 +640,36 @@ def test_tensor_core_conv_vs_reference_order(geo):
 
 
 @pytest.mark.parametrize("geo", [
+    (32, 128, 1, 1, 16, 16),     # chain at the end, one group
+    (64, 256, 1, 1, 16, 16),     # chain at the end, two groups, CTA pairs
+    (128, 512, 1, 1, 12, 12),    # 128-channel warp-specialised CTAs
+    (128, 64, 1, 1, 12, 12),     # 64-channel warp-specialised CTAs
+    (576, 256, 1, 1, 8, 8),      # two-role streaming kernel (9 stages)
+])
+def test_silu_with_overflowing_exp_vs_reference_order(geo):
+    """Biases far below zero (-100 on every other channel) push the SiLU's
+    exp(-x) past the float range (1 + e is infinite, the reciprocal's Newton
+    step needs the clamp to the largest float): every tensor-core conv family
+    bit-identical to the CUDA-core kernel."""
+    cin, cout, k, st, din, dout = geo
+    rng = np.random.default_rng(cin * 11 + cout)
+    frames = 2
+    m, b = W.conv_weights(rng, cin, cout, k, False), W.bias(rng, cout)
+    b[::2] = -100.0
+    layer = A.ConvLayer(cin, cout, k, st, din, dout, disable_activation=False)
+    layer.load_weights(t(m), t(b))
+    x = torch.from_numpy(rng.standard_normal((frames * din * din * cin,)).astype(np.float32)).to(DEV)
+    xw, xs = A.pack_f32(x)
+    rows = frames * dout * dout
+    ow, os_ = A.empty_f(rows, cout)
+    ew, es = A.empty_f(rows, cout)
+    layer.forward_exact(xw, xs, ew, es, frames)
+    layer.forward(xw, xs, ow, os_, frames)
+    assert_f_equal(ow, h(os_), u32(ew), h(es), f"ordered vs CUDA cores, overflowing SiLU {geo}")
+    assert_no_device_error()
+
+
+@pytest.mark.parametrize("geo", [
     (32, 128, 1, 1, 8, 8, 1),    # chain at the end, one group
     (64, 128, 1, 1, 8, 8, 0),    # chain at the end, two groups
     (512, 256, 1, 1, 4, 4, 0),   # 128-channel CTA pair, 16 groups
