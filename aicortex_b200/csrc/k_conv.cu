@@ -75,15 +75,19 @@ __global__ void __launch_bounds__(kThreads) conv_dw_kernel(const uint32_t* __res
 // the bias in order and packs the 32-channel group across 8 lanes. Pixel
 // quads are stored XOR-swizzled so both the staging stores and the tap loads
 // are bank-conflict free.
-template <int K, int S, int TH>
+// CC, DIN: the channel count and input size when known at compile time (0:
+// taken from the arguments); the cortex's layers each have their own.
+template <int K, int S, int TH, int CC = 0, int DIN = 0>
 __global__ void __launch_bounds__(kThreads) conv_dw_tiled_kernel(const uint32_t* __restrict__ in, const int8_t* __restrict__ in_s,
                                                                const float* __restrict__ wf, const float* __restrict__ bias,
                                                                uint32_t* __restrict__ out, int8_t* __restrict__ out_s,
-                                                               int C, int Din, int Dout, int tiles_x, int tiles_y, int lg_g,
-                                                               int lg_tx, int lg_tpf)
+                                                               int C_arg, int Din_arg, int Dout_arg, int tiles_x, int tiles_y,
+                                                               int lg_g, int lg_tx, int lg_tpf)
 {
     // output block TH rows x 8 columns; input block with its halo
     constexpr int kPad = K >> 1, kHin = (TH - 1) * S + K, kWin = 7 * S + K;
+    constexpr int DOUT = DIN ? (DIN + 2 * kPad - K) / S + 1 : 0;
+    const int C = CC ? CC : C_arg, Din = DIN ? DIN : Din_arg, Dout = DIN ? DOUT : Dout_arg;
     extern __shared__ float4 xs[];  // [kHin * kWin][8] float4, quad q of pixel i at i * 8 + (q ^ (i & 7))
     const int G = C >> 5;
     // the channel groups of one tile are consecutive blocks, so they run
@@ -383,15 +387,15 @@ cudaError_t launch_dw_weights(const uint32_t* w, const int8_t* w_s, int64_t n, f
     return cudaGetLastError();
 }
 
-template <int K, int S, int TH = 8>
+template <int K, int S, int TH = 8, int CC = 0, int DIN = 0>
 cudaError_t launch_dw_tiled(const uint32_t* in, const int8_t* in_s, const float* wf, const float* bias, uint32_t* out,
                             int8_t* out_s, int64_t frames, int C, int Din, int Dout, cudaStream_t stream)
 {
     constexpr int kHin = (TH - 1) * S + K, kWin = 7 * S + K;
     const size_t smem = static_cast<size_t>(kHin) * kWin * 8 * sizeof(float4);
     if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(conv_dw_tiled_kernel<K, S, TH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(smem));
+        cudaError_t e = cudaFuncSetAttribute(conv_dw_tiled_kernel<K, S, TH, CC, DIN>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         if (e != cudaSuccess) return e;
     }
     const int tiles_x = (Dout + 7) / 8, tiles_y = (Dout + TH - 1) / TH;
@@ -399,9 +403,9 @@ cudaError_t launch_dw_tiled(const uint32_t* in, const int8_t* in_s, const float*
     if (blocks > 0x7FFFFFFF) return cudaErrorInvalidValue;
     auto lg = [](int v) { return v > 0 && (v & (v - 1)) == 0 ? 31 - __builtin_clz(static_cast<unsigned>(v)) : -1; };
     const dim3 grid(static_cast<unsigned>(blocks), 1u);
-    conv_dw_tiled_kernel<K, S, TH><<<grid, kThreads, smem, stream>>>(in, in_s, wf, bias, out, out_s, C, Din, Dout,
-                                                                     tiles_x, tiles_y, lg(C >> 5), lg(tiles_x),
-                                                                     lg(tiles_x * tiles_y));
+    conv_dw_tiled_kernel<K, S, TH, CC, DIN><<<grid, kThreads, smem, stream>>>(in, in_s, wf, bias, out, out_s, C, Din, Dout,
+                                                                              tiles_x, tiles_y, lg(C >> 5), lg(tiles_x),
+                                                                              lg(tiles_x * tiles_y));
     return cudaGetLastError();
 }
 
@@ -417,10 +421,21 @@ cudaError_t launch_conv_dw(const uint32_t* in, const int8_t* in_s, const float* 
     // very high register counts, so they run direct
     if (ksize == 3 && stride == 1)
         return launch_dw_tiled<3, 1>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
-    if (ksize == 3 && stride == 2 && Dout <= 8)
+    if (ksize == 3 && stride == 2 && Dout <= 8) {
+        if (C == 256 && Din == 16 && Dout == 8)  // the cortex's block 3 (shapes known at compile time)
+            return launch_dw_tiled<3, 2, 8, 256, 16>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
         return launch_dw_tiled<3, 2, 8>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
-    if (ksize == 3 && stride == 2)
+    }
+    if (ksize == 3 && stride == 2) {
+        // the cortex's blocks 0-2 (shapes known at compile time)
+        if (C == 32 && Din == 128 && Dout == 64)
+            return launch_dw_tiled<3, 2, 16, 32, 128>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+        if (C == 64 && Din == 64 && Dout == 32)
+            return launch_dw_tiled<3, 2, 16, 64, 64>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+        if (C == 128 && Din == 32 && Dout == 16)
+            return launch_dw_tiled<3, 2, 16, 128, 32>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
         return launch_dw_tiled<3, 2, 16>(in, in_s, wf, bias, out, out_s, frames, C, Din, Dout, stream);
+    }
     return launch_conv_dw_direct(in, in_s, wf, bias, out, out_s, frames, C, ksize, stride, Din, Dout, stream);
 }
 

@@ -712,8 +712,10 @@ def test_conv_overflow_vs_oracle(geo):
 
 
 @pytest.mark.parametrize("geo", [
-    (32, 3, 2, 128, 64),    # the stack's first block, full 8x8 tiles
+    (32, 3, 2, 128, 64),    # the stack's first block, full 8x8 tiles (each cortex block: compile-time shape)
     (64, 3, 2, 64, 32),
+    (128, 3, 2, 32, 16),
+    (160, 3, 2, 32, 16),    # a shape the compile-time variants do not cover
     (96, 3, 1, 16, 16),     # stride 1, three groups
     (256, 3, 2, 16, 8),
     (32, 3, 2, 8, 4),       # one partial tile
