@@ -758,7 +758,10 @@ struct WsCfg {
 __host__ __device__ constexpr int ws_slots(int ks, int nc) { return ks == 1 && nc == 128 ? 4 : 3; }
 constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
 
-template <int KS, int CS, bool ACT, bool G1, int ROWS, int NC>
+// GV: the input's 32-channel groups per tap when known at compile time (0:
+// from the arguments); it fixes the stage count and the tap boundaries, so the
+// consumers' stage loop unrolls with its folds resolved.
+template <int KS, int CS, bool ACT, bool G1, int ROWS, int NC, int GV = 0>
 __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kernel(OrdParams p)
 {
     using Cfg = WsCfg<ROWS, NC>;
@@ -770,7 +773,8 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
     const int n0 = static_cast<int>(blockIdx.y / CS) * kNormChunk + static_cast<int>(blockIdx.y % CS) * NC;
     const int n_cta = min(NC, p.out_c - n0);  // <= 0: a CTA past the end of a narrow chunk (NC = 64 only)
     const bool live = n_cta > 0;
-    const int S = p.stages, GK = p.gk_total, G = p.in_c >> 5;
+    constexpr int kGkFixed = GV * KS * KS, kStagesFixed = (kGkFixed + 1) / 2;
+    const int S = GV ? kStagesFixed : p.stages, GK = GV ? kGkFixed : p.gk_total, G = GV ? GV : p.in_c >> 5;
     uint8_t* a_slots = base;                                                   // [slot][half][kTileA]
     uint8_t* b_codes = a_slots + kWsSlots * kWsHalves * kTileA;                        // [stage][n_max][128 B]
     float* b_units = reinterpret_cast<float*>(b_codes + S * p.n_max * 128);   // [stage][2][n_max]
@@ -1010,6 +1014,7 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
         for (int t = 0; t < my_tiles; ++t) {
             bool ok = !*abort_flag;
             int next_fold = G;  // the group index at which the current tap's chain ends
+#pragma unroll(GV ? kStagesFixed : 1)
             for (int sc = 0; sc < S; ++sc) {
                 const int gs = t * S + sc, slot = gs % kWsSlots, buf = gs & 1;
                 if (live && ok) {
@@ -1228,16 +1233,17 @@ cudaError_t launch_ord_cs(const OrdParams& p, size_t smem, cudaStream_t stream)
     return launch_ord<KS, 4>(q, smem, chunks, stream);
 }
 
-template <int KS, int CS, int ROWS, int NC = kNCta>
+template <int KS, int CS, int ROWS, int NC = kNCta, int GV = 0>
 cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
 {
     using Cfg = WsCfg<ROWS, NC>;
-    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false, ROWS, NC>
-                      : conv_gemm_tc_ws_kernel<KS, CS, false, false, ROWS, NC>;
+    if (GV && p.in_c != 32 * GV) return cudaErrorInvalidValue;
+    auto kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, false, ROWS, NC, GV>
+                      : conv_gemm_tc_ws_kernel<KS, CS, false, false, ROWS, NC, GV>;
     if constexpr (KS == 2 && NC == kNCta) {
         if (p.in_c == 32)  // one group per tap
-            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true, ROWS, NC>
-                         : conv_gemm_tc_ws_kernel<KS, CS, false, true, ROWS, NC>;
+            kern = p.act ? conv_gemm_tc_ws_kernel<KS, CS, true, true, ROWS, NC, GV>
+                         : conv_gemm_tc_ws_kernel<KS, CS, false, true, ROWS, NC, GV>;
     }
     if (NC != kNCta && (p.out_c % NC != 0 || p.n_max != NC || (KS == 2 && p.in_c == 32)))
         return cudaErrorNotSupported;  // 128-channel CTAs: full chunks only, no one-group-per-tap form
@@ -1306,6 +1312,8 @@ cudaError_t launch_ws_cs(const OrdParams& p, cudaStream_t stream)
         if (p.in_c > 32)
             return cs == 1 ? launch_ws<KS, 1, 2 * kBM>(p, chunks, stream) : launch_ws<KS, 2, 2 * kBM>(p, chunks, stream);
     }
+    // the cortex's block-0 layers with their group count fixed at compile time
+    if (cs == 1 && p.in_c == (KS == 1 ? 128 : 32)) return launch_ws<KS, 1, kBM, kNCta, KS == 1 ? 4 : 1>(p, chunks, stream);
     return cs == 1 ? launch_ws<KS, 1, kBM>(p, chunks, stream) : launch_ws<KS, 2, kBM>(p, chunks, stream);
 }
 
@@ -1315,8 +1323,18 @@ template <int KS>
 cudaError_t launch_ws_wide(const OrdParams& p, cudaStream_t stream)
 {
     const unsigned chunks = static_cast<unsigned>((p.out_c + kNormChunk - 1) / kNormChunk);
-    return p.out_c >= kNormChunk ? launch_ws<KS, 2, kBM, 2 * kNCta>(p, chunks, stream)
-                                 : launch_ws<KS, 1, kBM, 2 * kNCta>(p, chunks, stream);
+    constexpr int N = 2 * kNCta;
+    const bool pair = p.out_c >= kNormChunk;
+    // the cortex's layers with their group count fixed at compile time
+    if constexpr (KS == 1) {
+        if (p.in_c == 256 && pair) return launch_ws<1, 2, kBM, N, 8>(p, chunks, stream);
+        if (p.in_c == 128 && pair) return launch_ws<1, 2, kBM, N, 4>(p, chunks, stream);
+        if (p.in_c == 512 && pair) return launch_ws<1, 2, kBM, N, 16>(p, chunks, stream);
+    } else {
+        if (p.in_c == 64 && !pair) return launch_ws<2, 1, kBM, N, 2>(p, chunks, stream);
+        if (p.in_c == 128 && pair) return launch_ws<2, 2, kBM, N, 4>(p, chunks, stream);
+    }
+    return pair ? launch_ws<KS, 2, kBM, N>(p, chunks, stream) : launch_ws<KS, 1, kBM, N>(p, chunks, stream);
 }
 
 }  // namespace
