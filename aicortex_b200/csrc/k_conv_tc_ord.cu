@@ -756,7 +756,8 @@ struct WsCfg {
 // faster on the 512 -> 256 layer with 8 stages per tile; equal or slower on
 // the 2x2 convs, whose shared memory the fold's shapes need elsewhere)
 __host__ __device__ constexpr int ws_slots(int ks, int nc) { return ks == 1 && nc == 128 ? 4 : 3; }
-constexpr int kWsMaxStages = 4;  // stages per tile up to which the warp-specialised kernel is used
+constexpr int kWsMaxStages = 4;
+constexpr int kWsCodeSlots = 4;  // ring of weight-code stages when a tile's stages do not all stay resident  // stages per tile up to which the warp-specialised kernel is used
 
 // GV: the input's 32-channel groups per tap when known at compile time (0:
 // from the arguments); it fixes the stage count and the tap boundaries, so the
@@ -775,9 +776,13 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
     const bool live = n_cta > 0;
     constexpr int kGkFixed = GV * KS * KS, kStagesFixed = (kGkFixed + 1) / 2;
     const int S = GV ? kStagesFixed : p.stages, GK = GV ? kGkFixed : p.gk_total, G = GV ? GV : p.in_c >> 5;
+    // More stages than stay resident (128-channel CTAs only): the weight codes
+    // stream through a ring of kWsCodeSlots stages; the units stay resident.
+    const bool stream_w = S > kResidentStages;
+    const int code_stages = stream_w ? kWsCodeSlots : S;
     uint8_t* a_slots = base;                                                   // [slot][half][kTileA]
-    uint8_t* b_codes = a_slots + kWsSlots * kWsHalves * kTileA;                        // [stage][n_max][128 B]
-    float* b_units = reinterpret_cast<float*>(b_codes + S * p.n_max * 128);   // [stage][2][n_max]
+    uint8_t* b_codes = a_slots + kWsSlots * kWsHalves * kTileA;                        // [stage or ring slot][n_max][128 B]
+    float* b_units = reinterpret_cast<float*>(b_codes + code_stages * p.n_max * 128);  // [stage][2][n_max]
     float* din_s = b_units + S * 2 * p.n_max;                                 // [slot][2 groups][kWsRows]
     float* bias_s = din_s + kWsSlots * 2 * kWsRows;                           // [NC]
     float* part = bias_s + NC;                                                // [2 tiles][8][kWsRows]
@@ -788,7 +793,9 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
     uint64_t* full_acc = empty + kWsSlots;         // [buf] the stage's MMAs completed
     uint64_t* part_full = full_acc + 2;        // [tile & 1] the chunk's sums of squares arrived
     uint64_t* drain = part_full + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* code_full = drain + 1;               // [ring slot] a stage's codes landed (streamed weights)
+    uint64_t* code_free = code_full + kWsCodeSlots;  // [ring slot] the MMAs reading the slot completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(code_free + kWsCodeSlots);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -805,6 +812,10 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
             mbar_init(smem_addr(&part_full[i]), CS * kWsConsumerWarps);
         }
         mbar_init(smem_addr(drain), 1);
+        for (int i = 0; i < kWsCodeSlots; ++i) {
+            mbar_init(smem_addr(&code_full[i]), 1);
+            mbar_init(smem_addr(&code_free[i]), 1);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -831,6 +842,32 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
             const int stage_bytes = n_cta * kImgRow;
             const uint8_t* wimg = p.wimg + static_cast<int64_t>(n0) * S * kImgRow;
             const uint32_t idesc = instr_desc_h(n_cta);
+            // streamed codes: stage k's codes of both 64-channel image chunks into
+            // ring slot ws, completing on code_full[ws]
+            auto fetch_codes = [&](int k, int ws) {
+                mbar_expect_tx(smem_addr(&code_full[ws]), static_cast<uint32_t>(n_cta * 128));
+                for (int hn = 0; hn < NC / kNCta; ++hn) {
+                    const uint8_t* img = p.wimg + static_cast<int64_t>(n0 + hn * kNCta) * S * kImgRow +
+                                         static_cast<int64_t>(k) * kNCta * kImgRow;
+                    bulk_g2s(smem_addr(b_codes + (ws * p.n_max + hn * kNCta) * 128), img, kNCta * 128u,
+                             smem_addr(&code_full[ws]));
+                }
+            };
+            int fills = 0;  // code stages fetched into the ring (streamed weights)
+            if (stream_w) {
+                // units of every stage once; the first kWsCodeSlots stages' codes
+                mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * n_cta * 8));
+                for (int hn = 0; hn < NC / kNCta; ++hn) {
+                    const uint8_t* wimg_h = p.wimg + static_cast<int64_t>(n0 + hn * kNCta) * S * kImgRow;
+                    for (int k = 0; k < S; ++k)
+#pragma unroll
+                        for (int j = 0; j < 2; ++j)
+                            bulk_g2s(smem_addr(b_units + (k * 2 + j) * p.n_max + hn * kNCta),
+                                     wimg_h + static_cast<int64_t>(k) * kNCta * kImgRow + kNCta * 128 + j * kNCta * 4,
+                                     kNCta * 4u, smem_addr(&full_b[0]));
+                }
+                for (; fills < kWsCodeSlots && fills < total; ++fills) fetch_codes(fills % S, fills);
+            } else {
             mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
             if constexpr (NC == kNCta) {
                 for (int k = 0; k < S; ++k) {
@@ -857,18 +894,22 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
                     }
                 }
             }
-            int sp = 0;
+            }
+            int sp = 0, landed = 0;  // landed: ring fills whose codes were awaited
             for (int gs = 0; gs < total; ++gs) {
-                const int slot = gs % kWsSlots, buf = gs & 1;
+                const int slot = gs % kWsSlots, buf = gs & 1, ws = gs % kWsCodeSlots;
                 // staged; weights landed; TMEM buffer free once the consumers ran the chain of gs - 2
                 bool ok = !*abort_flag &&
                           mbar_wait(smem_addr(&staged[slot]), static_cast<uint32_t>(gs / kWsSlots) & 1u, p.err, 39) &&
                           (gs > 0 || mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 32)) &&
                           (gs < 2 || mbar_wait(smem_addr(&empty[(gs - 2) % kWsSlots]),
-                                               static_cast<uint32_t>((gs - 2) / kWsSlots) & 1u, p.err, 33));
+                                               static_cast<uint32_t>((gs - 2) / kWsSlots) & 1u, p.err, 33)) &&
+                          (!stream_w ||
+                           mbar_wait(smem_addr(&code_full[ws]), static_cast<uint32_t>(gs / kWsCodeSlots) & 1u, p.err, 46));
+                if (ok && stream_w) landed = gs + 1;
                 if (ok) {
                     tc_fence_after();
-                    const uint64_t db = smem_desc(smem_addr(b_codes + sp * p.n_max * 128));
+                    const uint64_t db = smem_desc(smem_addr(b_codes + (stream_w ? ws : sp) * p.n_max * 128));
                     const int n_mma = 2 * sp + 1 < GK ? kBK / 16 : kBK / 32;
 #pragma unroll
                     for (int hh = 0; hh < kWsHalves; ++hh) {
@@ -880,14 +921,28 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
                                         da + 16 * j, db + 2 * j, idesc, static_cast<uint32_t>(j & 1));
                     }
                     mma_commit(smem_addr(&full_acc[buf]));
+                    if (stream_w) mma_commit(smem_addr(&code_free[ws]));  // the slot's MMAs completed
                 } else {
                     *abort_flag = 1;
                 }
+                // streamed codes: once the MMAs of stage gs - 1 completed, its ring slot
+                // takes the stage kWsCodeSlots further on
+                if (stream_w && ok && gs >= 1 && fills < total) {
+                    const int wf = (gs - 1) % kWsCodeSlots;
+                    if (mbar_wait(smem_addr(&code_free[wf]), static_cast<uint32_t>((gs - 1) / kWsCodeSlots) & 1u, p.err, 47)) {
+                        fetch_codes(fills % S, wf);
+                        ++fills;
+                    } else {
+                        *abort_flag = 1;
+                    }
+                }
                 if (++sp == S) sp = 0;
             }
-            // every MMA issued has completed (and the weight copy landed) before TMEM is released
-            // (a timeout records 37 / 34; the drain gets a second bounded window, as above)
+            // every MMA issued has completed (and the weight copies landed) before TMEM is released
+            // (a timeout records 37 / 48 / 34; the drain gets a second bounded window, as above)
             mbar_wait(smem_addr(&full_b[0]), 0u, p.err, 37);
+            for (int f = landed; f < fills; ++f)  // ring fills not awaited after an abort
+                mbar_wait(smem_addr(&code_full[f % kWsCodeSlots]), static_cast<uint32_t>(f / kWsCodeSlots) & 1u, p.err, 48);
             mma_commit(smem_addr(drain));
             if (!mbar_wait(smem_addr(drain), 0u, p.err, 34)) mbar_wait(smem_addr(drain), 0u, p.err, 34);
         }
@@ -1254,13 +1309,17 @@ cudaError_t launch_ws(const OrdParams& p, unsigned chunks, cudaStream_t stream)
     cudaError_t e = cudaFuncGetAttributes(&fa, kern);
     if (e != cudaSuccess) return e;
     if (fa.numRegs != Cfg::kLaunchRegs) return cudaErrorNotSupported;
-    if (p.stages > kResidentStages) return cudaErrorNotSupported;  // the weights must stay resident
+    // 64-channel CTAs keep every stage's weights resident; 128-channel CTAs
+    // stream the codes of longer layers through a ring (the units stay resident)
+    const bool stream_w = p.stages > kResidentStages;
+    if (stream_w && NC == kNCta) return cudaErrorNotSupported;
     if (p.rows * KS * KS > 0x7FFFFFFFll) return cudaErrorNotSupported;  // input pixel indices are 32-bit
     constexpr int kWsSlots = ws_slots(KS, NC);
     const size_t smem = 1024 + static_cast<size_t>(kWsSlots) * Cfg::kHalves * kTileA +
-                        static_cast<size_t>(p.stages) * p.n_max * kImgRow +
+                        static_cast<size_t>(stream_w ? kWsCodeSlots : p.stages) * p.n_max * 128 +
+                        static_cast<size_t>(p.stages) * p.n_max * 8 +
                         (static_cast<size_t>(kWsSlots) * 2 * ROWS + NC + 16 * ROWS) * sizeof(float) +
-                        (2 * kWsSlots + 6) * 8 + 16;
+                        (2 * kWsSlots + 6 + 2 * kWsCodeSlots) * 8 + 16;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
@@ -1433,10 +1492,11 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // norm clusters of up to two CTAs (two 128-row CTAs per SM: 15-19 % on the
     // block-0 layers of the cortex); on clusters of four it is equal or slower,
     // and longer K needs more resident weights than two CTAs' shared memory holds
-    // 128-channel CTAs where the channels come in whole 128-channel CTAs and
-    // every stage's weights stay resident: the staged A tile serves twice the
-    // channels, and a 256-channel norm chunk is a cluster of two
-    if (p.out_c % (2 * kNCta) == 0 && p.stages <= kResidentStages && !one_group_taps) {
+    // 128-channel CTAs where the channels come in whole 128-channel CTAs: the
+    // staged A tile serves twice the channels, and a 256-channel norm chunk is
+    // a cluster of two (weights resident up to kResidentStages stages per tile,
+    // the codes of longer layers streamed through a ring)
+    if (p.out_c % (2 * kNCta) == 0 && !one_group_taps) {
         OrdParams w = p;
         w.n_max = 2 * kNCta;
         const cudaError_t e = ksize == 1 ? launch_ws_wide<1>(w, stream) : launch_ws_wide<2>(w, stream);

@@ -600,7 +600,7 @@ def test_cortex_small_vs_oracle():
     (128, 256, 2, 2, 32, 16, 0),    # shortcut conv 2x2 / stride 2, 128-channel CTA pair, tap fold
     (32, 64, 4, 4, 64, 16, 0),      # patcher conv 4x4 / stride 4
     (160, 96, 2, 2, 16, 8, 1),
-    (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps (16 stages: two-role kernel, clusters of 4)
+    (256, 256, 2, 2, 16, 8, 0),     # 32 groups over 4 taps (16 stages: 128-channel CTAs, weight codes streamed)
     (32, 64, 2, 2, 32, 16, 1),      # one group per tap
     (128, 64, 1, 1, 12, 12, 0),     # warp-specialised, 128-row tiles: 288 rows, a partial tile
     (256, 128, 1, 1, 10, 10, 1),    # 128-channel CTA, 200 rows, SiLU
@@ -636,6 +636,27 @@ def test_tensor_core_conv_vs_reference_order(geo):
     # fp32 summation order only: a code flips where the value sits within a
     # few ulp of a rounding boundary
     assert_f_close(ow, h(os_), ew, h(es), flip_rate=1e-4, what=f"fast vs CUDA cores {geo}")
+    assert_no_device_error()
+
+
+def test_streamed_weight_codes_over_many_tiles():
+    """A 2x2 conv with 16 stages per tile (the codes of its weights stream
+    through a ring of 4 stages) over 160 frames, so every CTA runs two tiles
+    and the ring wraps across the tile boundary: bit-identical to the
+    CUDA-core kernel."""
+    cin, cout, din, dout, frames = 256, 256, 16, 8, 160
+    rng = np.random.default_rng(4242)
+    m, b = W.conv_weights(rng, cin, cout, 2, False), W.bias(rng, cout)
+    layer = A.ConvLayer(cin, cout, 2, 2, din, dout, disable_activation=True)
+    layer.load_weights(t(m), t(b))
+    x = torch.from_numpy(rng.standard_normal((frames * din * din * cin,)).astype(np.float32)).to(DEV)
+    xw, xs = A.pack_f32(x)
+    rows = frames * dout * dout
+    ow, os_ = A.empty_f(rows, cout)
+    ew, es = A.empty_f(rows, cout)
+    layer.forward_exact(xw, xs, ew, es, frames)
+    layer.forward(xw, xs, ow, os_, frames)
+    assert_f_equal(ow, h(os_), u32(ew), h(es), "streamed weight codes, 160 frames")
     assert_no_device_error()
 
 
