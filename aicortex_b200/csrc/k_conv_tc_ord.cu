@@ -103,9 +103,9 @@ __device__ __forceinline__ float tree_sq32(const float (&a)[32])
     return t[0];
 }
 
-// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j) in
-// scalar arithmetic: fewer live registers than the pair form below.
-__device__ __forceinline__ float tree_sq32x2_scalar(const float2 (&a)[16])
+// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j), in
+// scalar arithmetic (a square feeding a sum must not be fused).
+__device__ __forceinline__ float tree_sq32x2(const float2 (&a)[16])
 {
     float f[32];
 #pragma unroll
@@ -114,25 +114,6 @@ __device__ __forceinline__ float tree_sq32x2_scalar(const float2 (&a)[16])
         f[2 * i + 1] = a[i].y;
     }
     return tree_sq32(f);
-}
-
-// tree_sq32 over 32 values held as 16 pairs (value 2i + j in a[i].j), on
-// pairs: each square is fma(a, a, -0), the rounded square itself (adding -0
-// changes no value, and a zero square stays +0 as __fmul_rn gives it), so the
-// sums that follow add rounded squares as the reference does; a plain pair
-// multiply feeding a pair add would be fused into one rounding. Value i and
-// value i + 16 sit in the same lane of pairs k and k + 8, so every level of
-// the tree but the last is one pair add per two sums, in the reference's order.
-__device__ __forceinline__ float tree_sq32x2(const float2 (&a)[16])
-{
-    float2 t[8];  // the first level formed as the squares are, so no more than 8 pairs are live
-#pragma unroll
-    for (int i = 0; i < 8; ++i) t[i] = add2(fma2(a[i], a[i], dup2(-0.0f)), fma2(a[i + 8], a[i + 8], dup2(-0.0f)));
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1)
-#pragma unroll
-        for (int i = 0; i < o; ++i) t[i] = add2(t[i], t[i + o]);
-    return __fadd_rn(t[0].x, t[0].y);
 }
 
 // TMEM columns: per-group accumulators of n channels, double buffered over
@@ -1156,10 +1137,7 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
                 for (int i = 0; i < 16; ++i) acc[i] = add2(sacc[kFold ? i : 0], acc[i]);
             }
             if (emit) {
-                // the pair-arithmetic tree, except where its live registers spill (64-channel CTAs
-                // with several groups per output, and the generic tap-fold shape of 128-channel CTAs)
-                constexpr bool kScalarTree = (NC == kNCta && !G1) || (NC == 2 * kNCta && KS == 2 && !G1 && GV == 0);
-                const float gs2 = kScalarTree ? tree_sq32x2_scalar(acc) : tree_sq32x2(acc);
+                const float gs2 = tree_sq32x2(acc);
                 float* dst = &part_t[gidx * kWsRows + trow];
                 if (CS > 1) {
 #pragma unroll
