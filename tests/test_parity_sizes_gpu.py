@@ -130,3 +130,35 @@ def test_mamba_layer_long_sequence_sample_vs_oracle():
     layer.forward(t(xw.view(np.int32)), t(xs), out, B, T)
     assert max_rel(h(out), o_ref) <= RTOL, max_rel(h(out), o_ref)
     assert max_rel(h(layer.state_tensor()), ref.h) <= RTOL
+
+
+def test_cortex_multi_tile_ctas_vs_cuda_cores():
+    """The full cortex at its real dimensions in 256-frame conv chunks (B=8 x
+    T=32), so that every tensor-core conv CTA runs a long run of row tiles
+    (2 to 14 per CTA) as in the benchmark's large launches: features, actor
+    and critic of AIC_CONV_ORDERED bit-identical to AIC_CONV_SIMT. Rare
+    one-step code flips only show up over this many outputs."""
+    B, T = 8, 32
+    desc = W.cortex_desc(batch_chunk=256)
+    wts = W.cortex_weights(5)
+    planes = W.planes_u01(np.random.default_rng(41), B * T)
+    cx = A.Cortex(desc)
+    for blk, layers in zip(cx.blocks, wts["blocks"]):
+        for lay, (m, b) in zip(blk.layers, layers):
+            lay.load_weights(t(m), t(b))
+    for u, (m, b) in zip(cx.units, wts["units"]):
+        u.load_weights(t(m), t(b))
+    cx.actor.load_weights(t(wts["actor"][0]), t(wts["actor"][1]))
+    cx.critic.load_weights(*(t(a) for a in wts["critic"]))
+    cx.bind_state(B)
+    outs = {}
+    for mode in (A.AIC_CONV_ORDERED, A.AIC_CONV_SIMT):
+        cx.set_conv_mode(mode)
+        cx.reset()
+        actor = torch.empty(B * T, 64, dtype=torch.float32, device=DEV)
+        critic = torch.empty(B * T, dtype=torch.float32, device=DEV)
+        fw, fs = A.empty_f(B * T, 256)
+        cx.forward(t(planes), B, T, actor, critic, features=(fw, fs))
+        outs[mode] = (h(fw), h(fs), h(actor), h(critic))
+    for x, y, name in zip(outs[A.AIC_CONV_ORDERED], outs[A.AIC_CONV_SIMT], ("words", "exponents", "actor", "critic")):
+        assert np.array_equal(x, y), f"tensor cores (reference order) vs CUDA cores over multi-tile CTAs: {name} differ"
