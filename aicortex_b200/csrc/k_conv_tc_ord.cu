@@ -756,8 +756,8 @@ struct WsCfg {
 // faster on the 512 -> 256 layer with 8 stages per tile; equal or slower on
 // the 2x2 convs, whose shared memory the fold's shapes need elsewhere)
 __host__ __device__ constexpr int ws_slots(int ks, int nc) { return ks == 1 && nc == 128 ? 4 : 3; }
-constexpr int kWsMaxStages = 4;
-constexpr int kWsCodeSlots = 4;  // ring of weight-code stages when a tile's stages do not all stay resident  // stages per tile up to which the warp-specialised kernel is used
+constexpr int kWsMaxStages = 4;  // stages per tile up to which the 64-channel warp-specialised kernel is used
+constexpr int kWsCodeSlots = 4;  // ring of weight-code stages when a tile's stages do not all stay resident
 
 // GV: the input's 32-channel groups per tap when known at compile time (0:
 // from the arguments); it fixes the stage count and the tap boundaries, so the
@@ -867,33 +867,33 @@ __global__ void __maxnreg__((WsCfg<ROWS, NC>::kLaunchRegs)) conv_gemm_tc_ws_kern
                                      kNCta * 4u, smem_addr(&full_b[0]));
                 }
                 for (; fills < kWsCodeSlots && fills < total; ++fills) fetch_codes(fills % S, fills);
-            } else {
-            mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
-            if constexpr (NC == kNCta) {
-                for (int k = 0; k < S; ++k) {
-                    const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
-                    bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
-                             smem_addr(&full_b[0]));
-                    bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
-                             smem_addr(&full_b[0]));
-                }
-            } else {
-                // the 64-channel image chunks side by side (every chunk of a layer
-                // on this shape is full): codes [stage][NC][128 B], units
-                // [stage][group][NC]
-                for (int hn = 0; hn < NC / kNCta; ++hn) {
-                    const uint8_t* wimg_h = p.wimg + static_cast<int64_t>(n0 + hn * kNCta) * S * kImgRow;
+            } else {  // every stage's codes and units, once
+                mbar_expect_tx(smem_addr(&full_b[0]), static_cast<uint32_t>(S * stage_bytes));
+                if constexpr (NC == kNCta) {
                     for (int k = 0; k < S; ++k) {
-                        const uint8_t* img = wimg_h + static_cast<int64_t>(k) * kNCta * kImgRow;
-                        bulk_g2s(smem_addr(b_codes + (k * p.n_max + hn * kNCta) * 128), img, kNCta * 128u,
+                        const uint8_t* img = wimg + static_cast<int64_t>(k) * stage_bytes;
+                        bulk_g2s(smem_addr(b_codes + k * p.n_max * 128), img, static_cast<uint32_t>(n_cta * 128),
                                  smem_addr(&full_b[0]));
+                        bulk_g2s(smem_addr(b_units + k * 2 * p.n_max), img + n_cta * 128, static_cast<uint32_t>(n_cta * 8),
+                                 smem_addr(&full_b[0]));
+                    }
+                } else {
+                    // the 64-channel image chunks side by side (every chunk of a layer
+                    // on this shape is full): codes [stage][NC][128 B], units
+                    // [stage][group][NC]
+                    for (int hn = 0; hn < NC / kNCta; ++hn) {
+                        const uint8_t* wimg_h = p.wimg + static_cast<int64_t>(n0 + hn * kNCta) * S * kImgRow;
+                        for (int k = 0; k < S; ++k) {
+                            const uint8_t* img = wimg_h + static_cast<int64_t>(k) * kNCta * kImgRow;
+                            bulk_g2s(smem_addr(b_codes + (k * p.n_max + hn * kNCta) * 128), img, kNCta * 128u,
+                                     smem_addr(&full_b[0]));
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)
-                            bulk_g2s(smem_addr(b_units + (k * 2 + j) * p.n_max + hn * kNCta), img + kNCta * 128 + j * kNCta * 4,
-                                     kNCta * 4u, smem_addr(&full_b[0]));
+                            for (int j = 0; j < 2; ++j)
+                                bulk_g2s(smem_addr(b_units + (k * 2 + j) * p.n_max + hn * kNCta), img + kNCta * 128 + j * kNCta * 4,
+                                         kNCta * 4u, smem_addr(&full_b[0]));
+                        }
                     }
                 }
-            }
             }
             int sp = 0, landed = 0;  // landed: ring fills whose codes were awaited
             for (int gs = 0; gs < total; ++gs) {
@@ -1488,10 +1488,6 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
     // the streaming kernel from three on
     if (p.gk_total <= 2)  // only pointwise convs have so few groups (a 2x2 conv has >= 4)
         return launch_cae_pw(p, stream);
-    // measured: the warp-specialised kernel wins up to four stages per tile and
-    // norm clusters of up to two CTAs (two 128-row CTAs per SM: 15-19 % on the
-    // block-0 layers of the cortex); on clusters of four it is equal or slower,
-    // and longer K needs more resident weights than two CTAs' shared memory holds
     // 128-channel CTAs where the channels come in whole 128-channel CTAs: the
     // staged A tile serves twice the channels, and a 256-channel norm chunk is
     // a cluster of two (weights resident up to kResidentStages stages per tile,
@@ -1503,6 +1499,11 @@ cudaError_t launch_conv_gemm_tc_ord(const uint32_t* in, const int8_t* in_s, cons
         if (e != cudaErrorNotSupported) return e;
         (void)cudaGetLastError();  // that build is unusable: the kernels below
     }
+    // 64-channel CTAs otherwise. Measured: the warp-specialised kernel wins up
+    // to four stages per tile and norm clusters of up to two CTAs (two 128-row
+    // CTAs per SM: 15-19 % on the block-0 layers of the cortex); on clusters of
+    // four it is equal or slower, and longer K needs more resident weights than
+    // two CTAs' shared memory holds, so those shapes take the two-role kernel
     const int w_chunk = p.out_c < kNormChunk ? p.out_c : kNormChunk;
     if (p.stages <= kWsMaxStages && w_chunk <= 2 * kNCta) {
         const cudaError_t e = ksize == 1 ? launch_ws_cs<1>(p, stream) : launch_ws_cs<2>(p, stream);
