@@ -5,6 +5,12 @@
     python -m aicortex_b200.kbench layer --d-model 256 --d-state 512 --batch 256 --seq 128
     python -m aicortex_b200.kbench scan --d-model 1024 --d-state 512 --batch 32 --seq 8192
     python -m aicortex_b200.kbench outproj --d-model 1024 --d-state 512 --batch 32 --seq 8192 [--mode exact]
+    python -m aicortex_b200.kbench sweep [--mode fast]
+
+`sweep` runs the packed-operand GEMM sweep M in {4096, 65536, 1048576} x
+K in {256, 1024} x N in {512, 2048, 4096} as pointwise convs (M pixel rows
+= frames x 64 x 64, K input channels, N output channels, the fused RMSNorm,
+bias and requant epilogue), one JSON line per case.
 
 Times `--iters` launches with CUDA events after `--warmup` launches and prints
 one JSON line with the mean time per launch and the algorithmic throughput
@@ -42,7 +48,7 @@ def _f_bytes(n: float) -> float:
 
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["conv", "dw", "layer", "scan", "outproj"])
+    ap.add_argument("kind", choices=["conv", "dw", "layer", "scan", "outproj", "sweep"])
     ap.add_argument("--cin", type=int, default=32)
     ap.add_argument("--cout", type=int, default=128)
     ap.add_argument("--k", type=int, default=1)
@@ -66,24 +72,37 @@ def main(argv=None) -> None:
     def t(x):
         return torch.from_numpy(np.ascontiguousarray(x)).to(dev)
 
-    if a.kind in ("conv", "dw"):
-        k = a.k
-        depthwise = a.kind == "dw"
-        cout = a.cin if depthwise else a.cout
-        stride = a.stride if depthwise else k
-        dout = (a.dim - 1) // stride + 1 if depthwise else a.dim // k
-        layer = L.ConvLayer(a.cin, cout, k, stride, a.dim, dout, disable_activation=not a.act)
-        layer.load_weights(t(W.conv_weights(rng, a.cin, cout, k, depthwise)), t(W.bias(rng, cout)))
-        x = torch.randn(a.frames * a.dim * a.dim * a.cin, device=dev)
+    def conv_case(kind, cin, cout, k, stride, dim, frames, act):
+        depthwise = kind == "dw"
+        cout = cin if depthwise else cout
+        stride = stride if depthwise else k
+        dout = (dim - 1) // stride + 1 if depthwise else dim // k
+        layer = L.ConvLayer(cin, cout, k, stride, dim, dout, disable_activation=not act)
+        layer.load_weights(t(W.conv_weights(rng, cin, cout, k, depthwise)), t(W.bias(rng, cout)))
+        x = torch.randn(frames * dim * dim * cin, device=dev)
         xw, xs = L.pack_f32(x)
         del x
-        ow, os_ = L.empty_f(a.frames * dout * dout, cout, dev)
+        ow, os_ = L.empty_f(frames * dout * dout, cout, dev)
         layer.set_mode({"ordered": 0, "fast": 1, "simt": 2}[a.mode or "ordered"])
         fwd = layer.forward_exact if a.exact else layer.forward
-        ms = _time(lambda: fwd(xw, xs, ow, os_, a.frames), a.iters, a.warmup)
-        rows = a.frames * dout * dout
-        flops = 2.0 * rows * cout * k * k * a.cin if not depthwise else 2.0 * rows * cout * k * k
-        nbytes = _f_bytes(a.frames * a.dim * a.dim * a.cin) + _f_bytes(rows * cout) + _f_bytes(layer.weight_elems)
+        ms = _time(lambda: fwd(xw, xs, ow, os_, frames), a.iters, a.warmup)
+        rows = frames * dout * dout
+        flops = 2.0 * rows * cout * k * k * cin if not depthwise else 2.0 * rows * cout * k * k
+        nbytes = _f_bytes(frames * dim * dim * cin) + _f_bytes(rows * cout) + _f_bytes(layer.weight_elems)
+        return ms, flops, nbytes
+
+    if a.kind == "sweep":
+        for m in (4096, 65536, 1048576):
+            for kk in (256, 1024):
+                for n in (512, 2048, 4096):
+                    ms, flops, nbytes = conv_case("conv", kk, n, 1, 1, 64, m // 4096, False)
+                    print(json.dumps({"kind": "sweep", "M": m, "K": kk, "N": n, "mode": a.mode or "ordered",
+                                      "ms_per_launch": ms, "tflops": flops / ms / 1e9, "gbs": nbytes / ms / 1e6}),
+                          flush=True)
+                    torch.cuda.empty_cache()
+        return
+    if a.kind in ("conv", "dw"):
+        ms, flops, nbytes = conv_case(a.kind, a.cin, a.cout, a.k, a.stride, a.dim, a.frames, a.act)
     else:
         E = 2 * a.d_model
         layer = L.MambaLayer(a.d_model, a.d_state, a.d_model, 1)
